@@ -1,0 +1,122 @@
+/*
+ * infvino_b200 - C ABI of the B200 plan executor (drop-in for infvino's
+ * OpenCL `PlanModel` / `ClBackend`).
+ *
+ * Plain C types only: handles are opaque pointers, tensors are raw pointers plus
+ * element counts, CUDA streams are passed as `void *` (a cudaStream_t).  Every
+ * call returns an ivc_status; the message of the last failure on a handle is
+ * available from ivc_last_error().  Calls on one handle are serialised
+ * internally (as `ClBackend::infer` is, src/ClBackend.cpp:33 in the reference).
+ *
+ * Batching: plans declare batch 1 (dim 0 of every activation).  A handle is
+ * created for `max_batch` images; each call names the batch it processes and
+ * every buffer holds `batch * numel` elements, image-major.
+ *
+ * Reference interfaces each entry point replaces (paths inside the reference):
+ *   ivc_create ............ PlanModel::PlanModel  include/infvino/PlanModel.hpp:57-59
+ *                            ClBackend::ClBackend  include/infvino/ClBackend.hpp:32
+ *   ivc_input_* / output_*  PlanModel::inputName/inputDims/inputNumel/outputCount/
+ *                            outputName/outputDims/outputNumel  PlanModel.hpp:64-73
+ *   ivc_tensor_numel ....... PlanModel::tensorNumel  PlanModel.hpp:85-86
+ *   ivc_infer_f32 .......... ClBackend::infer(const float*, size_t)  ClBackend.hpp:38-39
+ *   ivc_set_input_f16 ...... PlanModel::setInput(const void*)  PlanModel.hpp:75-76
+ *   ivc_run ................ PlanModel::run()  PlanModel.hpp:77-78
+ *   ivc_read_output_f16 .... PlanModel::readOutput(size_t, void*)  PlanModel.hpp:79-80
+ *   ivc_read_tensor_f16 .... PlanModel::readTensor(name, void*)  PlanModel.hpp:82-84
+ *   ivc_last_infer_ms ...... ClBackend::lastInferMs / PlanModel::lastRunMs
+ *                            ClBackend.hpp:41, PlanModel.hpp:190-191
+ *   ivc_profile / ivc_step_* PlanModel::profile() / PlanProfile  PlanModel.hpp:204-224
+ *   ivc_pool_stats ......... PlanModel::poolRequestedBytes/poolAllocatedBytes/
+ *                            poolBufferCount  PlanModel.hpp:94-97
+ *   ivc_infer_f16_device ... (new) zero-copy device-pointer inference on a caller stream
+ *   ivc_destroy ............ PlanModel::~PlanModel / ClBackend destructor
+ */
+#ifndef INFVINO_B200_H_
+#define INFVINO_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ivc_model ivc_model;
+
+typedef enum ivc_status {
+  IVC_OK = 0,
+  IVC_ERR_ARGUMENT = 1,   /* bad pointer / index / batch */
+  IVC_ERR_PLAN = 2,       /* plan parse, missing init, unknown op (reference: std::runtime_error) */
+  IVC_ERR_CUDA = 3,       /* CUDA runtime / device failure */
+  IVC_ERR_NUMEL = 4,      /* input element count does not match the plan */
+  IVC_ERR_KERNEL = 5,     /* a kernel reported a bounded-wait timeout (status word) */
+  IVC_ERR_NOT_FOUND = 6   /* unknown tensor name */
+} ivc_status;
+
+/* creation flags */
+#define IVC_FLAG_NO_GRAPH 0x1u        /* eager launches instead of CUDA graph replay */
+#define IVC_FLAG_NO_FUSION 0x2u       /* skip concat->conv1x1 / residual load-time rewrites */
+#define IVC_FLAG_DRY_RUN 0x4u         /* host only: parse, layout, allocate; no GPU is touched */
+#define IVC_FLAG_NO_TENSOR_CORES 0x8u /* convolutions on the CUDA-core direct kernel (diagnostic) */
+
+/* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
+int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);
+void ivc_destroy(ivc_model *m);
+/* Message of the last failed call on `m`; with m == NULL, of the last failed ivc_create. */
+const char *ivc_last_error(const ivc_model *m);
+
+int ivc_input_name(const ivc_model *m, const char **name);
+int ivc_input_dims(const ivc_model *m, int64_t *dims, int max_rank, int *rank);
+int64_t ivc_input_numel(const ivc_model *m);
+int ivc_output_count(const ivc_model *m);
+int ivc_output_name(const ivc_model *m, int i, const char **name);
+int ivc_output_dims(const ivc_model *m, int i, int64_t *dims, int max_rank, int *rank);
+int64_t ivc_output_numel(const ivc_model *m, int i);
+/* per-image element count of any declared tensor, 0 if unknown */
+int64_t ivc_tensor_numel(const ivc_model *m, const char *name);
+int ivc_max_batch(const ivc_model *m);
+
+/* ClBackend::infer: `input` holds batch*input_numel f32 values (host memory,
+ * pinned or pageable); converted to fp16 with the reference's truncating cast,
+ * run, and every output written as f32 to outputs[i] (batch*output_numel(i)
+ * values, host memory).  Synchronous. */
+int ivc_infer_f32(ivc_model *m, const float *input, size_t numel, int batch, float *const *outputs);
+
+/* PlanModel-style split calls (fp16 host buffers, synchronous). */
+int ivc_set_input_f16(ivc_model *m, const uint16_t *input_f16, int batch);
+int ivc_run(ivc_model *m, int batch);
+int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch);
+/* Copies tensor `name` for `batch` images in plan (NCHW) order; IVC_ERR_NOT_FOUND if unknown. */
+int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch);
+
+/* Zero-copy: device fp16 input / outputs, enqueued on `stream` (cudaStream_t,
+ * NULL = the handle's stream) without host synchronisation. */
+int ivc_infer_f16_device(ivc_model *m, const void *d_input, int batch, void *const *d_outputs, void *stream);
+/* Device f32 input (truncating cast on the device) -> device f32 outputs, asynchronous. */
+int ivc_infer_f32_device(ivc_model *m, const float *d_input, int batch, float *const *d_outputs, void *stream);
+/* Binds the handle to a caller stream (NULL restores a private stream). */
+int ivc_set_stream(ivc_model *m, void *stream);
+int ivc_synchronize(ivc_model *m);
+double ivc_last_infer_ms(const ivc_model *m);
+
+/* Profiling: eager run with CUDA events around every kernel launch. */
+int ivc_step_count(const ivc_model *m);
+int ivc_step_info(const ivc_model *m, int i, const char **name, const char **family, double *flops_per_image,
+                  double *act_bytes_per_image, double *fixed_bytes);
+int ivc_profile(ivc_model *m, int batch, float *step_ms, int n);
+
+/* Activation pool statistics (bytes at max_batch). */
+int ivc_pool_stats(const ivc_model *m, int64_t *requested_bytes, int64_t *arena_bytes, int64_t *weight_bytes,
+                   int *roots, int *views, int *nhwc_tensors, int *fusions_concat, int *fusions_res);
+/* Human-readable dump of tensors (layout, arena offset, lifetime) and launches. */
+int ivc_describe(const ivc_model *m, char *buf, size_t cap);
+
+/* Host conversions with the reference's semantics (include/infvino/Half.hpp:14-49). */
+void ivc_f32_to_f16(const float *in, uint16_t *out, size_t n);
+void ivc_f16_to_f32(const uint16_t *in, float *out, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INFVINO_B200_H_ */

@@ -1,0 +1,362 @@
+// C ABI over the engine (include/infvino_b200.h).  Exceptions never cross the
+// boundary: every entry point maps them to an ivc_status and keeps the message.
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/infvino_b200.h"
+#include "engine.h"
+
+struct ivc_model {
+  std::unique_ptr<ivb::Engine> eng;
+  mutable std::mutex mu;
+  std::string err;
+  double last_ms = 0.0;
+  std::string describe_cache;
+};
+
+namespace {
+
+std::string g_create_err;
+std::mutex g_create_mu;
+
+int fail(ivc_model *m, int code, const std::string &msg) {
+  if (m) m->err = msg;
+  return code;
+}
+
+int classify(const std::string &msg) {
+  if (msg.find("numel mismatch") != std::string::npos) return IVC_ERR_NUMEL;
+  if (msg.find("PlanModel:") == 0) return IVC_ERR_PLAN;
+  if (msg.find("CudaPlanModel: cuda") != std::string::npos) return IVC_ERR_CUDA;
+  return msg.find("CudaPlanModel:") == 0 && msg.find(": ") != std::string::npos &&
+                 (msg.find("cuda") != std::string::npos || msg.find("launch") != std::string::npos)
+             ? IVC_ERR_CUDA
+             : IVC_ERR_PLAN;
+}
+
+template <class F>
+int guarded(ivc_model *m, F &&f) {
+  if (!m || !m->eng) return IVC_ERR_ARGUMENT;
+  std::lock_guard<std::mutex> lk(m->mu);
+  try {
+    return f();
+  } catch (const std::exception &e) {
+    return fail(m, classify(e.what()), e.what());
+  }
+}
+
+int status_check(ivc_model *m) {
+  const int s = m->eng->device_status();
+  if (s != 0) return fail(m, IVC_ERR_KERNEL, "CudaPlanModel: kernel bounded wait timed out (status " + std::to_string(s) + ")");
+  return IVC_OK;
+}
+
+// include/infvino/Half.hpp:14-24 (truncating) and :26-47 (exact widening)
+inline uint16_t f2h_trunc(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const int32_t e = (int32_t)((x >> 23) & 0xff) - 112;
+  const uint32_t mant = x & 0x7fffffu;
+  if (e <= 0) return (uint16_t)sign;
+  if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+  return (uint16_t)(sign | ((uint32_t)e << 10) | (mant >> 13));
+}
+inline float h2f(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t e = (h >> 10) & 0x1fu, mant = h & 0x3ffu, f;
+  if (e == 0) {
+    if (mant == 0) {
+      f = sign;
+    } else {
+      int ee = 113;
+      while (!(mant & 0x400u)) {
+        mant <<= 1;
+        --ee;
+      }
+      f = sign | ((uint32_t)ee << 23) | ((mant & 0x3ffu) << 13);
+    }
+  } else if (e == 31) {
+    f = sign | 0x7f800000u | (mant << 13);
+  } else {
+    f = sign | ((e + 112u) << 23) | (mant << 13);
+  }
+  float out;
+  std::memcpy(&out, &f, 4);
+  return out;
+}
+
+template <class F>
+void parallel_for(size_t n, F &&f) {
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t nt = n < (1u << 20) ? 1 : std::min<size_t>(hw, 16);
+  if (nt <= 1) {
+    f(0, n);
+    return;
+  }
+  std::vector<std::thread> th;
+  const size_t chunk = (n + nt - 1) / nt;
+  for (size_t t = 0; t < nt; ++t) {
+    const size_t b = t * chunk, e = std::min(n, b + chunk);
+    if (b < e) th.emplace_back([&f, b, e] { f(b, e); });
+  }
+  for (auto &x : th) x.join();
+}
+
+}  // namespace
+
+extern "C" {
+
+int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out) {
+  if (!out) return IVC_ERR_ARGUMENT;
+  *out = nullptr;
+  if (!plan_path || !*plan_path) {
+    std::lock_guard<std::mutex> lk(g_create_mu);
+    g_create_err = "ClBackend: ModelInfo.plan is empty";
+    return IVC_ERR_ARGUMENT;
+  }
+  try {
+    auto m = std::make_unique<ivc_model>();
+    m->eng = std::make_unique<ivb::Engine>(plan_path, device_ordinal, max_batch, flags);
+    *out = m.release();
+    return IVC_OK;
+  } catch (const std::exception &e) {
+    std::lock_guard<std::mutex> lk(g_create_mu);
+    g_create_err = e.what();
+    return classify(e.what());
+  }
+}
+
+void ivc_destroy(ivc_model *m) { delete m; }
+
+const char *ivc_last_error(const ivc_model *m) {
+  if (!m) {
+    std::lock_guard<std::mutex> lk(g_create_mu);
+    return g_create_err.c_str();
+  }
+  return m->err.c_str();
+}
+
+int ivc_input_name(const ivc_model *m, const char **name) {
+  if (!m || !name) return IVC_ERR_ARGUMENT;
+  *name = m->eng->input_name().c_str();
+  return IVC_OK;
+}
+
+int ivc_input_dims(const ivc_model *m, int64_t *dims, int max_rank, int *rank) {
+  if (!m) return IVC_ERR_ARGUMENT;
+  const auto &d = m->eng->input_dims();
+  if (rank) *rank = (int)d.size();
+  for (int i = 0; dims && i < (int)d.size() && i < max_rank; ++i) dims[i] = d[(size_t)i];
+  return IVC_OK;
+}
+
+int64_t ivc_input_numel(const ivc_model *m) { return m ? m->eng->input_numel() : 0; }
+int ivc_output_count(const ivc_model *m) { return m ? m->eng->output_count() : 0; }
+
+int ivc_output_name(const ivc_model *m, int i, const char **name) {
+  if (!m || !name || i < 0 || i >= m->eng->output_count()) return IVC_ERR_ARGUMENT;
+  *name = m->eng->output_name(i).c_str();
+  return IVC_OK;
+}
+
+int ivc_output_dims(const ivc_model *m, int i, int64_t *dims, int max_rank, int *rank) {
+  if (!m || i < 0 || i >= m->eng->output_count()) return IVC_ERR_ARGUMENT;
+  const auto &d = m->eng->output_dims(i);
+  if (rank) *rank = (int)d.size();
+  for (int k = 0; dims && k < (int)d.size() && k < max_rank; ++k) dims[k] = d[(size_t)k];
+  return IVC_OK;
+}
+
+int64_t ivc_output_numel(const ivc_model *m, int i) {
+  if (!m || i < 0 || i >= m->eng->output_count()) return 0;
+  return m->eng->output_numel(i);
+}
+
+int64_t ivc_tensor_numel(const ivc_model *m, const char *name) {
+  if (!m || !name) return 0;
+  return m->eng->tensor_numel(name);
+}
+
+int ivc_max_batch(const ivc_model *m) { return m ? m->eng->max_batch() : 0; }
+
+int ivc_infer_f32(ivc_model *m, const float *input, size_t numel, int batch, float *const *outputs) {
+  return guarded(m, [&]() -> int {
+    if (!input || !outputs || batch < 1 || batch > m->eng->max_batch())
+      return fail(m, IVC_ERR_ARGUMENT, "ivc_infer_f32: bad arguments");
+    const size_t expect = (size_t)m->eng->input_numel() * (size_t)batch;
+    if (numel != expect)
+      return fail(m, IVC_ERR_NUMEL,
+                  "ClBackend: input numel mismatch: got " + std::to_string(numel) + ", expected " + std::to_string(expect));
+    for (int i = 0; i < m->eng->output_count(); ++i)
+      if (!outputs[i]) return fail(m, IVC_ERR_ARGUMENT, "ivc_infer_f32: null output buffer");
+    const auto t0 = std::chrono::steady_clock::now();
+    m->eng->upload_input_f32(input, batch, false);
+    m->eng->run(batch);
+    for (int i = 0; i < m->eng->output_count(); ++i) m->eng->download_output_f32(i, outputs[i], batch, false);
+    m->eng->synchronize();
+    m->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return status_check(m);
+  });
+}
+
+int ivc_set_input_f16(ivc_model *m, const uint16_t *input_f16, int batch) {
+  return guarded(m, [&]() -> int {
+    if (!input_f16 || batch < 1 || batch > m->eng->max_batch()) return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    m->eng->upload_input_f16(input_f16, batch, false);
+    m->eng->synchronize();
+    return IVC_OK;
+  });
+}
+
+int ivc_run(ivc_model *m, int batch) {
+  return guarded(m, [&]() -> int {
+    if (batch < 1 || batch > m->eng->max_batch()) return fail(m, IVC_ERR_ARGUMENT, "bad batch");
+    const auto t0 = std::chrono::steady_clock::now();
+    m->eng->run(batch);
+    m->eng->synchronize();
+    m->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return status_check(m);
+  });
+}
+
+int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch) {
+  return guarded(m, [&]() -> int {
+    if (!dst || i < 0 || i >= m->eng->output_count() || batch < 1 || batch > m->eng->max_batch())
+      return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    m->eng->download_output_f16(i, dst, batch, false);
+    m->eng->synchronize();
+    return IVC_OK;
+  });
+}
+
+int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch) {
+  return guarded(m, [&]() -> int {
+    if (!name || !dst || batch < 1 || batch > m->eng->max_batch()) return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    if (!m->eng->read_tensor_f16(name, dst, batch))
+      return fail(m, IVC_ERR_NOT_FOUND, std::string("PlanModel: no tensor ") + name);
+    return IVC_OK;
+  });
+}
+
+int ivc_infer_f16_device(ivc_model *m, const void *d_input, int batch, void *const *d_outputs, void *stream) {
+  return guarded(m, [&]() -> int {
+    if (!d_input || !d_outputs || batch < 1 || batch > m->eng->max_batch())
+      return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    cudaStream_t prev = m->eng->stream();
+    if (stream && stream != (void *)prev) m->eng->set_stream((cudaStream_t)stream);
+    m->eng->upload_input_f16(d_input, batch, true);
+    m->eng->run(batch);
+    for (int i = 0; i < m->eng->output_count(); ++i)
+      if (d_outputs[i]) m->eng->download_output_f16(i, d_outputs[i], batch, true);
+    return IVC_OK;
+  });
+}
+
+int ivc_infer_f32_device(ivc_model *m, const float *d_input, int batch, float *const *d_outputs, void *stream) {
+  return guarded(m, [&]() -> int {
+    if (!d_input || !d_outputs || batch < 1 || batch > m->eng->max_batch())
+      return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    cudaStream_t prev = m->eng->stream();
+    if (stream && stream != (void *)prev) m->eng->set_stream((cudaStream_t)stream);
+    m->eng->upload_input_f32(d_input, batch, true);
+    m->eng->run(batch);
+    for (int i = 0; i < m->eng->output_count(); ++i)
+      if (d_outputs[i]) m->eng->download_output_f32(i, d_outputs[i], batch, true);
+    return IVC_OK;
+  });
+}
+
+int ivc_set_stream(ivc_model *m, void *stream) {
+  return guarded(m, [&]() -> int {
+    if (!stream) {
+      cudaStream_t s = nullptr;
+      if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(m, IVC_ERR_CUDA, "cudaStreamCreate failed");
+      m->eng->set_stream(s);
+      return IVC_OK;
+    }
+    m->eng->set_stream((cudaStream_t)stream);
+    return IVC_OK;
+  });
+}
+
+int ivc_synchronize(ivc_model *m) {
+  return guarded(m, [&]() -> int {
+    m->eng->synchronize();
+    return status_check(m);
+  });
+}
+
+double ivc_last_infer_ms(const ivc_model *m) { return m ? m->last_ms : 0.0; }
+
+int ivc_step_count(const ivc_model *m) { return m ? (int)m->eng->steps().size() : 0; }
+
+int ivc_step_info(const ivc_model *m, int i, const char **name, const char **family, double *flops, double *act_bytes,
+                  double *fixed_bytes) {
+  if (!m || i < 0 || i >= (int)m->eng->steps().size()) return IVC_ERR_ARGUMENT;
+  const ivb::Step &s = m->eng->steps()[(size_t)i];
+  if (name) *name = s.name.c_str();
+  if (family) *family = s.family.c_str();
+  if (flops) *flops = s.flops_img;
+  if (act_bytes) *act_bytes = s.bytes_img;
+  if (fixed_bytes) *fixed_bytes = s.bytes_fixed;
+  return IVC_OK;
+}
+
+int ivc_profile(ivc_model *m, int batch, float *step_ms, int n) {
+  return guarded(m, [&]() -> int {
+    if (!step_ms || n < (int)m->eng->steps().size() || batch < 1 || batch > m->eng->max_batch())
+      return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    std::vector<float> ms;
+    m->eng->run_profiled(batch, &ms);
+    std::memcpy(step_ms, ms.data(), ms.size() * sizeof(float));
+    return status_check(m);
+  });
+}
+
+int ivc_pool_stats(const ivc_model *m, int64_t *requested, int64_t *arena, int64_t *weights, int *roots, int *views,
+                   int *nhwc, int *fc, int *fr) {
+  if (!m) return IVC_ERR_ARGUMENT;
+  const ivb::EngineStats &s = m->eng->stats();
+  if (requested) *requested = s.requested_bytes;
+  if (arena) *arena = s.arena_bytes;
+  if (weights) *weights = s.weight_bytes;
+  if (roots) *roots = s.roots;
+  if (views) *views = s.views;
+  if (nhwc) *nhwc = s.nhwc_tensors;
+  if (fc) *fc = s.fusions_concat;
+  if (fr) *fr = s.fusions_res;
+  return IVC_OK;
+}
+
+int ivc_describe(const ivc_model *m, char *buf, size_t cap) {
+  if (!m) return IVC_ERR_ARGUMENT;
+  const std::string d = m->eng->describe();
+  if (buf && cap) {
+    const size_t n = d.size() < cap - 1 ? d.size() : cap - 1;
+    std::memcpy(buf, d.data(), n);
+    buf[n] = '\0';
+  }
+  return (int)d.size();
+}
+
+void ivc_f32_to_f16(const float *in, uint16_t *out, size_t n) {
+  parallel_for(n, [&](size_t b, size_t e) {
+    for (size_t i = b; i < e; ++i) out[i] = f2h_trunc(in[i]);
+  });
+}
+
+void ivc_f16_to_f32(const uint16_t *in, float *out, size_t n) {
+  parallel_for(n, [&](size_t b, size_t e) {
+    for (size_t i = b; i < e; ++i) out[i] = h2f(in[i]);
+  });
+}
+
+}  // extern "C"

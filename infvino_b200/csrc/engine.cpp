@@ -1,0 +1,1184 @@
+// CudaPlanModel engine implementation.
+//
+// Correspondence with the reference executor (src/PlanModel.cpp):
+//   parse ............................ Plan (plan.cpp), same grammar and errors
+//   fuseConcatConv1x1 / fuseResidualAdd  Plan::fuse_* (numerically transparent)
+//   allocateActivations + ActPool ..... Engine::allocate (liveness intervals over
+//                                       node indices, views share their root's
+//                                       interval, largest-first gap placement in
+//                                       ONE device arena, self-check for overlap)
+//   planBlockedLayout / LayoutSolver .. Engine::plan_layouts (NHWC vs planar)
+//   run() dispatch + capture/replay ... Engine::lower + CUDA graph per batch size
+#include "engine.h"
+
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <set>
+#include <sstream>
+#include <stdexcept>
+
+#include "kernels/common.cuh"
+#include "kernels/conv_tc.cuh"
+#include "tma.h"
+
+namespace ivb {
+
+namespace {
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+std::vector<int64_t> parse_ints(const std::string &s) {
+  std::vector<int64_t> v;
+  std::stringstream ss(s);
+  std::string tok;
+  while (std::getline(ss, tok, ',')) v.push_back(std::atoll(tok.c_str()));
+  return v;
+}
+
+uint16_t f32_to_f16_rne_host(float f) {  // host packing of padded weights only (exact values)
+  const __half h = __float2half_rn(f);
+  uint16_t u;
+  std::memcpy(&u, &h, 2);
+  return u;
+}
+
+}  // namespace
+
+// ============================================================================ setup
+Engine::Engine(const std::string &plan_path, int device, int max_batch, unsigned flags)
+    : device_(device), max_batch_(max_batch), flags_(flags), dry_((flags & kFlagDryRun) != 0) {
+  if (max_batch < 1) throw std::runtime_error("CudaPlanModel: max_batch must be >= 1");
+  plan_ = std::make_unique<Plan>(plan_path);
+  if (!dry_) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    cudaDeviceProp prop{};
+    check(cudaGetDeviceProperties(&prop, device_), "cudaGetDeviceProperties");
+    if (prop.major != 10)
+      throw std::runtime_error("CudaPlanModel: device " + std::to_string(device_) + " (" + prop.name +
+                               ") is not an sm_100 GPU");
+    num_sms_ = prop.multiProcessorCount;
+    check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    own_stream_ = true;
+  }
+  plan_layouts();
+  build_tensors();
+  allocate();
+  upload_weights();
+  lower();
+}
+
+Engine::~Engine() {
+  if (dry_) return;
+  cudaSetDevice(device_);
+  for (auto &kv : graphs_) cudaGraphExecDestroy(kv.second);
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (void *p : dev_allocs_) cudaFree(p);
+  if (arena_) cudaFree(arena_);
+  if (status_) cudaFree(status_);
+  if (in_f32_) cudaFree(in_f32_);
+  if (scratch_) cudaFree(scratch_);
+  if (own_stream_ && stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::check(cudaError_t e, const char *what) const {
+  if (e != cudaSuccess) throw std::runtime_error(std::string("CudaPlanModel: ") + what + ": " + cudaGetErrorString(e));
+}
+
+int Engine::tid(const std::string &name) const {
+  auto it = tid_.find(name);
+  if (it == tid_.end()) throw std::runtime_error("PlanModel: missing tensor: " + name);
+  return it->second;
+}
+
+const std::vector<int64_t> &Engine::input_dims() const { return plan_->ref(plan_->input()).dims; }
+int64_t Engine::input_numel() const { return plan_->ref(plan_->input()).numel(); }
+const std::vector<int64_t> &Engine::output_dims(int i) const { return plan_->ref(output_name(i)).dims; }
+int64_t Engine::output_numel(int i) const { return plan_->ref(output_name(i)).numel(); }
+int64_t Engine::tensor_numel(const std::string &name) const {
+  return plan_->has(name) ? plan_->ref(name).numel() : 0;
+}
+
+// ============================================================================ layouts
+namespace {
+
+bool is_act4(const PlanTensor &t) { return !t.is_init && t.dims.size() == 4 && t.dims[0] == 1; }
+
+// ew_binary broadcast of a [1,C,1,1] operand over a [1,C,H,W] output (SE scale).
+bool per_channel_bcast(const Plan &p, const PlanNode &n, int *scale_slot) {
+  if (n.ins.size() < 2) return false;
+  const PlanTensor &o = p.ref(n.outs[0]);
+  if (o.dims.size() != 4) return false;
+  for (int k = 0; k < 2; ++k) {
+    const PlanTensor &s = p.ref(n.ins[(size_t)k]);
+    const PlanTensor &v = p.ref(n.ins[(size_t)(1 - k)]);
+    if (v.dims != o.dims) continue;
+    std::vector<int64_t> al(4, 1);
+    for (size_t i = 0; i < s.dims.size() && i < 4; ++i) al[4 - s.dims.size() + i] = s.dims[i];
+    if (s.dims.size() <= 4 && al[0] == 1 && al[1] == o.dims[1] && al[2] == 1 && al[3] == 1) {
+      if (scale_slot) *scale_slot = k;
+      return true;
+    }
+  }
+  return false;
+}
+
+bool elementwise_same(const PlanNode &n) { return !n.has("bdims") || n.ai("b_scalar", 0) == 1; }
+
+}  // namespace
+
+void Engine::plan_layouts() {
+  Plan &p = *plan_;
+  const auto &nodes = p.nodes();
+  // consumers per tensor
+  std::map<std::string, std::vector<std::pair<int, int>>> cons;
+  std::map<std::string, int> prod;
+  for (size_t i = 0; i < nodes.size(); ++i) {
+    for (size_t s = 0; s < nodes[i].ins.size(); ++s)
+      if (nodes[i].ins[s] != "-") cons[nodes[i].ins[s]].push_back({(int)i, (int)s});
+    for (const auto &o : nodes[i].outs) prod[o] = (int)i;
+  }
+  auto consumer_ok = [&](const PlanNode &n, int slot) -> bool {
+    const std::string &op = n.op;
+    if (op == "conv3x3") return slot == 0 || slot == 3;
+    if (op == "conv1x1") return slot == 1 || slot == 3;
+    if (op == "conv_general") return slot == 0;
+    if (op == "maxpool" || op == "resize_nn" || op == "gap" || op == "ew_unary" || op == "copy_c") return slot == 0;
+    if (op == "concat4") return n.ai("outer", 1) == 1 && p.ref(n.outs[0]).dims.size() == 4;
+    if (op == "ew_binary") return elementwise_same(n) || per_channel_bcast(p, n, nullptr);
+    return false;
+  };
+  auto producer_ok = [&](const PlanNode &n) -> bool {
+    const std::string &op = n.op;
+    if (op == "conv3x3" || op == "conv_general" || op == "maxpool" || op == "resize_nn" || op == "ew_unary" ||
+        op == "copy_c")
+      return true;
+    if (op == "conv1x1") return p.ref(n.outs[0]).dims.size() == 4;
+    if (op == "concat4") return n.ai("outer", 1) == 1;
+    if (op == "ew_binary") return elementwise_same(n) || per_channel_bcast(p, n, nullptr);
+    return false;
+  };
+  for (auto &kv : p.tensors()) {
+    const PlanTensor &t = kv.second;
+    if (!is_act4(t) || t.is_input || t.is_output) continue;
+    if (t.dims[2] * t.dims[3] <= 1) continue;
+    auto pit = prod.find(t.name);
+    if (pit == prod.end() || !producer_ok(nodes[(size_t)pit->second])) continue;
+    bool ok = true;
+    auto cit = cons.find(t.name);
+    if (cit != cons.end())
+      for (const auto &c : cit->second)
+        if (!consumer_ok(nodes[(size_t)c.first], c.second)) ok = false;
+    if (ok) nhwc_names_.insert(t.name);
+  }
+  // copy_c: channels-last output only as a view of a channels-last parent at an
+  // aligned channel offset (16-byte TMA base alignment), else it stays planar.
+  for (const auto &n : nodes) {
+    if (n.op != "copy_c") continue;
+    const bool parent = nhwc_names_.count(n.ins[0]) != 0;
+    if (!parent || n.ai("c0", 0) % 8 != 0 || n.ai("dst_off", 0) != 0) nhwc_names_.erase(n.outs[0]);
+  }
+  // load-time fusions
+  if (!(flags_ & kFlagNoFusion)) {
+    std::vector<std::string> allowed;
+    for (const auto &n : nodes) {
+      if (n.op != "concat4" || !nhwc_names_.count(n.outs[0])) continue;
+      bool ok = true;
+      for (size_t s = 0; s < n.ins.size() && s < 4; ++s)
+        if (n.ins[s] != "-" && !nhwc_names_.count(n.ins[s])) ok = false;
+      if (ok) allowed.push_back(n.outs[0]);
+    }
+    p.fuse_concat_conv1x1(allowed);
+    p.fuse_residual_add();
+  }
+  stats_.fusions_concat = p.fusions_concat;
+  stats_.fusions_res = p.fusions_res;
+}
+
+// ============================================================================ tensors
+void Engine::build_tensors() {
+  Plan &p = *plan_;
+  const auto &nodes = p.nodes();
+  std::set<std::string> used;
+  used.insert(p.input());
+  for (const auto &o : p.outputs()) used.insert(o);
+  for (const auto &n : nodes) {
+    for (const auto &i : n.ins)
+      if (i != "-") used.insert(i);
+    for (const auto &o : n.outs)
+      if (o != "-") used.insert(o);
+  }
+  for (const auto &name : used) {
+    const PlanTensor &pt = p.ref(name);
+    TensorRt t;
+    t.name = name;
+    t.dims = pt.dims;
+    t.numel = pt.numel();
+    t.is_init = pt.is_init;
+    t.is_input = pt.is_input;
+    t.is_output = pt.is_output;
+    if (!t.is_init && !t.dims.empty() && t.dims[0] != 1)
+      throw std::runtime_error("CudaPlanModel: activation '" + name + "' must have batch dimension 1 in the plan");
+    if (t.dims.size() == 4) {
+      t.C = (int)t.dims[1];
+      t.H = (int)t.dims[2];
+      t.W = (int)t.dims[3];
+    }
+    tid_[name] = (int)T_.size();
+    T_.push_back(t);
+  }
+  auto set_dense = [](TensorRt &t) {
+    t.nhwc = false;
+    t.dense = true;
+    t.Cs = t.C;
+    if (t.dims.size() == 4) {
+      t.sx = 1;
+      t.sy = t.W;
+      t.sc = (int64_t)t.H * t.W;
+    }
+    t.sb = t.is_init ? 0 : t.numel;
+    t.bytes_per_img = t.numel * 2;
+  };
+  auto set_nhwc = [](TensorRt &t) {
+    t.nhwc = true;
+    t.dense = false;
+    t.Cs = (int)round_up(t.C, 8);
+    t.sc = 1;
+    t.sx = t.Cs;
+    t.sy = (int64_t)t.W * t.Cs;
+    t.sb = (int64_t)t.H * t.W * t.Cs;
+    t.bytes_per_img = t.sb * 2;
+  };
+  // defaults: every tensor owns dense storage
+  for (size_t i = 0; i < T_.size(); ++i) {
+    set_dense(T_[i]);
+    T_[i].root = (int)i;
+  }
+  // channels-last roots and views, in node order (parents first)
+  for (const auto &n : nodes) {
+    const std::string &on = n.outs[0];
+    TensorRt &o = T_[(size_t)tid(on)];
+    if (n.op == "reshape" || n.op == "flatten") {
+      const TensorRt &in = T_[(size_t)tid(n.ins[0])];
+      if (!in.dense) throw std::runtime_error("CudaPlanModel: reshape of a non-planar tensor: " + n.ins[0]);
+      o.root = in.root;
+      o.elem_off = in.elem_off;
+      continue;
+    }
+    if (!nhwc_names_.count(on)) continue;
+    if (n.op == "copy_c") {
+      const TensorRt &in = T_[(size_t)tid(n.ins[0])];
+      o.nhwc = true;
+      o.dense = false;
+      o.root = in.root;
+      o.elem_off = in.elem_off + n.ai("c0", 0);
+      o.Cs = in.Cs;
+      o.sc = 1;
+      o.sx = in.sx;
+      o.sy = in.sy;
+      o.sb = in.sb;
+      o.bytes_per_img = 0;
+      continue;
+    }
+    set_nhwc(o);
+  }
+  for (auto &t : T_) {
+    if (t.root != tid(t.name)) ++stats_.views;
+    else if (!t.is_init) ++stats_.roots;
+    if (t.nhwc) ++stats_.nhwc_tensors;
+  }
+}
+
+// ============================================================================ allocation
+void Engine::allocate() {
+  const auto &nodes = plan_->nodes();
+  const int N = (int)nodes.size();
+  auto touch = [&](const std::string &name, int i) {
+    if (name == "-") return;
+    TensorRt &t = T_[(size_t)tid(name)];
+    if (t.is_init) return;
+    TensorRt &r = T_[(size_t)t.root];
+    if (r.birth < 0 || i < r.birth) r.birth = i;
+    if (i > r.death) r.death = i;
+  };
+  touch(plan_->input(), 0);
+  for (int i = 0; i < N; ++i) {
+    for (const auto &in : nodes[(size_t)i].ins) touch(in, i);
+    for (const auto &o : nodes[(size_t)i].outs) touch(o, i);
+  }
+  for (const auto &o : plan_->outputs()) T_[(size_t)T_[(size_t)tid(o)].root].death = N;
+
+  std::vector<int> roots;
+  for (size_t i = 0; i < T_.size(); ++i)
+    if ((int)i == T_[i].root && !T_[i].is_init && T_[i].birth >= 0) roots.push_back((int)i);
+  auto bytes_of = [&](int r) { return round_up(T_[(size_t)r].bytes_per_img * max_batch_, 256); };
+  std::sort(roots.begin(), roots.end(), [&](int a, int b) {
+    if (bytes_of(a) != bytes_of(b)) return bytes_of(a) > bytes_of(b);
+    return T_[(size_t)a].birth < T_[(size_t)b].birth;
+  });
+  std::vector<int> placed;
+  int64_t top = 0;
+  for (int r : roots) {
+    const int64_t sz = bytes_of(r);
+    stats_.requested_bytes += sz;
+    std::vector<std::pair<int64_t, int64_t>> busy;
+    for (int q : placed) {
+      const TensorRt &a = T_[(size_t)r], &b = T_[(size_t)q];
+      if (a.birth <= b.death && b.birth <= a.death) busy.push_back({b.arena_off, b.arena_off + bytes_of(q)});
+    }
+    std::sort(busy.begin(), busy.end());
+    int64_t cur = 0;
+    for (const auto &iv : busy) {
+      if (cur + sz <= iv.first) break;
+      cur = std::max(cur, round_up(iv.second, 256));
+    }
+    T_[(size_t)r].arena_off = cur;
+    top = std::max(top, cur + sz);
+    placed.push_back(r);
+  }
+  arena_bytes_ = std::max<int64_t>(top, 256);
+  stats_.arena_bytes = arena_bytes_;
+  // self-check: roots with intersecting lifetimes never share bytes
+  for (size_t i = 0; i < placed.size(); ++i)
+    for (size_t j = i + 1; j < placed.size(); ++j) {
+      const TensorRt &a = T_[(size_t)placed[i]], &b = T_[(size_t)placed[j]];
+      if (!(a.birth <= b.death && b.birth <= a.death)) continue;
+      const int64_t a0 = a.arena_off, a1 = a0 + bytes_of(placed[i]);
+      const int64_t b0 = b.arena_off, b1 = b0 + bytes_of(placed[j]);
+      if (a0 < b1 && b0 < a1) ++stats_.overlap_errors;
+    }
+  if (stats_.overlap_errors) throw std::runtime_error("CudaPlanModel: activation allocator produced overlaps");
+  if (!dry_) {
+    check(cudaMalloc(&arena_, (size_t)arena_bytes_), "cudaMalloc(arena)");
+    check(cudaMemset(arena_, 0, (size_t)arena_bytes_), "cudaMemset(arena)");
+    check(cudaMalloc(&status_, sizeof(int)), "cudaMalloc(status)");
+    check(cudaMemset(status_, 0, sizeof(int)), "cudaMemset(status)");
+    check(cudaMalloc(&in_f32_, (size_t)input_numel() * max_batch_ * sizeof(float)), "cudaMalloc(input f32)");
+  }
+  uint8_t *base = dry_ ? nullptr : arena_;
+  for (auto &t : T_) {
+    if (t.is_init) continue;
+    const TensorRt &r = T_[(size_t)t.root];
+    if (r.arena_off < 0) continue;
+    t.dptr = reinterpret_cast<__half *>(base + r.arena_off) + t.elem_off;
+  }
+}
+
+void Engine::upload_weights() {
+  int64_t total = 0;
+  for (auto &t : T_)
+    if (t.is_init) total += round_up(t.numel * 2, 256);
+  stats_.weight_bytes = total;
+  if (dry_ || total == 0) return;
+  void *w = nullptr;
+  check(cudaMalloc(&w, (size_t)total), "cudaMalloc(weights)");
+  dev_allocs_.push_back(w);
+  int64_t off = 0;
+  for (auto &t : T_) {
+    if (!t.is_init) continue;
+    const PlanTensor &pt = plan_->ref(t.name);
+    t.dptr = reinterpret_cast<__half *>(static_cast<uint8_t *>(w) + off);
+    check(cudaMemcpy(t.dptr, pt.host.data(), (size_t)t.numel * 2, cudaMemcpyHostToDevice), "upload init");
+    off += round_up(t.numel * 2, 256);
+  }
+}
+
+View4 Engine::view(int i) const {
+  const TensorRt &t = T_[(size_t)i];
+  View4 v{};
+  v.ptr = t.dptr;
+  if (t.dims.size() == 4) {
+    v.C = t.C;
+    v.H = t.H;
+    v.W = t.W;
+    v.sc = t.sc;
+    v.sy = t.sy;
+    v.sx = t.sx;
+  } else if (t.dims.size() == 2) {  // [1, K] -> K channels of a 1x1 image
+    v.C = (int)t.dims[1];
+    v.H = v.W = 1;
+    v.sc = 1;
+    v.sy = v.sx = v.C;
+  } else if (t.dims.size() >= 3) {  // [1, C, rest...] -> C x 1 x rest (planar)
+    v.C = (int)t.dims[1];
+    int64_t rest = 1;
+    for (size_t k = 2; k < t.dims.size(); ++k) rest *= t.dims[k];
+    v.H = 1;
+    v.W = (int)rest;
+    v.sc = rest;
+    v.sy = rest;
+    v.sx = 1;
+  } else {
+    v.C = (int)t.numel;
+    v.H = v.W = 1;
+    v.sc = 1;
+    v.sy = v.sx = v.C;
+  }
+  v.sb = t.is_init ? 0 : t.sb;
+  return v;
+}
+
+__half *Engine::input_device_ptr() const { return T_[(size_t)tid(plan_->input())].dptr; }
+
+// ============================================================================ lowering
+namespace {
+
+struct ConvCfg {
+  int ksize = 1, stride = 1, pad = 0;
+  int nsrc = 1;
+  int src[kConvMaxSrc] = {-1, -1, -1, -1};
+  int srcC[kConvMaxSrc] = {0, 0, 0, 0};
+  int chunks[kConvMaxSrc] = {0, 0, 0, 0};
+  int cin_total = 0;
+  int cout = 0, Np = 0, BN = 0, BK = 0, n_tiles = 1, num_kb = 0, taps = 1;
+  int Ho = 0, Wo = 0, TH = 0, TW = 0;
+  int act = 0, act_kind = kActGemm;
+  int out = -1, res = -1;
+  int stages = 2, resident_b = 0, smem = 0, tmem_cols = 32;
+  __half *wp = nullptr;    // packed [Np][Kp]
+  __half *bias = nullptr;  // [Np] padded
+};
+
+int pick_bk(int c) {
+  const int c16 = (int)round_up(c, 16);
+  if (c16 >= 64) return 64;
+  if (c16 >= 32) return 32;
+  return 16;
+}
+
+int pow2_at_least(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+void Engine::lower() {
+  Plan &p = *plan_;
+  const auto &nodes = p.nodes();
+  const bool no_tc = (flags_ & kFlagNoTensorCores) != 0;
+  int *status = status_;
+  const int sms = num_sms_;
+
+  auto act_bytes = [&](int t) -> double { return T_[(size_t)t].is_init ? 0.0 : (double)T_[(size_t)t].numel * 2.0; };
+  auto init_bytes = [&](int t) -> double { return T_[(size_t)t].is_init ? (double)T_[(size_t)t].numel * 2.0 : 0.0; };
+  auto opt = [&](const PlanNode &n, size_t i) -> int {
+    return (i < n.ins.size() && n.ins[i] != "-") ? tid(n.ins[i]) : -1;
+  };
+  auto tc_ok = [&](int t) -> bool {  // activation usable as a K-major TMA source
+    const TensorRt &x = T_[(size_t)t];
+    if (x.is_init) return false;
+    const View4 v = view(t);
+    if (v.H * v.W == 1) return v.C == 1 || (v.sc == 1 && v.sb % 8 == 0 && (x.elem_off * 2) % 16 == 0);
+    if (v.sc != 1) return false;
+    if (v.sx % 8 != 0 || v.sy % 8 != 0 || v.sb % 8 != 0) return false;
+    return (x.elem_off * 2) % 16 == 0;
+  };
+
+  for (size_t ni = 0; ni < nodes.size(); ++ni) {
+    const PlanNode &n = nodes[ni];
+    const std::string &op = n.op;
+    if (op == "reshape" || op == "flatten") continue;
+    const int out = tid(n.outs[0]);
+    Step st;
+    st.node = (int)ni;
+    st.name = op + ":" + n.outs[0];
+    st.family = op;
+
+    // ---------------------------------------------------------------- convolutions
+    const bool is_conv = op == "conv3x3" || op == "conv1x1" || op == "conv1x1_cat4";
+    if (is_conv) {
+      ConvCfg c;
+      int w = -1, bias = -1;
+      if (op == "conv3x3") {
+        c.ksize = 3;
+        c.stride = n.ai("stride", 1);
+        c.pad = n.ai("pad", 1);
+        c.src[0] = tid(n.ins[0]);
+        w = tid(n.ins[1]);
+        bias = opt(n, 2);
+        c.res = opt(n, 3);
+        c.act_kind = kActConv3x3;
+      } else if (op == "conv1x1") {
+        w = tid(n.ins[0]);
+        c.src[0] = tid(n.ins[1]);
+        bias = opt(n, 2);
+        c.res = opt(n, 3);
+        if (opt(n, 4) >= 0) throw std::runtime_error("CudaPlanModel: conv1x1 scale input is not supported");
+      } else {
+        w = tid(n.ins[0]);
+        c.nsrc = 0;
+        const int cnt[4] = {n.ai("cat_ca", 0), n.ai("cat_cb", 0), n.ai("cat_cc", 0), n.ai("cat_cd", 0)};
+        for (int s = 0; s < 4; ++s)
+          if (cnt[s] > 0) c.src[c.nsrc++] = tid(n.ins[(size_t)(1 + s)]);
+        bias = opt(n, 5);
+        c.res = opt(n, 6);
+      }
+      c.act = n.ai("act", 0);
+      c.out = out;
+      const TensorRt &wt = T_[(size_t)w];
+      const TensorRt &ot = T_[(size_t)out];
+      c.cout = (int)wt.dims[0];
+      for (int s = 0; s < c.nsrc; ++s) {
+        c.srcC[s] = view(c.src[s]).C;
+        c.cin_total += c.srcC[s];
+      }
+      if (c.nsrc == 1 && c.ksize == 1) c.cin_total = (int)wt.dims[1];
+      const View4 ov = view(out);
+      c.Ho = ov.H;
+      c.Wo = ov.W;
+      if (c.ksize == 3) {
+        c.Ho = n.ai("Hout", ov.H);
+        c.Wo = n.ai("Wout", ov.W);
+      }
+      c.taps = c.ksize * c.ksize;
+      // FLOPs / bytes (algorithmic, per image) for the roofline
+      st.flops_img = 2.0 * c.cout * c.cin_total * c.taps * (double)c.Ho * c.Wo;
+      for (int s = 0; s < c.nsrc; ++s) st.bytes_img += act_bytes(c.src[s]);
+      st.bytes_img += act_bytes(out) + (c.res >= 0 ? act_bytes(c.res) : 0.0);
+      st.bytes_fixed = init_bytes(w) + (bias >= 0 ? init_bytes(bias) : 0.0);
+      const View4 xv0 = view(c.src[0]);
+      // consistency with the reference's derivation of the GEMM sizes
+      if (c.ksize == 1) {
+        const int64_t xn = T_[(size_t)c.src[0]].numel;
+        if (c.nsrc == 1 && (int64_t)xv0.C * xv0.H * xv0.W != xn)
+          throw std::runtime_error("CudaPlanModel: conv1x1 input view mismatch for " + n.outs[0]);
+        if (c.nsrc == 1 && xv0.C != c.cin_total)
+          throw std::runtime_error("CudaPlanModel: conv1x1 Cin mismatch for " + n.outs[0]);
+      }
+      bool use_tc = !no_tc;
+      for (int s = 0; s < c.nsrc; ++s) use_tc = use_tc && tc_ok(c.src[s]);
+      if (c.ksize == 3 && xv0.C <= 4) use_tc = false;  // stem: dedicated kernel
+      if (c.ksize == 1 && c.nsrc == 1 && (xv0.H != ov.H || xv0.W != ov.W)) use_tc = false;
+      if (!use_tc) {
+        if (c.nsrc != 1) throw std::runtime_error("CudaPlanModel: concatenated sources need channels-last input");
+        const int x = c.src[0];
+        const int res = c.res;
+        const int K = c.ksize, S = c.stride, P = c.pad, act = c.act;
+        const __half *wptr = T_[(size_t)w].dptr;
+        const __half *bptr = bias >= 0 ? T_[(size_t)bias].dptr : nullptr;
+        if (c.ksize == 3 && xv0.C <= 4 && res < 0) {
+          st.family = "stem3x3";
+          const int cout = c.cout;
+          st.launch = [this, x, out, wptr, bptr, cout, S, P, act](int B, cudaStream_t s) {
+            return launch_stem3x3_v4(view(x), wptr, bptr, view(out), B, cout, S, P, act, s);
+          };
+        } else {
+          st.family = "conv_direct";
+          const int epi = (c.ksize == 3) ? 2 : 1;
+          const int cout = c.cout;
+          st.launch = [this, x, out, res, wptr, bptr, cout, K, S, P, act, epi](int B, cudaStream_t s) {
+            View4 xv = view(x), ov = view(out);
+            if (K == 1 && (xv.H != ov.H || xv.W != ov.W)) {  // 1x1 over [C, N] planar rows
+              xv.W = xv.H * xv.W;
+              xv.H = 1;
+            }
+            const View4 rv = res >= 0 ? view(res) : View4{};
+            return launch_conv_direct_v4(xv, wptr, bptr, res >= 0 ? view(res).ptr : nullptr, rv, ov, B, cout, K, S,
+                                         P, 1, act, epi, s);
+          };
+        }
+        steps_.push_back(std::move(st));
+        continue;
+      }
+      // ---- tensor-core path: tile choice
+      c.BK = 64;
+      for (int s = 0; s < c.nsrc; ++s) c.BK = std::min(c.BK, pick_bk(c.srcC[s]));
+      for (int s = 0; s < c.nsrc; ++s) c.chunks[s] = (int)((c.srcC[s] + c.BK - 1) / c.BK);
+      c.num_kb = 0;
+      for (int s = 0; s < c.nsrc; ++s) c.num_kb += c.taps * c.chunks[s];
+      const int np16 = (int)round_up(c.cout, 16);
+      if (np16 <= 256) {
+        c.BN = np16;
+        c.n_tiles = 1;
+      } else {
+        c.BN = 128;
+        c.n_tiles = (int)((np16 + 127) / 128);
+      }
+      c.Np = c.BN * c.n_tiles;
+      c.tmem_cols = pow2_at_least(2 * c.BN);
+      if (c.ksize == 3) {
+        if (c.Wo % 16 == 0) {
+          c.TW = 16;
+          c.TH = 8;
+        } else {
+          c.TW = std::min(c.Wo, 128);
+          c.TH = std::max(1, 128 / c.TW);
+        }
+      }
+      const int a_tile = 128 * c.BK * 2;
+      const int b_tile = (int)round_up((int64_t)c.BN * c.BK * 2, 1024);
+      const int budget = 232448 - 1024 - 2048 /*static smem + barriers*/ - 1024 /*align*/ - a_tile /*slack*/;
+      const int bres = b_tile * c.num_kb;
+      c.resident_b = (c.n_tiles == 1 && bres <= 96 * 1024 && budget - bres >= 2 * a_tile) ? 1 : 0;
+      const int stage_bytes = a_tile + (c.resident_b ? 0 : b_tile);
+      c.stages = std::min(kConvMaxStages, (budget - (c.resident_b ? bres : 0)) / stage_bytes);
+      if (c.stages < 2) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
+      c.smem = (c.resident_b ? bres : 0) + c.stages * stage_bytes + 1024 + a_tile;
+      c.smem = std::max(c.smem, 120 * 1024);  // one CTA per SM (TMEM never contended)
+      // ---- weight repack: Wp[Np][Kp], K order (source, tap, chunk, channel)
+      const int Kp = c.num_kb * c.BK;
+      std::vector<uint16_t> wp((size_t)c.Np * Kp, 0), bp((size_t)c.Np, 0);
+      const PlanTensor &pw = p.ref(wt.name);
+      const int wcin = (int)(pw.numel() / (c.cout * c.taps));
+      {
+        int kb = 0, cbase = 0;
+        for (int s = 0; s < c.nsrc; ++s) {
+          for (int tap = 0; tap < c.taps; ++tap)
+            for (int ch = 0; ch < c.chunks[s]; ++ch, ++kb)
+              for (int j = 0; j < c.BK; ++j) {
+                const int cl = ch * c.BK + j;
+                if (cl >= c.srcC[s]) continue;
+                const int ci = cbase + cl;
+                if (ci >= wcin) throw std::runtime_error("CudaPlanModel: weight/input channel mismatch: " + wt.name);
+                for (int nn = 0; nn < c.cout; ++nn)
+                  wp[(size_t)nn * Kp + (size_t)kb * c.BK + j] = pw.host[((size_t)nn * wcin + ci) * c.taps + tap];
+              }
+          cbase += c.srcC[s];
+        }
+        if (cbase != wcin) throw std::runtime_error("CudaPlanModel: weight/input channel mismatch: " + wt.name);
+      }
+      if (bias >= 0) {
+        const PlanTensor &pb = p.ref(T_[(size_t)bias].name);
+        for (int nn = 0; nn < c.cout && nn < (int)pb.host.size(); ++nn) bp[(size_t)nn] = pb.host[(size_t)nn];
+      }
+      (void)f32_to_f16_rne_host;
+      if (!dry_) {
+        void *dw = nullptr, *db = nullptr;
+        check(cudaMalloc(&dw, wp.size() * 2), "cudaMalloc(packed weights)");
+        check(cudaMalloc(&db, bp.size() * 2), "cudaMalloc(packed bias)");
+        dev_allocs_.push_back(dw);
+        dev_allocs_.push_back(db);
+        check(cudaMemcpy(dw, wp.data(), wp.size() * 2, cudaMemcpyHostToDevice), "upload packed weights");
+        check(cudaMemcpy(db, bp.data(), bp.size() * 2, cudaMemcpyHostToDevice), "upload packed bias");
+        c.wp = static_cast<__half *>(dw);
+        c.bias = bias >= 0 ? static_cast<__half *>(db) : nullptr;
+      }
+      st.family = c.ksize == 3 ? "conv3x3_tc" : "conv1x1_tc";
+      auto cache = std::make_shared<std::map<int, ConvTcArgs>>();
+      st.launch = [this, c, cache, status, sms](int B, cudaStream_t s) -> cudaError_t {
+        auto it = cache->find(B);
+        if (it == cache->end()) {
+          ConvTcArgs a;
+          std::memset(&a, 0, sizeof(a));
+          std::string err;
+          const int Kp = c.num_kb * c.BK;
+          for (int sidx = 0; sidx < c.nsrc; ++sidx) {
+            const View4 v = view(c.src[sidx]);
+            bool ok;
+            if (c.ksize == 1) {
+              const int64_t pix = (v.H * v.W == 1) ? v.sb : v.sx;
+              const uint64_t dims[2] = {(uint64_t)v.C, (uint64_t)B * v.H * v.W};
+              const uint64_t strides[1] = {(uint64_t)pix * 2};
+              const uint32_t box[2] = {(uint32_t)c.BK, 128};
+              const uint32_t es[2] = {1, 1};
+              ok = encode_tiled_f16(&a.mapA[sidx], 2, v.ptr, dims, strides, box, es,
+                                    swizzle_for_row_bytes(c.BK * 2), &err);
+            } else {
+              const uint64_t dims[4] = {(uint64_t)v.C, (uint64_t)v.W, (uint64_t)v.H, (uint64_t)B};
+              const uint64_t strides[3] = {(uint64_t)v.sx * 2, (uint64_t)v.sy * 2, (uint64_t)v.sb * 2};
+              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)(c.TW * c.stride), (uint32_t)(c.TH * c.stride), 1};
+              const uint32_t es[4] = {1, (uint32_t)c.stride, (uint32_t)c.stride, 1};
+              ok = encode_tiled_f16(&a.mapA[sidx], 4, v.ptr, dims, strides, box, es,
+                                    swizzle_for_row_bytes(c.BK * 2), &err);
+            }
+            if (!ok) throw std::runtime_error("CudaPlanModel: tensor map (activation) " + err);
+          }
+          {
+            const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)c.Np};
+            const uint64_t strides[1] = {(uint64_t)Kp * 2};
+            const uint32_t box[2] = {(uint32_t)c.BK, (uint32_t)c.BN};
+            const uint32_t es[2] = {1, 1};
+            if (!encode_tiled_f16(&a.mapB, 2, c.wp, dims, strides, box, es, swizzle_for_row_bytes(c.BK * 2), &err))
+              throw std::runtime_error("CudaPlanModel: tensor map (weights) " + err);
+          }
+          a.ksize = c.ksize;
+          a.stride = c.stride;
+          a.pad = c.pad;
+          a.nsrc = c.nsrc;
+          for (int sidx = 0; sidx < c.nsrc; ++sidx) a.src_chunks[sidx] = c.chunks[sidx];
+          a.taps = c.taps;
+          a.BK = c.BK;
+          a.BN = c.BN;
+          a.n_tiles = c.n_tiles;
+          a.num_kb = c.num_kb;
+          a.stages = c.stages;
+          a.resident_b = c.resident_b;
+          a.Ho = c.Ho;
+          a.Wo = c.Wo;
+          if (c.ksize == 1) {
+            a.m_total = (long long)B * c.Ho * c.Wo;
+            a.m_tiles = (int)((a.m_total + 127) / 128);
+            a.tile_rows = 128;
+            a.TH = a.TW = 1;
+            a.tiles_x = a.tiles_per_img = 1;
+          } else {
+            a.TH = c.TH;
+            a.TW = c.TW;
+            a.tiles_x = (c.Wo + c.TW - 1) / c.TW;
+            const int tiles_y = (c.Ho + c.TH - 1) / c.TH;
+            a.tiles_per_img = a.tiles_x * tiles_y;
+            a.m_tiles = a.tiles_per_img * B;
+            a.m_total = (long long)B * c.Ho * c.Wo;
+            a.tile_rows = c.TH * c.TW;
+          }
+          a.bias = c.bias;
+          a.cout = c.cout;
+          a.act = c.act;
+          a.act_kind = c.act_kind;
+          const View4 ov = view(c.out);
+          a.out = ov.ptr;
+          a.o_sb = ov.sb;
+          a.o_sc = ov.sc;
+          a.o_sy = ov.sy;
+          a.o_sx = ov.sx;
+          if (c.ksize == 1 && (ov.H != c.Ho || ov.W != c.Wo)) throw std::runtime_error("conv1x1 output view mismatch");
+          a.out_vec = (ov.sc == 1 && ov.sx % 8 == 0 && ov.sy % 8 == 0 && ov.sb % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(ov.ptr) & 15) == 0)
+                          ? 1
+                          : 0;
+          if (c.res >= 0) {
+            const View4 rv = view(c.res);
+            a.res = rv.ptr;
+            a.r_sb = rv.sb;
+            a.r_sc = rv.sc;
+            a.r_sy = rv.sy;
+            a.r_sx = rv.sx;
+            a.res_vec = (rv.sc == 1 && rv.sx % 8 == 0 && rv.sy % 8 == 0 && rv.sb % 8 == 0 &&
+                         (reinterpret_cast<uintptr_t>(rv.ptr) & 15) == 0)
+                            ? 1
+                            : 0;
+          }
+          a.tmem_cols = c.tmem_cols;
+          a.smem_bytes = c.smem;
+          a.status = status;
+          it = cache->emplace(B, a).first;
+        }
+        const ConvTcArgs &a = it->second;
+        const int tiles = a.m_tiles * a.n_tiles;
+        const int grid = std::max(1, std::min(tiles, sms));
+        return launch_conv_tc(a, grid, s);
+      };
+      steps_.push_back(std::move(st));
+      continue;
+    }
+
+    // ---------------------------------------------------------------- depthwise / generic conv
+    if (op == "conv_general") {
+      const int x = tid(n.ins[0]), w = tid(n.ins[1]), bias = opt(n, 2);
+      const int K = n.ai("K", 3), S = n.ai("S", 1), P = n.ai("P", 1), G = n.ai("G", 1), act = n.ai("act", 0);
+      const View4 xv = view(x), ov = view(out);
+      st.flops_img = 2.0 * ov.C * (xv.C / G) * K * K * (double)ov.H * ov.W;
+      st.bytes_img = act_bytes(x) + act_bytes(out);
+      st.bytes_fixed = init_bytes(w) + (bias >= 0 ? init_bytes(bias) : 0.0);
+      const __half *bptr = bias >= 0 ? T_[(size_t)bias].dptr : nullptr;
+      if (G == xv.C && (K == 3 || K == 5) && xv.C == ov.C) {
+        st.family = "depthwise";
+        // repack [C][1][K][K] -> [K*K][C]
+        const PlanTensor &pw = p.ref(T_[(size_t)w].name);
+        const int C = xv.C;
+        std::vector<uint16_t> r((size_t)K * K * C);
+        for (int ch = 0; ch < C; ++ch)
+          for (int t = 0; t < K * K; ++t) r[(size_t)t * C + ch] = pw.host[(size_t)ch * K * K + t];
+        __half *dw = nullptr;
+        if (!dry_) {
+          void *d = nullptr;
+          check(cudaMalloc(&d, r.size() * 2), "cudaMalloc(depthwise weights)");
+          dev_allocs_.push_back(d);
+          check(cudaMemcpy(d, r.data(), r.size() * 2, cudaMemcpyHostToDevice), "upload depthwise weights");
+          dw = static_cast<__half *>(d);
+        }
+        st.launch = [this, x, out, dw, bptr, K, S, P, act](int B, cudaStream_t s) {
+          return launch_depthwise_v4(view(x), dw, bptr, view(out), B, K, S, P, act, s);
+        };
+      } else {
+        st.family = "conv_direct";
+        const __half *wptr = T_[(size_t)w].dptr;
+        st.launch = [this, x, out, wptr, bptr, K, S, P, G, act](int B, cudaStream_t s) {
+          const View4 ov = view(out);
+          return launch_conv_direct_v4(view(x), wptr, bptr, nullptr, View4{}, ov, B, ov.C, K, S, P, G, act, 0, s);
+        };
+      }
+      steps_.push_back(std::move(st));
+      continue;
+    }
+
+    // ---------------------------------------------------------------- small ops
+    for (const auto &in : n.ins)
+      if (in != "-") st.bytes_img += act_bytes(tid(in)), st.bytes_fixed += init_bytes(tid(in));
+    st.bytes_img += act_bytes(out);
+    const TensorRt &ot = T_[(size_t)out];
+    if (op == "ew_binary") {
+      const int a = tid(n.ins[0]), b = tid(n.ins[1]), opc = n.ai("op", 0);
+      const bool same = elementwise_same(n);
+      const int bsc = n.ai("b_scalar", 0);
+      const bool all_dense = ot.dense && T_[(size_t)a].dense && T_[(size_t)b].dense;
+      if (same && all_dense) {
+        const int64_t per = ot.numel;
+        st.launch = [this, a, b, out, per, opc, bsc](int B, cudaStream_t s) {
+          const TensorRt &ta = T_[(size_t)a], &tb = T_[(size_t)b];
+          return launch_ew_binary_flat(ta.dptr, tb.dptr, T_[(size_t)out].dptr, per * B, opc, bsc, per, B,
+                                       ta.is_init ? 0 : ta.numel, tb.is_init ? 0 : tb.numel, s);
+        };
+      } else if (same || per_channel_bcast(p, n, nullptr)) {
+        int scale_slot = -1;
+        const bool pc = !same && per_channel_bcast(p, n, &scale_slot);
+        st.launch = [this, a, b, out, opc, bsc, pc, scale_slot](int B, cudaStream_t s) {
+          const View4 ov = view(out);
+          auto operand = [&](int t, bool bcast) {
+            View4 v = view(t);
+            if (bcast) {  // [1,C,1,1] (or scalar) broadcast over H, W
+              const TensorRt &tt = T_[(size_t)t];
+              v.C = ov.C;
+              v.H = ov.H;
+              v.W = ov.W;
+              v.sc = tt.numel == 1 ? 0 : 1;
+              v.sy = v.sx = 0;
+              v.sb = tt.is_init ? 0 : tt.numel;
+            }
+            return v;
+          };
+          const View4 av = operand(a, pc && scale_slot == 0);
+          const View4 bv = operand(b, (pc && scale_slot == 1) || bsc == 1);
+          return launch_ew_binary_v4(av, bv, ov, B, opc, s);
+        };
+      } else {
+        // rank-generic broadcast on planar operands; dim 0 is the batch
+        const std::vector<int64_t> bd = parse_ints(n.attr.at("bdims"));
+        const int rank = (int)bd.size() / 3;
+        if (rank < 1 || rank > kMaxRank) throw std::runtime_error("CudaPlanModel: bad bdims for " + n.outs[0]);
+        st.launch = [this, a, b, out, opc, bd, rank](int B, cudaStream_t s) {
+          BcastArgs g{};
+          g.rank = rank;
+          for (int r = 0; r < rank; ++r) {
+            g.dims[r] = bd[(size_t)r];
+            g.as[r] = bd[(size_t)(rank + r)];
+            g.bs[r] = bd[(size_t)(2 * rank + r)];
+          }
+          const TensorRt &ta = T_[(size_t)a], &tb = T_[(size_t)b];
+          g.dims[0] = B;
+          g.as[0] = (ta.is_init || ta.dims.size() != (size_t)rank) ? 0 : ta.numel;
+          g.bs[0] = (tb.is_init || tb.dims.size() != (size_t)rank) ? 0 : tb.numel;
+          return launch_ew_binary_bcast(ta.dptr, tb.dptr, T_[(size_t)out].dptr, g, opc, s);
+        };
+      }
+    } else if (op == "ew_unary") {
+      const int x = tid(n.ins[0]), opc = n.ai("op", 0);
+      if (ot.dense && T_[(size_t)x].dense) {
+        st.launch = [this, x, out, opc](int B, cudaStream_t s) {
+          return launch_ew_unary_flat(T_[(size_t)x].dptr, T_[(size_t)out].dptr, T_[(size_t)out].numel * B, opc, s);
+        };
+      } else {
+        st.launch = [this, x, out, opc](int B, cudaStream_t s) {
+          return launch_ew_unary_v4(view(x), view(out), B, opc, s);
+        };
+      }
+    } else if (op == "copy_c") {
+      if (ot.root != out) continue;  // zero-copy channel view
+      const int x = tid(n.ins[0]);
+      const int c0 = n.ai("c0", 0), cnt = n.ai("cnt", 0), HW = n.ai("HW", 1);
+      if (n.ai("dst_off", 0) != 0) throw std::runtime_error("CudaPlanModel: copy_c with dst_off is not supported");
+      st.launch = [this, x, out, c0, cnt, HW](int B, cudaStream_t s) {
+        View4 xv = view(x);
+        const View4 ov = view(out);
+        if (T_[(size_t)x].dims.size() != 4) {  // generic [1, C, HW...] planar source
+          xv.C = (int)(T_[(size_t)x].numel / HW);
+          xv.H = 1;
+          xv.W = HW;
+          xv.sc = HW;
+          xv.sy = HW;
+          xv.sx = 1;
+        }
+        xv.ptr += (int64_t)c0 * xv.sc;
+        xv.C = cnt;
+        View4 o2 = ov;
+        if (T_[(size_t)out].dims.size() != 4) {
+          o2.C = cnt;
+          o2.H = 1;
+          o2.W = HW;
+          o2.sc = HW;
+          o2.sy = HW;
+          o2.sx = 1;
+        }
+        xv.H = o2.H;
+        xv.W = o2.W;
+        return launch_copy_v4(xv, o2, B, s);
+      };
+    } else if (op == "slice_axis") {
+      const int x = tid(n.ins[0]);
+      const int64_t outer = n.ai("outer", 1), inner = n.ai("inner", 1);
+      const int axdim = n.ai("axdim", 0), start = n.ai("start", 0), len = n.ai("len", 0);
+      st.launch = [this, x, out, outer, inner, axdim, start, len](int B, cudaStream_t s) {
+        return launch_slice_axis(T_[(size_t)x].dptr, T_[(size_t)out].dptr, outer * B, axdim, inner, start, len, s);
+      };
+    } else if (op == "concat4") {
+      const int cnt[4] = {n.ai("ca", 0), n.ai("cb", 0), n.ai("cc", 0), n.ai("cd", 0)};
+      const int64_t outer = n.ai("outer", 1), inner = n.ai("inner", 1);
+      int srcs[4] = {-1, -1, -1, -1};
+      for (int s = 0; s < 4; ++s)
+        if (cnt[s] > 0) srcs[s] = tid(n.ins[(size_t)s]);
+      if (ot.nhwc) {
+        st.launch = [this, srcs, cnt, out](int B, cudaStream_t s) {
+          int c0 = 0;
+          for (int k = 0; k < 4; ++k) {
+            if (cnt[k] <= 0) continue;
+            View4 ov = view(out);
+            ov.ptr += (int64_t)c0 * ov.sc;
+            ov.C = cnt[k];
+            const cudaError_t e = launch_copy_v4(view(srcs[k]), ov, B, s);
+            if (e != cudaSuccess) return e;
+            c0 += cnt[k];
+          }
+          return cudaSuccess;
+        };
+      } else {
+        for (int s = 0; s < 4; ++s)
+          if (srcs[s] >= 0 && !T_[(size_t)srcs[s]].dense && !T_[(size_t)srcs[s]].is_init)
+            throw std::runtime_error("CudaPlanModel: planar concat of a channels-last source: " + n.outs[0]);
+        st.launch = [this, srcs, cnt, out, outer, inner](int B, cudaStream_t s) {
+          ConcatSrc cs[4];
+          for (int k = 0; k < 4; ++k) {
+            cs[k].ptr = srcs[k] >= 0 ? T_[(size_t)srcs[k]].dptr : nullptr;
+            cs[k].c = cnt[k];
+            cs[k].shared = (srcs[k] >= 0 && T_[(size_t)srcs[k]].is_init) ? 1 : 0;
+          }
+          return launch_concat_planar(cs, 4, T_[(size_t)out].dptr, outer * B, outer, inner, s);
+        };
+      }
+    } else if (op == "maxpool") {
+      const int x = tid(n.ins[0]);
+      const int K = n.ai("K", 5), S = n.ai("S", 1), P = n.ai("P", 2);
+      st.launch = [this, x, out, K, S, P](int B, cudaStream_t s) {
+        return launch_maxpool_v4(view(x), view(out), B, K, S, P, s);
+      };
+    } else if (op == "resize_nn") {
+      const int x = tid(n.ins[0]);
+      const int S = n.ai("S", 2);
+      st.launch = [this, x, out, S](int B, cudaStream_t s) { return launch_resize_nn_v4(view(x), view(out), B, S, s); };
+    } else if (op == "softmax_axis") {
+      const int x = tid(n.ins[0]);
+      const int64_t outer = n.ai("outer", 1), inner = n.ai("inner", 1);
+      const int axdim = n.ai("axdim", 0);
+      st.launch = [this, x, out, outer, inner, axdim](int B, cudaStream_t s) {
+        return launch_softmax_axis(T_[(size_t)x].dptr, T_[(size_t)out].dptr, outer * B, axdim, inner, s);
+      };
+    } else if (op == "permute_0213") {
+      const int x = tid(n.ins[0]);
+      const int D1 = n.ai("D1", 1), D2 = n.ai("D2", 1), mode = n.ai("mode", 0);
+      const int64_t I = n.ai("I", 1);
+      st.launch = [this, x, out, D1, D2, I, mode](int B, cudaStream_t s) {
+        return launch_permute_0213(T_[(size_t)x].dptr, T_[(size_t)out].dptr, B, D1, D2, I, mode, s);
+      };
+    } else if (op == "gap") {
+      const int x = tid(n.ins[0]);
+      st.launch = [this, x, out](int B, cudaStream_t s) { return launch_gap_v4(view(x), T_[(size_t)out].dptr, B, s); };
+    } else if (op == "bmm") {
+      const int a = tid(n.ins[0]), b = tid(n.ins[1]);
+      const auto &ad = T_[(size_t)a].dims, &bd = T_[(size_t)b].dims;
+      if (ad.size() != 4 || bd.size() != 4) throw std::runtime_error("CudaPlanModel: bmm expects 4-D operands");
+      const int B1 = (int)ad[1], M = (int)ad[2], K = (int)ad[3], Nn = (int)bd[3];
+      st.flops_img = 2.0 * B1 * M * K * Nn;
+      st.launch = [this, a, b, out, B1, M, K, Nn](int B, cudaStream_t s) {
+        const TensorRt &ta = T_[(size_t)a], &tb = T_[(size_t)b];
+        return launch_bmm(ta.dptr, tb.dptr, T_[(size_t)out].dptr, B, B1, M, K, Nn, ta.is_init ? 0 : ta.numel,
+                          tb.is_init ? 0 : tb.numel, s);
+      };
+    } else if (op == "bias_add") {
+      const int x = tid(n.ins[0]), b = tid(n.ins[1]);
+      const int HW = n.ai("HW", 1);
+      st.launch = [this, x, b, out, HW](int B, cudaStream_t s) {
+        return launch_bias_add(T_[(size_t)x].dptr, T_[(size_t)b].dptr, T_[(size_t)out].dptr, T_[(size_t)out].numel,
+                               HW, B, s);
+      };
+    } else {
+      throw std::runtime_error("PlanModel: unknown op: " + op);
+    }
+    // small ops read/write their operands densely unless they are views
+    for (const auto &in : n.ins) {
+      if (in == "-") continue;
+      const TensorRt &t = T_[(size_t)tid(in)];
+      if (!t.dense && !t.nhwc && !t.is_init)
+        throw std::runtime_error("CudaPlanModel: internal layout error at " + n.outs[0]);
+    }
+    steps_.push_back(std::move(st));
+  }
+  stats_.steps = (int)steps_.size();
+}
+
+// ============================================================================ execution
+void Engine::set_stream(cudaStream_t s) {
+  if (own_stream_ && stream_ && s != stream_) {
+    cudaStreamSynchronize(stream_);
+    cudaStreamDestroy(stream_);
+    own_stream_ = false;
+  }
+  stream_ = s;
+  for (auto &kv : graphs_) cudaGraphExecDestroy(kv.second);
+  graphs_.clear();
+}
+
+void Engine::upload_input_f16(const void *src, int batch, bool on_device) {
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  check(cudaMemcpyAsync(input_device_ptr(), src, (size_t)input_numel() * batch * 2,
+                        on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream_),
+        "input copy");
+}
+
+void Engine::upload_input_f32(const float *src, int batch, bool on_device) {
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  const int64_t n = input_numel() * batch;
+  const float *d = src;
+  if (!on_device) {
+    check(cudaMemcpyAsync(in_f32_, src, (size_t)n * 4, cudaMemcpyHostToDevice, stream_), "input copy");
+    d = in_f32_;
+  }
+  check(launch_f32_to_f16_trunc(d, input_device_ptr(), n, stream_), "input conversion");
+}
+
+void Engine::capture(int batch) {
+  cudaGraph_t g = nullptr;
+  check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  cudaError_t le = cudaSuccess;
+  std::string where;
+  try {
+    for (auto &s : steps_) {
+      le = s.launch(batch, stream_);
+      if (le != cudaSuccess) {
+        where = s.name;
+        break;
+      }
+    }
+  } catch (...) {
+    cudaStreamEndCapture(stream_, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  const cudaError_t ee = cudaStreamEndCapture(stream_, &g);
+  if (le != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    throw std::runtime_error("CudaPlanModel: launch failed during capture at " + where + ": " + cudaGetErrorString(le));
+  }
+  check(ee, "cudaStreamEndCapture");
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  check(ie, "cudaGraphInstantiate");
+  graphs_[batch] = ex;
+}
+
+void Engine::run(int batch) {
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  if (flags_ & kFlagNoGraph) {
+    for (auto &s : steps_) {
+      const cudaError_t e = s.launch(batch, stream_);
+      if (e != cudaSuccess) throw std::runtime_error("CudaPlanModel: launch failed at " + s.name + ": " + cudaGetErrorString(e));
+    }
+    return;
+  }
+  auto it = graphs_.find(batch);
+  if (it == graphs_.end()) {
+    capture(batch);
+    it = graphs_.find(batch);
+  }
+  check(cudaGraphLaunch(it->second, stream_), "cudaGraphLaunch");
+}
+
+void Engine::run_profiled(int batch, std::vector<float> *step_ms) {
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  std::vector<cudaEvent_t> ev(steps_.size() + 1);
+  for (auto &e : ev) check(cudaEventCreate(&e), "cudaEventCreate");
+  check(cudaEventRecord(ev[0], stream_), "cudaEventRecord");
+  for (size_t i = 0; i < steps_.size(); ++i) {
+    const cudaError_t e = steps_[i].launch(batch, stream_);
+    if (e != cudaSuccess) throw std::runtime_error("CudaPlanModel: launch failed at " + steps_[i].name);
+    check(cudaEventRecord(ev[i + 1], stream_), "cudaEventRecord");
+  }
+  check(cudaEventSynchronize(ev.back()), "cudaEventSynchronize");
+  step_ms->assign(steps_.size(), 0.0f);
+  for (size_t i = 0; i < steps_.size(); ++i) check(cudaEventElapsedTime(&(*step_ms)[i], ev[i], ev[i + 1]), "elapsed");
+  for (auto &e : ev) cudaEventDestroy(e);
+}
+
+void Engine::download_output_f16(int i, void *dst, int batch, bool on_device) {
+  const TensorRt &t = T_[(size_t)tid(output_name(i))];
+  if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
+  check(cudaMemcpyAsync(dst, t.dptr, (size_t)t.numel * batch * 2,
+                        on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, stream_),
+        "output copy");
+}
+
+void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
+  const TensorRt &t = T_[(size_t)tid(output_name(i))];
+  if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
+  const int64_t n = t.numel * batch;
+  if (on_device) {
+    check(launch_f16_to_f32(t.dptr, dst, n, stream_), "output conversion");
+    return;
+  }
+  // convert on the device into the f32 staging buffer, then one copy
+  if (scratch_elems_ < n) {
+    if (scratch_) cudaFree(scratch_);
+    check(cudaMalloc(&scratch_, (size_t)n * 4), "cudaMalloc(scratch)");
+    scratch_elems_ = n * 2;  // counted in halves
+  }
+  float *tmp = reinterpret_cast<float *>(scratch_);
+  check(launch_f16_to_f32(t.dptr, tmp, n, stream_), "output conversion");
+  check(cudaMemcpyAsync(dst, tmp, (size_t)n * 4, cudaMemcpyDeviceToHost, stream_), "output copy");
+}
+
+bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {
+  auto it = tid_.find(name);
+  if (it == tid_.end()) return false;
+  const TensorRt &t = T_[(size_t)it->second];
+  if (t.dptr == nullptr) return false;
+  const int64_t n = t.numel * (t.is_init ? 1 : batch);
+  if (t.dense) {
+    check(cudaMemcpyAsync(host_dst, t.dptr, (size_t)n * 2, cudaMemcpyDeviceToHost, stream_), "tensor copy");
+  } else {
+    if (scratch_elems_ < n) {
+      if (scratch_) cudaFree(scratch_);
+      check(cudaMalloc(&scratch_, (size_t)n * 4), "cudaMalloc(scratch)");
+      scratch_elems_ = n * 2;
+    }
+    View4 src = view(it->second);
+    View4 dst = src;
+    dst.ptr = scratch_;
+    dst.sx = 1;
+    dst.sy = dst.W;
+    dst.sc = (int64_t)dst.H * dst.W;
+    dst.sb = (int64_t)dst.C * dst.H * dst.W;
+    check(launch_copy_v4(src, dst, batch, stream_), "tensor relayout");
+    check(cudaMemcpyAsync(host_dst, scratch_, (size_t)n * 2, cudaMemcpyDeviceToHost, stream_), "tensor copy");
+  }
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  return true;
+}
+
+void Engine::synchronize() { check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize"); }
+
+int Engine::device_status() {
+  int v = 0;
+  check(cudaMemcpyAsync(&v, status_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "status read");
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  if (v) check(cudaMemsetAsync(status_, 0, sizeof(int), stream_), "status reset");
+  return v;
+}
+
+std::string Engine::describe() const {
+  std::ostringstream os;
+  for (const auto &t : T_) {
+    os << "tensor " << t.name << (t.is_init ? " init" : "") << (t.nhwc ? " nhwc" : " planar") << " root="
+       << T_[(size_t)t.root].name << " off=" << t.elem_off;
+    if ((int)(&t - &T_[0]) == t.root && !t.is_init)
+      os << " arena=" << t.arena_off << " life=[" << t.birth << "," << t.death << "] bytes/img=" << t.bytes_per_img;
+    os << "\n";
+  }
+  for (const auto &s : steps_) os << "step " << s.family << " " << s.name << "\n";
+  return os.str();
+}
+
+}  // namespace ivb

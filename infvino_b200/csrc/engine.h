@@ -1,0 +1,144 @@
+// CudaPlanModel engine: one plan, one device, batch 1..max_batch.
+//
+// Load: parse -> layout planning (NHWC for convolution-region 4-D tensors,
+// planar NCHW elsewhere) -> load-time fusions -> liveness arena allocation ->
+// lowering of every node to a kernel launch with all weights repacked and
+// resident.  Run: the lowered launch list is captured once per batch size into
+// a CUDA graph and replayed.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "kernels/ops.cuh"
+#include "plan.h"
+
+namespace ivb {
+
+enum EngineFlags : unsigned {
+  kFlagNoGraph = 1u << 0,     // eager launches instead of CUDA graph replay
+  kFlagNoFusion = 1u << 1,    // skip the concat->conv1x1 and residual rewrites
+  kFlagDryRun = 1u << 2,      // host-only: plan, layout, allocation; no device work
+  kFlagNoTensorCores = 1u << 3,  // route convolutions to the CUDA-core direct kernel
+};
+
+struct TensorRt {
+  std::string name;
+  std::vector<int64_t> dims;
+  int64_t numel = 0;            // per image
+  bool is_init = false, is_input = false, is_output = false;
+  bool nhwc = false;            // channels-last storage (4-D only)
+  bool dense = true;            // contiguous per image in plan (row-major) order
+  int root = -1;                // storage owner (self when it owns storage)
+  int64_t elem_off = 0;         // element offset inside the root's storage
+  int C = 0, H = 0, W = 0;      // 4-D view geometry (rank-4 tensors)
+  int Cs = 0;                   // NHWC channel stride of the storage
+  int64_t sb = 0, sc = 0, sy = 0, sx = 0;  // per-image element strides
+  int64_t bytes_per_img = 0;    // roots only
+  int64_t arena_off = -1;       // roots only, bytes
+  int birth = -1, death = -1;   // roots only, node indices
+  __half *dptr = nullptr;       // element (image 0, offset) on the device
+};
+
+struct Step {
+  std::string name;             // node op + output tensor
+  std::string family;           // kernel family (profiling key)
+  int node = -1;
+  double flops_img = 0.0;       // algorithmic FLOPs per image (2 * MACs)
+  double bytes_img = 0.0;       // algorithmic activation bytes per image (inputs + outputs, once)
+  double bytes_fixed = 0.0;     // weights / constants, read once per launch
+  std::function<cudaError_t(int, cudaStream_t)> launch;
+};
+
+struct EngineStats {
+  int64_t requested_bytes = 0;  // sum of per-tensor storage at max_batch
+  int64_t arena_bytes = 0;      // liveness-packed arena
+  int64_t weight_bytes = 0;
+  int roots = 0, views = 0, nhwc_tensors = 0, steps = 0;
+  int fusions_concat = 0, fusions_res = 0;
+  int overlap_errors = 0;       // allocator self-check (must be 0)
+};
+
+class Engine {
+ public:
+  Engine(const std::string &plan_path, int device, int max_batch, unsigned flags);
+  ~Engine();
+  Engine(const Engine &) = delete;
+  Engine &operator=(const Engine &) = delete;
+
+  // ---- plan facts
+  const std::string &input_name() const { return plan_->input(); }
+  const std::vector<int64_t> &input_dims() const;
+  int64_t input_numel() const;
+  int output_count() const { return (int)plan_->outputs().size(); }
+  const std::string &output_name(int i) const { return plan_->outputs().at((size_t)i); }
+  const std::vector<int64_t> &output_dims(int i) const;
+  int64_t output_numel(int i) const;
+  int64_t tensor_numel(const std::string &name) const;
+  int max_batch() const { return max_batch_; }
+  int device() const { return device_; }
+  const EngineStats &stats() const { return stats_; }
+  const std::vector<Step> &steps() const { return steps_; }
+  std::string describe() const;  // one line per tensor / step (diagnostics)
+
+  // ---- execution (asynchronous on the engine stream unless stated)
+  void set_stream(cudaStream_t s);
+  cudaStream_t stream() const { return stream_; }
+  void upload_input_f16(const void *src, int batch, bool src_on_device);
+  void upload_input_f32(const float *src, int batch, bool src_on_device);  // reference truncating cast
+  void run(int batch);
+  void run_profiled(int batch, std::vector<float> *step_ms);  // eager, events around each step
+  void download_output_f16(int i, void *dst, int batch, bool dst_on_device);
+  void download_output_f32(int i, float *dst, int batch, bool dst_on_device);
+  // Plan-order (NCHW) copy of any tensor for `batch` images into host memory.
+  bool read_tensor_f16(const std::string &name, void *host_dst, int batch);
+  void synchronize();
+  int device_status();  // kernel status word (0 = ok), resets it
+  __half *input_device_ptr() const;
+  float *input_f32_staging() const { return in_f32_; }
+
+ private:
+  void plan_layouts();
+  void build_tensors();
+  void allocate();
+  void upload_weights();
+  void lower();
+  void check(cudaError_t e, const char *what) const;
+  int tid(const std::string &name) const;
+  View4 view(int t) const;                 // image-0 view with per-image strides
+  void capture(int batch);
+
+  std::unique_ptr<Plan> plan_;
+  int device_ = 0;
+  int max_batch_ = 1;
+  unsigned flags_ = 0;
+  bool dry_ = false;
+  int num_sms_ = 148;
+
+  std::vector<TensorRt> T_;
+  std::map<std::string, int> tid_;
+  std::set<std::string> nhwc_names_;
+  std::vector<Step> steps_;
+  EngineStats stats_;
+
+  cudaStream_t stream_ = nullptr;
+  bool own_stream_ = false;
+  uint8_t *arena_ = nullptr;
+  int64_t arena_bytes_ = 0;
+  std::vector<void *> dev_allocs_;  // weights and packed weights
+  int *status_ = nullptr;           // device status word
+  float *in_f32_ = nullptr;         // device staging for f32 input
+  __half *scratch_ = nullptr;       // read_tensor staging
+  int64_t scratch_elems_ = 0;
+  std::map<int, cudaGraphExec_t> graphs_;
+};
+
+}  // namespace ivb

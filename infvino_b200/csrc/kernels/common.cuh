@@ -1,0 +1,211 @@
+// Shared device helpers for the sm_100a kernels: fp16 epilogue math, mbarriers,
+// TMA (cp.async.bulk.tensor, no multicast), tcgen05 (TMEM alloc / MMA / commit /
+// load) and a bounded wait that reports a timeout instead of spinning forever.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ivb {
+
+// ------------------------------------------------------------------ activations
+// Canonical conv / gemm codes: 1=SiLU 2=ReLU 3=HardSwish 4=HardSigmoid 5=Sigmoid.
+// `kind` selects the reference kernel family whose exact f32 expression is used:
+//   0 = conv3x3_ov (only 1 and 3 act, kernels/conv_ov.cl:121-131)
+//   1 = gemm / gemv (1..5, kernels/gemm.cl:137-153, kernels/conv1x1.cl:52-68)
+//   2 = depthwise_f16 (1..4, HardSwish written f*(clamp/6), conv_general.cl:71-83)
+enum ActKind : int { kActConv3x3 = 0, kActGemm = 1, kActDepthwise = 2 };
+
+__device__ __forceinline__ float act_f32(float f, int act, int kind) {
+  switch (act) {
+    case 1:
+      return f / (1.0f + expf(-f));
+    case 2:
+      return (kind == kActConv3x3) ? f : fmaxf(f, 0.0f);
+    case 3:
+      if (kind == kActDepthwise) return f * (fminf(fmaxf(f + 3.0f, 0.0f), 6.0f) / 6.0f);
+      return f * fminf(fmaxf(f + 3.0f, 0.0f), 6.0f) / 6.0f;
+    case 4:
+      return (kind == kActConv3x3) ? f : fminf(fmaxf(f + 3.0f, 0.0f), 6.0f) / 6.0f;
+    case 5:
+      return (kind == kActConv3x3 || kind == kActDepthwise) ? f : 1.0f / (1.0f + expf(-f));
+    default:
+      return f;
+  }
+}
+
+// Epilogue rounding points of the reference: v = half(half(acc) + bias);
+// v = half(act(float(v))); v = half(v + res).  f32 arithmetic on two halves
+// followed by one rounding equals the correctly rounded half operation.
+__device__ __forceinline__ __half epilogue(float acc, float bias, int act, int kind) {
+  const float v = __half2float(__float2half_rn(acc)) + bias;
+  const float a = act_f32(__half2float(__float2half_rn(v)), act, kind);
+  return __float2half_rn(a);
+}
+
+// ------------------------------------------------------------------ smem/mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Error codes a kernel writes to its status word (first error wins).
+enum KernelStatus : int {
+  kStatusOk = 0,
+  kStatusTimeoutFull = 1,
+  kStatusTimeoutEmpty = 2,
+  kStatusTimeoutAcc = 3,
+  kStatusTimeoutAccEmpty = 4,
+  kStatusTimeoutDrain = 5,
+  kStatusBadConfig = 6,
+};
+
+// Bounded wait: gives up after ~`limit_cycles` SM clocks, records `code` in the
+// global status word and raises the CTA-wide abort flag so the other roles stop.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                                  int *status, int code,
+                                                  long long limit_cycles = 4000000000LL) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (*abort_flag) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - t0 > limit_cycles) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+// ------------------------------------------------------------------ TMA
+__device__ __forceinline__ void tma_prefetch_desc(const void *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (fp16 in, fp32 accumulate).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once all prior tcgen05.mma of this thread have completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major operand with a swizzled canonical
+// layout: rows of `row_bytes` (= swizzle span 32/64/128 B), 8-row groups
+// `8*row_bytes` apart (stride byte offset); version field 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t row_bytes) {
+  uint32_t layout;
+  switch (row_bytes) {
+    case 128: layout = 2; break;  // SWIZZLE_128B
+    case 64: layout = 4; break;   // SWIZZLE_64B
+    default: layout = 6; break;   // SWIZZLE_32B
+  }
+  const uint64_t start = (saddr & 0x3FFFFu) >> 4;
+  const uint64_t lbo = 1;                         // ignored for swizzled K-major
+  const uint64_t sbo = (8u * row_bytes) >> 4;     // 8-row group stride
+  return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B f16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4)                       // D format f32
+         | (0u << 7) | (0u << 10)        // A, B f16
+         | (0u << 15) | (0u << 16)       // K-major A and B
+         | ((uint32_t)(N >> 3) << 17)    // N / 8
+         | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+}  // namespace ivb

@@ -1,0 +1,52 @@
+// Parameter block of the tcgen05 implicit-GEMM convolution (1x1 / 3x3, stride
+// 1 or 2, up to four concatenated NHWC sources), shared by host and device.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+namespace ivb {
+
+constexpr int kConvMaxSrc = 4;
+constexpr int kConvMaxStages = 12;
+constexpr int kConvThreads = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
+
+struct alignas(64) ConvTcArgs {
+  CUtensorMap mapA[kConvMaxSrc];  // 1x1: 2-D (C, pixels); 3x3: 4-D (C, W, H, B)
+  CUtensorMap mapB;               // packed weights, 2-D (Kp, Np), K-major
+  int ksize;                      // 1 or 3
+  int stride, pad;
+  int nsrc;
+  int src_chunks[kConvMaxSrc];    // BK-chunks per source
+  int taps;                       // ksize * ksize
+  int BK;                         // 16 / 32 / 64 halves (one swizzle span)
+  int BN;                         // N tile, multiple of 16, <= 256
+  int n_tiles;                    // Np / BN
+  int num_kb;                     // K blocks per tile
+  int stages;
+  int resident_b;                 // 1: all of B stays in smem
+  // M tiling
+  long long m_total;              // 1x1: pixels (B*H*W)
+  int m_tiles;
+  int Ho, Wo, TH, TW, tiles_x, tiles_per_img;
+  int tile_rows;                  // rows of the A tile actually filled (TH*TW or 128)
+  // epilogue
+  const __half *bias;             // [Np] or null
+  int cout;
+  int act, act_kind;
+  __half *out;
+  long long o_sb, o_sc, o_sy, o_sx;
+  int out_vec;                    // NHWC-contiguous channels, 16B aligned
+  const __half *res;
+  long long r_sb, r_sc, r_sy, r_sx;
+  int res_vec;
+  int tmem_cols;
+  int smem_bytes;
+  int *status;
+};
+
+// Host-side launcher (conv_tc.cu).
+cudaError_t launch_conv_tc(const ConvTcArgs &args, int grid, cudaStream_t stream);
+
+}  // namespace ivb

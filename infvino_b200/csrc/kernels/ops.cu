@@ -1,0 +1,560 @@
+// Bandwidth-bound kernels of the plan executor (CUDA cores, no tensor cores):
+// elementwise / broadcast, layout copies, concat, slice, maxpool, nearest
+// resize, softmax, permute, global average pool, batched matmul, depthwise and
+// direct convolutions, the Cin<=4 stem, and the f32<->f16 conversions.
+//
+// Arithmetic follows the reference kernels (kernels/ops.cl, kernels/conv_general.cl):
+// inputs are widened to f32, the op is evaluated in f32 and rounded once to fp16.
+// 4-D operands are strided views so one kernel serves NHWC and planar tensors.
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace ivb {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(long long n, int threads = kThreads) {
+  long long g = (n + threads - 1) / threads;
+  if (g > 148LL * 64) g = 148LL * 64;  // grid-stride loops beyond this
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+__device__ __forceinline__ float binop(float a, float b, int op) {
+  if (op == 0) return a + b;
+  if (op == 1) return a - b;
+  if (op == 2) return a * b;
+  return a / b;
+}
+
+// ew_unary codes (kernels/ops.cl:49-62): 0=sigmoid 1=silu 2=relu 3=hswish 4=hsigmoid
+__device__ __forceinline__ float unop(float v, int op) {
+  if (op == 0) return 1.0f / (1.0f + expf(-v));
+  if (op == 1) return v / (1.0f + expf(-v));
+  if (op == 2) return fmaxf(v, 0.0f);
+  if (op == 3) return v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f) / 6.0f;
+  if (op == 4) return fminf(fmaxf(v + 3.0f, 0.0f), 6.0f) / 6.0f;
+  return v;
+}
+
+// decompose a linear index over (b, c, y, x) in the iteration order that makes
+// the OUTPUT view coalesced: channel-fastest for NHWC, x-fastest otherwise.
+struct Idx4 {
+  long long b;
+  int c, y, x;
+};
+__device__ __forceinline__ Idx4 idx4(long long i, const View4 &o, bool cfast) {
+  Idx4 r;
+  if (cfast) {
+    r.c = (int)(i % o.C);
+    long long t = i / o.C;
+    r.x = (int)(t % o.W);
+    t /= o.W;
+    r.y = (int)(t % o.H);
+    r.b = t / o.H;
+  } else {
+    r.x = (int)(i % o.W);
+    long long t = i / o.W;
+    r.y = (int)(t % o.H);
+    t /= o.H;
+    r.c = (int)(t % o.C);
+    r.b = t / o.C;
+  }
+  return r;
+}
+__device__ __forceinline__ long long at(const View4 &v, const Idx4 &i) {
+  return i.b * v.sb + (long long)i.c * v.sc + (long long)i.y * v.sy + (long long)i.x * v.sx;
+}
+
+// ------------------------------------------------------------------ elementwise
+__global__ void ew_binary_flat_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
+                                 long long n, int op, int b_scalar, long long per_img, long long a_bs,
+                                 long long b_bs) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long img = i / per_img, r = i - img * per_img;
+    const float av = __half2float(a[img * a_bs + r]);
+    const float bv = __half2float(b_scalar ? b[img * b_bs] : b[img * b_bs + r]);
+    y[i] = __float2half_rn(binop(av, bv, op));
+  }
+}
+
+__global__ void ew_binary_v4_k(View4 a, View4 b, View4 y, long long n, int op, bool cfast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 ix = idx4(i, y, cfast);
+    const float av = __half2float(a.ptr[at(a, ix)]);
+    const float bv = __half2float(b.ptr[at(b, ix)]);
+    y.ptr[at(y, ix)] = __float2half_rn(binop(av, bv, op));
+  }
+}
+
+__global__ void ew_binary_bcast_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
+                                  BcastArgs g, long long n, int op) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long rem = i, ai = 0, bi = 0;
+    for (int r = g.rank - 1; r >= 0; --r) {
+      const long long coord = rem % g.dims[r];
+      rem /= g.dims[r];
+      ai += coord * g.as[r];
+      bi += coord * g.bs[r];
+    }
+    y[i] = __float2half_rn(binop(__half2float(a[ai]), __half2float(b[bi]), op));
+  }
+}
+
+__global__ void ew_unary_flat_k(const __half *__restrict__ x, __half *__restrict__ y, long long n, int op) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(unop(__half2float(x[i]), op));
+}
+
+__global__ void ew_unary_v4_k(View4 x, View4 y, long long n, int op, bool cfast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 ix = idx4(i, y, cfast);
+    y.ptr[at(y, ix)] = __float2half_rn(unop(__half2float(x.ptr[at(x, ix)]), op));
+  }
+}
+
+__global__ void copy_v4_k(View4 x, View4 y, long long n, bool cfast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 ix = idx4(i, y, cfast);
+    y.ptr[at(y, ix)] = x.ptr[at(x, ix)];
+  }
+}
+
+// ------------------------------------------------------------------ layout ops
+__global__ void slice_axis_k(const __half *__restrict__ x, __half *__restrict__ y, long long outer, int axdim,
+                             long long inner, int start, int len) {
+  const long long n = outer * len * inner;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long o = i / ((long long)len * inner), rem = i - o * ((long long)len * inner);
+    y[i] = x[(o * axdim + start) * inner + rem];
+  }
+}
+
+struct ConcatArgs {
+  ConcatSrc s[4];
+  int nsrc;
+  int sum;
+};
+__global__ void concat_k(ConcatArgs g, __half *__restrict__ y, long long outer, long long per_img_outer,
+                         long long inner) {
+  const long long n = outer * g.sum * inner;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i % inner;
+    const long long t = i / inner;
+    int ax = (int)(t % g.sum);
+    const long long o = t / g.sum;
+    int s = 0;
+    while (s < g.nsrc - 1 && ax >= g.s[s].c) {
+      ax -= g.s[s].c;
+      ++s;
+    }
+    const long long oo = g.s[s].shared ? (o % per_img_outer) : o;
+    y[i] = g.s[s].ptr[(oo * g.s[s].c + ax) * inner + r];
+  }
+}
+
+__global__ void maxpool_v4_k(View4 x, View4 y, long long n, int K, int S, int P, bool cfast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 o = idx4(i, y, cfast);
+    float m = -3.4e38f;
+    for (int kh = 0; kh < K; ++kh) {
+      const int yy = o.y * S - P + kh;
+      if (yy < 0 || yy >= x.H) continue;
+      for (int kw = 0; kw < K; ++kw) {
+        const int xx = o.x * S - P + kw;
+        if (xx < 0 || xx >= x.W) continue;
+        m = fmaxf(m, __half2float(x.ptr[o.b * x.sb + (long long)o.c * x.sc + (long long)yy * x.sy + (long long)xx * x.sx]));
+      }
+    }
+    y.ptr[at(y, o)] = __float2half_rn(m);
+  }
+}
+
+__global__ void resize_nn_v4_k(View4 x, View4 y, long long n, int S, bool cfast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 o = idx4(i, y, cfast);
+    y.ptr[at(y, o)] = x.ptr[o.b * x.sb + (long long)o.c * x.sc + (long long)(o.y / S) * x.sy + (long long)(o.x / S) * x.sx];
+  }
+}
+
+// serial softmax over the axis, one thread per (outer, inner) column (ops.cl:181-196)
+__global__ void softmax_axis_k(const __half *__restrict__ x, __half *__restrict__ y, long long outer, int axdim,
+                               long long inner) {
+  const long long n = outer * inner;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long o = i / inner, r = i - o * inner;
+    const __half *xp = x + o * axdim * inner + r;
+    __half *yp = y + o * axdim * inner + r;
+    float m = -3.4e38f;
+    for (int a = 0; a < axdim; ++a) m = fmaxf(m, __half2float(xp[(long long)a * inner]));
+    float s = 0.0f;
+    for (int a = 0; a < axdim; ++a) s += expf(__half2float(xp[(long long)a * inner]) - m);
+    for (int a = 0; a < axdim; ++a)
+      yp[(long long)a * inner] = __float2half_rn(expf(__half2float(xp[(long long)a * inner]) - m) / s);
+  }
+}
+
+__global__ void permute_0213_k(const __half *__restrict__ x, __half *__restrict__ y, long long n, int D1, int D2,
+                               long long I, int mode) {
+  const long long per = (long long)D1 * D2 * I;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long img = i / per, j = i - img * per;
+    const long long d1 = j / ((long long)D2 * I), rem = j - d1 * ((long long)D2 * I);
+    const long long d2 = rem / I, r = rem - d2 * I;
+    const long long o = (mode == 0) ? ((d2 * D1 + d1) * I + r) : ((d1 * I + r) * D2 + d2);
+    y[img * per + o] = x[i];
+  }
+}
+
+// global average pool: grid (batch, ceil(C/32)); 32 channels x 8 pixel lanes
+__global__ void gap_v4_k(View4 x, __half *__restrict__ y) {
+  __shared__ float part[8][33];
+  const int cl = threadIdx.x & 31, pl = threadIdx.x >> 5;
+  const long long b = blockIdx.x;
+  const int c = blockIdx.y * 32 + cl;
+  const int HW = x.H * x.W;
+  float acc = 0.0f;
+  if (c < x.C) {
+    for (int p = pl; p < HW; p += 8) {
+      const int yy = p / x.W, xx = p - yy * x.W;
+      acc += __half2float(x.ptr[b * x.sb + (long long)c * x.sc + (long long)yy * x.sy + (long long)xx * x.sx]);
+    }
+  }
+  part[pl][cl] = acc;
+  __syncthreads();
+  if (pl == 0 && c < x.C) {
+    float s = 0.0f;
+    for (int k = 0; k < 8; ++k) s += part[k][cl];
+    y[b * x.C + c] = __float2half_rn(s / (float)HW);
+  }
+}
+
+__global__ void bmm_k(const __half *__restrict__ A, const __half *__restrict__ B, __half *__restrict__ Y, long long n,
+                      int B1, int M, int K, int N, long long a_bs, long long b_bs) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int nn = (int)(i % N);
+    long long t = i / N;
+    const int m = (int)(t % M);
+    t /= M;
+    const int b1 = (int)(t % B1);
+    const long long b0 = t / B1;
+    const __half *ap = A + b0 * a_bs + ((long long)b1 * M + m) * K;
+    const __half *bp = B + b0 * b_bs + (long long)b1 * K * N + nn;
+    float acc = 0.0f;
+    for (int k = 0; k < K; ++k) acc += __half2float(ap[k]) * __half2float(bp[(long long)k * N]);
+    Y[i] = __float2half_rn(acc);
+  }
+}
+
+__global__ void bias_add_k(const __half *__restrict__ x, const __half *__restrict__ b, __half *__restrict__ y,
+                           long long n, long long per_img, int HW) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i % per_img;
+    y[i] = __float2half_rn(__half2float(x[i]) + __half2float(b[r / HW]));
+  }
+}
+
+// ------------------------------------------------------------------ convolutions
+// depthwise, weights repacked [K*K][C]; fp32 accumulation in (ky, kx) order,
+// then half(half(acc) + bias) -> act (depthwise_f16 expressions).
+__global__ void depthwise_v4_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias, View4 y,
+                               long long n, int K, int S, int P, int act, bool cfast) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 o = idx4(i, y, cfast);
+    float acc = 0.0f;
+    for (int ky = 0; ky < K; ++ky) {
+      const int iy = o.y * S - P + ky;
+      if (iy < 0 || iy >= x.H) continue;
+      for (int kx = 0; kx < K; ++kx) {
+        const int ix = o.x * S - P + kx;
+        if (ix < 0 || ix >= x.W) continue;
+        acc += __half2float(x.ptr[o.b * x.sb + (long long)o.c * x.sc + (long long)iy * x.sy + (long long)ix * x.sx]) *
+               __half2float(w[(ky * K + kx) * y.C + o.c]);
+      }
+    }
+    const float bv = bias ? __half2float(bias[o.c]) : 0.0f;
+    y.ptr[at(y, o)] = epilogue(acc, bv, act, kActDepthwise);
+  }
+}
+
+// NHWC fast path: 8 channels per thread with 16-byte loads/stores.
+__global__ void depthwise_nhwc8_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias, View4 y,
+                                  long long n8, int K, int S, int P, int act) {
+  const int C8 = y.C / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % C8);
+    long long t = i / C8;
+    const int ox = (int)(t % y.W);
+    t /= y.W;
+    const int oy = (int)(t % y.H);
+    const long long b = t / y.H;
+    const int c = c8 * 8;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    for (int ky = 0; ky < K; ++ky) {
+      const int iy = oy * S - P + ky;
+      if (iy < 0 || iy >= x.H) continue;
+      for (int kx = 0; kx < K; ++kx) {
+        const int ix = ox * S - P + kx;
+        if (ix < 0 || ix >= x.W) continue;
+        const uint4 xv = *reinterpret_cast<const uint4 *>(x.ptr + b * x.sb + (long long)iy * x.sy + (long long)ix * x.sx + c);
+        const uint4 wv = *reinterpret_cast<const uint4 *>(w + (ky * K + kx) * y.C + c);
+        const __half *xh = reinterpret_cast<const __half *>(&xv);
+        const __half *wh = reinterpret_cast<const __half *>(&wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __half2float(xh[j]) * __half2float(wh[j]);
+      }
+    }
+    __align__(16) __half out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = epilogue(acc[j], bias ? __half2float(bias[c + j]) : 0.0f, act, kActDepthwise);
+    *reinterpret_cast<uint4 *>(y.ptr + b * y.sb + (long long)oy * y.sy + (long long)ox * y.sx + c) =
+        *reinterpret_cast<const uint4 *>(out);
+  }
+}
+
+// generic direct convolution, weights in the plan layout [Cout][Cin/G][K][K]
+__global__ void conv_direct_v4_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias,
+                                 const __half *res_ptr, View4 res, View4 y, long long n, int K, int S, int P, int G,
+                                 int act, int epi, bool cfast) {
+  const int cin_g = x.C / G, cout_g = y.C / G;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const Idx4 o = idx4(i, y, cfast);
+    const int g = o.c / cout_g, ic0 = g * cin_g;
+    float acc = (epi == 0 && bias) ? __half2float(bias[o.c]) : 0.0f;
+    for (int ic = 0; ic < cin_g; ++ic)
+      for (int ky = 0; ky < K; ++ky) {
+        const int iy = o.y * S - P + ky;
+        if (iy < 0 || iy >= x.H) continue;
+        for (int kx = 0; kx < K; ++kx) {
+          const int ix = o.x * S - P + kx;
+          if (ix < 0 || ix >= x.W) continue;
+          acc += __half2float(x.ptr[o.b * x.sb + (long long)(ic0 + ic) * x.sc + (long long)iy * x.sy + (long long)ix * x.sx]) *
+                 __half2float(w[(((long long)o.c * cin_g + ic) * K + ky) * K + kx]);
+        }
+      }
+    __half v;
+    if (epi == 0) {  // conv_general.cl:42-47, codes 1=SiLU 2=HardSwish 3=ReLU 4=HardSigmoid
+      float r = acc;
+      if (act == 1) r = acc / (1.0f + expf(-acc));
+      else if (act == 2) r = acc * fminf(fmaxf(acc + 3.0f, 0.0f), 6.0f) / 6.0f;
+      else if (act == 3) r = fmaxf(acc, 0.0f);
+      else if (act == 4) r = fminf(fmaxf(acc + 3.0f, 0.0f), 6.0f) / 6.0f;
+      v = __float2half_rn(r);
+    } else {
+      v = epilogue(acc, bias ? __half2float(bias[o.c]) : 0.0f, act, epi == 1 ? kActGemm : kActConv3x3);
+    }
+    if (res_ptr) v = __float2half_rn(__half2float(v) + __half2float(res_ptr[at(res, o)]));
+    y.ptr[at(y, o)] = v;
+  }
+}
+
+// Stem conv3x3 with Cin <= 4: one thread per output pixel, all Cout channels.
+// Weights in shared memory as f32 [Cout][Cin*9]; accumulation order (ci, ky, kx).
+constexpr int kStemMaxCout = 64;
+__global__ void stem3x3_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias, View4 y,
+                          long long npix, int Cout, int S, int P, int act) {
+  __shared__ float ws[kStemMaxCout * 36];
+  __shared__ float bs[kStemMaxCout];
+  const int cin = x.C, kk = cin * 9;
+  for (int i = threadIdx.x; i < Cout * kk; i += blockDim.x) ws[i] = __half2float(w[i]);
+  for (int i = threadIdx.x; i < Cout; i += blockDim.x) bs[i] = bias ? __half2float(bias[i]) : 0.0f;
+  __syncthreads();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix; i += (long long)gridDim.x * blockDim.x) {
+    const int ox = (int)(i % y.W);
+    long long t = i / y.W;
+    const int oy = (int)(t % y.H);
+    const long long b = t / y.H;
+    float in[36];
+    for (int ci = 0; ci < cin; ++ci)
+      for (int ky = 0; ky < 3; ++ky) {
+        const int iy = oy * S - P + ky;
+        for (int kx = 0; kx < 3; ++kx) {
+          const int ix = ox * S - P + kx;
+          const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W;
+          in[ci * 9 + ky * 3 + kx] =
+              ok ? __half2float(x.ptr[b * x.sb + (long long)ci * x.sc + (long long)iy * x.sy + (long long)ix * x.sx]) : 0.0f;
+        }
+      }
+    const long long obase = b * y.sb + (long long)oy * y.sy + (long long)ox * y.sx;
+    for (int co = 0; co < Cout; co += 8) {
+      __align__(16) __half out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = co + j;
+        if (c < Cout) {
+          float acc = 0.0f;
+          for (int k = 0; k < kk; ++k) acc += in[k] * ws[c * kk + k];
+          out[j] = epilogue(acc, bs[c], act, kActConv3x3);
+        }
+      }
+      if (y.sc == 1 && co + 8 <= Cout && ((obase + co) & 7) == 0 && (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0) {
+        *reinterpret_cast<uint4 *>(y.ptr + obase + co) = *reinterpret_cast<const uint4 *>(out);
+      } else {
+        for (int j = 0; j < 8 && co + j < Cout; ++j) y.ptr[obase + (long long)(co + j) * y.sc] = out[j];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ conversions
+// include/infvino/Half.hpp:14-24: truncate the mantissa, flush exp <= 0 to +-0,
+// exp >= 31 to +-inf.
+__global__ void f32_to_f16_trunc_k(const float *__restrict__ x, __half *__restrict__ y, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const uint32_t u = __float_as_uint(x[i]);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const int e = (int)((u >> 23) & 0xff) - 112;
+    const uint32_t mant = u & 0x7fffffu;
+    uint16_t h;
+    if (e <= 0) h = (uint16_t)sign;
+    else if (e >= 31) h = (uint16_t)(sign | 0x7c00u);
+    else h = (uint16_t)(sign | ((uint32_t)e << 10) | (mant >> 13));
+    y[i] = __ushort_as_half(h);
+  }
+}
+
+__global__ void f16_to_f32_k(const __half *__restrict__ x, float *__restrict__ y, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = __half2float(x[i]);
+}
+
+inline bool cfast_of(const View4 &y) { return y.sc == 1; }
+inline long long numel4(const View4 &v, int batch) { return (long long)batch * v.C * v.H * v.W; }
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_ew_binary_flat(const __half *a, const __half *b, __half *y, long long n, int op, int b_scalar,
+                                  long long per_img, int batch, long long a_bs, long long b_bs, cudaStream_t st) {
+  (void)batch;
+  ew_binary_flat_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, n, op, b_scalar, per_img, a_bs, b_bs);
+  return cudaGetLastError();
+}
+cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cudaStream_t st) {
+  const long long n = numel4(y, batch);
+  ew_binary_v4_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, n, op, cfast_of(y));
+  return cudaGetLastError();
+}
+cudaError_t launch_ew_binary_bcast(const __half *a, const __half *b, __half *y, const BcastArgs &g, int op,
+                                   cudaStream_t st) {
+  long long n = 1;
+  for (int r = 0; r < g.rank; ++r) n *= g.dims[r];
+  ew_binary_bcast_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, g, n, op);
+  return cudaGetLastError();
+}
+cudaError_t launch_ew_unary_flat(const __half *x, __half *y, long long n, int op, cudaStream_t st) {
+  ew_unary_flat_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, op);
+  return cudaGetLastError();
+}
+cudaError_t launch_ew_unary_v4(View4 x, View4 y, int batch, int op, cudaStream_t st) {
+  const long long n = numel4(y, batch);
+  ew_unary_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, op, cfast_of(y));
+  return cudaGetLastError();
+}
+cudaError_t launch_copy_v4(View4 x, View4 y, int batch, cudaStream_t st) {
+  const long long n = numel4(y, batch);
+  copy_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, cfast_of(y));
+  return cudaGetLastError();
+}
+cudaError_t launch_slice_axis(const __half *x, __half *y, long long outer, int axdim, long long inner, int start,
+                              int len, cudaStream_t st) {
+  slice_axis_k<<<grid_for(outer * len * inner), kThreads, 0, st>>>(x, y, outer, axdim, inner, start, len);
+  return cudaGetLastError();
+}
+cudaError_t launch_concat_planar(const ConcatSrc *src, int nsrc, __half *y, long long outer, long long per_img_outer,
+                                 long long inner, cudaStream_t st) {
+  ConcatArgs g{};
+  g.nsrc = 0;
+  g.sum = 0;
+  for (int i = 0; i < nsrc; ++i) {
+    if (src[i].c <= 0) continue;
+    g.s[g.nsrc++] = src[i];
+    g.sum += src[i].c;
+  }
+  if (g.nsrc == 0) return cudaSuccess;
+  concat_k<<<grid_for(outer * g.sum * inner), kThreads, 0, st>>>(g, y, outer, per_img_outer, inner);
+  return cudaGetLastError();
+}
+cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, cudaStream_t st) {
+  const long long n = numel4(y, batch);
+  maxpool_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, K, S, P, cfast_of(y));
+  return cudaGetLastError();
+}
+cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t st) {
+  const long long n = numel4(y, batch);
+  resize_nn_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, S, cfast_of(y));
+  return cudaGetLastError();
+}
+cudaError_t launch_softmax_axis(const __half *x, __half *y, long long outer, int axdim, long long inner,
+                                cudaStream_t st) {
+  softmax_axis_k<<<grid_for(outer * inner), kThreads, 0, st>>>(x, y, outer, axdim, inner);
+  return cudaGetLastError();
+}
+cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, int D2, long long I, int mode,
+                                cudaStream_t st) {
+  const long long n = (long long)batch * D1 * D2 * I;
+  permute_0213_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, D1, D2, I, mode);
+  return cudaGetLastError();
+}
+cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st) {
+  dim3 grid(batch, (x.C + 31) / 32);
+  gap_v4_k<<<grid, 256, 0, st>>>(x, y);
+  return cudaGetLastError();
+}
+cudaError_t launch_bmm(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
+                       long long a_bs, long long b_bs, cudaStream_t st) {
+  const long long n = (long long)batch * B1 * M * N;
+  bmm_k<<<grid_for(n), kThreads, 0, st>>>(A, B, Y, n, B1, M, K, N, a_bs, b_bs);
+  return cudaGetLastError();
+}
+cudaError_t launch_bias_add(const __half *x, const __half *b, __half *y, long long per_img, int HW, int batch,
+                            cudaStream_t st) {
+  const long long n = per_img * batch;
+  bias_add_k<<<grid_for(n), kThreads, 0, st>>>(x, b, y, n, per_img, HW);
+  return cudaGetLastError();
+}
+cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int K, int S, int P,
+                                int act, cudaStream_t st) {
+  const bool vec = x.sc == 1 && y.sc == 1 && (y.C % 8) == 0 && (x.sx % 8) == 0 && (x.sy % 8) == 0 &&
+                   (x.sb % 8) == 0 && (y.sx % 8) == 0 && (y.sy % 8) == 0 && (y.sb % 8) == 0 &&
+                   (reinterpret_cast<uintptr_t>(x.ptr) & 15) == 0 && (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  if (vec) {
+    const long long n8 = numel4(y, batch) / 8;
+    depthwise_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, w, bias, y, n8, K, S, P, act);
+  } else {
+    const long long n = numel4(y, batch);
+    depthwise_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, w, bias, y, n, K, S, P, act, cfast_of(y));
+  }
+  return cudaGetLastError();
+}
+cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, const __half *res_ptr, View4 res,
+                                  View4 y, int batch, int Cout, int K, int S, int P, int G, int act, int epi,
+                                  cudaStream_t st) {
+  (void)Cout;
+  const long long n = numel4(y, batch);
+  conv_direct_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, w, bias, res_ptr, res, y, n, K, S, P, G, act, epi,
+                                                     cfast_of(y));
+  return cudaGetLastError();
+}
+cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int Cout, int S,
+                              int P, int act, cudaStream_t st) {
+  if (Cout > kStemMaxCout || x.C > 4) return cudaErrorInvalidValue;
+  const long long npix = (long long)batch * y.H * y.W;
+  stem3x3_k<<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, Cout, S, P, act);
+  return cudaGetLastError();
+}
+cudaError_t launch_f32_to_f16_trunc(const float *x, __half *y, long long n, cudaStream_t st) {
+  f32_to_f16_trunc_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_f16_to_f32(const __half *x, float *y, long long n, cudaStream_t st) {
+  f16_to_f32_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+}  // namespace ivb

@@ -1,0 +1,73 @@
+// Host-visible declarations of the bandwidth-bound kernels (ops.cu).
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ivb {
+
+// A 4-D activation view: element (b, c, y, x) lives at ptr[b*sb + c*sc + y*sy + x*sx].
+// NHWC: sc = 1, sx = Cs, sy = W*Cs, sb = H*W*Cs.  Planar NCHW: sx = 1, sy = W,
+// sc = H*W, sb = C*H*W.  A stride of 0 broadcasts that dimension.
+struct View4 {
+  __half *ptr;
+  int C, H, W;
+  long long sb, sc, sy, sx;
+};
+
+constexpr int kMaxRank = 8;
+
+struct BcastArgs {          // rank-generic broadcast binary op (planar operands)
+  int rank;
+  long long dims[kMaxRank];  // output dims, dims[0] = batch
+  long long as[kMaxRank], bs[kMaxRank];
+};
+
+cudaError_t launch_ew_binary_flat(const __half *a, const __half *b, __half *y, long long n, int op, int b_scalar,
+                                  long long per_img, int batch, long long a_bstride, long long b_bstride,
+                                  cudaStream_t st);
+cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cudaStream_t st);
+cudaError_t launch_ew_binary_bcast(const __half *a, const __half *b, __half *y, const BcastArgs &args, int op,
+                                   cudaStream_t st);
+cudaError_t launch_ew_unary_flat(const __half *x, __half *y, long long n, int op, cudaStream_t st);
+cudaError_t launch_ew_unary_v4(View4 x, View4 y, int batch, int op, cudaStream_t st);
+cudaError_t launch_copy_v4(View4 x, View4 y, int batch, cudaStream_t st);
+cudaError_t launch_slice_axis(const __half *x, __half *y, long long outer, int axdim, long long inner, int start,
+                              int len, cudaStream_t st);
+struct ConcatSrc {
+  const __half *ptr;
+  int c;           // extent along the concat axis
+  int shared;      // 1: initializer (same data for every image)
+};
+cudaError_t launch_concat_planar(const ConcatSrc *src, int nsrc, __half *y, long long outer, long long per_img_outer,
+                                 long long inner, cudaStream_t st);
+cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, cudaStream_t st);
+cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t st);
+cudaError_t launch_softmax_axis(const __half *x, __half *y, long long outer, int axdim, long long inner,
+                                cudaStream_t st);
+cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, int D2, long long I, int mode,
+                                cudaStream_t st);
+cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st);
+cudaError_t launch_bmm(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
+                       long long a_bstride, long long b_bstride, cudaStream_t st);
+cudaError_t launch_bias_add(const __half *x, const __half *b, __half *y, long long per_img, int HW, int batch,
+                            cudaStream_t st);
+
+// Depthwise KxK (groups == C), reference depthwise_f16 epilogue.
+cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int K, int S,
+                                int P, int act, cudaStream_t st);
+// Direct CUDA-core convolution over views (any K/S/P/G).  epi: 0 = conv_general
+// (fp32 accumulator starting at bias, activation on f32, codes 2=HardSwish
+// 3=ReLU), 1 = gemm-family rounding, 2 = conv3x3 rounding.
+cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, const __half *res_ptr, View4 res,
+                                  View4 y, int batch, int Cout, int K, int S, int P, int G, int act, int epi,
+                                  cudaStream_t st);
+// Stem: 3x3 conv with Cin <= 4 (tiny K), conv3x3 rounding, NHWC or planar output.
+cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int Cout, int S,
+                              int P, int act, cudaStream_t st);
+// Reference host conversion on the device: f32 -> f16 by mantissa truncation.
+cudaError_t launch_f32_to_f16_trunc(const float *x, __half *y, long long n, cudaStream_t st);
+cudaError_t launch_f16_to_f32(const __half *x, float *y, long long n, cudaStream_t st);
+
+}  // namespace ivb

@@ -1,0 +1,128 @@
+"""Host-side logic, no GPU: C-ABI exports, plan parsing and its errors, the
+load-time rewrites, layout planning and the liveness arena allocator
+(IVC_FLAG_DRY_RUN builds everything except device state)."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import infvino_b200 as ivb
+from infvino_b200 import _native, plangen
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_exports_every_declared_symbol():
+    hdr = open(os.path.join(ROOT, "include", "infvino_b200.h")).read()
+    declared = set(re.findall(r"\b(ivc_[a-z0-9_]+)\s*\(", hdr))
+    assert declared == set(_native.SIGNATURES), declared ^ set(_native.SIGNATURES)
+    L = _native.lib()
+    for name in declared:
+        assert hasattr(L, name), name
+
+
+def dry(plan, max_batch=64, flags=0):
+    return ivb.PlanModel(plan, max_batch=max_batch, flags=ivb.FLAG_DRY_RUN | flags)
+
+
+def test_yolov8n_pose_plan_facts(model_plans):
+    m = dry(model_plans["yolov8n-pose"])
+    assert m.inputName() == "images" and m.inputDims() == [1, 3, 640, 640]
+    assert m.outputCount() == 1 and m.outputDims(0) == [1, 56, 8400]
+    steps = m.steps()
+    gflop = sum(s["flops_per_image"] for s in steps) / 1e9
+    # the reference publishes 9.178 GFLOP for yolov8n-pose conv+gemm work
+    # (docs/budget-analysis-3models.md:73)
+    assert abs(gflop - 9.178) < 0.002, gflop
+    st = m.pool_stats()
+    assert st["fusions_concat"] == 13 and st["fusions_res"] == 6
+    assert 0 < st["arena_bytes"] < st["requested_bytes"] / 4
+    fam = {s["family"] for s in steps}
+    assert {"conv3x3_tc", "conv1x1_tc", "stem3x3"} <= fam
+
+
+def test_mobilenet_and_yolo11_plan_facts(model_plans):
+    m = dry(model_plans["mobilenetv3-small"], 8)
+    assert m.outputDims(0) == [1, 1000]
+    gflop = sum(s["flops_per_image"] for s in m.steps()) / 1e9
+    assert 0.10 < gflop < 0.13
+    m11 = dry(model_plans["yolo11n-pose"], 8)
+    fam = [s["family"] for s in m11.steps()]
+    assert "bmm" in fam and "depthwise" in fam
+
+
+def test_allocator_reuses_memory_and_views(model_plans):
+    m = dry(model_plans["yolov8n-pose"], 1)
+    st = m.pool_stats()
+    assert st["views"] > 0            # reshape + zero-copy channel splits
+    text = m.describe()
+    # every arena placement line has a lifetime; check pairwise disjointness here too
+    roots = []
+    for line in text.splitlines():
+        mm = re.search(r"arena=(\d+) life=\[(-?\d+),(-?\d+)\] bytes/img=(\d+)", line)
+        if mm:
+            off, b, d, sz = map(int, mm.groups())
+            roots.append((off, off + ((sz + 255) // 256) * 256, b, d))
+    assert len(roots) == st["roots"]
+    for i in range(len(roots)):
+        for j in range(i + 1, len(roots)):
+            a, c = roots[i], roots[j]
+            if a[2] <= c[3] and c[2] <= a[3]:
+                assert a[1] <= c[0] or c[1] <= a[0], (a, c)
+
+
+def test_no_fusion_flag(model_plans):
+    m = dry(model_plans["yolov8n-pose"], 1, ivb.FLAG_NO_FUSION)
+    st = m.pool_stats()
+    assert st["fusions_concat"] == 0 and st["fusions_res"] == 0
+
+
+def _write(tmp_path, text, inits=()):
+    d = tmp_path
+    for name, n in inits:
+        np.zeros(n, dtype=np.float16).tofile(os.path.join(d, f"init_{name}.bin"))
+    p = os.path.join(d, "model.plan")
+    open(p, "w").write(text)
+    return p
+
+
+@pytest.mark.parametrize("text,msg", [
+    ("tensor y 1 4\noutput y\n", "plan has no 'input' line"),
+    ("input x 1 4\ntensor y 1 4\nnode ew_unary x y op=0 n=4\n", "plan has no 'output' line"),
+    ("input x 1 4\noutput y\n", "output tensor not declared"),
+    ("input x 1 4\ninit w init_w.bin 4\noutput x\n", "cannot open init"),
+    ("input x 1 4\ntensor y 1 4\nnode frobnicate x y\noutput y\n", "unknown op"),
+    ("input x 1 4\ntensor y 1 4\nnode ew_unary x,zz y op=0\noutput y\n", "missing tensor"),
+])
+def test_plan_errors(tmp_path, text, msg):
+    p = _write(str(tmp_path), text)
+    with pytest.raises(ivb.NativeError) as e:
+        dry(p, 1)
+    assert msg in str(e.value)
+
+
+def test_short_init_file(tmp_path):
+    p = _write(str(tmp_path), "input x 1 4\ninit w init_w.bin 8\ntensor y 1 4\n"
+               "node ew_binary x,w y op=0 n=4 b_scalar=0\noutput y\n", inits=[("w", 4)])
+    with pytest.raises(ivb.NativeError) as e:
+        dry(p, 1)
+    assert "too short" in str(e.value)
+
+
+def test_empty_plan_path():
+    with pytest.raises(RuntimeError):
+        ivb.CudaBackend(ivb.ModelInfo(plan=""))
+
+
+def test_plangen_matches_onnx2plan_conventions(tmp_path):
+    p = plangen.yolov8n_pose(str(tmp_path / "y8"))
+    lines = open(p).read().splitlines()
+    assert lines[0] == "input images 1 3 640 640"
+    conv0 = next(l for l in lines if l.startswith("node conv3x3"))
+    assert conv0 == ("node conv3x3 images,model.0.weight,model.0.bias,- model.0.out "
+                     "stride=2 pad=1 Hout=320 Wout=320 act=1 cfg=64,8,1,32,8,2")
+    # dbox * strides: ONNX-style right-aligned broadcast strides (onnx2plan.py:244-277)
+    mul = [l for l in lines if l.startswith("node ew_binary") and "bdims=1,4,8400" in l]
+    assert mul and mul[0].endswith("op=2 n=33600 b_scalar=0 bdims=1,4,8400,33600,8400,1,8400,0,1")
+    assert lines[-1] == "output output0"
