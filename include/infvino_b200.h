@@ -21,6 +21,7 @@
  *   ivc_infer_f32 .......... ClBackend::infer(const float*, size_t)  ClBackend.hpp:38-39
  *   ivc_set_input_f16 ...... PlanModel::setInput(const void*)  PlanModel.hpp:75-76
  *   ivc_run ................ PlanModel::run()  PlanModel.hpp:77-78
+ *   ivc_run_async .......... PlanModel::run() without the final finish (PlanModel.cpp:4175)
  *   ivc_read_output_f16 .... PlanModel::readOutput(size_t, void*)  PlanModel.hpp:79-80
  *   ivc_read_tensor_f16 .... PlanModel::readTensor(name, void*)  PlanModel.hpp:82-84
  *   ivc_last_infer_ms ...... ClBackend::lastInferMs / PlanModel::lastRunMs
@@ -85,6 +86,9 @@ int ivc_infer_f32(ivc_model *m, const float *input, size_t numel, int batch, flo
 /* PlanModel-style split calls (fp16 host buffers, synchronous). */
 int ivc_set_input_f16(ivc_model *m, const uint16_t *input_f16, int batch);
 int ivc_run(ivc_model *m, int batch);
+/* PlanModel::run without the host wait: enqueues the network for the input set
+ * last, on `stream` (NULL = the handle's stream). */
+int ivc_run_async(ivc_model *m, int batch, void *stream);
 int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch);
 /* Copies tensor `name` for `batch` images in plan (NCHW) order; IVC_ERR_NOT_FOUND if unknown. */
 int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch);
@@ -104,6 +108,8 @@ int ivc_step_count(const ivc_model *m);
 int ivc_step_info(const ivc_model *m, int i, const char **name, const char **family, double *flops_per_image,
                   double *act_bytes_per_image, double *fixed_bytes);
 int ivc_profile(ivc_model *m, int batch, float *step_ms, int n);
+/* Number of kernel launches one ivc_run(batch) performs (kernel nodes of its CUDA graph). */
+int ivc_launch_count(ivc_model *m, int batch, int *count);
 
 /* Activation pool statistics (bytes at max_batch). */
 int ivc_pool_stats(const ivc_model *m, int64_t *requested_bytes, int64_t *arena_bytes, int64_t *weight_bytes,

@@ -173,6 +173,9 @@ class PlanModel:
     def run(self, batch: int = 1) -> None:
         check(lib().ivc_run(self._h, batch), self._h)
 
+    def run_async(self, batch: int = 1, stream: int = 0) -> None:
+        check(lib().ivc_run_async(self._h, batch, stream or None), self._h)
+
     def readOutput(self, i: int, batch: int = 1) -> np.ndarray:
         out = np.empty(self.outputNumel(i) * batch, dtype=np.uint16)
         check(lib().ivc_read_output_f16(self._h, i, out.ctypes.data, batch), self._h)
@@ -233,6 +236,11 @@ class PlanModel:
         ms = (ctypes.c_float * max(1, n))()
         check(lib().ivc_profile(self._h, batch, ms, n), self._h)
         return [float(ms[i]) for i in range(n)]
+
+    def launch_count(self, batch: int = 1) -> int:
+        n = ctypes.c_int(0)
+        check(lib().ivc_launch_count(self._h, batch, ctypes.byref(n)), self._h)
+        return int(n.value)
 
     # ---- device-pointer paths (C ABI zero-copy entry points)
     def infer_f16_device(self, d_input: int, batch: int, d_outputs: Sequence[int], stream: int = 0) -> None:

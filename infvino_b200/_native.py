@@ -38,6 +38,7 @@ SIGNATURES = {
     "ivc_infer_f32": (_i32, [_vp, _vp, _sz, _i32, _P(_vp)]),
     "ivc_set_input_f16": (_i32, [_vp, _vp, _i32]),
     "ivc_run": (_i32, [_vp, _i32]),
+    "ivc_run_async": (_i32, [_vp, _i32, _vp]),
     "ivc_read_output_f16": (_i32, [_vp, _i32, _vp, _i32]),
     "ivc_read_tensor_f16": (_i32, [_vp, _cp, _vp, _i32]),
     "ivc_infer_f16_device": (_i32, [_vp, _vp, _i32, _P(_vp), _vp]),
@@ -48,6 +49,7 @@ SIGNATURES = {
     "ivc_step_count": (_i32, [_vp]),
     "ivc_step_info": (_i32, [_vp, _i32, _P(_cp), _P(_cp), _P(_f64), _P(_f64), _P(_f64)]),
     "ivc_profile": (_i32, [_vp, _i32, _P(ctypes.c_float), _i32]),
+    "ivc_launch_count": (_i32, [_vp, _i32, _P(_i32)]),
     "ivc_pool_stats": (_i32, [_vp, _P(_i64), _P(_i64), _P(_i64), _P(_i32), _P(_i32), _P(_i32), _P(_i32),
                               _P(_i32)]),
     "ivc_describe": (_i32, [_vp, _cp, _sz]),

@@ -226,6 +226,15 @@ int ivc_run(ivc_model *m, int batch) {
   });
 }
 
+int ivc_run_async(ivc_model *m, int batch, void *stream) {
+  return guarded(m, [&]() -> int {
+    if (batch < 1 || batch > m->eng->max_batch()) return fail(m, IVC_ERR_ARGUMENT, "bad batch");
+    if (stream && stream != (void *)m->eng->stream()) m->eng->set_stream((cudaStream_t)stream);
+    m->eng->run(batch);
+    return IVC_OK;
+  });
+}
+
 int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch) {
   return guarded(m, [&]() -> int {
     if (!dst || i < 0 || i >= m->eng->output_count() || batch < 1 || batch > m->eng->max_batch())
@@ -318,6 +327,14 @@ int ivc_profile(ivc_model *m, int batch, float *step_ms, int n) {
     m->eng->run_profiled(batch, &ms);
     std::memcpy(step_ms, ms.data(), ms.size() * sizeof(float));
     return status_check(m);
+  });
+}
+
+int ivc_launch_count(ivc_model *m, int batch, int *count) {
+  return guarded(m, [&]() -> int {
+    if (!count) return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    *count = m->eng->graph_kernel_count(batch);
+    return IVC_OK;
   });
 }
 

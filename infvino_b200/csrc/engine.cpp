@@ -1158,6 +1158,26 @@ bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch)
   return true;
 }
 
+int Engine::graph_kernel_count(int batch) {
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  cudaGraph_t g = nullptr;
+  check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  for (auto &s : steps_) s.launch(batch, stream_);
+  check(cudaStreamEndCapture(stream_, &g), "cudaStreamEndCapture");
+  size_t n = 0;
+  check(cudaGraphGetNodes(g, nullptr, &n), "cudaGraphGetNodes");
+  std::vector<cudaGraphNode_t> nodes(n);
+  check(cudaGraphGetNodes(g, nodes.data(), &n), "cudaGraphGetNodes");
+  int kernels = 0;
+  for (auto nd : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+  }
+  cudaGraphDestroy(g);
+  return kernels;
+}
+
 void Engine::synchronize() { check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize"); }
 
 int Engine::device_status() {

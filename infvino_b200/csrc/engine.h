@@ -102,6 +102,7 @@ class Engine {
   bool read_tensor_f16(const std::string &name, void *host_dst, int batch);
   void synchronize();
   int device_status();  // kernel status word (0 = ok), resets it
+  int graph_kernel_count(int batch);  // kernel nodes in the CUDA graph of `batch`
   __half *input_device_ptr() const;
   float *input_f32_staging() const { return in_f32_; }
 

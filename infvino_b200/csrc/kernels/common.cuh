@@ -101,17 +101,19 @@ enum KernelStatus : int {
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                                   int *status, int code,
                                                   long long limit_cycles = 4000000000LL) {
+  // try_wait itself suspends the thread for a hardware-defined interval, so the
+  // loop spins without an extra sleep (a sleep here adds its granularity to
+  // every pipeline hand-off).
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (*abort_flag) return false;
     if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
     if (clock64() - t0 > limit_cycles) {
       *abort_flag = 1;
       if (status) atomicCAS(status, 0, code);
       return false;
     }
-    __nanosleep(64);
   }
 }
 

@@ -6,6 +6,8 @@
 // Arithmetic follows the reference kernels (kernels/ops.cl, kernels/conv_general.cl):
 // inputs are widened to f32, the op is evaluated in f32 and rounded once to fp16.
 // 4-D operands are strided views so one kernel serves NHWC and planar tensors.
+#include <algorithm>
+
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -400,6 +402,59 @@ __global__ void stem3x3_k(View4 x, const __half *__restrict__ w, const __half *_
   }
 }
 
+// Compile-time specialised stem (CIN and COUT known): the 9*CIN input taps and
+// COUT accumulators live in registers; same (ci, ky, kx) accumulation order.
+template <int CIN, int COUT>
+__global__ void __launch_bounds__(128) stem3x3_t(View4 x, const __half *__restrict__ w,
+                                                 const __half *__restrict__ bias, View4 y, long long npix, int S,
+                                                 int P, int act, int vec_out) {
+  constexpr int KK = CIN * 9;
+  __shared__ float ws[COUT * KK];
+  __shared__ float bs[COUT];
+  for (int i = threadIdx.x; i < COUT * KK; i += blockDim.x) ws[i] = __half2float(w[i]);
+  for (int i = threadIdx.x; i < COUT; i += blockDim.x) bs[i] = bias ? __half2float(bias[i]) : 0.0f;
+  __syncthreads();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix; i += (long long)gridDim.x * blockDim.x) {
+    const int ox = (int)(i % y.W);
+    const long long t = i / y.W;
+    const int oy = (int)(t % y.H);
+    const long long b = t / y.H;
+    float in[KK];
+#pragma unroll
+    for (int ci = 0; ci < CIN; ++ci)
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky) {
+        const int iy = oy * S - P + ky;
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const int ix = ox * S - P + kx;
+          const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W;
+          in[ci * 9 + ky * 3 + kx] =
+              ok ? __half2float(x.ptr[b * x.sb + (long long)ci * x.sc + (long long)iy * x.sy + (long long)ix * x.sx])
+                 : 0.0f;
+        }
+      }
+    const long long obase = b * y.sb + (long long)oy * y.sy + (long long)ox * y.sx;
+#pragma unroll
+    for (int c0 = 0; c0 < COUT; c0 += 8) {
+      __align__(16) __half out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KK; ++k) acc += in[k] * ws[(c0 + j) * KK + k];
+        out[j] = epilogue(acc, bs[c0 + j], act, kActConv3x3);
+      }
+      if (vec_out) {
+        *reinterpret_cast<uint4 *>(y.ptr + obase + c0) = *reinterpret_cast<const uint4 *>(out);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y.ptr[obase + (long long)(c0 + j) * y.sc] = out[j];
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ conversions
 // include/infvino/Half.hpp:14-24: truncate the mantissa, flush exp <= 0 to +-0,
 // exp >= 31 to +-inf.
@@ -422,6 +477,132 @@ __global__ void f16_to_f32_k(const __half *__restrict__ x, float *__restrict__ y
     y[i] = __half2float(x[i]);
 }
 
+// ------------------------------------------------------------------ NHWC fast paths
+// 8 channels (16 bytes) per thread; valid when every view is channels-last with
+// channel / pixel strides that keep 16-byte alignment.
+inline bool vec8_ok(const View4 &v) {
+  return v.sc == 1 && (v.C % 8) == 0 && (v.sx % 8) == 0 && (v.sy % 8) == 0 && (v.sb % 8) == 0 &&
+         (reinterpret_cast<uintptr_t>(v.ptr) & 15) == 0;
+}
+
+struct Pix {
+  int b, y, x, c;
+};
+__device__ __forceinline__ Pix pix8(unsigned long long i, const View4 &o) {
+  Pix p;
+  const unsigned C8 = (unsigned)o.C >> 3;
+  p.c = (int)(i % C8) * 8;
+  unsigned long long t = i / C8;
+  p.x = (int)(t % (unsigned)o.W);
+  t /= (unsigned)o.W;
+  p.y = (int)(t % (unsigned)o.H);
+  p.b = (int)(t / (unsigned)o.H);
+  return p;
+}
+__device__ __forceinline__ long long at8(const View4 &v, int b, int y, int x, int c) {
+  return (long long)b * v.sb + (long long)y * v.sy + (long long)x * v.sx + c;
+}
+
+__global__ void copy_nhwc8_k(View4 x, View4 y, long long n8) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const Pix p = pix8((unsigned long long)i, y);
+    *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) =
+        *reinterpret_cast<const uint4 *>(x.ptr + at8(x, p.b, p.y, p.x, p.c));
+  }
+}
+
+__global__ void resize_nhwc8_k(View4 x, View4 y, long long n8, int S) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const Pix p = pix8((unsigned long long)i, y);
+    *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) =
+        *reinterpret_cast<const uint4 *>(x.ptr + at8(x, p.b, p.y / S, p.x / S, p.c));
+  }
+}
+
+__global__ void maxpool_nhwc8_k(View4 x, View4 y, long long n8, int K, int S, int P) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const Pix p = pix8((unsigned long long)i, y);
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = -3.4e38f;
+    for (int kh = 0; kh < K; ++kh) {
+      const int yy = p.y * S - P + kh;
+      if (yy < 0 || yy >= x.H) continue;
+      for (int kw = 0; kw < K; ++kw) {
+        const int xx = p.x * S - P + kw;
+        if (xx < 0 || xx >= x.W) continue;
+        const uint4 v = *reinterpret_cast<const uint4 *>(x.ptr + at8(x, p.b, yy, xx, p.c));
+        const __half *h = reinterpret_cast<const __half *>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], __half2float(h[j]));
+      }
+    }
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(m[j]);
+    *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) = *reinterpret_cast<const uint4 *>(o);
+  }
+}
+
+// binary op; `b` may broadcast over pixels (bpix = 0: per-image channel vector)
+__global__ void ew_binary_nhwc8_k(View4 a, View4 b, View4 y, long long n8, int op, int bpix, int bscalar) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const Pix p = pix8((unsigned long long)i, y);
+    const uint4 av = *reinterpret_cast<const uint4 *>(a.ptr + at8(a, p.b, p.y, p.x, p.c));
+    const __half *ah = reinterpret_cast<const __half *>(&av);
+    __align__(16) __half bh[8];
+    if (bscalar) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bh[j] = b.ptr[(long long)p.b * b.sb];
+    } else {
+      const long long bo = bpix ? at8(b, p.b, p.y, p.x, p.c) : (long long)p.b * b.sb + p.c;
+      *reinterpret_cast<uint4 *>(bh) = *reinterpret_cast<const uint4 *>(b.ptr + bo);
+    }
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(binop(__half2float(ah[j]), __half2float(bh[j]), op));
+    *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) = *reinterpret_cast<const uint4 *>(o);
+  }
+}
+
+__global__ void ew_unary_nhwc8_k(View4 x, View4 y, long long n8, int op) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const Pix p = pix8((unsigned long long)i, y);
+    const uint4 v = *reinterpret_cast<const uint4 *>(x.ptr + at8(x, p.b, p.y, p.x, p.c));
+    const __half *h = reinterpret_cast<const __half *>(&v);
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(unop(__half2float(h[j]), op));
+    *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) = *reinterpret_cast<const uint4 *>(o);
+  }
+}
+
+// planar "row" copies: concat / slice / permute move contiguous runs; each row
+// is (dst offset, src pointer + offset, length), elements copied 8 at a time
+// when the run and both ends are 16-byte aligned.
+__global__ void concat_rows_k(ConcatArgs g, __half *__restrict__ y, long long outer, long long per_img_outer,
+                              long long inner) {
+  const long long rows = outer * g.nsrc;
+  for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int s = (int)(r % g.nsrc);
+    const long long o = r / g.nsrc;
+    int base = 0;
+    for (int k = 0; k < s; ++k) base += g.s[k].c;
+    const long long len = (long long)g.s[s].c * inner;
+    const long long oo = g.s[s].shared ? (o % per_img_outer) : o;
+    const __half *src = g.s[s].ptr + oo * len;
+    __half *dst = y + (o * g.sum + base) * inner;
+    const bool v8 = (len % 8) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+    if (v8) {
+      for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < len / 8; i += (long long)gridDim.x * blockDim.x)
+        reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
+    } else {
+      for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < len; i += (long long)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+    }
+  }
+}
+
 inline bool cfast_of(const View4 &y) { return y.sc == 1; }
 inline long long numel4(const View4 &v, int batch) { return (long long)batch * v.C * v.H * v.W; }
 
@@ -435,6 +616,16 @@ cudaError_t launch_ew_binary_flat(const __half *a, const __half *b, __half *y, l
   return cudaGetLastError();
 }
 cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cudaStream_t st) {
+  if (vec8_ok(y) && vec8_ok(a)) {
+    const bool bpix = b.sx != 0 || b.sy != 0;
+    const bool bscalar = !bpix && b.sc == 0;
+    if ((bpix && vec8_ok(b)) || (!bpix && !bscalar && (b.sb % 8) == 0 && (reinterpret_cast<uintptr_t>(b.ptr) & 15) == 0) ||
+        bscalar) {
+      const long long n8 = numel4(y, batch) / 8;
+      ew_binary_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(a, b, y, n8, op, bpix ? 1 : 0, bscalar ? 1 : 0);
+      return cudaGetLastError();
+    }
+  }
   const long long n = numel4(y, batch);
   ew_binary_v4_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, n, op, cfast_of(y));
   return cudaGetLastError();
@@ -451,11 +642,21 @@ cudaError_t launch_ew_unary_flat(const __half *x, __half *y, long long n, int op
   return cudaGetLastError();
 }
 cudaError_t launch_ew_unary_v4(View4 x, View4 y, int batch, int op, cudaStream_t st) {
+  if (vec8_ok(x) && vec8_ok(y)) {
+    const long long n8 = numel4(y, batch) / 8;
+    ew_unary_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, op);
+    return cudaGetLastError();
+  }
   const long long n = numel4(y, batch);
   ew_unary_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, op, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_copy_v4(View4 x, View4 y, int batch, cudaStream_t st) {
+  if (vec8_ok(x) && vec8_ok(y)) {
+    const long long n8 = numel4(y, batch) / 8;
+    copy_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8);
+    return cudaGetLastError();
+  }
   const long long n = numel4(y, batch);
   copy_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, cfast_of(y));
   return cudaGetLastError();
@@ -476,15 +677,30 @@ cudaError_t launch_concat_planar(const ConcatSrc *src, int nsrc, __half *y, long
     g.sum += src[i].c;
   }
   if (g.nsrc == 0) return cudaSuccess;
-  concat_k<<<grid_for(outer * g.sum * inner), kThreads, 0, st>>>(g, y, outer, per_img_outer, inner);
+  long long maxlen = 0;
+  for (int i = 0; i < g.nsrc; ++i) maxlen = std::max(maxlen, (long long)g.s[i].c * inner);
+  const long long rows = outer * g.nsrc;
+  dim3 grid((unsigned)std::max<long long>(1, std::min<long long>((maxlen / 8 + kThreads - 1) / kThreads, 64)),
+            (unsigned)std::min<long long>(rows, 65535));
+  concat_rows_k<<<grid, kThreads, 0, st>>>(g, y, outer, per_img_outer, inner);
   return cudaGetLastError();
 }
 cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, cudaStream_t st) {
+  if (vec8_ok(x) && vec8_ok(y)) {
+    const long long n8 = numel4(y, batch) / 8;
+    maxpool_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, K, S, P);
+    return cudaGetLastError();
+  }
   const long long n = numel4(y, batch);
   maxpool_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, K, S, P, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t st) {
+  if (vec8_ok(x) && vec8_ok(y)) {
+    const long long n8 = numel4(y, batch) / 8;
+    resize_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, S);
+    return cudaGetLastError();
+  }
   const long long n = numel4(y, batch);
   resize_nn_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, S, cfast_of(y));
   return cudaGetLastError();
@@ -545,6 +761,16 @@ cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, View
                               int P, int act, cudaStream_t st) {
   if (Cout > kStemMaxCout || x.C > 4) return cudaErrorInvalidValue;
   const long long npix = (long long)batch * y.H * y.W;
+  const int vec_out = (y.sc == 1 && y.sx % 8 == 0 && y.sy % 8 == 0 && y.sb % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0) ? 1 : 0;
+  if (x.C == 3 && Cout == 16) {
+    stem3x3_t<3, 16><<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, S, P, act, vec_out);
+    return cudaGetLastError();
+  }
+  if (x.C == 3 && Cout == 32) {
+    stem3x3_t<3, 32><<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, S, P, act, vec_out);
+    return cudaGetLastError();
+  }
   stem3x3_k<<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, Cout, S, P, act);
   return cudaGetLastError();
 }

@@ -567,9 +567,13 @@ def mobilenetv3_small(out_dir: str, seed: int = 1234, imgsz: int = 224) -> str:
 # ---------------------------------------------------------------------------
 
 def op_conv(out_dir: str, cin: int, cout: int, h: int, w: int, k: int, s: int = 1, act: int = 1,
-            groups: int = 1, residual: bool = False, seed: int = 7) -> str:
+            groups: int = 1, residual: bool = False, seed: int = 7, producer: bool = False) -> str:
+    """One convolution node; `producer` puts a 1x1 conv in front so that the
+    measured conv reads a channels-last activation (as inside a network)."""
     pw = PlanWriter(seed)
     x = pw.input("x", [1, cin, h, w])
+    if producer:
+        x = pw.conv(x, cin, 1, act=1, name="pre")
     y = pw.conv(x, cout, k, s, act=act, groups=groups, name="op")
     if residual:
         y = pw.add(y, x, 0, name="res")
@@ -582,7 +586,7 @@ def op_cat_conv1x1(out_dir: str, chans: Sequence[int], cout: int, h: int, w: int
     """concat4 -> conv1x1 (exercises the CAT4 load-time rewrite)."""
     pw = PlanWriter(seed)
     x = pw.input("x", [1, chans[0], h, w])
-    srcs = [x]
+    srcs = [pw.conv(x, chans[0], 1, act=1, name="pre")]
     for i, c in enumerate(chans[1:]):
         srcs.append(pw.conv(srcs[-1], c, 1, act=1, name=f"pre{i}"))
     cat = pw.concat(srcs, 1)

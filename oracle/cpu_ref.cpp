@@ -214,7 +214,10 @@ struct Model {
   std::map<std::string, Tensor> T;
   std::vector<Node> nodes;
   int batch = 0;
-  int acc_order = 0;  // 0 = natural K order, 1 = reversed (noise-floor probe)
+  // 0 = fp32 accumulation in natural K order (the build's contract), 1 = fp32 in
+  // reversed order (noise-floor probe), 2 = depthwise only: the reference's fp16
+  // accumulator (depthwise_f16's mad chain), used to pin against its kernel
+  int acc_order = 0;
 
   Tensor &ref(const std::string &n) {
     auto it = T.find(n);
@@ -318,7 +321,7 @@ static void conv3x3(const uint16_t *x, const uint16_t *w, const uint16_t *bias, 
     for (int oy = 0; oy < Ho; ++oy) {
       std::vector<float> acc((size_t)Wo, 0.0f);
       for (int t = 0; t < Cin * 9; ++t) {
-        const int tt = order ? (Cin * 9 - 1 - t) : t;
+        const int tt = (order == 1) ? (Cin * 9 - 1 - t) : t;
         const int ci = tt / 9, ky = (tt % 9) / 3, kx = tt % 3;
         const int iy = oy * S - P + ky;
         if (iy < 0 || iy >= H) continue;
@@ -346,7 +349,7 @@ static void conv1x1(const uint16_t *w, const uint16_t *x, const uint16_t *bias, 
   for (int co = 0; co < Cout; ++co) {
     std::vector<float> acc((size_t)N, 0.0f);
     for (int t = 0; t < Cin; ++t) {
-      const int ci = order ? (Cin - 1 - t) : t;
+      const int ci = (order == 1) ? (Cin - 1 - t) : t;
       const float wv = h2f(w[(size_t)co * Cin + ci]);
       const uint16_t *xr = x + (size_t)ci * N;
       for (int64_t n = 0; n < N; ++n) acc[(size_t)n] += h2f(xr[n]) * wv;
@@ -368,15 +371,19 @@ static void depthwise(const uint16_t *x, const uint16_t *w, const uint16_t *bias
     for (int oy = 0; oy < Ho; ++oy)
       for (int ox = 0; ox < Wo; ++ox) {
         float acc = 0.0f;
+        uint16_t hacc = 0;  // order == 2: the reference's fp16 accumulator, mad(x, w, acc) per tap
         for (int t = 0; t < K * K; ++t) {
-          const int tt = order ? (K * K - 1 - t) : t;
+          const int tt = (order == 1) ? (K * K - 1 - t) : t;
           const int ky = tt / K, kx = tt % K;
           const int iy = oy * S - P + ky, ix = ox * S - P + kx;
           if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
-          acc += h2f(x[((size_t)c * H + iy) * W + ix]) * h2f(w[(size_t)c * K * K + tt]);
+          const float xv = h2f(x[((size_t)c * H + iy) * W + ix]), wv = h2f(w[(size_t)c * K * K + tt]);
+          if (order == 2) hacc = f2h(xv * wv + h2f(hacc));
+          else acc += xv * wv;
         }
         const uint16_t b = bias ? bias[c] : 0;
-        y[((size_t)c * Ho + oy) * Wo + ox] = act_dw(hadd(f2h(acc), b), act);
+        const uint16_t a16 = (order == 2) ? hacc : f2h(acc);
+        y[((size_t)c * Ho + oy) * Wo + ox] = act_dw(hadd(a16, b), act);
       }
 }
 

@@ -1,0 +1,217 @@
+"""Parity of the CUDA path (through the C ABI) against the CPU oracle.
+
+Op level: every kernel family on seeded inputs, batch 1 and batch > 1; fp16
+outputs must agree within 1 fp16 ulp (both sides accumulate in fp32 and apply
+the reference's rounding points, so almost all elements are bit-identical).
+Network level (BASELINE tolerances): raw head tensors max-abs <= 2e-2 and
+relative L2 <= 1e-3; decoded box / keypoint coordinates within 0.5 px; identical
+post-NMS detection sets; two different inputs in one process (reuse check).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import infvino_b200 as ivb
+from infvino_b200 import plangen
+from oracle import decode, ivref
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_diff(a16: np.ndarray, b16: np.ndarray) -> np.ndarray:
+    """Distance in fp16 ulps between two arrays of fp16 bit patterns."""
+    def ordinal(h):
+        h = h.astype(np.int32)
+        return np.where(h & 0x8000, -(h & 0x7FFF), h & 0x7FFF)
+    return np.abs(ordinal(a16) - ordinal(b16))
+
+
+def run_both(plan, batch, seed=0, flags=0):
+    o = ivref.OraclePlan(plan)
+    x = np.random.default_rng(seed).random(batch * o.input_numel, dtype=np.float32)
+    x16 = ivref.f32_to_f16_trunc(x)
+    o.run_f16(x16, batch)
+    m = ivb.PlanModel(plan, device=0, max_batch=batch, flags=flags)
+    m.setInput(x16, batch)
+    m.run(batch)
+    return o, m
+
+
+def check_op(plan, batch, max_ulp=1):
+    o, m = run_both(plan, batch)
+    for i in range(m.outputCount()):
+        got = m.readOutput(i, batch)
+        ref = o.read_f16(m.outputName(i))
+        assert got.shape == ref.shape
+        d = ulp_diff(got, ref)
+        assert d.max() <= max_ulp, (plan, int(d.max()), float(np.mean(d > 0)))
+    m.close()
+
+
+CONV1 = [(16, 16, 80), (32, 64, 40), (64, 32, 40), (128, 128, 20), (256, 64, 20), (48, 256, 20), (24, 88, 14)]
+
+
+@pytest.mark.parametrize("cin,cout,hw", CONV1)
+@pytest.mark.parametrize("batch", [1, 5])
+def test_conv1x1(plan_dir, cin, cout, hw, batch):
+    p = plangen.op_conv(os.path.join(plan_dir, f"c1_{cin}_{cout}_{hw}"), cin, cout, hw, hw, 1, act=1, producer=True)
+    check_op(p, batch)
+
+
+CONV3 = [(16, 16, 40, 1), (32, 32, 20, 1), (64, 64, 40, 2), (16, 32, 80, 2), (64, 51, 20, 1), (51, 51, 40, 1),
+         (128, 128, 10, 1), (128, 256, 20, 2), (64, 64, 7, 1), (256, 64, 20, 1)]
+
+
+@pytest.mark.parametrize("cin,cout,hw,s", CONV3)
+@pytest.mark.parametrize("batch", [1, 3])
+def test_conv3x3(plan_dir, cin, cout, hw, s, batch):
+    p = plangen.op_conv(os.path.join(plan_dir, f"c3_{cin}_{cout}_{hw}_{s}"), cin, cout, hw, hw, 3, s, act=1,
+                        producer=True)
+    check_op(p, batch)
+
+
+@pytest.mark.parametrize("act", [0, 3])
+def test_conv3x3_activations(plan_dir, act):
+    p = plangen.op_conv(os.path.join(plan_dir, f"c3act{act}"), 32, 32, 20, 20, 3, 1, act=act)
+    check_op(p, 2)
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3, 4])
+def test_conv1x1_activations(plan_dir, act):
+    p = plangen.op_conv(os.path.join(plan_dir, f"c1act{act}"), 32, 48, 20, 20, 1, 1, act=act)
+    check_op(p, 2)
+
+
+def test_conv3x3_residual(plan_dir):
+    p = plangen.op_conv(os.path.join(plan_dir, "c3res"), 32, 32, 20, 20, 3, 1, residual=True, producer=True)
+    check_op(p, 3)
+
+
+def test_concat_conv1x1_cat4(plan_dir):
+    p = plangen.op_cat_conv1x1(os.path.join(plan_dir, "cat"), [16, 16, 32, 64], 64, 40, 40)
+    m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
+    assert m.pool_stats()["fusions_concat"] == 1
+    check_op(p, 4)
+
+
+@pytest.mark.parametrize("c,k,s,act", [(16, 3, 2, 2), (72, 3, 2, 2), (88, 3, 1, 2), (96, 5, 2, 3), (240, 5, 1, 3),
+                                       (576, 5, 1, 3), (64, 3, 1, 1), (20, 3, 1, 4)])
+def test_depthwise(plan_dir, c, k, s, act):
+    p = plangen.op_conv(os.path.join(plan_dir, f"dw_{c}_{k}_{s}_{act}"), c, c, 14, 14, k, s, act=act, groups=c,
+                        producer=True)
+    check_op(p, 3)
+
+
+def test_generic_grouped_conv(plan_dir):
+    # conv_general with groups != Cin: the reference's generic kernel (act code 2 = HardSwish there)
+    p = plangen.op_conv(os.path.join(plan_dir, "grp"), 32, 32, 12, 12, 3, 1, act=2, groups=4)
+    check_op(p, 2)
+
+
+def test_stem(plan_dir):
+    p = plangen.op_conv(os.path.join(plan_dir, "stem"), 3, 16, 96, 96, 3, 2, act=1)
+    check_op(p, 3)
+
+
+def test_no_tensor_core_route_matches(plan_dir):
+    p = plangen.op_conv(os.path.join(plan_dir, "c3ntc"), 32, 64, 20, 20, 3, 1, act=1)
+    o, m = run_both(p, 2, flags=ivb.FLAG_NO_TENSOR_CORES)
+    assert ulp_diff(m.readOutput(0, 2), o.read_f16(m.outputName(0))).max() <= 1
+
+
+# ------------------------------------------------------------------ networks
+HEADS_V8 = [f"model.22.cv{b}.{i}.2.out" for b in (2, 3, 4) for i in range(3)]
+
+
+def head_check(m, o, names, batch):
+    for n in names:
+        g = ivref.f16_to_f32(m.readTensor(n, batch)).astype(np.float64)
+        r = ivref.f16_to_f32(o.read_f16(n)).astype(np.float64)
+        maxabs = np.abs(g - r).max()
+        rel = np.linalg.norm(g - r) / max(1e-30, np.linalg.norm(r))
+        assert maxabs <= 2e-2 and rel <= 1e-3, (n, maxabs, rel)
+
+
+def decode_check(out_gpu, out_ref):
+    # coordinates: box xywh (channels 0-3) and keypoint x, y (5 + 3k, 6 + 3k)
+    coord = [0, 1, 2, 3] + [5 + 3 * k for k in range(17)] + [6 + 3 * k for k in range(17)]
+    d = np.abs(out_gpu[coord].astype(np.float64) - out_ref[coord])
+    assert d.max() <= 0.5, float(d.max())
+    dg = decode.pose_decode(out_gpu, conf=0.25, iou=0.7)
+    dr = decode.pose_decode(out_ref, conf=0.25, iou=0.7)
+    assert sorted(a for a, *_ in dg) == sorted(a for a, *_ in dr)
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_yolov8n_pose(model_plans, batch):
+    p = model_plans["yolov8n-pose"]
+    o, m = run_both(p, batch, seed=10 + batch)
+    head_check(m, o, HEADS_V8, batch)
+    got = ivref.f16_to_f32(m.readOutput(0, batch)).reshape(batch, 56, 8400)
+    ref = ivref.f16_to_f32(o.read_f16("output0")).reshape(batch, 56, 8400)
+    for b in range(batch):
+        decode_check(got[b], ref[b])
+    m.close()
+
+
+def test_yolo11n_pose(model_plans):
+    p = model_plans["yolo11n-pose"]
+    o, m = run_both(p, 1, seed=21)
+    head_check(m, o, [f"model.23.cv{b}.{i}.2.out" for b in (2, 3, 4) for i in range(3)], 1)
+    got = ivref.f16_to_f32(m.readOutput(0, 1)).reshape(56, 8400)
+    ref = ivref.f16_to_f32(o.read_f16("output0")).reshape(56, 8400)
+    decode_check(got, ref)
+    m.close()
+
+
+@pytest.mark.parametrize("batch", [1, 4])
+def test_mobilenetv3_small(model_plans, batch):
+    p = model_plans["mobilenetv3-small"]
+    o, m = run_both(p, batch, seed=30 + batch)
+    g = ivref.f16_to_f32(m.readOutput(0, batch)).astype(np.float64)
+    r = ivref.f16_to_f32(o.read_f16(m.outputName(0))).astype(np.float64)
+    assert np.abs(g - r).max() <= 2e-2
+    assert np.linalg.norm(g - r) / np.linalg.norm(r) <= 2e-3
+    assert np.array_equal(g.reshape(batch, -1).argmax(1), r.reshape(batch, -1).argmax(1))
+    m.close()
+
+
+def test_backend_reuse_two_inputs(model_plans):
+    """ClBackend-style f32 API; frame B after frame A equals a fresh B-only run
+    (the reference's reuse check, scripts/reuse_check.py:6-11)."""
+    p = model_plans["yolov8n-pose"]
+    be = ivb.CudaBackend(ivb.ModelInfo(plan=p))
+    n = int(np.prod(be.inputDims()))
+    xa = np.random.default_rng(1).random(n, dtype=np.float32)
+    xb = np.random.default_rng(2).random(n, dtype=np.float32)
+    be.infer(xa)
+    yb = be.infer(xb)[0].data.copy()
+    fresh = ivb.CudaBackend(ivb.ModelInfo(plan=p)).infer(xb)[0].data
+    assert np.array_equal(yb, fresh)
+    assert be.lastInferMs() > 0
+    with pytest.raises(ivb.NativeError) as e:
+        be.model.infer_f32(xa[:-1], 1)
+    assert "numel mismatch" in str(e.value)
+
+
+def test_batched_equals_single(model_plans):
+    """Image b of a batch-3 run equals the same image run alone (batch sharding is exact)."""
+    p = model_plans["yolov8n-pose"]
+    m = ivb.PlanModel(p, max_batch=3)
+    n = m.inputNumel()
+    x = np.random.default_rng(5).random(3 * n, dtype=np.float32)
+    yb = m.infer_f32(x, 3)[0].reshape(3, -1)
+    for b in range(3):
+        y1 = m.infer_f32(x[b * n:(b + 1) * n], 1)[0]
+        assert np.array_equal(y1, yb[b])
+    m.close()
+
+
+def test_graph_and_eager_agree(model_plans):
+    p = model_plans["mobilenetv3-small"]
+    x = np.random.default_rng(9).random(2 * 3 * 224 * 224, dtype=np.float32)
+    a = ivb.PlanModel(p, max_batch=2).infer_f32(x, 2)[0]
+    b = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_GRAPH).infer_f32(x, 2)[0]
+    c = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_FUSION).infer_f32(x, 2)[0]
+    assert np.array_equal(a, b) and np.array_equal(a, c)
