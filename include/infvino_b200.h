@@ -59,6 +59,8 @@ typedef enum ivc_status {
 #define IVC_FLAG_NO_FUSION 0x2u       /* skip concat->conv1x1 / residual load-time rewrites */
 #define IVC_FLAG_DRY_RUN 0x4u         /* host only: parse, layout, allocate; no GPU is touched */
 #define IVC_FLAG_NO_TENSOR_CORES 0x8u /* convolutions on the CUDA-core direct kernel (diagnostic) */
+#define IVC_FLAG_NO_POOL 0x10u        /* no activation memory reuse, every tensor stays readable
+                                         (reference INFVINO_NO_POOL, src/PlanModel.cpp:887) */
 
 /* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
 int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);

@@ -322,9 +322,11 @@ void Engine::allocate() {
     const int64_t sz = bytes_of(r);
     stats_.requested_bytes += sz;
     std::vector<std::pair<int64_t, int64_t>> busy;
+    const bool no_pool = (flags_ & kFlagNoPool) != 0;  // diagnostics: no reuse, every tensor stays readable
     for (int q : placed) {
       const TensorRt &a = T_[(size_t)r], &b = T_[(size_t)q];
-      if (a.birth <= b.death && b.birth <= a.death) busy.push_back({b.arena_off, b.arena_off + bytes_of(q)});
+      if (no_pool || (a.birth <= b.death && b.birth <= a.death))
+        busy.push_back({b.arena_off, b.arena_off + bytes_of(q)});
     }
     std::sort(busy.begin(), busy.end());
     int64_t cur = 0;

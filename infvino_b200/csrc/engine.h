@@ -28,6 +28,7 @@ enum EngineFlags : unsigned {
   kFlagNoFusion = 1u << 1,    // skip the concat->conv1x1 and residual rewrites
   kFlagDryRun = 1u << 2,      // host-only: plan, layout, allocation; no device work
   kFlagNoTensorCores = 1u << 3,  // route convolutions to the CUDA-core direct kernel
+  kFlagNoPool = 1u << 4,      // every tensor keeps its own storage (reference INFVINO_NO_POOL)
 };
 
 struct TensorRt {
