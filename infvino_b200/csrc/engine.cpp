@@ -729,6 +729,7 @@ void Engine::lower() {
           a.cout = c.cout;
           a.act = c.act;
           a.act_kind = c.act_kind;
+          a.act_fn = resolve_act(c.act, c.act_kind);
           const View4 ov = view(c.out);
           a.out = ov.ptr;
           a.o_sb = ov.sb;

@@ -45,6 +45,101 @@ __device__ __forceinline__ __half epilogue(float acc, float bias, int act, int k
   return __float2half_rn(a);
 }
 
+// ------------------------------------------------------------------ resolved activations
+// The (act code, kernel family) pair resolved on the host to one function, so
+// epilogues are compiled per function with no per-element dispatch.
+enum ActFn : int {
+  kFnNone = 0,
+  kFnSilu = 1,
+  kFnRelu = 2,
+  kFnHswishA = 3,   // f * clamp(f + 3, 0, 6) / 6          (conv3x3_ov, gemm)
+  kFnHsigmoid = 4,  // clamp(f + 3, 0, 6) / 6
+  kFnSigmoid = 5,   // 1 / (1 + exp(-f))
+  kFnHswishB = 6,   // f * (clamp(f + 3, 0, 6) / 6)        (depthwise_f16)
+};
+
+__host__ __device__ inline int resolve_act(int act, int kind) {
+  if (act == 1) return kFnSilu;
+  if (kind == kActConv3x3) return act == 3 ? kFnHswishA : kFnNone;
+  if (act == 2) return kFnRelu;
+  if (act == 3) return kind == kActDepthwise ? kFnHswishB : kFnHswishA;
+  if (act == 4) return kFnHsigmoid;
+  if (act == 5) return kind == kActDepthwise ? kFnNone : kFnSigmoid;
+  return kFnNone;
+}
+
+// Reference-expression value of a resolved activation (accurate expf, IEEE division).
+template <int FN>
+__device__ __forceinline__ float act_exact(float f) {
+  if (FN == kFnSilu) return f / (1.0f + expf(-f));
+  if (FN == kFnRelu) return fmaxf(f, 0.0f);
+  if (FN == kFnHswishA) return f * fminf(fmaxf(f + 3.0f, 0.0f), 6.0f) / 6.0f;
+  if (FN == kFnHsigmoid) return fminf(fmaxf(f + 3.0f, 0.0f), 6.0f) / 6.0f;
+  if (FN == kFnSigmoid) return 1.0f / (1.0f + expf(-f));
+  if (FN == kFnHswishB) return f * (fminf(fmaxf(f + 3.0f, 0.0f), 6.0f) / 6.0f);
+  return f;
+}
+
+// True when an approximation `y` (relative error below 2^-19) may round to a
+// different fp16 value than the exact result: y lies within 48 f32 ulps of an
+// fp16 rounding midpoint, or outside the normal fp16 range.
+__device__ __forceinline__ bool fp16_round_ambiguous(float y) {
+  const uint32_t u = __float_as_uint(y) & 0x7fffffffu;
+  const int low = (int)(u & 0x1fffu) - 0x1000;
+  return (u < 0x38800000u) | (u >= 0x477fe000u) | (low <= 48 && low >= -48);
+}
+
+// SiLU through the MUFU exp2 and reciprocal (relative error ~2^-19.7: the
+// rounding of -f*log2(e) dominates).
+__device__ __forceinline__ float silu_fast(float f) {
+  const float t = -f * 1.4426950408889634f;
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+  const float d = 1.0f + e;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return f * r;
+}
+
+// Reference epilogue for 8 consecutive output channels of one pixel:
+// half(half(acc) + bias) -> act (f32) -> half.  The half additions are packed
+// f16x2 operations (correctly rounded, like the reference's half arithmetic).
+// SiLU takes the fast path; lanes whose result could round differently redo
+// the reference expression, so the fp16 output equals act_exact's.
+template <int FN>
+__device__ __forceinline__ uint4 epilogue8(const uint32_t (&acc)[8], uint4 bias8) {
+  const __half2 *hb = reinterpret_cast<const __half2 *>(&bias8);
+  float v[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __half2 h = __hadd2(__floats2half2_rn(__uint_as_float(acc[2 * k]), __uint_as_float(acc[2 * k + 1])), hb[k]);
+    const float2 f = __half22float2(h);
+    v[2 * k] = f.x;
+    v[2 * k + 1] = f.y;
+  }
+  float y[8];
+  if (FN == kFnSilu) {
+    uint32_t amb = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      y[j] = silu_fast(v[j]);
+      amb |= (fp16_round_ambiguous(y[j]) ? 1u : 0u) << j;
+    }
+    if (__builtin_expect(amb != 0, 0)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (amb & (1u << j)) y[j] = act_exact<kFnSilu>(v[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = act_exact<FN>(v[j]);
+  }
+  uint4 out;
+  __half2 *ho = reinterpret_cast<__half2 *>(&out);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) ho[k] = __floats2half2_rn(y[2 * k], y[2 * k + 1]);
+  return out;
+}
+
 // ------------------------------------------------------------------ smem/mbarrier
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -85,6 +180,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or `ns` nanoseconds pass, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Error codes a kernel writes to its status word (first error wins).
 enum KernelStatus : int {
   kStatusOk = 0,
@@ -101,13 +210,12 @@ enum KernelStatus : int {
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                                   int *status, int code,
                                                   long long limit_cycles = 4000000000LL) {
-  // try_wait itself suspends the thread for a hardware-defined interval, so the
-  // loop spins without an extra sleep (a sleep here adds its granularity to
-  // every pipeline hand-off).
+  // The thread sleeps inside try_wait (woken when the phase completes) rather
+  // than spinning, so idle roles do not take issue slots from working warps.
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > limit_cycles) {
       *abort_flag = 1;
@@ -182,6 +290,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+// 32 lanes x 32 bit, 8 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 

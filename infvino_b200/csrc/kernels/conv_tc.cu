@@ -12,7 +12,9 @@
 // Persistent, warp-specialised CTA (one per SM):
 //   warp 0      : TMA producer (one elected lane), ring of `stages` A (+B) slots
 //   warp 1      : TMEM allocator + MMA issuer (one lane), two accumulator buffers
-//   warps 2..5  : epilogue, TMEM lanes 32*(warp%4) .. +31  (one output row each)
+//   warps 2..17 : epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (one output
+//                 row each) and, with the other three warps of its lane quarter,
+//                 splits the accumulator columns in 8-column chunks
 // Every wait is bounded; a timeout records a status code, raises a CTA abort
 // flag and all roles drain and exit (TMEM is always released).
 #include <cstdio>
@@ -76,6 +78,82 @@ __device__ __forceinline__ const CUtensorMap *mapA_ptr(const ConvTcArgs &a, int 
   }
 }
 
+// Epilogue role: warp w reads TMEM lane quarter (w % 4), i.e. tile rows
+// 32*(w%4) .. +31 (one output pixel per thread), and with the other warps of
+// its quarter splits the accumulator columns in 8-column chunks.
+template <int FN>
+__device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int lane, uint32_t tmem_base,
+                                              uint64_t *accf_bar, uint64_t *acce_bar, volatile int *abort_sh) {
+  constexpr int kGroups = kConvEpiWarps / 4;  // warps per lane quarter
+  const int q = warp & 3;
+  const int grp = (warp - 2) >> 2;
+  const int row = q * 32 + lane;
+  const int num_tiles = a.m_tiles * a.n_tiles;
+  uint32_t tcount = 0;
+  for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+    const uint32_t buf = tcount & 1u;
+    if (!mbar_wait_bounded(smem_u32(&accf_bar[buf]), (tcount >> 1) & 1u, abort_sh, a.status, kStatusTimeoutAcc))
+      break;
+    tc_fence_after();
+    const TileCoord tc = decode_tile(a, t);
+    bool valid;
+    long long obase, rbase;
+    if (a.ksize == 1) {
+      const long long p = tc.p0 + row;
+      valid = p < a.m_total;
+      const long long hw = (long long)a.Ho * a.Wo;
+      const long long bimg = valid ? p / hw : 0;
+      const long long r2 = valid ? p - bimg * hw : 0;
+      const long long oy = r2 / a.Wo, ox = r2 - oy * a.Wo;
+      obase = bimg * a.o_sb + oy * a.o_sy + ox * a.o_sx;
+      rbase = bimg * a.r_sb + oy * a.r_sy + ox * a.r_sx;
+    } else {
+      const int ty = row / a.TW, tx = row - ty * a.TW;
+      const int oy = tc.oy0 + ty, ox = tc.ox0 + tx;
+      valid = row < a.tile_rows && oy < a.Ho && ox < a.Wo;
+      obase = (long long)tc.b * a.o_sb + (long long)oy * a.o_sy + (long long)ox * a.o_sx;
+      rbase = (long long)tc.b * a.r_sb + (long long)oy * a.r_sy + (long long)ox * a.r_sx;
+    }
+    const int n0 = tc.n * a.BN;
+    const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * (uint32_t)a.BN;
+    for (int c0 = grp * 8; c0 < a.BN; c0 += 8 * kGroups) {
+      uint32_t r[8];
+      tmem_ld8(taddr + (uint32_t)c0, r);
+      tmem_ld_wait();
+      const int ch0 = n0 + c0;
+      if (!valid || ch0 >= a.cout) continue;
+      const bool full = ch0 + 8 <= a.cout;
+      // the bias is padded to the N tile, so 8 values are always readable
+      const uint4 bias8 = a.bias != nullptr ? *reinterpret_cast<const uint4 *>(a.bias + ch0) : make_uint4(0, 0, 0, 0);
+      uint4 packed = epilogue8<FN>(r, bias8);
+      __half *v = reinterpret_cast<__half *>(&packed);
+      if (a.res != nullptr) {
+        if (a.res_vec && full) {
+          const uint4 rv = *reinterpret_cast<const uint4 *>(a.res + rbase + ch0);
+          __half2 *h2 = reinterpret_cast<__half2 *>(&packed);
+          const __half2 *r2 = reinterpret_cast<const __half2 *>(&rv);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) h2[k] = __hadd2(h2[k], r2[k]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (ch0 + j < a.cout)
+              v[j] = __float2half_rn(__half2float(v[j]) + __half2float(a.res[rbase + (long long)(ch0 + j) * a.r_sc]));
+        }
+      }
+      if (a.out_vec && full) {
+        *reinterpret_cast<uint4 *>(a.out + obase + ch0) = packed;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (ch0 + j < a.cout) a.out[obase + (long long)(ch0 + j) * a.o_sc] = v[j];
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(smem_u32(&acce_bar[buf]));
+  }
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_constant__ ConvTcArgs a) {
@@ -111,7 +189,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(smem_u32(&accf_bar[j]), 1);
-      mbar_init(smem_u32(&acce_bar[j]), 128);
+      mbar_init(smem_u32(&acce_bar[j]), 32 * kConvEpiWarps);
     }
     mbar_init(smem_u32(&bres_bar), 1);
     mbar_init(smem_u32(&done_bar), 1);
@@ -227,74 +305,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
   } else {
     // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;               // TMEM lane group of this warp
-    const int row = q * 32 + lane;        // tile row == output pixel
-    uint32_t tcount = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
-      const uint32_t buf = tcount & 1u;
-      if (!mbar_wait_bounded(smem_u32(&accf_bar[buf]), (tcount >> 1) & 1u, &abort_sh, a.status,
-                             kStatusTimeoutAcc))
-        break;
-      tc_fence_after();
-      const TileCoord tc = decode_tile(a, t);
-      bool valid;
-      long long obase, rbase;
-      if (a.ksize == 1) {
-        const long long p = tc.p0 + row;
-        valid = p < a.m_total;
-        const long long hw = (long long)a.Ho * a.Wo;
-        const long long bimg = valid ? p / hw : 0;
-        const long long r2 = valid ? p - bimg * hw : 0;
-        const long long oy = r2 / a.Wo, ox = r2 - (r2 / a.Wo) * a.Wo;
-        obase = bimg * a.o_sb + oy * a.o_sy + ox * a.o_sx;
-        rbase = bimg * a.r_sb + oy * a.r_sy + ox * a.r_sx;
-      } else {
-        const int ty = row / a.TW, tx = row - (row / a.TW) * a.TW;
-        const int oy = tc.oy0 + ty, ox = tc.ox0 + tx;
-        valid = row < a.tile_rows && oy < a.Ho && ox < a.Wo;
-        obase = (long long)tc.b * a.o_sb + (long long)oy * a.o_sy + (long long)ox * a.o_sx;
-        rbase = (long long)tc.b * a.r_sb + (long long)oy * a.r_sy + (long long)ox * a.r_sx;
-      }
-      const int n0 = tc.n * a.BN;
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * (uint32_t)a.BN;
-      for (int c0 = 0; c0 < a.BN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + (uint32_t)c0, r);
-        tmem_ld_wait();
-        const int ch0 = n0 + c0;
-        if (!valid || ch0 >= a.cout) continue;
-        __align__(16) __half v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int ch = ch0 + j;
-          const float bias = (a.bias != nullptr) ? __half2float(a.bias[ch]) : 0.0f;
-          v[j] = epilogue(__uint_as_float(r[j]), bias, a.act, a.act_kind);
-        }
-        const bool full = ch0 + 16 <= a.cout;
-        if (a.res != nullptr) {
-          if (a.res_vec && full) {
-            const uint4 *rp = reinterpret_cast<const uint4 *>(a.res + rbase + ch0);
-            __align__(16) __half rv[16];
-            *reinterpret_cast<uint4 *>(&rv[0]) = rp[0];
-            *reinterpret_cast<uint4 *>(&rv[8]) = rp[1];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __float2half_rn(__half2float(v[j]) + __half2float(rv[j]));
-          } else {
-            for (int j = 0; j < 16 && ch0 + j < a.cout; ++j)
-              v[j] = __float2half_rn(__half2float(v[j]) +
-                                     __half2float(a.res[rbase + (long long)(ch0 + j) * a.r_sc]));
-          }
-        }
-        if (a.out_vec && full) {
-          uint4 *op = reinterpret_cast<uint4 *>(a.out + obase + ch0);
-          op[0] = *reinterpret_cast<const uint4 *>(&v[0]);
-          op[1] = *reinterpret_cast<const uint4 *>(&v[8]);
-        } else {
-          for (int j = 0; j < 16 && ch0 + j < a.cout; ++j) a.out[obase + (long long)(ch0 + j) * a.o_sc] = v[j];
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(smem_u32(&acce_bar[buf]));
+    switch (a.act_fn) {
+      case kFnSilu: epilogue_role<kFnSilu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
+      case kFnRelu: epilogue_role<kFnRelu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
+      case kFnHswishA: epilogue_role<kFnHswishA>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
+      case kFnHsigmoid: epilogue_role<kFnHsigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
+      case kFnSigmoid: epilogue_role<kFnSigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
+      default: epilogue_role<kFnNone>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
     }
   }
 

@@ -10,7 +10,8 @@ namespace ivb {
 
 constexpr int kConvMaxSrc = 4;
 constexpr int kConvMaxStages = 12;
-constexpr int kConvThreads = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
+constexpr int kConvEpiWarps = 16;   // four warps per TMEM lane quarter, splitting the columns
+constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;  // warp0 TMA, warp1 MMA, then epilogue
 
 struct alignas(64) ConvTcArgs {
   CUtensorMap mapA[kConvMaxSrc];  // 1x1: 2-D (C, pixels); 3x3: 4-D (C, W, H, B)
@@ -35,6 +36,7 @@ struct alignas(64) ConvTcArgs {
   const __half *bias;             // [Np] or null
   int cout;
   int act, act_kind;
+  int act_fn;                     // resolve_act(act, act_kind)
   __half *out;
   long long o_sb, o_sc, o_sy, o_sx;
   int out_vec;                    // NHWC-contiguous channels, 16B aligned
