@@ -563,8 +563,13 @@ void Engine::lower() {
         if (c.ksize == 3 && xv0.C <= 4 && res < 0) {
           st.family = "stem3x3";
           const int cout = c.cout;
-          st.launch = [this, x, out, wptr, bptr, cout, S, P, act](int B, cudaStream_t s) {
-            return launch_stem3x3_v4(view(x), wptr, bptr, view(out), B, cout, S, P, act, s);
+          auto blob = std::make_shared<std::vector<float>>();
+          if (!stem_params(xv0.C, cout, p.ref(T_[(size_t)w].name).host.data(),
+                           bias >= 0 ? p.ref(T_[(size_t)bias].name).host.data() : nullptr, blob.get()))
+            blob.reset();
+          st.launch = [this, x, out, wptr, bptr, blob, cout, S, P, act](int B, cudaStream_t s) {
+            return launch_stem3x3_v4(view(x), wptr, bptr, blob ? blob->data() : nullptr, view(out), B, cout, S, P,
+                                     act, s);
           };
         } else {
           st.family = "conv_direct";

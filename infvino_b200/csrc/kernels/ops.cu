@@ -7,6 +7,8 @@
 // inputs are widened to f32, the op is evaluated in f32 and rounded once to fp16.
 // 4-D operands are strided views so one kernel serves NHWC and planar tensors.
 #include <algorithm>
+#include <vector>
+#include <cstring>
 
 #include "common.cuh"
 #include "ops.cuh"
@@ -402,18 +404,20 @@ __global__ void stem3x3_k(View4 x, const __half *__restrict__ w, const __half *_
   }
 }
 
-// Compile-time specialised stem (CIN and COUT known): the 9*CIN input taps and
-// COUT accumulators live in registers; same (ci, ky, kx) accumulation order.
+// Compile-time specialised stem (CIN, COUT and the activation known): weights
+// and bias travel in the kernel parameters (constant bank, read directly by the
+// FMAs), the 9*CIN input taps and COUT accumulators live in registers;
+// accumulation order per output channel is (ci, ky, kx) as in the reference.
 template <int CIN, int COUT>
-__global__ void __launch_bounds__(128) stem3x3_t(View4 x, const __half *__restrict__ w,
-                                                 const __half *__restrict__ bias, View4 y, long long npix, int S,
-                                                 int P, int act, int vec_out) {
+struct StemWeights {
+  float w[CIN * 9][COUT];  // [tap][channel]
+  uint4 b8[COUT / 8];      // fp16 bias, 8 channels per uint4
+};
+
+template <int CIN, int COUT, int FN>
+__global__ void __launch_bounds__(128) stem3x3_t(View4 x, const __grid_constant__ StemWeights<CIN, COUT> p,
+                                                 View4 y, long long npix, int S, int P, int vec_out) {
   constexpr int KK = CIN * 9;
-  __shared__ float ws[COUT * KK];
-  __shared__ float bs[COUT];
-  for (int i = threadIdx.x; i < COUT * KK; i += blockDim.x) ws[i] = __half2float(w[i]);
-  for (int i = threadIdx.x; i < COUT; i += blockDim.x) bs[i] = bias ? __half2float(bias[i]) : 0.0f;
-  __syncthreads();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix; i += (long long)gridDim.x * blockDim.x) {
     const int ox = (int)(i % y.W);
     const long long t = i / y.W;
@@ -434,25 +438,43 @@ __global__ void __launch_bounds__(128) stem3x3_t(View4 x, const __half *__restri
                  : 0.0f;
         }
       }
+    float acc[COUT];
+#pragma unroll
+    for (int c = 0; c < COUT; ++c) acc[c] = 0.0f;
+#pragma unroll
+    for (int k = 0; k < KK; ++k)
+#pragma unroll
+      for (int c = 0; c < COUT; ++c) acc[c] += in[k] * p.w[k][c];
     const long long obase = b * y.sb + (long long)oy * y.sy + (long long)ox * y.sx;
 #pragma unroll
     for (int c0 = 0; c0 < COUT; c0 += 8) {
-      __align__(16) __half out[8];
+      uint32_t a8[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int k = 0; k < KK; ++k) acc += in[k] * ws[(c0 + j) * KK + k];
-        out[j] = epilogue(acc, bs[c0 + j], act, kActConv3x3);
-      }
+      for (int j = 0; j < 8; ++j) a8[j] = __float_as_uint(acc[c0 + j]);
+      const uint4 out = epilogue8<FN>(a8, p.b8[c0 / 8]);
       if (vec_out) {
-        *reinterpret_cast<uint4 *>(y.ptr + obase + c0) = *reinterpret_cast<const uint4 *>(out);
+        *reinterpret_cast<uint4 *>(y.ptr + obase + c0) = out;
       } else {
+        const __half *h = reinterpret_cast<const __half *>(&out);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y.ptr[obase + (long long)(c0 + j) * y.sc] = out[j];
+        for (int j = 0; j < 8; ++j) y.ptr[obase + (long long)(c0 + j) * y.sc] = h[j];
       }
     }
   }
+}
+
+template <int CIN, int COUT>
+cudaError_t launch_stem_t(View4 x, const float *blob, View4 y, long long npix, int S, int P, int act, int vec_out,
+                          cudaStream_t st) {
+  StemWeights<CIN, COUT> p;
+  std::memcpy(&p, blob, sizeof(p));
+  const dim3 g(grid_for(npix, 128)), b(128);
+  switch (resolve_act(act, kActConv3x3)) {
+    case kFnSilu: stem3x3_t<CIN, COUT, kFnSilu><<<g, b, 0, st>>>(x, p, y, npix, S, P, vec_out); break;
+    case kFnHswishA: stem3x3_t<CIN, COUT, kFnHswishA><<<g, b, 0, st>>>(x, p, y, npix, S, P, vec_out); break;
+    default: stem3x3_t<CIN, COUT, kFnNone><<<g, b, 0, st>>>(x, p, y, npix, S, P, vec_out); break;
+  }
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ conversions
@@ -757,20 +779,30 @@ cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, 
                                                      cfast_of(y));
   return cudaGetLastError();
 }
-cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int Cout, int S,
-                              int P, int act, cudaStream_t st) {
+bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_host, std::vector<float> *blob) {
+  if (!(cin == 3 && cout == 16)) return false;
+  StemWeights<3, 16> p;
+  std::memset(&p, 0, sizeof(p));
+  for (int c = 0; c < cout; ++c) {
+    for (int k = 0; k < cin * 9; ++k) {
+      __half h;
+      std::memcpy(&h, &w_host[(size_t)c * cin * 9 + k], 2);
+      p.w[k][c] = __half2float(h);
+    }
+    if (b_host) reinterpret_cast<uint16_t *>(&p.b8[c / 8])[c % 8] = b_host[c];
+  }
+  blob->assign((sizeof(p) + sizeof(float) - 1) / sizeof(float), 0.0f);
+  std::memcpy(blob->data(), &p, sizeof(p));
+  return true;
+}
+
+cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, const float *blob, View4 y, int batch,
+                              int Cout, int S, int P, int act, cudaStream_t st) {
   if (Cout > kStemMaxCout || x.C > 4) return cudaErrorInvalidValue;
   const long long npix = (long long)batch * y.H * y.W;
   const int vec_out = (y.sc == 1 && y.sx % 8 == 0 && y.sy % 8 == 0 && y.sb % 8 == 0 &&
                        (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0) ? 1 : 0;
-  if (x.C == 3 && Cout == 16) {
-    stem3x3_t<3, 16><<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, S, P, act, vec_out);
-    return cudaGetLastError();
-  }
-  if (x.C == 3 && Cout == 32) {
-    stem3x3_t<3, 32><<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, S, P, act, vec_out);
-    return cudaGetLastError();
-  }
+  if (x.C == 3 && Cout == 16 && blob) return launch_stem_t<3, 16>(x, blob, y, npix, S, P, act, vec_out, st);
   stem3x3_k<<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, Cout, S, P, act);
   return cudaGetLastError();
 }

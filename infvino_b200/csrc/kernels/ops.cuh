@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <vector>
+
 namespace ivb {
 
 // A 4-D activation view: element (b, c, y, x) lives at ptr[b*sb + c*sc + y*sy + x*sx].
@@ -64,8 +66,11 @@ cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, 
                                   View4 y, int batch, int Cout, int K, int S, int P, int G, int act, int epi,
                                   cudaStream_t st);
 // Stem: 3x3 conv with Cin <= 4 (tiny K), conv3x3 rounding, NHWC or planar output.
-cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int Cout, int S,
-                              int P, int act, cudaStream_t st);
+// `blob` (from stem_params, host memory) selects the register / constant-bank
+// specialisation; without it the generic kernel reads `w` / `bias` on the device.
+bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_host, std::vector<float> *blob);
+cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, const float *blob, View4 y, int batch,
+                              int Cout, int S, int P, int act, cudaStream_t st);
 // Reference host conversion on the device: f32 -> f16 by mantissa truncation.
 cudaError_t launch_f32_to_f16_trunc(const float *x, __half *y, long long n, cudaStream_t st);
 cudaError_t launch_f16_to_f32(const __half *x, float *y, long long n, cudaStream_t st);
