@@ -571,6 +571,14 @@ void Engine::lower() {
             return launch_stem3x3_v4(view(x), wptr, bptr, blob ? blob->data() : nullptr, view(out), B, cout, S, P,
                                      act, s);
           };
+        } else if (c.ksize == 1 && res < 0 && T_[(size_t)x].dense && T_[(size_t)out].dense && c.cout <= 8 &&
+                   c.cin_total <= 64) {
+          st.family = "conv1x1_planar";
+          const int cin = c.cin_total, cout = c.cout;
+          const long long N = T_[(size_t)x].numel / cin;
+          st.launch = [this, x, out, wptr, bptr, cin, cout, N, act](int B, cudaStream_t s) {
+            return launch_conv1x1_planar(T_[(size_t)x].dptr, wptr, bptr, T_[(size_t)out].dptr, B, N, cin, cout, act, s);
+          };
         } else {
           st.family = "conv_direct";
           const int epi = (c.ksize == 3) ? 2 : 1;

@@ -625,6 +625,94 @@ __global__ void concat_rows_k(ConcatArgs g, __half *__restrict__ y, long long ou
   }
 }
 
+// ---- row-vectorised planar kernels (decode tail): 8 elements per thread
+__host__ __device__ __forceinline__ bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// slice_axis as rows: `outer` rows of len*inner contiguous elements
+__global__ void slice_rows8_k(const __half *__restrict__ x, __half *__restrict__ y, long long outer, int axdim,
+                              long long inner, int start, int len) {
+  const long long row = (long long)len * inner / 8;  // vectors per row
+  const long long n = outer * row;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long o = i / row, v = i - o * row;
+    reinterpret_cast<uint4 *>(y + o * len * inner)[v] =
+        reinterpret_cast<const uint4 *>(x + (o * axdim + start) * inner)[v];
+  }
+}
+
+// permute_0213 mode 0 moves whole I-rows: [D1][D2][I] -> [D2][D1][I]
+__global__ void permute0_rows8_k(const __half *__restrict__ x, __half *__restrict__ y, long long n8, int D1, int D2,
+                                 long long I) {
+  const long long I8 = I / 8;
+  const long long per = (long long)D1 * D2 * I;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const long long v = i % I8;
+    long long t = i / I8;
+    const int d2 = (int)(t % D2);
+    t /= D2;
+    const int d1 = (int)(t % D1);
+    const long long img = t / D1;
+    reinterpret_cast<uint4 *>(y + img * per + ((long long)d2 * D1 + d1) * I)[v] =
+        reinterpret_cast<const uint4 *>(x + img * per + ((long long)d1 * D2 + d2) * I)[v];
+  }
+}
+
+// broadcast binary op when the innermost output dim is contiguous (stride 1)
+// or broadcast (stride 0) for both operands and a multiple of 8
+__global__ void ew_bcast_rows8_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
+                                 BcastArgs g, long long n8, int op) {
+  const int r = g.rank - 1;
+  const long long last8 = g.dims[r] / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const long long v = i % last8;
+    long long rem = i / last8, ai = v * 8 * g.as[r], bi = v * 8 * g.bs[r];
+    for (int d = r - 1; d >= 0; --d) {
+      const long long coord = rem % g.dims[d];
+      rem /= g.dims[d];
+      ai += coord * g.as[d];
+      bi += coord * g.bs[d];
+    }
+    __align__(16) __half av[8], bv[8], o[8];
+    if (g.as[r] == 1) {
+      *reinterpret_cast<uint4 *>(av) = *reinterpret_cast<const uint4 *>(a + ai);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) av[j] = a[ai];
+    }
+    if (g.bs[r] == 1) {
+      *reinterpret_cast<uint4 *>(bv) = *reinterpret_cast<const uint4 *>(b + bi);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bv[j] = b[bi];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(binop(__half2float(av[j]), __half2float(bv[j]), op));
+    reinterpret_cast<uint4 *>(y)[i] = *reinterpret_cast<const uint4 *>(o);
+  }
+}
+
+// 1x1 convolution on planar [Cin][N] rows with a handful of output channels
+// (the DFL projection 16 -> 1): one thread per pixel, gemm-family epilogue,
+// fp32 accumulation over ci in order.
+constexpr int kPlanarMaxCout = 8;
+constexpr int kPlanarMaxCin = 64;
+__global__ void conv1x1_planar_k(const __half *__restrict__ x, const __half *__restrict__ w,
+                                 const __half *__restrict__ bias, __half *__restrict__ y, long long npix, long long N,
+                                 int Cin, int Cout, int act) {
+  __shared__ float ws[kPlanarMaxCout * kPlanarMaxCin];
+  for (int i = threadIdx.x; i < Cin * Cout; i += blockDim.x) ws[i] = __half2float(w[i]);
+  __syncthreads();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix; i += (long long)gridDim.x * blockDim.x) {
+    const long long img = i / N, n = i - img * N;
+    const __half *xp = x + img * Cin * N + n;
+    for (int co = 0; co < Cout; ++co) {
+      float acc = 0.0f;
+      for (int ci = 0; ci < Cin; ++ci) acc += __half2float(xp[(long long)ci * N]) * ws[co * Cin + ci];
+      y[img * Cout * N + (long long)co * N + n] = epilogue(acc, bias ? __half2float(bias[co]) : 0.0f, act, kActGemm);
+    }
+  }
+}
+
 inline bool cfast_of(const View4 &y) { return y.sc == 1; }
 inline long long numel4(const View4 &v, int batch) { return (long long)batch * v.C * v.H * v.W; }
 
@@ -656,6 +744,17 @@ cudaError_t launch_ew_binary_bcast(const __half *a, const __half *b, __half *y, 
                                    cudaStream_t st) {
   long long n = 1;
   for (int r = 0; r < g.rank; ++r) n *= g.dims[r];
+  {
+    const int r = g.rank - 1;
+    bool rows = r >= 0 && g.dims[r] % 8 == 0 && (g.as[r] == 0 || g.as[r] == 1) && (g.bs[r] == 0 || g.bs[r] == 1) &&
+                al16(y) && (g.as[r] == 0 || al16(a)) && (g.bs[r] == 0 || al16(b));
+    for (int d = 0; d < r && rows; ++d)
+      rows = (g.as[r] == 0 || g.as[d] % 8 == 0) && (g.bs[r] == 0 || g.bs[d] % 8 == 0);
+    if (rows) {
+      ew_bcast_rows8_k<<<grid_for(n / 8), kThreads, 0, st>>>(a, b, y, g, n / 8, op);
+      return cudaGetLastError();
+    }
+  }
   ew_binary_bcast_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, g, n, op);
   return cudaGetLastError();
 }
@@ -685,6 +784,12 @@ cudaError_t launch_copy_v4(View4 x, View4 y, int batch, cudaStream_t st) {
 }
 cudaError_t launch_slice_axis(const __half *x, __half *y, long long outer, int axdim, long long inner, int start,
                               int len, cudaStream_t st) {
+  if (((long long)len * inner) % 8 == 0 && ((long long)axdim * inner) % 8 == 0 && ((long long)start * inner) % 8 == 0 &&
+      al16(x) && al16(y)) {
+    const long long n8 = outer * len * inner / 8;
+    slice_rows8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, outer, axdim, inner, start, len);
+    return cudaGetLastError();
+  }
   slice_axis_k<<<grid_for(outer * len * inner), kThreads, 0, st>>>(x, y, outer, axdim, inner, start, len);
   return cudaGetLastError();
 }
@@ -734,6 +839,11 @@ cudaError_t launch_softmax_axis(const __half *x, __half *y, long long outer, int
 }
 cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, int D2, long long I, int mode,
                                 cudaStream_t st) {
+  if (mode == 0 && I % 8 == 0 && al16(x) && al16(y)) {
+    const long long n8 = (long long)batch * D1 * D2 * I / 8;
+    permute0_rows8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, D1, D2, I);
+    return cudaGetLastError();
+  }
   const long long n = (long long)batch * D1 * D2 * I;
   permute_0213_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, D1, D2, I, mode);
   return cudaGetLastError();
@@ -806,6 +916,14 @@ cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, cons
   stem3x3_k<<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, Cout, S, P, act);
   return cudaGetLastError();
 }
+cudaError_t launch_conv1x1_planar(const __half *x, const __half *w, const __half *bias, __half *y, int batch,
+                                  long long N, int Cin, int Cout, int act, cudaStream_t st) {
+  if (Cin > kPlanarMaxCin || Cout > kPlanarMaxCout) return cudaErrorInvalidValue;
+  const long long npix = (long long)batch * N;
+  conv1x1_planar_k<<<grid_for(npix), kThreads, 0, st>>>(x, w, bias, y, npix, N, Cin, Cout, act);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_f32_to_f16_trunc(const float *x, __half *y, long long n, cudaStream_t st) {
   f32_to_f16_trunc_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n);
   return cudaGetLastError();

@@ -71,6 +71,10 @@ cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, 
 bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_host, std::vector<float> *blob);
 cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, const float *blob, View4 y, int batch,
                               int Cout, int S, int P, int act, cudaStream_t st);
+// 1x1 conv over planar [Cin][N] rows with few outputs (Cin <= 64, Cout <= 8),
+// gemm-family rounding, fp32 accumulation over ci in order.
+cudaError_t launch_conv1x1_planar(const __half *x, const __half *w, const __half *bias, __half *y, int batch,
+                                  long long N, int Cin, int Cout, int act, cudaStream_t st);
 // Reference host conversion on the device: f32 -> f16 by mantissa truncation.
 cudaError_t launch_f32_to_f16_trunc(const float *x, __half *y, long long n, cudaStream_t st);
 cudaError_t launch_f16_to_f32(const __half *x, float *y, long long n, cudaStream_t st);
