@@ -300,7 +300,7 @@ def _anchors(levels: Sequence[int], strides: Sequence[int], offset: float = 0.5)
 
 
 def _pose_head(pw: PlanWriter, feats: Sequence[str], c2: int, c3: int, c4: int, tag: str,
-               dw_cls: bool = False) -> str:
+               dw_cls: bool = False, cls_gain: float = 1.0, cls_shift: float = 0.0) -> str:
     """Pose head + in-graph decode (DFL, dist2bbox, keypoint decode) -> [1, 56, A]."""
     nk, reg = 51, 16
     hws = [pw.shapes[f][2] for f in feats]
@@ -329,7 +329,10 @@ def _pose_head(pw: PlanWriter, feats: Sequence[str], c2: int, c3: int, c4: int, 
         else:
             u = pw.conv(f, c3, 3, act=1, name=f"{tag}.cv3.{i}.0")
             u = pw.conv(u, c3, 3, act=1, name=f"{tag}.cv3.{i}.1")
-        u = pw.conv(u, 1, 1, act=0, name=f"{tag}.cv3.{i}.2")
+        u = pw.conv(u, 1, 1, act=0, name=f"{tag}.cv3.{i}.2", gain=cls_gain)
+        if cls_shift:
+            bname = f"{tag}.cv3.{i}.2.bias"
+            pw.inits[bname] = (pw.inits[bname].astype(np.float32) + cls_shift).astype(FP16)
         cv.append(pw.reshape(u, [1, 1, hws[i] * hws[i]]))
     box = pw.concat(bv, 2, name=f"{tag}.box_cat")
     cls = pw.concat(cv, 2, name=f"{tag}.cls_cat")
@@ -370,7 +373,12 @@ def _pose_head(pw: PlanWriter, feats: Sequence[str], c2: int, c3: int, c4: int, 
     return out
 
 
-def yolov8n_pose(out_dir: str, seed: int = 1234, imgsz: int = 640) -> str:
+def yolov8n_pose(out_dir: str, seed: int = 1234, imgsz: int = 640, cls_gain: float = 1.0,
+                 cls_shift: float = 0.0) -> str:
+    """`cls_gain` scales the final class-conv weights and `cls_shift` offsets its
+    bias (defaults: plain He-normal / N(0, 0.01)).  The NMS parity test uses a
+    large gain and a negative shift so that a few anchors score high, as with
+    trained weights, and the post-NMS detection set is well defined."""
     pw = PlanWriter(seed)
     x = pw.input("images", [1, 3, imgsz, imgsz])
     x = pw.conv(x, 16, 3, 2, act=1, name="model.0")
@@ -395,7 +403,8 @@ def yolov8n_pose(out_dir: str, seed: int = 1234, imgsz: int = 640) -> str:
     x = pw.conv(o4, 128, 3, 2, act=1, name="model.19")
     x = pw.concat([x, p5], 1, name="model.20")
     o5 = _c2f(pw, x, 256, 1, False, "model.21")
-    out = _pose_head(pw, [o3, o4, o5], c2=64, c3=64, c4=51, tag="model.22")
+    out = _pose_head(pw, [o3, o4, o5], c2=64, c3=64, c4=51, tag="model.22", cls_gain=cls_gain,
+                     cls_shift=cls_shift)
     pw.output(out)
     return pw.save(out_dir)
 
