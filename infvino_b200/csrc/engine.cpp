@@ -436,7 +436,7 @@ struct ConvCfg {
   int Ho = 0, Wo = 0, TH = 0, TW = 0;
   int act = 0, act_kind = kActGemm;
   int out = -1, res = -1;
-  int stages = 2, resident_b = 0, smem = 0, tmem_cols = 32;
+  int stages = 2, resident_b = 0, smem = 0, tmem_cols = 32, nbuf = 2, kb_per_stage = 1;
   __half *wp = nullptr;    // packed [Np][Kp]
   __half *bias = nullptr;  // [Np] padded
 };
@@ -612,7 +612,10 @@ void Engine::lower() {
         c.n_tiles = (int)((np16 + 127) / 128);
       }
       c.Np = c.BN * c.n_tiles;
-      c.tmem_cols = pow2_at_least(2 * c.BN);
+      // up to 4 accumulator buffers (= epilogue teams working on different
+      // tiles at once) within the 512 TMEM columns
+      c.nbuf = c.BN <= 128 ? 4 : 2;
+      c.tmem_cols = pow2_at_least(c.nbuf * c.BN);
       if (c.ksize == 3) {
         if (c.Wo % 16 == 0) {
           c.TW = 16;
@@ -627,8 +630,19 @@ void Engine::lower() {
       const int budget = 232448 - 1024 - 2048 /*static smem + barriers*/ - 1024 /*align*/ - a_tile /*slack*/;
       const int bres = b_tile * c.num_kb;
       c.resident_b = (c.n_tiles == 1 && bres <= 96 * 1024 && budget - bres >= 2 * a_tile) ? 1 : 0;
-      const int stage_bytes = a_tile + (c.resident_b ? 0 : b_tile);
-      c.stages = std::min(kConvMaxStages, (budget - (c.resident_b ? bres : 0)) / stage_bytes);
+      const int kb_bytes = a_tile + (c.resident_b ? 0 : b_tile);
+      const int ring = budget - (c.resident_b ? bres : 0);
+      // k-blocks per pipeline stage: one full/empty handshake costs a few
+      // hundred cycles, far more than a 16-channel k-block's MMA, so small
+      // k-blocks travel in groups (a divisor of num_kb, <= 48 KB, >= 3 stages)
+      c.kb_per_stage = 1;
+      for (int g = c.num_kb; g >= 2; --g)
+        if (c.num_kb % g == 0 && g * kb_bytes <= 48 * 1024 && ring / (g * kb_bytes) >= 3) {
+          c.kb_per_stage = g;
+          break;
+        }
+      const int stage_bytes = c.kb_per_stage * kb_bytes;
+      c.stages = std::min(kConvMaxStages, ring / stage_bytes);
       if (c.stages < 2) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
       c.smem = (c.resident_b ? bres : 0) + c.stages * stage_bytes + 1024 + a_tile;
       c.smem = std::max(c.smem, 120 * 1024);  // one CTA per SM (TMEM never contended)
@@ -719,6 +733,7 @@ void Engine::lower() {
           a.n_tiles = c.n_tiles;
           a.num_kb = c.num_kb;
           a.stages = c.stages;
+          a.kb_per_stage = c.kb_per_stage;
           a.resident_b = c.resident_b;
           a.Ho = c.Ho;
           a.Wo = c.Wo;
@@ -767,8 +782,17 @@ void Engine::lower() {
                             : 0;
           }
           a.tmem_cols = c.tmem_cols;
+          {
+            // teams per CTA from its tile count: with few tiles each tile wants
+            // all 16 epilogue warps; with many, tiles overlap in the epilogue
+            const long long tiles = (long long)a.m_tiles * a.n_tiles;
+            const long long per_cta = (tiles + sms - 1) / sms;
+            a.nbuf = per_cta >= 8 ? c.nbuf : per_cta >= 2 ? 2 : 1;
+          }
           a.smem_bytes = c.smem;
           a.status = status;
+          const char *why = nullptr;
+          if (!conv_tc_finalize(a, &why)) throw std::runtime_error(std::string("CudaPlanModel: ") + why);
           it = cache->emplace(B, a).first;
         }
         const ConvTcArgs &a = it->second;

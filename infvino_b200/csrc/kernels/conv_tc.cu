@@ -11,10 +11,12 @@
 //
 // Persistent, warp-specialised CTA (one per SM):
 //   warp 0      : TMA producer (one elected lane), ring of `stages` A (+B) slots
-//   warp 1      : TMEM allocator + MMA issuer (one lane), two accumulator buffers
-//   warps 2..17 : epilogue; warp w reads TMEM lanes 32*(w%4) .. +31 (one output
-//                 row each) and, with the other three warps of its lane quarter,
-//                 splits the accumulator columns in 8-column chunks
+//   warp 1      : TMEM allocator + MMA issuer (one lane), `nbuf` (1, 2 or 4)
+//                 accumulator buffers used round robin
+//   warps 2..17 : epilogue in `nbuf` teams, team j drains buffer j, so nbuf
+//                 tiles are in the epilogue at once; warp w reads TMEM lanes
+//                 32*(w%4) .. +31 (one output row each), and the team's warps
+//                 of a lane quarter split the columns in 8-column chunks
 // Every wait is bounded; a timeout records a status code, raises a CTA abort
 // flag and all roles drain and exit (TMEM is always released).
 #include <cstdio>
@@ -24,49 +26,189 @@
 
 namespace ivb {
 
+// Optional per-CTA cycle counters (compiled only with -DIVB_CONV_TRACE, for a
+// diagnostic build of the library): where each role spends its time.
+#ifdef IVB_CONV_TRACE
+constexpr int kTraceSlots = 8;  // wait-empty, wait-full, wait-acc-empty, wait-acc-full, epi-work, total, tiles, kblocks
+__device__ unsigned long long g_conv_trace[256 * kTraceSlots];
+#define CONV_TRACE_ADD(slot, v) \
+  atomicAdd(&g_conv_trace[(blockIdx.x & 255) * kTraceSlots + (slot)], (unsigned long long)(v))
+#define CONV_TRACE_T0() const long long trace_t0_ = clock64()
+#define CONV_TRACE_SINCE(slot) CONV_TRACE_ADD(slot, clock64() - trace_t0_)
+#else
+#define CONV_TRACE_ADD(slot, v) ((void)0)
+#define CONV_TRACE_T0() ((void)0)
+#define CONV_TRACE_SINCE(slot) ((void)0)
+#endif
+
 namespace {
 
-struct TileCoord {
-  int m, n;          // m tile, n tile
-  int b, oy0, ox0;   // 3x3: image and output origin
-  long long p0;      // 1x1: first pixel
-};
-
-__device__ __forceinline__ TileCoord decode_tile(const ConvTcArgs &a, int t) {
-  TileCoord c;
-  c.m = t / a.n_tiles;
-  c.n = t - c.m * a.n_tiles;
-  if (a.ksize == 1) {
-    c.p0 = (long long)c.m * 128;
-    c.b = c.oy0 = c.ox0 = 0;
-  } else {
-    c.b = c.m / a.tiles_per_img;
-    const int rem = c.m - c.b * a.tiles_per_img;
-    const int ty = rem / a.tiles_x;
-    c.oy0 = ty * a.TH;
-    c.ox0 = (rem - ty * a.tiles_x) * a.TW;
-    c.p0 = 0;
-  }
-  return c;
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// k-block -> (source, tap, chunk)
-__device__ __forceinline__ void decode_kb(const ConvTcArgs &a, int kb, int &src, int &tap, int &chunk) {
-  src = 0;
-  int base = 0;
-#pragma unroll 1
-  for (int s = 0; s < a.nsrc; ++s) {
-    const int n = a.taps * a.src_chunks[s];
-    if (kb < base + n) {
-      src = s;
-      break;
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, FastDiv f) {
+  return (uint32_t)(((uint64_t)n * f.m) >> (31u + f.s));
+}
+
+// Epilogue role: warp w reads TMEM lane quarter (w % 4), i.e. tile rows
+// 32*(w%4) .. +31 (one output pixel per thread), and with the other warps of
+// its quarter splits the accumulator columns in 8-column chunks.  Every field
+// of the parameter block is read once, before the tile loop: inside the loop
+// the global stores and the barrier asm would otherwise force reloads.
+template <int FN>
+__device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int lane, uint32_t tmem_base,
+                                              uint64_t *accf_bar, uint64_t *acce_bar, volatile int *abort_sh,
+                                              volatile int *epi_go, const uint4 *bias_sh) {
+  // The 16 warps form `nbuf` teams; team j owns accumulator buffer j and the
+  // CTA's tiles j, j + nbuf, ...  so that nbuf tiles are in the epilogue at
+  // once.  Inside a team the (4 / nbuf) warps of a lane quarter split the
+  // columns in 8-column chunks.
+  const int nbuf = a.nbuf;
+  const int q = warp & 3;
+  const int grp = (warp - 2) >> 2;                 // 0..3: groups of four consecutive warps
+  const int team = grp & (nbuf - 1);
+  const int sub = grp / nbuf;                      // position among the team's warps of this quarter
+  const int kq = 4 / nbuf;                         // team warps per lane quarter
+  const int team_threads = 32 * kConvEpiWarps / nbuf;
+  const bool team_lead = warp == 2 + 4 * team;     // its lane 0 waits for the accumulator
+  const int row = q * 32 + lane;
+  const bool leader = (warp == 2 && lane == 0);    // tracer
+  (void)leader;
+  const int ksize = a.ksize, BN = a.BN, n_tiles = a.n_tiles, cout = a.cout;
+  const int num_tiles = a.m_tiles * n_tiles;
+  const uint32_t m_total = (uint32_t)a.m_total;
+  const int Ho = a.Ho, Wo = a.Wo, TH = a.TH, TW = a.TW, tiles_x = a.tiles_x, tiles_per_img = a.tiles_per_img;
+  const FastDiv fd_nt = a.fd_ntiles, fd_tpi = a.fd_tiles_per_img, fd_tx = a.fd_tiles_x, fd_hw = a.fd_hw,
+                fd_wo = a.fd_wo;
+  const uint32_t hw = (uint32_t)(Ho * Wo);
+  const __half *__restrict__ bias = a.bias;
+  __half *__restrict__ out = a.out;
+  const __half *__restrict__ res = a.res;
+  const long long o_sb = a.o_sb, o_sc = a.o_sc, o_sy = a.o_sy, o_sx = a.o_sx;
+  const long long r_sb = a.r_sb, r_sc = a.r_sc, r_sy = a.r_sy, r_sx = a.r_sx;
+  const bool out_vec = a.out_vec != 0, res_vec = a.res_vec != 0, has_res = res != nullptr;
+  const bool bias_in_smem = n_tiles == 1 && bias != nullptr;
+  int *status = a.status;
+  // 3x3: this thread's pixel inside the tile is fixed
+  const int tyr = ksize == 1 ? 0 : (int)fdiv((uint32_t)row, a.fd_tw);
+  const int txr = ksize == 1 ? 0 : row - tyr * TW;
+  const bool row_in_tile = row < a.tile_rows;
+
+  // bias of chunk cc (tile-relative column) of the current N tile; the bias is
+  // padded to the N tile, so 8 values are always readable
+  int n0 = 0;
+  auto load_bias8 = [&](int cc) -> uint4 {
+    if (bias_in_smem) return bias_sh[cc >> 3];
+    if (bias != nullptr) return *reinterpret_cast<const uint4 *>(bias + n0 + cc);
+    return make_uint4(0, 0, 0, 0);
+  };
+  const uint32_t buf = (uint32_t)team;
+  volatile int *go = epi_go + 2 * team;
+  uint32_t use = 0;
+  for (int t = blockIdx.x + team * gridDim.x; t < num_tiles; t += nbuf * gridDim.x, ++use) {
+    // One thread per team waits for the accumulator; the team's other warps
+    // block in a hardware barrier (no issue slots).  The go flag is
+    // double-buffered so a late reader never sees the next tile's value.
+    if (team_lead) {
+      if (lane == 0) {
+        CONV_TRACE_T0();
+        go[use & 1u] = mbar_wait_bounded(smem_u32(&accf_bar[buf]), use & 1u, abort_sh, status, kStatusTimeoutAcc)
+                           ? 1
+                           : 0;
+        CONV_TRACE_SINCE(3);
+      }
+      __syncwarp();  // reconverge before the warp-aligned barrier
     }
-    base += n;
+    named_bar_sync(1 + team, team_threads);
+    if (!go[use & 1u]) break;
+    tc_fence_after();
+#ifdef IVB_CONV_TRACE
+    const long long work_t0 = clock64();
+#endif
+    const int mt = (int)fdiv((uint32_t)t, fd_nt);
+    const int nt = t - mt * n_tiles;
+    bool valid;
+    long long obase, rbase;
+    if (ksize == 1) {
+      const uint32_t p = (uint32_t)mt * 128u + (uint32_t)row;
+      valid = p < m_total;
+      const uint32_t bimg = valid ? fdiv(p, fd_hw) : 0u;
+      const uint32_t r2 = valid ? p - bimg * hw : 0u;
+      const uint32_t oy = fdiv(r2, fd_wo), ox = r2 - oy * (uint32_t)Wo;
+      obase = (long long)bimg * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
+      rbase = (long long)bimg * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
+    } else {
+      const int b = (int)fdiv((uint32_t)mt, fd_tpi);
+      const int rem = mt - b * tiles_per_img;
+      const int ty = (int)fdiv((uint32_t)rem, fd_tx);
+      const int oy = ty * TH + tyr, ox = (rem - ty * tiles_x) * TW + txr;
+      valid = row_in_tile && oy < Ho && ox < Wo;
+      obase = (long long)b * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
+      rbase = (long long)b * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
+    }
+    n0 = nt * BN;
+    const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * (uint32_t)BN;
+    // two chunks per TMEM wait: c0 and c0 + 8 * kq
+    for (int c0 = sub * 8; c0 < BN; c0 += 16 * kq) {
+      const int c1 = c0 + 8 * kq;
+      const bool two = c1 < BN;
+      uint32_t r[2][8];
+      tmem_ld8(taddr + (uint32_t)c0, r[0]);
+      if (two) tmem_ld8(taddr + (uint32_t)c1, r[1]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) asm volatile("" : "+r"(r[h][k]));  // uses stay after the wait
+      }
+      // one epilogue call per chunk (one call over both chunks measured slower)
+      const int nch = (n0 + c0 < cout ? 1 : 0) + (two && n0 + c1 < cout ? 1 : 0);  // warp-uniform
+      if (nch == 0) continue;
+      uint4 packed[2];
+      packed[0] = epilogue8<FN>(r[0], load_bias8(c0));
+      if (nch == 2) packed[1] = epilogue8<FN>(r[1], load_bias8(c1));
+      if (!valid) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (h >= nch) break;
+        const int ch0 = n0 + (h == 0 ? c0 : c1);
+        const bool full = ch0 + 8 <= cout;
+        __half *v = reinterpret_cast<__half *>(&packed[h]);
+        if (has_res) {
+          if (res_vec && full) {
+            const uint4 rv = *reinterpret_cast<const uint4 *>(res + rbase + ch0);
+            __half2 *h2 = reinterpret_cast<__half2 *>(&packed[h]);
+            const __half2 *rr = reinterpret_cast<const __half2 *>(&rv);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) h2[k] = __hadd2(h2[k], rr[k]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (ch0 + j < cout)
+                v[j] = __float2half_rn(__half2float(v[j]) + __half2float(res[rbase + (long long)(ch0 + j) * r_sc]));
+          }
+        }
+        if (out_vec && full) {
+          *reinterpret_cast<uint4 *>(out + obase + ch0) = packed[h];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (ch0 + j < cout) out[obase + (long long)(ch0 + j) * o_sc] = v[j];
+        }
+      }
+    }
+    tc_fence_before();
+    // one arrival per warp: single-thread arrivals on one mbarrier serialise
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&acce_bar[buf]));
+#ifdef IVB_CONV_TRACE
+    if (leader) {
+      CONV_TRACE_ADD(4, clock64() - work_t0);
+      CONV_TRACE_ADD(6, 1);
+    }
+#endif
   }
-  const int r = kb - base;
-  const int nc = a.src_chunks[src];
-  tap = r / nc;
-  chunk = r - tap * nc;
 }
 
 __device__ __forceinline__ const CUtensorMap *mapA_ptr(const ConvTcArgs &a, int s) {
@@ -78,118 +220,49 @@ __device__ __forceinline__ const CUtensorMap *mapA_ptr(const ConvTcArgs &a, int 
   }
 }
 
-// Epilogue role: warp w reads TMEM lane quarter (w % 4), i.e. tile rows
-// 32*(w%4) .. +31 (one output pixel per thread), and with the other warps of
-// its quarter splits the accumulator columns in 8-column chunks.
-template <int FN>
-__device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int lane, uint32_t tmem_base,
-                                              uint64_t *accf_bar, uint64_t *acce_bar, volatile int *abort_sh) {
-  constexpr int kGroups = kConvEpiWarps / 4;  // warps per lane quarter
-  const int q = warp & 3;
-  const int grp = (warp - 2) >> 2;
-  const int row = q * 32 + lane;
-  const int num_tiles = a.m_tiles * a.n_tiles;
-  uint32_t tcount = 0;
-  for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
-    const uint32_t buf = tcount & 1u;
-    if (!mbar_wait_bounded(smem_u32(&accf_bar[buf]), (tcount >> 1) & 1u, abort_sh, a.status, kStatusTimeoutAcc))
-      break;
-    tc_fence_after();
-    const TileCoord tc = decode_tile(a, t);
-    bool valid;
-    long long obase, rbase;
-    if (a.ksize == 1) {
-      const long long p = tc.p0 + row;
-      valid = p < a.m_total;
-      const long long hw = (long long)a.Ho * a.Wo;
-      const long long bimg = valid ? p / hw : 0;
-      const long long r2 = valid ? p - bimg * hw : 0;
-      const long long oy = r2 / a.Wo, ox = r2 - oy * a.Wo;
-      obase = bimg * a.o_sb + oy * a.o_sy + ox * a.o_sx;
-      rbase = bimg * a.r_sb + oy * a.r_sy + ox * a.r_sx;
-    } else {
-      const int ty = row / a.TW, tx = row - ty * a.TW;
-      const int oy = tc.oy0 + ty, ox = tc.ox0 + tx;
-      valid = row < a.tile_rows && oy < a.Ho && ox < a.Wo;
-      obase = (long long)tc.b * a.o_sb + (long long)oy * a.o_sy + (long long)ox * a.o_sx;
-      rbase = (long long)tc.b * a.r_sb + (long long)oy * a.r_sy + (long long)ox * a.r_sx;
-    }
-    const int n0 = tc.n * a.BN;
-    const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * (uint32_t)a.BN;
-    for (int c0 = grp * 8; c0 < a.BN; c0 += 8 * kGroups) {
-      uint32_t r[8];
-      tmem_ld8(taddr + (uint32_t)c0, r);
-      tmem_ld_wait();
-      const int ch0 = n0 + c0;
-      if (!valid || ch0 >= a.cout) continue;
-      const bool full = ch0 + 8 <= a.cout;
-      // the bias is padded to the N tile, so 8 values are always readable
-      const uint4 bias8 = a.bias != nullptr ? *reinterpret_cast<const uint4 *>(a.bias + ch0) : make_uint4(0, 0, 0, 0);
-      uint4 packed = epilogue8<FN>(r, bias8);
-      __half *v = reinterpret_cast<__half *>(&packed);
-      if (a.res != nullptr) {
-        if (a.res_vec && full) {
-          const uint4 rv = *reinterpret_cast<const uint4 *>(a.res + rbase + ch0);
-          __half2 *h2 = reinterpret_cast<__half2 *>(&packed);
-          const __half2 *r2 = reinterpret_cast<const __half2 *>(&rv);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) h2[k] = __hadd2(h2[k], r2[k]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (ch0 + j < a.cout)
-              v[j] = __float2half_rn(__half2float(v[j]) + __half2float(a.res[rbase + (long long)(ch0 + j) * a.r_sc]));
-        }
-      }
-      if (a.out_vec && full) {
-        *reinterpret_cast<uint4 *>(a.out + obase + ch0) = packed;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (ch0 + j < a.cout) a.out[obase + (long long)(ch0 + j) * a.o_sc] = v[j];
-      }
-    }
-    tc_fence_before();
-    mbar_arrive(smem_u32(&acce_bar[buf]));
-  }
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_constant__ ConvTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kConvMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kConvMaxStages];
-  __shared__ __align__(8) uint64_t accf_bar[2];
-  __shared__ __align__(8) uint64_t acce_bar[2];
+  __shared__ __align__(8) uint64_t accf_bar[kConvMaxBufs];
+  __shared__ __align__(8) uint64_t acce_bar[kConvMaxBufs];
   __shared__ __align__(8) uint64_t bres_bar;
   __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
+  __shared__ volatile int epi_go[2 * kConvMaxBufs];
+  __shared__ uint4 bias_sh[256 / 8];  // the bias of the single N tile (n_tiles == 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // parameters every role uses, read once
+  const int BK = a.BK, BN = a.BN, num_kb = a.num_kb, stages = a.stages, n_tiles = a.n_tiles;
+  const bool resident_b = a.resident_b != 0;
+  const int num_tiles = a.m_tiles * n_tiles;
+  int *const status = a.status;
   // 1024-byte aligned operand area (128B-swizzle atoms repeat every 1024 B)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
-  const uint32_t a_tile = 128u * (uint32_t)a.BK * 2u;                       // bytes
-  const uint32_t b_tile = (((uint32_t)a.BN * (uint32_t)a.BK * 2u) + 1023u) & ~1023u;
-  const uint32_t bres_bytes = a.resident_b ? b_tile * (uint32_t)a.num_kb : 0u;
-  const uint32_t stage_bytes = a_tile + (a.resident_b ? 0u : b_tile);
+  const uint32_t a_tile = 128u * (uint32_t)BK * 2u;  // bytes
+  const uint32_t b_tile = (((uint32_t)BN * (uint32_t)BK * 2u) + 1023u) & ~1023u;
+  const uint32_t bres_bytes = resident_b ? b_tile * (uint32_t)num_kb : 0u;
+  const int kbs = a.kb_per_stage;                      // k-blocks per stage
+  const uint32_t kb_bytes = a_tile + (resident_b ? 0u : b_tile);
+  const uint32_t stage_bytes = (uint32_t)kbs * kb_bytes;
   const uint32_t bres_base = base;
   const uint32_t ring_base = base + bres_bytes;
-  const uint32_t row_bytes = (uint32_t)a.BK * 2u;
-  const int stages = a.stages;
-  const int num_tiles = a.m_tiles * a.n_tiles;
+  const uint32_t row_bytes = (uint32_t)BK * 2u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < kConvMaxBufs; ++j) {
       mbar_init(smem_u32(&accf_bar[j]), 1);
-      mbar_init(smem_u32(&acce_bar[j]), 32 * kConvEpiWarps);
+      mbar_init(smem_u32(&acce_bar[j]), kConvEpiWarps / a.nbuf);  // one arrival per team warp
     }
     mbar_init(smem_u32(&bres_bar), 1);
     mbar_init(smem_u32(&done_bar), 1);
@@ -204,123 +277,222 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     tmem_alloc(smem_u32(&tmem_base_sh), (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
+  if (warp >= 2 && n_tiles == 1 && a.bias != nullptr) {
+    // bias padded to BN (a multiple of 16), 16 B per thread
+    const int i = threadIdx.x - 64;
+    if (i < BN / 8) bias_sh[i] = reinterpret_cast<const uint4 *>(a.bias)[i];
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+#ifdef IVB_CONV_TRACE
+  const long long kernel_t0 = clock64();
+#endif
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
+      const int ksize = a.ksize, stride = a.stride, pad = a.pad, nsrc = a.nsrc, taps = a.taps;
+      const int TH = a.TH, TW = a.TW, tiles_x = a.tiles_x, tiles_per_img = a.tiles_per_img;
+      const FastDiv fd_nt = a.fd_ntiles, fd_tpi = a.fd_tiles_per_img, fd_tx = a.fd_tiles_x;
+      int sc[kConvMaxSrc];
+#pragma unroll
+      for (int i = 0; i < kConvMaxSrc; ++i) sc[i] = a.src_chunks[i];
       // bytes one A box delivers: 128 pixel rows (1x1) or TH*TW rows (3x3)
-      const uint32_t a_tx = (uint32_t)(a.ksize == 1 ? 128 : a.tile_rows) * (uint32_t)a.BK * 2u;
-      const uint32_t b_tx = (uint32_t)a.BN * (uint32_t)a.BK * 2u;
-      if (a.resident_b) {
-        mbar_expect_tx(smem_u32(&bres_bar), b_tx * (uint32_t)a.num_kb);
-        for (int kb = 0; kb < a.num_kb; ++kb)
-          tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * a.BK, 0);
+      const uint32_t a_tx = (uint32_t)(ksize == 1 ? 128 : a.tile_rows) * (uint32_t)BK * 2u;
+      const uint32_t b_tx = (uint32_t)BN * (uint32_t)BK * 2u;
+      const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx);
+      if (resident_b) {
+        mbar_expect_tx(smem_u32(&bres_bar), b_tx * (uint32_t)num_kb);
+        for (int kb = 0; kb < num_kb; ++kb)
+          tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * BK, 0);
       }
-      uint32_t it = 0;
+      uint32_t stage = 0, wrap = 0, issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = decode_tile(a, t);
-        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
-          const uint32_t s = it % (uint32_t)stages;
-          const uint32_t use = it / (uint32_t)stages;
-          if (use > 0 && !mbar_wait_bounded(smem_u32(&empty_bar[s]), (use - 1) & 1u, &abort_sh, a.status,
+        const int mt = (int)fdiv((uint32_t)t, fd_nt);
+        const int nt = t - mt * n_tiles;
+        int p0 = 0, b = 0, iy0 = 0, ix0 = 0;
+        if (ksize == 1) {
+          p0 = mt * 128;
+        } else {
+          b = (int)fdiv((uint32_t)mt, fd_tpi);
+          const int rem = mt - b * tiles_per_img;
+          const int ty = (int)fdiv((uint32_t)rem, fd_tx);
+          iy0 = ty * TH * stride - pad;
+          ix0 = (rem - ty * tiles_x) * TW * stride - pad;
+        }
+        // k-block walk: chunk fastest, then tap (ky, kx), then source
+        int src = 0, nc = sc[0], chunk = 0, tap = 0, ky = 0, kx = 0;
+        for (int kb = 0; kb < num_kb;) {
+          CONV_TRACE_T0();
+          if (wrap > 0 && !mbar_wait_bounded(smem_u32(&empty_bar[stage]), (wrap - 1u) & 1u, &abort_sh, status,
                                              kStatusTimeoutEmpty)) {
             ok = false;
             break;
           }
-          const uint32_t fb = smem_u32(&full_bar[s]);
-          const uint32_t sa = ring_base + s * stage_bytes;
-          mbar_expect_tx(fb, a_tx + (a.resident_b ? 0u : b_tx));
-          int src, tap, chunk;
-          decode_kb(a, kb, src, tap, chunk);
-          if (a.ksize == 1) {
-            tma_load_2d(sa, mapA_ptr(a, src), fb, chunk * a.BK, (int)tc.p0);
-          } else {
-            const int ky = tap / 3, kx = tap - ky * 3;
-            tma_load_4d(sa, mapA_ptr(a, src), fb, chunk * a.BK, tc.ox0 * a.stride - a.pad + kx,
-                        tc.oy0 * a.stride - a.pad + ky, tc.b);
+          CONV_TRACE_SINCE(0);
+          CONV_TRACE_ADD(7, 1);
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_expect_tx(fb, tx_bytes * (uint32_t)kbs);
+          for (int g = 0; g < kbs; ++g, ++kb) {
+            const uint32_t sa = ring_base + stage * stage_bytes + (uint32_t)g * kb_bytes;
+            if (ksize == 1)
+              tma_load_2d(sa, mapA_ptr(a, src), fb, chunk * BK, p0);
+            else
+              tma_load_4d(sa, mapA_ptr(a, src), fb, chunk * BK, ix0 + kx, iy0 + ky, b);
+            if (!resident_b) tma_load_2d(sa + a_tile, &a.mapB, fb, kb * BK, nt * BN);
+            if (++chunk == nc) {
+              chunk = 0;
+              if (++kx == ksize) {
+                kx = 0;
+                ++ky;
+              }
+              if (++tap == taps) {
+                tap = ky = kx = 0;
+                if (++src < nsrc) nc = src == 1 ? sc[1] : src == 2 ? sc[2] : sc[3];
+              }
+            }
           }
-          if (!a.resident_b) tma_load_2d(sa + a_tile, &a.mapB, fb, kb * a.BK, tc.n * a.BN);
+          ++issued;
+          if (++stage == (uint32_t)stages) {
+            stage = 0;
+            ++wrap;
+          }
         }
       }
       // drain: wait (bounded, regardless of the abort flag) until the latest load
       // issued into every ring slot has landed, so no TMA write outlives the CTA
       volatile int no_abort = 0;
-      const uint32_t issued = it;
       const uint32_t first = issued > (uint32_t)stages ? issued - (uint32_t)stages : 0u;
       for (uint32_t j = first; j < issued; ++j) {
         const uint32_t s = j % (uint32_t)stages;
-        mbar_wait_bounded(smem_u32(&full_bar[s]), (j / (uint32_t)stages) & 1u, &no_abort, a.status,
+        mbar_wait_bounded(smem_u32(&full_bar[s]), (j / (uint32_t)stages) & 1u, &no_abort, status,
                           kStatusTimeoutDrain, 400000000LL);
       }
-      if (a.resident_b)
-        mbar_wait_bounded(smem_u32(&bres_bar), 0, &no_abort, a.status, kStatusTimeoutDrain, 400000000LL);
+      if (resident_b)
+        mbar_wait_bounded(smem_u32(&bres_bar), 0, &no_abort, status, kStatusTimeoutDrain, 400000000LL);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
-      const uint32_t idesc = idesc_f16_f32(128, a.BN);
+      const uint32_t idesc = idesc_f16_f32(128, BN);
+      const int ksteps = BK / 16;
       bool ok = true;
-      if (a.resident_b)
-        ok = mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, a.status, kStatusTimeoutFull);
-      uint32_t it = 0, tcount = 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tcount) {
-        const uint32_t buf = tcount & 1u;
-        const uint32_t use = tcount >> 1;
-        if (use > 0 && !mbar_wait_bounded(smem_u32(&acce_bar[buf]), (use - 1) & 1u, &abort_sh, a.status,
+      if (resident_b) ok = mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull);
+      const uint32_t nbuf = (uint32_t)a.nbuf;
+      uint32_t stage = 0, wrap = 0, buf = 0, use = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        CONV_TRACE_T0();
+        if (use > 0 && !mbar_wait_bounded(smem_u32(&acce_bar[buf]), (use - 1) & 1u, &abort_sh, status,
                                            kStatusTimeoutAccEmpty)) {
           ok = false;
           break;
         }
+        CONV_TRACE_SINCE(2);
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * (uint32_t)a.BN;
-        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
-          const uint32_t s = it % (uint32_t)stages;
-          if (!mbar_wait_bounded(smem_u32(&full_bar[s]), (it / (uint32_t)stages) & 1u, &abort_sh, a.status,
-                                 kStatusTimeoutFull)) {
+        const uint32_t d_tmem = tmem_base + buf * (uint32_t)BN;
+        for (int kb = 0; kb < num_kb;) {
+          CONV_TRACE_T0();
+          if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), wrap & 1u, &abort_sh, status, kStatusTimeoutFull)) {
             ok = false;
             break;
           }
+          CONV_TRACE_SINCE(1);
           tc_fence_after();
-          const uint32_t sa = ring_base + s * stage_bytes;
-          const uint32_t sb = a.resident_b ? bres_base + (uint32_t)kb * b_tile : sa + a_tile;
-          for (int k = 0; k < a.BK / 16; ++k) {
-            const uint64_t ad = smem_desc_kmajor(sa + (uint32_t)k * 32u, row_bytes);
-            const uint64_t bd = smem_desc_kmajor(sb + (uint32_t)k * 32u, row_bytes);
-            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int g = 0; g < kbs; ++g, ++kb) {
+            const uint32_t sa = ring_base + stage * stage_bytes + (uint32_t)g * kb_bytes;
+            const uint32_t sb = resident_b ? bres_base + (uint32_t)kb * b_tile : sa + a_tile;
+            for (int k = 0; k < ksteps; ++k) {
+              const uint64_t ad = smem_desc_kmajor(sa + (uint32_t)k * 32u, row_bytes);
+              const uint64_t bd = smem_desc_kmajor(sb + (uint32_t)k * 32u, row_bytes);
+              umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
-          umma_commit(smem_u32(&empty_bar[s]));  // slot free once these MMAs retire
+          umma_commit(smem_u32(&empty_bar[stage]));  // slot free once these MMAs retire
+          if (++stage == (uint32_t)stages) {
+            stage = 0;
+            ++wrap;
+          }
         }
         if (!ok) break;
         umma_commit(smem_u32(&accf_bar[buf]));   // accumulator ready
+        if (++buf == nbuf) {
+          buf = 0;
+          ++use;
+        }
       }
       // every MMA issued by this thread must retire before TMEM is released
       volatile int no_abort = 0;
       umma_commit(smem_u32(&done_bar));
-      mbar_wait_bounded(smem_u32(&done_bar), 0, &no_abort, a.status, kStatusTimeoutDrain, 400000000LL);
+      mbar_wait_bounded(smem_u32(&done_bar), 0, &no_abort, status, kStatusTimeoutDrain, 400000000LL);
     }
   } else {
     // -------------------------------------------------------------- epilogue
     switch (a.act_fn) {
-      case kFnSilu: epilogue_role<kFnSilu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
-      case kFnRelu: epilogue_role<kFnRelu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
-      case kFnHswishA: epilogue_role<kFnHswishA>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
-      case kFnHsigmoid: epilogue_role<kFnHsigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
-      case kFnSigmoid: epilogue_role<kFnSigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
-      default: epilogue_role<kFnNone>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh); break;
+      case kFnSilu: epilogue_role<kFnSilu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
+      case kFnRelu: epilogue_role<kFnRelu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
+      case kFnHswishA: epilogue_role<kFnHswishA>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
+      case kFnHsigmoid: epilogue_role<kFnHsigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
+      case kFnSigmoid: epilogue_role<kFnSigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
+      default: epilogue_role<kFnNone>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
     }
   }
 
   tc_fence_before();
   __syncthreads();
+#ifdef IVB_CONV_TRACE
+  if (threadIdx.x == 0) CONV_TRACE_ADD(5, clock64() - kernel_t0);
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, (uint32_t)a.tmem_cols);
   }
+}
+
+#ifdef IVB_CONV_TRACE
+extern "C" int ivb_conv_trace_read(unsigned long long *dst, int n, int clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(dst, g_conv_trace, sizeof(unsigned long long) * (size_t)n);
+  if (e == cudaSuccess && clear) {
+    static unsigned long long zeros[256 * kTraceSlots] = {};
+    e = cudaMemcpyToSymbol(g_conv_trace, zeros, sizeof(zeros));
+  }
+  return (int)e;
+}
+#endif
+
+FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f{0u, 0u};
+  if (d == 0) return f;
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  f.s = s;
+  f.m = (uint32_t)(((1ull << (31 + s)) / d) + 1ull);
+  return f;
+}
+
+bool conv_tc_finalize(ConvTcArgs &a, const char **why) {
+  const long long lim = (1ll << 31) - 1;
+  if (a.m_total > lim - 128 || (long long)a.m_tiles * a.n_tiles > lim || (long long)a.Ho * a.Wo > lim) {
+    if (why) *why = "conv output too large for 32-bit tile indexing";
+    return false;
+  }
+  if (a.kb_per_stage < 1 || a.num_kb % a.kb_per_stage != 0) {
+    if (why) *why = "conv k-blocks per stage must divide the k-block count";
+    return false;
+  }
+  if (a.BN > 256 || (a.nbuf != 1 && a.nbuf != 2 && a.nbuf != 4) || a.nbuf * a.BN > a.tmem_cols || a.tmem_cols > 512) {
+    if (why) *why = "conv N tile / accumulator buffers out of range";
+    return false;
+  }
+  a.fd_ntiles = make_fastdiv((uint32_t)a.n_tiles);
+  a.fd_tiles_per_img = make_fastdiv((uint32_t)a.tiles_per_img);
+  a.fd_tiles_x = make_fastdiv((uint32_t)a.tiles_x);
+  a.fd_tw = make_fastdiv((uint32_t)a.TW);
+  a.fd_hw = make_fastdiv((uint32_t)(a.Ho * a.Wo));
+  a.fd_wo = make_fastdiv((uint32_t)a.Wo);
+  return true;
 }
 
 cudaError_t launch_conv_tc(const ConvTcArgs &args, int grid, cudaStream_t stream) {

@@ -10,8 +10,18 @@ namespace ivb {
 
 constexpr int kConvMaxSrc = 4;
 constexpr int kConvMaxStages = 12;
-constexpr int kConvEpiWarps = 16;   // four warps per TMEM lane quarter, splitting the columns
+constexpr int kConvEpiWarps = 16;   // four groups of four warps (one per TMEM lane quarter)
+constexpr int kConvMaxBufs = 4;     // TMEM accumulator buffers (= epilogue teams)
 constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;  // warp0 TMA, warp1 MMA, then epilogue
+
+// Division by a launch-invariant divisor as a multiply-high:
+//   q = (n * m) >> (31 + s),  s = ceil(log2 d),  m = floor(2^(31+s) / d) + 1,
+// exact for 0 <= n < 2^31 and 1 <= d < 2^31 (n * (m - 2^(31+s)/d) < 2^(31+s)/d).
+struct FastDiv {
+  uint32_t m;
+  uint32_t s;
+};
+FastDiv make_fastdiv(uint32_t d);  // host (conv_tc.cu)
 
 struct alignas(64) ConvTcArgs {
   CUtensorMap mapA[kConvMaxSrc];  // 1x1: 2-D (C, pixels); 3x3: 4-D (C, W, H, B)
@@ -26,6 +36,7 @@ struct alignas(64) ConvTcArgs {
   int n_tiles;                    // Np / BN
   int num_kb;                     // K blocks per tile
   int stages;
+  int kb_per_stage;               // k-blocks per pipeline stage (divides num_kb)
   int resident_b;                 // 1: all of B stays in smem
   // M tiling
   long long m_total;              // 1x1: pixels (B*H*W)
@@ -44,9 +55,16 @@ struct alignas(64) ConvTcArgs {
   long long r_sb, r_sc, r_sy, r_sx;
   int res_vec;
   int tmem_cols;
+  int nbuf;                       // accumulator buffers / epilogue teams: 1, 2 or 4
   int smem_bytes;
   int *status;
+  // derived by conv_tc_finalize(): divisors of the per-tile index arithmetic
+  FastDiv fd_ntiles, fd_tiles_per_img, fd_tiles_x, fd_tw, fd_hw, fd_wo;
 };
+
+// Fills the derived fields and checks the 32-bit index ranges the kernel uses;
+// returns false (with a message) when a size is out of range.
+bool conv_tc_finalize(ConvTcArgs &args, const char **why);
 
 // Host-side launcher (conv_tc.cu).
 cudaError_t launch_conv_tc(const ConvTcArgs &args, int grid, cudaStream_t stream);

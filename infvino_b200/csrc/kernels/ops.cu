@@ -141,23 +141,6 @@ struct ConcatArgs {
   int nsrc;
   int sum;
 };
-__global__ void concat_k(ConcatArgs g, __half *__restrict__ y, long long outer, long long per_img_outer,
-                         long long inner) {
-  const long long n = outer * g.sum * inner;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i % inner;
-    const long long t = i / inner;
-    int ax = (int)(t % g.sum);
-    const long long o = t / g.sum;
-    int s = 0;
-    while (s < g.nsrc - 1 && ax >= g.s[s].c) {
-      ax -= g.s[s].c;
-      ++s;
-    }
-    const long long oo = g.s[s].shared ? (o % per_img_outer) : o;
-    y[i] = g.s[s].ptr[(oo * g.s[s].c + ax) * inner + r];
-  }
-}
 
 __global__ void maxpool_v4_k(View4 x, View4 y, long long n, int K, int S, int P, bool cfast) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -895,9 +878,9 @@ bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_ho
   std::memset(&p, 0, sizeof(p));
   for (int c = 0; c < cout; ++c) {
     for (int k = 0; k < cin * 9; ++k) {
-      __half h;
-      std::memcpy(&h, &w_host[(size_t)c * cin * 9 + k], 2);
-      p.w[k][c] = __half2float(h);
+      __half_raw hr;
+      hr.x = w_host[(size_t)c * cin * 9 + k];
+      p.w[k][c] = __half2float(__half(hr));
     }
     if (b_host) reinterpret_cast<uint16_t *>(&p.b8[c / 8])[c % 8] = b_host[c];
   }

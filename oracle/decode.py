@@ -61,3 +61,75 @@ def pose_decode(out: np.ndarray, conf: float = 0.25, iou: float = 0.7, max_det: 
         dets.append((a, float(scores[a]), boxes[k], np.stack(kp, 1)))
     dets.sort(key=lambda d: -d[1])
     return dets[:max_det]
+
+
+def _xywh(out: np.ndarray, idx: np.ndarray) -> np.ndarray:
+    cx, cy, w, h = (out[i, idx].astype(np.float64) for i in range(4))
+    return np.stack([cx - w / 2.0, cy - h / 2.0, w, h], 1)
+
+
+def undecided_anchors(out_ref: np.ndarray, out_cmp: np.ndarray, conf: float = 0.25, iou: float = 0.7,
+                      max_det: int = 300, chunk: int = 512):
+    """Anchors whose post-NMS membership is not decided at the deviation between
+    two outputs of the same image (test infrastructure for the NMS-set check).
+
+    delta = max |score_cmp - score_ref|, eps = max |IoU_cmp - IoU_ref| over the
+    pairs of potential candidates that come near the IoU threshold.  The greedy
+    NMS of `pose_decode` takes three kinds of decisions; an anchor is undecided
+    when one of its decisions lies within twice the deviation of the boundary:
+      * candidate or not: |score - conf| <= 2 delta;
+      * suppressed or not: it has a partner with |IoU - iou| <= 2 eps;
+      * who suppresses whom: it overlaps (IoU > iou - 2 eps) a partner whose
+        score is within 2 delta of its own (the greedy order may swap);
+      * the `max_det` cut, when reached: its score is within 2 delta of the cut.
+    A flipped decision can cascade, so the set is closed under overlap (any
+    anchor with IoU > iou - 2 eps to an undecided one is undecided as well).
+    Outside this set both outputs must give the same detections.
+    Returns (undecided anchor set, delta, eps)."""
+    s_ref = out_ref[4].astype(np.float64)
+    s_cmp = out_cmp[4].astype(np.float64)
+    delta = float(np.abs(s_ref - s_cmp).max()) if s_ref.size else 0.0
+    pot = np.nonzero((s_ref >= conf - 2 * delta) | (s_cmp >= conf))[0]
+    und = set(int(a) for a in pot[np.abs(s_ref[pot] - conf) <= 2 * delta])
+    br, bc = _xywh(out_ref, pot), _xywh(out_cmp, pot)
+    # pairwise IoU over the potential candidates, in row chunks
+    eps = 0.0
+    near = []  # (i, j, iou_ref) for pairs that come within 0.3 of the threshold
+    for c0 in range(0, pot.size, chunk):
+        rows = range(c0, min(c0 + chunk, pot.size))
+        ir = np.stack([_iou_one_to_many(br[i], br) for i in rows])
+        ic = np.stack([_iou_one_to_many(bc[i], bc) for i in rows])
+        mask = np.maximum(ir, ic) > iou - 0.3
+        for k in range(mask.shape[0]):
+            mask[k, c0 + k] = False
+        ii, jj = np.nonzero(mask)
+        if ii.size:
+            eps = max(eps, float(np.abs(ir[ii, jj] - ic[ii, jj]).max()))
+            near.extend(zip((ii + c0).tolist(), jj.tolist(), ir[ii, jj].tolist()))
+    adj = {}
+    for i, j, v in near:
+        a, b = int(pot[i]), int(pot[j])
+        if v > iou - 2 * eps:
+            adj.setdefault(a, set()).add(b)
+            if abs(s_ref[a] - s_ref[b]) <= 2 * delta:
+                und.update((a, b))
+        if abs(v - iou) <= 2 * eps:
+            und.update((a, b))
+    dets = pose_decode(out_ref, conf=conf, iou=iou, max_det=10 ** 9)
+    if len(dets) >= max_det:
+        cut = dets[max_det - 1][1]
+        und.update(int(a) for a in pot[np.abs(s_ref[pot] - cut) <= 2 * delta])
+    todo = list(und)
+    while todo:
+        a = todo.pop()
+        for b in adj.get(a, ()):
+            if b not in und:
+                und.add(b)
+                todo.append(b)
+    if und and len(dets) >= max_det:
+        # a flip ahead of the cut moves the cut by one detection per flip
+        kept = [d[1] for d in dets]
+        lo = kept[min(len(kept) - 1, max_det - 1 + len(und))]
+        hi = kept[max(0, max_det - 1 - len(und))]
+        und.update(int(a) for a in pot[(s_ref[pot] >= lo - 2 * delta) & (s_ref[pot] <= hi + 2 * delta)])
+    return und, delta, eps

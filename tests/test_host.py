@@ -126,3 +126,26 @@ def test_plangen_matches_onnx2plan_conventions(tmp_path):
     mul = [l for l in lines if l.startswith("node ew_binary") and "bdims=1,4,8400" in l]
     assert mul and mul[0].endswith("op=2 n=33600 b_scalar=0 bdims=1,4,8400,33600,8400,1,8400,0,1")
     assert lines[-1] == "output output0"
+
+
+def test_fastdiv_formula_exact():
+    """The conv kernel's multiply-high division (conv_tc.cuh FastDiv):
+    s = ceil(log2 d), m = floor(2^(31+s)/d) + 1, q = (n*m) >> (31+s) equals n // d
+    for 0 <= n < 2^31.  Checked at the ends of the range and on random n for
+    divisors of every size, including powers of two and their neighbours."""
+    rng = np.random.default_rng(5)
+    divs = set(range(1, 300)) | {(1 << k) + e for k in range(1, 31) for e in (-1, 0, 1)}
+    divs |= set(int(v) for v in rng.integers(1, 1 << 31, 2000))
+    for d in sorted(divs):
+        if not 1 <= d < (1 << 31):
+            continue
+        s = 0
+        while (1 << s) < d:
+            s += 1
+        m = (1 << (31 + s)) // d + 1
+        assert m < (1 << 32)
+        n = np.concatenate([np.arange(0, 64), (1 << 31) - 1 - np.arange(64), rng.integers(0, 1 << 31, 200),
+                            d * rng.integers(0, (1 << 31) // d, 50), d * rng.integers(1, (1 << 31) // d + 1, 50) - 1])
+        n = n[(n >= 0) & (n < (1 << 31))].astype(object)
+        q = [(int(x) * m) >> (31 + s) for x in n]
+        assert q == [int(x) // d for x in n], d
