@@ -53,6 +53,39 @@ def dist_env():
     return rank, world, local
 
 
+class RankGroup:
+    """Timing plumbing of a multi-GPU run: a barrier and the max over ranks,
+    over gloo on CPU tensors (no data-path collective; images are independent)."""
+
+    def __init__(self, world: int):
+        self.world = world
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            if not dist.is_initialized():
+                dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -217,11 +250,9 @@ def main() -> int:
         return run_kernels_only(args, local)
 
     import torch
-    import torch.distributed as dist
     import infvino_b200 as ivb
 
-    if world > 1:
-        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+    group = RankGroup(world)
     torch.cuda.set_device(local)
     B = args.batch
     plan = make_plan(rank)
@@ -237,16 +268,8 @@ def main() -> int:
     y_host = torch.empty(B * n_out, dtype=torch.float32, pin_memory=True)
     x_dev = x_host.to(f"cuda:{local}", non_blocking=False)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier = group.barrier
+    max_over_ranks = group.max
 
     # ---- device-resident throughput: input converted once, K graph replays
     y_dev = torch.empty(B * n_out, dtype=torch.float32, device=f"cuda:{local}")
@@ -374,9 +397,7 @@ def main() -> int:
         }
         print(json.dumps(line), flush=True)
     model.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    group.close()
     return 0
 
 
