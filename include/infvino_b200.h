@@ -94,6 +94,17 @@ int ivc_run_async(ivc_model *m, int batch, void *stream);
 int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch);
 /* Copies tensor `name` for `batch` images in plan (NCHW) order; IVC_ERR_NOT_FOUND if unknown. */
 int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch);
+/* ivc_read_tensor_f16 without any allocation (no counterpart in the reference).
+ * The NHWC -> NCHW relayout is staged through a static 4 MiB device buffer per
+ * device instead of a scratch buffer grown with cudaMalloc; a tensor that needs
+ * more than 4 MiB for `batch` images fails with IVC_ERR_ARGUMENT.  For callers
+ * that must not allocate or free device memory after set-up: a process whose
+ * device memory is owned by another allocator, or a diagnostic read inside a
+ * latency-critical loop (cudaFree synchronises the whole device).  Make the
+ * first call on each device before any stream capture (it resolves the
+ * buffer's address, which may load the module).  Overlapping calls on one
+ * device (from any handle) share the buffer and race. */
+int ivc_read_tensor_f16_noalloc(ivc_model *m, const char *name, uint16_t *dst, int batch);
 
 /* Zero-copy: device fp16 input / outputs, enqueued on `stream` (cudaStream_t,
  * NULL = the handle's stream) without host synchronisation. */

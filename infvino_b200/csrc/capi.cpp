@@ -254,6 +254,50 @@ int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch
   });
 }
 
+// ---- ivc_read_tensor_f16_noalloc: the relayout of ivc_read_tensor_f16 staged
+// through one static device buffer per device instead of a cudaMalloc'd one.
+// Overlapping calls on the same device (any handles) share the buffer and race.
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 4ll << 20;  // 4 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[kNoAllocMaxDevices] = {};
+}  // namespace
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+int ivc_read_tensor_f16_noalloc(ivc_model *m, const char *name, uint16_t *dst, int batch) {
+  return guarded(m, [&]() -> int {
+    if (!name || !dst || batch < 1 || batch > m->eng->max_batch()) return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    const int dev = m->eng->device();
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(m, IVC_ERR_ARGUMENT, "read_tensor_f16_noalloc: device ordinal out of range");
+    void *scratch = nullptr;
+    {
+      // device address of the static buffer, resolved once per device (the first
+      // call may load the module, so it belongs before any stream capture)
+      std::lock_guard<std::mutex> lk(g_noalloc_mu);
+      if (g_noalloc_addr[dev] == nullptr) {
+        cudaError_t e = cudaSetDevice(dev);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&g_noalloc_addr[dev], g_noalloc_scratch);
+        if (e != cudaSuccess) {
+          g_noalloc_addr[dev] = nullptr;
+          return fail(m, IVC_ERR_CUDA,
+                      std::string("CudaPlanModel: cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(e));
+        }
+      }
+      scratch = g_noalloc_addr[dev];
+    }
+    int64_t need = 0;
+    const int r = m->eng->read_tensor_f16_staged(name, dst, batch, scratch, kNoAllocScratchBytes, &need);
+    if (r == 1) return fail(m, IVC_ERR_NOT_FOUND, std::string("PlanModel: no tensor ") + name);
+    if (r == 2)
+      return fail(m, IVC_ERR_ARGUMENT,
+                  std::string("read_tensor_f16_noalloc: tensor ") + name + " needs " + std::to_string(need) +
+                      " bytes of relayout scratch for " + std::to_string(batch) +
+                      " image(s); the static scratch holds " + std::to_string(kNoAllocScratchBytes) + " bytes");
+    return IVC_OK;
+  });
+}
+
 int ivc_infer_f16_device(ivc_model *m, const void *d_input, int batch, void *const *d_outputs, void *stream) {
   return guarded(m, [&]() -> int {
     if (!d_input || !d_outputs || batch < 1 || batch > m->eng->max_batch())

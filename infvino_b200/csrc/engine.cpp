@@ -1198,6 +1198,33 @@ bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch)
   return true;
 }
 
+int Engine::read_tensor_f16_staged(const std::string &name, void *host_dst, int batch, void *scratch,
+                                   int64_t scratch_bytes, int64_t *need_bytes) {
+  auto it = tid_.find(name);
+  if (it == tid_.end()) return 1;
+  const TensorRt &t = T_[(size_t)it->second];
+  if (t.dptr == nullptr) return 1;
+  const int64_t n = t.numel * (t.is_init ? 1 : batch);
+  if (need_bytes) *need_bytes = t.dense ? 0 : n * 2;
+  if (t.dense) {
+    check(cudaMemcpyAsync(host_dst, t.dptr, (size_t)n * 2, cudaMemcpyDeviceToHost, stream_), "tensor copy");
+  } else {
+    if (n * 2 > scratch_bytes) return 2;
+    // the relayout writes every one of the n elements before the copy reads them
+    View4 src = view(it->second);
+    View4 dst = src;
+    dst.ptr = static_cast<__half *>(scratch);
+    dst.sx = 1;
+    dst.sy = dst.W;
+    dst.sc = (int64_t)dst.H * dst.W;
+    dst.sb = (int64_t)dst.C * dst.H * dst.W;
+    check(launch_copy_v4(src, dst, batch, stream_), "tensor relayout");
+    check(cudaMemcpyAsync(host_dst, scratch, (size_t)n * 2, cudaMemcpyDeviceToHost, stream_), "tensor copy");
+  }
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  return 0;
+}
+
 int Engine::graph_kernel_count(int batch) {
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");

@@ -101,6 +101,11 @@ class Engine {
   void download_output_f32(int i, float *dst, int batch, bool dst_on_device);
   // Plan-order (NCHW) copy of any tensor for `batch` images into host memory.
   bool read_tensor_f16(const std::string &name, void *host_dst, int batch);
+  // read_tensor_f16 staged through caller-provided device scratch (allocates
+  // nothing).  Returns 0 (copied), 1 (unknown tensor) or 2 (scratch too small;
+  // *need_bytes says how much the relayout needs).
+  int read_tensor_f16_staged(const std::string &name, void *host_dst, int batch, void *scratch,
+                             int64_t scratch_bytes, int64_t *need_bytes);
   void synchronize();
   int device_status();  // kernel status word (0 = ok), resets it
   int graph_kernel_count(int batch);  // kernel nodes in the CUDA graph of `batch`
