@@ -282,6 +282,71 @@ void Engine::build_tensors() {
     }
     set_nhwc(o);
   }
+  // Concat in place: when every source of a planar concat4 is a convolution
+  // output that nothing else reads (directly or through reshapes), the
+  // convolutions write their slices of the concat output through strided views
+  // and the concat launches nothing.  The head's anchor-axis concats
+  // (box/kpt/cls over the three scales) are of this kind.
+  if (!(flags_ & kFlagNoFusion)) {
+    std::map<int, std::vector<int>> readers;  // storage root -> reading nodes (views excluded)
+    std::map<int, std::string> producer;      // storage root -> producing op
+    for (size_t ni = 0; ni < nodes.size(); ++ni) {
+      const auto &n = nodes[ni];
+      if (n.op == "reshape" || n.op == "flatten") continue;
+      for (const auto &in : n.ins)
+        if (in != "-") readers[T_[(size_t)tid(in)].root].push_back((int)ni);
+      producer[T_[(size_t)tid(n.outs[0])].root] = n.op;
+    }
+    for (int ni = (int)nodes.size() - 1; ni >= 0; --ni) {
+      const auto &n = nodes[(size_t)ni];
+      if (n.op != "concat4") continue;
+      const int y = tid(n.outs[0]);
+      const TensorRt &Y = T_[(size_t)y];
+      if (Y.nhwc || !Y.dense || Y.root != y) continue;
+      const int cnt[4] = {n.ai("ca", 0), n.ai("cb", 0), n.ai("cc", 0), n.ai("cd", 0)};
+      const int64_t outer = n.ai("outer", 1), inner = n.ai("inner", 1);
+      const int64_t S = (int64_t)cnt[0] + cnt[1] + cnt[2] + cnt[3];
+      bool ok = true;
+      int roots[4] = {-1, -1, -1, -1};
+      for (int k = 0; k < 4 && ok; ++k) {
+        if (cnt[k] <= 0) continue;
+        if ((size_t)k >= n.ins.size() || n.ins[(size_t)k] == "-") { ok = false; break; }
+        const int r = T_[(size_t)tid(n.ins[(size_t)k])].root;
+        const TensorRt &R = T_[(size_t)r];
+        const std::string &pop = producer.count(r) ? producer[r] : std::string();
+        const bool conv = pop == "conv1x1" || pop == "conv3x3" || pop == "conv1x1_cat4";
+        const auto &rd = readers[r];
+        ok = conv && R.root == r && R.dense && !R.nhwc && !R.is_init && !R.is_input && !R.is_output &&
+             R.dims.size() == 4 && rd.size() == 1 && rd[0] == ni &&
+             ((outer == R.C && (int64_t)cnt[k] * inner == (int64_t)R.H * R.W) ||
+              (outer == 1 && (int64_t)cnt[k] * inner == R.numel));
+        for (int j = 0; j < k && ok; ++j) ok = roots[j] != r;
+        roots[k] = r;
+      }
+      if (!ok) continue;
+      int64_t off = 0;
+      for (int k = 0; k < 4; ++k) {
+        if (cnt[k] <= 0) continue;
+        TensorRt &R = T_[(size_t)roots[k]];
+        R.root = y;
+        R.elem_off = Y.elem_off + off * inner;
+        R.dense = false;
+        R.sx = 1;
+        R.sy = R.W;
+        R.sc = outer == 1 ? (int64_t)R.H * R.W : S * inner;
+        R.sb = Y.sb;
+        R.bytes_per_img = 0;
+        for (auto &v : T_)  // reshapes of the source follow it
+          if (&v != &R && v.root == roots[k]) {
+            v.root = y;
+            v.elem_off = R.elem_off;
+            v.dense = false;
+          }
+        off += cnt[k];
+      }
+      elided_nodes_.insert(ni);
+    }
+  }
   for (auto &t : T_) {
     if (t.root != tid(t.name)) ++stats_.views;
     else if (!t.is_init) ++stats_.roots;
@@ -478,10 +543,25 @@ void Engine::lower() {
     return (x.elem_off * 2) % 16 == 0;
   };
 
+  // storage root -> reading nodes (views excluded), for the fused-chain match
+  std::map<int, std::vector<int>> readers;
+  for (size_t ni = 0; ni < nodes.size(); ++ni) {
+    if (nodes[ni].op == "reshape" || nodes[ni].op == "flatten") continue;
+    for (const auto &in : nodes[ni].ins)
+      if (in != "-") readers[T_[(size_t)tid(in)].root].push_back((int)ni);
+  }
+  auto sole_reader = [&](int t) -> int {
+    const TensorRt &x = T_[(size_t)t];
+    if (x.is_output || x.root != t) return -1;
+    const auto it = readers.find(t);
+    return (it != readers.end() && it->second.size() == 1) ? it->second[0] : -1;
+  };
+
   for (size_t ni = 0; ni < nodes.size(); ++ni) {
     const PlanNode &n = nodes[ni];
     const std::string &op = n.op;
     if (op == "reshape" || op == "flatten") continue;
+    if (elided_nodes_.count((int)ni)) continue;  // folded into an earlier step
     const int out = tid(n.outs[0]);
     Step st;
     st.node = (int)ni;
@@ -842,6 +922,47 @@ void Engine::lower() {
       }
       steps_.push_back(std::move(st));
       continue;
+    }
+
+    // ------------------------------------------- DFL head: permute -> softmax -> 1x1
+    if (op == "permute_0213" && n.ai("mode", 0) == 0 && !(flags_ & kFlagNoFusion)) {
+      const int D1 = n.ai("D1", 1), D2 = n.ai("D2", 1);
+      const int64_t I = n.ai("I", 1);
+      const int x = tid(n.ins[0]);
+      const int sm_node = sole_reader(out);
+      const PlanNode *sm = sm_node >= 0 ? &nodes[(size_t)sm_node] : nullptr;
+      const bool sm_ok = sm && sm->op == "softmax_axis" && sm->ai("outer", 1) == 1 && sm->ai("axdim", 0) == D2 &&
+                         sm->ai("inner", 1) == (int64_t)D1 * I && sm->ins[0] == n.outs[0];
+      const int cv_node = sm_ok ? sole_reader(tid(sm->outs[0])) : -1;
+      const PlanNode *cv = cv_node >= 0 ? &nodes[(size_t)cv_node] : nullptr;
+      bool cv_ok = cv && cv->op == "conv1x1" && cv->ins.size() >= 2 && cv->ins[1] == sm->outs[0] &&
+                   (cv->ins.size() < 4 || cv->ins[3] == "-");
+      int cout = 0;
+      if (cv_ok) {
+        const TensorRt &wt = T_[(size_t)tid(cv->ins[0])];
+        cout = wt.dims.empty() ? 0 : (int)wt.dims[0];
+        cv_ok = wt.is_init && wt.numel == (int64_t)cout * D2 && dfl_fused_supported(D2, cout) && T_[(size_t)x].dense &&
+                T_[(size_t)tid(cv->outs[0])].dense && T_[(size_t)tid(cv->outs[0])].numel == (int64_t)cout * D1 * I;
+      }
+      if (cv_ok) {
+        const int y = tid(cv->outs[0]);
+        const __half *wptr = T_[(size_t)tid(cv->ins[0])].dptr;
+        const int bt = (cv->ins.size() > 2 && cv->ins[2] != "-") ? tid(cv->ins[2]) : -1;
+        const __half *bptr = bt >= 0 ? T_[(size_t)bt].dptr : nullptr;
+        const int act = cv->ai("act", 0);
+        st.name = "dfl:" + cv->outs[0];
+        st.family = "dfl_fused";
+        st.flops_img = 2.0 * cout * D2 * D1 * (double)I;
+        st.bytes_img = act_bytes(x) + act_bytes(y);
+        st.bytes_fixed = init_bytes(tid(cv->ins[0])) + (bt >= 0 ? init_bytes(bt) : 0.0);
+        st.launch = [this, x, y, wptr, bptr, D1, D2, I, cout, act](int B, cudaStream_t s) {
+          return launch_dfl_fused(T_[(size_t)x].dptr, wptr, bptr, T_[(size_t)y].dptr, B, D1, D2, I, cout, act, s);
+        };
+        elided_nodes_.insert(sm_node);
+        elided_nodes_.insert(cv_node);
+        steps_.push_back(std::move(st));
+        continue;
+      }
     }
 
     // ---------------------------------------------------------------- small ops

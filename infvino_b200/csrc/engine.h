@@ -133,6 +133,7 @@ class Engine {
   std::vector<TensorRt> T_;
   std::map<std::string, int> tid_;
   std::set<std::string> nhwc_names_;
+  std::set<int> elided_nodes_;       // concat4 nodes whose sources write in place
   std::vector<Step> steps_;
   EngineStats stats_;
 

@@ -696,6 +696,48 @@ __global__ void conv1x1_planar_k(const __half *__restrict__ x, const __half *__r
   }
 }
 
+// Distribution-focal-loss head in one pass: permute_0213 (mode 0) of the box
+// tensor, softmax_axis over the D2 bins, then the 1x1 projection bins -> Cout.
+// x [B][D1*D2][I] holds side j's bins in rows j*D2 .. +D2; y [B][Cout][D1][I].
+// The arithmetic is softmax_axis_k's followed by conv1x1_planar_k's (softmax
+// rounded to half, f32 accumulation in bin order, conv epilogue), without the
+// two intermediate tensors.
+template <int D2>
+__global__ void dfl_fused_k(const __half *__restrict__ x, const __half *__restrict__ w,
+                            const __half *__restrict__ bias, __half *__restrict__ y, long long n, int D1, long long I,
+                            int Cout, int act) {
+  __shared__ float ws[kPlanarMaxCout * D2];
+  for (int i = threadIdx.x; i < Cout * D2; i += blockDim.x) ws[i] = __half2float(w[i]);
+  __syncthreads();
+  const long long per = (long long)D1 * I;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long img = i / per, r = i - img * per;
+    const long long j = r / I, a = r - j * I;
+    const __half *xp = x + (img * D1 + j) * D2 * I + a;
+    float v[D2];
+#pragma unroll
+    for (int k = 0; k < D2; ++k) v[k] = __half2float(xp[(long long)k * I]);
+    float m = -3.4e38f;
+#pragma unroll
+    for (int k = 0; k < D2; ++k) m = fmaxf(m, v[k]);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < D2; ++k) {
+      v[k] = expf(v[k] - m);  // the same values softmax_axis_k computes twice
+      s += v[k];
+    }
+    float pr[D2];
+#pragma unroll
+    for (int k = 0; k < D2; ++k) pr[k] = __half2float(__float2half_rn(v[k] / s));
+    for (int co = 0; co < Cout; ++co) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < D2; ++k) acc += pr[k] * ws[co * D2 + k];
+      y[(img * Cout + co) * per + r] = epilogue(acc, bias ? __half2float(bias[co]) : 0.0f, act, kActGemm);
+    }
+  }
+}
+
 inline bool cfast_of(const View4 &y) { return y.sc == 1; }
 inline long long numel4(const View4 &v, int batch) { return (long long)batch * v.C * v.H * v.W; }
 
@@ -904,6 +946,16 @@ cudaError_t launch_conv1x1_planar(const __half *x, const __half *w, const __half
   if (Cin > kPlanarMaxCin || Cout > kPlanarMaxCout) return cudaErrorInvalidValue;
   const long long npix = (long long)batch * N;
   conv1x1_planar_k<<<grid_for(npix), kThreads, 0, st>>>(x, w, bias, y, npix, N, Cin, Cout, act);
+  return cudaGetLastError();
+}
+
+bool dfl_fused_supported(int D2, int Cout) { return D2 == 16 && Cout >= 1 && Cout <= kPlanarMaxCout; }
+
+cudaError_t launch_dfl_fused(const __half *x, const __half *w, const __half *bias, __half *y, int batch, int D1, int D2,
+                             long long I, int Cout, int act, cudaStream_t st) {
+  if (!dfl_fused_supported(D2, Cout)) return cudaErrorInvalidValue;
+  const long long n = (long long)batch * D1 * I;
+  dfl_fused_k<16><<<grid_for(n), kThreads, 0, st>>>(x, w, bias, y, n, D1, I, Cout, act);
   return cudaGetLastError();
 }
 

@@ -73,6 +73,11 @@ cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, cons
                               int Cout, int S, int P, int act, cudaStream_t st);
 // 1x1 conv over planar [Cin][N] rows with few outputs (Cin <= 64, Cout <= 8),
 // gemm-family rounding, fp32 accumulation over ci in order.
+// permute_0213 (mode 0) -> softmax over D2 bins -> 1x1 conv D2 -> Cout, fused
+// (the YOLO DFL head).  Supported for D2 == 16 and Cout <= 8.
+bool dfl_fused_supported(int D2, int Cout);
+cudaError_t launch_dfl_fused(const __half *x, const __half *w, const __half *bias, __half *y, int batch, int D1, int D2,
+                             long long I, int Cout, int act, cudaStream_t st);
 cudaError_t launch_conv1x1_planar(const __half *x, const __half *w, const __half *bias, __half *y, int batch,
                                   long long N, int Cin, int Cout, int act, cudaStream_t st);
 // Reference host conversion on the device: f32 -> f16 by mantissa truncation.

@@ -255,6 +255,23 @@ def test_batched_equals_single(model_plans):
     m.close()
 
 
+def test_head_fusions_bit_identical(plan_dir):
+    """Concat-in-place and the fused DFL step change no output bit: the default
+    handle equals a NO_FUSION handle (the plan run node by node, plus no CAT4/RES
+    rewrites) on the decoded output, and the in-place head tensors read back the same."""
+    p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_320"), imgsz=320)
+    n = 3 * 320 * 320
+    x = np.random.default_rng(17).random(2 * n, dtype=np.float32)
+    a = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_POOL)
+    b = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_FUSION)
+    ya, yb = a.infer_f32(x, 2)[0], b.infer_f32(x, 2)[0]
+    assert np.array_equal(ya, yb)
+    for name in ("model.22.cv2.1.2.out", "model.22.cv4.2.2.out", "model.22.cv3.0.2.out"):
+        assert np.array_equal(a.readTensor(name, 2), b.readTensor(name, 2)), name
+    a.close()
+    b.close()
+
+
 def test_graph_and_eager_agree(model_plans):
     p = model_plans["mobilenetv3-small"]
     x = np.random.default_rng(9).random(2 * 3 * 224 * 224, dtype=np.float32)

@@ -149,3 +149,21 @@ def test_fastdiv_formula_exact():
         n = n[(n >= 0) & (n < (1 << 31))].astype(object)
         q = [(int(x) * m) >> (31 + s) for x in n]
         assert q == [int(x) // d for x in n], d
+
+
+def test_head_concats_in_place_and_dfl_fused(model_plans):
+    """The head's anchor-axis concats are written in place by their convolutions
+    and the DFL chain (permute -> softmax -> 1x1) is one step; NO_FUSION keeps
+    the plan's node-per-step form."""
+    p = model_plans["yolov8n-pose"]
+    fused = ivb.PlanModel(p, device=0, max_batch=2, flags=ivb.FLAG_DRY_RUN)
+    plain = ivb.PlanModel(p, device=0, max_batch=2, flags=ivb.FLAG_DRY_RUN | ivb.FLAG_NO_FUSION)
+    fam = [s["family"] for s in fused.steps()]
+    names = [s["name"] for s in fused.steps()]
+    assert fam.count("dfl_fused") == 1 and "softmax_axis" not in fam and "permute_0213" not in fam
+    for cat in ("box_cat", "kpt_cat", "cls_cat"):
+        assert not any(n.endswith(cat) for n in names), cat
+    assert sum(n.endswith(c) for n in (s["name"] for s in plain.steps()) for c in ("box_cat", "kpt_cat", "cls_cat")) == 3
+    d = fused.describe()
+    assert "tensor model.22.cv2.0.2.out planar root=model.22.box_cat off=0" in d
+    assert "tensor model.22.cv2.1.2.out planar root=model.22.box_cat off=6400" in d
