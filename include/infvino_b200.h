@@ -61,6 +61,8 @@ typedef enum ivc_status {
 #define IVC_FLAG_NO_TENSOR_CORES 0x8u /* convolutions on the CUDA-core direct kernel (diagnostic) */
 #define IVC_FLAG_NO_POOL 0x10u        /* no activation memory reuse, every tensor stays readable
                                          (reference INFVINO_NO_POOL, src/PlanModel.cpp:887) */
+#define IVC_FLAG_NO_HALO 0x20u        /* diagnostic: 3x3 stride-1 convolutions load one box per tap
+                                         instead of one halo box per channel chunk */
 
 /* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
 int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);

@@ -502,6 +502,7 @@ struct ConvCfg {
   int act = 0, act_kind = kActGemm;
   int out = -1, res = -1;
   int stages = 2, resident_b = 0, smem = 0, tmem_cols = 32, nbuf = 2, kb_per_stage = 1;
+  int halo = 0, hx = 0, hy = 0, kern_kb = 0;  // 3x3 stride-1 halo mode (kern_kb: kernel k-blocks)
   __half *wp = nullptr;    // packed [Np][Kp]
   __half *bias = nullptr;  // [Np] padded
 };
@@ -705,19 +706,32 @@ void Engine::lower() {
           c.TH = std::max(1, 128 / c.TW);
         }
       }
-      const int a_tile = 128 * c.BK * 2;
       const int b_tile = (int)round_up((int64_t)c.BN * c.BK * 2, 1024);
-      const int budget = 232448 - 1024 - 2048 /*static smem + barriers*/ - 1024 /*align*/ - a_tile /*slack*/;
       const int bres = b_tile * c.num_kb;
-      c.resident_b = (c.n_tiles == 1 && bres <= 96 * 1024 && budget - bres >= 2 * a_tile) ? 1 : 0;
+      // 3x3 stride 1 with resident weights: one 16 x (TH+2) halo box per channel
+      // chunk feeds all nine taps (an eighth of the TMA rows of per-tap boxes)
+      c.kern_kb = c.num_kb;
+      if (c.ksize == 3 && c.stride == 1 && c.pad == 1 && c.nsrc == 1 && c.n_tiles == 1 && bres <= 96 * 1024 &&
+          !(flags_ & kFlagNoHalo)) {
+        c.halo = 1;
+        c.TW = 8;
+        c.TH = 16;
+        c.hx = 16;
+        c.hy = c.TH + 2;
+        c.kern_kb = c.chunks[0];
+      }
+      const int a_tile = c.halo ? (int)round_up((int64_t)c.hx * c.hy * c.BK * 2, 1024) : 128 * c.BK * 2;
+      const int budget = 232448 - 1024 - 2048 /*static smem + barriers*/ - 1024 /*align*/ - a_tile /*slack*/;
+      c.resident_b = c.halo || (c.n_tiles == 1 && bres <= 96 * 1024 && budget - bres >= 2 * a_tile) ? 1 : 0;
+      if (c.halo && budget - bres < 2 * a_tile) throw std::runtime_error("CudaPlanModel: halo conv does not fit shared memory");
       const int kb_bytes = a_tile + (c.resident_b ? 0 : b_tile);
       const int ring = budget - (c.resident_b ? bres : 0);
       // k-blocks per pipeline stage: one full/empty handshake costs a few
       // hundred cycles, far more than a 16-channel k-block's MMA, so small
       // k-blocks travel in groups (a divisor of num_kb, <= 48 KB, >= 3 stages)
       c.kb_per_stage = 1;
-      for (int g = c.num_kb; g >= 2; --g)
-        if (c.num_kb % g == 0 && g * kb_bytes <= 48 * 1024 && ring / (g * kb_bytes) >= 3) {
+      for (int g = c.kern_kb; g >= 2; --g)
+        if (c.kern_kb % g == 0 && g * kb_bytes <= 48 * 1024 && ring / (g * kb_bytes) >= 3) {
           c.kb_per_stage = g;
           break;
         }
@@ -787,7 +801,8 @@ void Engine::lower() {
             } else {
               const uint64_t dims[4] = {(uint64_t)v.C, (uint64_t)v.W, (uint64_t)v.H, (uint64_t)B};
               const uint64_t strides[3] = {(uint64_t)v.sx * 2, (uint64_t)v.sy * 2, (uint64_t)v.sb * 2};
-              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)(c.TW * c.stride), (uint32_t)(c.TH * c.stride), 1};
+              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)(c.halo ? c.hx : c.TW * c.stride),
+                                       (uint32_t)(c.halo ? c.hy : c.TH * c.stride), 1};
               const uint32_t es[4] = {1, (uint32_t)c.stride, (uint32_t)c.stride, 1};
               ok = encode_tiled_f16(&a.mapA[sidx], 4, v.ptr, dims, strides, box, es,
                                     swizzle_for_row_bytes(c.BK * 2), &err);
@@ -811,7 +826,11 @@ void Engine::lower() {
           a.BK = c.BK;
           a.BN = c.BN;
           a.n_tiles = c.n_tiles;
-          a.num_kb = c.num_kb;
+          a.num_kb = c.kern_kb;
+          a.halo = c.halo;
+          a.hx = c.hx;
+          a.hy = c.hy;
+          a.halo_bytes = c.halo ? (int)round_up((int64_t)c.hx * c.hy * c.BK * 2, 1024) : 0;
           a.stages = c.stages;
           a.kb_per_stage = c.kb_per_stage;
           a.resident_b = c.resident_b;

@@ -29,6 +29,7 @@ enum EngineFlags : unsigned {
   kFlagDryRun = 1u << 2,      // host-only: plan, layout, allocation; no device work
   kFlagNoTensorCores = 1u << 3,  // route convolutions to the CUDA-core direct kernel
   kFlagNoPool = 1u << 4,      // every tensor keeps its own storage (reference INFVINO_NO_POOL)
+  kFlagNoHalo = 1u << 5,      // 3x3 stride-1 convs with per-tap boxes instead of the halo tile
 };
 
 struct TensorRt {

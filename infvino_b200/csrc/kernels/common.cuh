@@ -253,6 +253,22 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
 }
 
 // Arrive on an mbarrier once all prior tcgen05.mma of this thread have completed.
+// Same MMA with the descriptors passed as (low, high) words: the low word holds
+// the start address (>> 4) and the leading byte offset, so an operand offset is
+// one 32-bit add on the low word (the start field never carries: shared memory
+// addresses stay below 2^18).
+__device__ __forceinline__ void umma_f16_lh(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                            uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -289,6 +305,26 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t ro
   const uint64_t lbo = 1;                         // ignored for swizzled K-major
   const uint64_t sbo = (8u * row_bytes) >> 4;     // 8-row group stride
   return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// Same layout with an explicit 8-row group stride and a start anywhere on a
+// 16-byte boundary of the operand (the 3x3 halo tile: a tap is a start offset
+// of whole rows).  `base_off` is the descriptor's matrix base offset field; the
+// MMA applies the swizzle to absolute shared-memory address bits, as TMA does
+// when it writes the tile, so shifted starts keep base_off = 0 (checked by the
+// conv3x3 parity tests: a phase-derived base offset gives wrong results).
+__device__ __forceinline__ uint64_t smem_desc_kmajor_at(uint32_t saddr, uint32_t row_bytes, uint32_t sbo_bytes,
+                                                       uint32_t base_off) {
+  uint32_t layout;
+  switch (row_bytes) {
+    case 128: layout = 2; break;
+    case 64: layout = 4; break;
+    default: layout = 6; break;
+  }
+  const uint64_t start = (saddr & 0x3FFFFu) >> 4;
+  const uint64_t sbo = sbo_bytes >> 4;
+  return start | (1ull << 16) | (sbo << 32) | (1ull << 46) | ((uint64_t)(base_off & 7u) << 49) |
+         ((uint64_t)layout << 61);
 }
 
 // Instruction descriptor, kind::f16: D f32, A/B f16, both K-major, M x N.

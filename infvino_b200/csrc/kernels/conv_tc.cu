@@ -245,9 +245,11 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   // 1024-byte aligned operand area (128B-swizzle atoms repeat every 1024 B)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
-  const uint32_t a_tile = 128u * (uint32_t)BK * 2u;  // bytes
+  const bool halo = a.halo != 0;
+  const uint32_t a_tile = halo ? (uint32_t)a.halo_bytes : 128u * (uint32_t)BK * 2u;  // bytes
   const uint32_t b_tile = (((uint32_t)BN * (uint32_t)BK * 2u) + 1023u) & ~1023u;
-  const uint32_t bres_bytes = resident_b ? b_tile * (uint32_t)num_kb : 0u;
+  const int b_blocks = halo ? num_kb * 9 : num_kb;  // resident weight blocks
+  const uint32_t bres_bytes = resident_b ? b_tile * (uint32_t)b_blocks : 0u;
   const int kbs = a.kb_per_stage;                      // k-blocks per stage
   const uint32_t kb_bytes = a_tile + (resident_b ? 0u : b_tile);
   const uint32_t stage_bytes = (uint32_t)kbs * kb_bytes;
@@ -299,13 +301,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       int sc[kConvMaxSrc];
 #pragma unroll
       for (int i = 0; i < kConvMaxSrc; ++i) sc[i] = a.src_chunks[i];
-      // bytes one A box delivers: 128 pixel rows (1x1) or TH*TW rows (3x3)
-      const uint32_t a_tx = (uint32_t)(ksize == 1 ? 128 : a.tile_rows) * (uint32_t)BK * 2u;
+      // bytes one A box delivers: 128 pixel rows (1x1), TH*TW rows (3x3) or
+      // the hx*hy halo
+      const uint32_t a_tx =
+          (uint32_t)(halo ? a.hx * a.hy : ksize == 1 ? 128 : a.tile_rows) * (uint32_t)BK * 2u;
       const uint32_t b_tx = (uint32_t)BN * (uint32_t)BK * 2u;
       const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx);
       if (resident_b) {
-        mbar_expect_tx(smem_u32(&bres_bar), b_tx * (uint32_t)num_kb);
-        for (int kb = 0; kb < num_kb; ++kb)
+        mbar_expect_tx(smem_u32(&bres_bar), b_tx * (uint32_t)b_blocks);
+        for (int kb = 0; kb < b_blocks; ++kb)
           tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * BK, 0);
       }
       uint32_t stage = 0, wrap = 0, issued = 0;
@@ -340,6 +344,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             const uint32_t sa = ring_base + stage * stage_bytes + (uint32_t)g * kb_bytes;
             if (ksize == 1)
               tma_load_2d(sa, mapA_ptr(a, src), fb, chunk * BK, p0);
+            else if (halo)  // the whole (hx x hy) window once per chunk; kb counts chunks
+              tma_load_4d(sa, mapA_ptr(a, src), fb, kb * BK, ix0, iy0, b);
             else
               tma_load_4d(sa, mapA_ptr(a, src), fb, chunk * BK, ix0 + kx, iy0 + ky, b);
             if (!resident_b) tma_load_2d(sa + a_tile, &a.mapB, fb, kb * BK, nt * BN);
@@ -377,8 +383,28 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
+      // One thread issues every MMA, so the scalar work between two MMAs is
+      // pure latency: descriptors are built once and advanced by 32-bit adds on
+      // their low word (start address >> 4), and the tap / k-step loops are
+      // unrolled with their offsets fixed before the tile loop.
       const uint32_t idesc = idesc_f16_f32(128, BN);
       const int ksteps = BK / 16;
+      const int hx = a.hx;
+      const uint32_t halo_sbo = (uint32_t)hx * row_bytes;  // one image row of the halo per 8-row group
+      const uint64_t a_desc0 =
+          halo ? smem_desc_kmajor_at(ring_base, row_bytes, halo_sbo, 0u) : smem_desc_kmajor(ring_base, row_bytes);
+      const uint64_t b_desc0 = smem_desc_kmajor(resident_b ? bres_base : ring_base + a_tile, row_bytes);
+      const uint32_t a_lo0 = (uint32_t)a_desc0, a_hi = (uint32_t)(a_desc0 >> 32);
+      const uint32_t b_lo0 = (uint32_t)b_desc0, b_hi = (uint32_t)(b_desc0 >> 32);
+      const uint32_t stage_step = stage_bytes >> 4, kb_step = kb_bytes >> 4, b_step = b_tile >> 4;
+      // halo: tap (dy, dx) starts dy*hx + dx rows into the halo, and its weights
+      // are resident block tap * num_kb + chunk
+      uint32_t tap_a[9], tap_b[9];
+#pragma unroll
+      for (int tap = 0; tap < 9; ++tap) {
+        tap_a[tap] = ((uint32_t)((tap / 3) * hx + tap % 3) * row_bytes) >> 4;
+        tap_b[tap] = (uint32_t)(tap * num_kb) * b_step;
+      }
       bool ok = true;
       if (resident_b) ok = mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull);
       const uint32_t nbuf = (uint32_t)a.nbuf;
@@ -402,12 +428,25 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
           CONV_TRACE_SINCE(1);
           tc_fence_after();
           for (int g = 0; g < kbs; ++g, ++kb) {
-            const uint32_t sa = ring_base + stage * stage_bytes + (uint32_t)g * kb_bytes;
-            const uint32_t sb = resident_b ? bres_base + (uint32_t)kb * b_tile : sa + a_tile;
-            for (int k = 0; k < ksteps; ++k) {
-              const uint64_t ad = smem_desc_kmajor(sa + (uint32_t)k * 32u, row_bytes);
-              const uint64_t bd = smem_desc_kmajor(sb + (uint32_t)k * 32u, row_bytes);
-              umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            const uint32_t a_lo = a_lo0 + stage * stage_step + (uint32_t)g * kb_step;
+            if (halo) {
+              const uint32_t b_lo = b_lo0 + (uint32_t)kb * b_step;
+#pragma unroll
+              for (int tap = 0; tap < 9; ++tap) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  if (k < ksteps)
+                    umma_f16_lh(d_tmem, a_lo + tap_a[tap] + 2u * k, a_hi, b_lo + tap_b[tap] + 2u * k, b_hi, idesc,
+                                (kb | tap | k) != 0 ? 1u : 0u);
+                }
+              }
+              continue;
+            }
+            const uint32_t b_lo = resident_b ? b_lo0 + (uint32_t)kb * b_step : a_lo + (a_tile >> 4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if (k < ksteps)
+                umma_f16_lh(d_tmem, a_lo + 2u * k, a_hi, b_lo + 2u * k, b_hi, idesc, (kb | k) != 0 ? 1u : 0u);
             }
           }
           umma_commit(smem_u32(&empty_bar[stage]));  // slot free once these MMAs retire

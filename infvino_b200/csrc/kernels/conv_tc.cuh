@@ -43,6 +43,12 @@ struct alignas(64) ConvTcArgs {
   int m_tiles;
   int Ho, Wo, TH, TW, tiles_x, tiles_per_img;
   int tile_rows;                  // rows of the A tile actually filled (TH*TW or 128)
+  // 3x3 stride-1 halo mode: one (hx x hy)-pixel box per channel chunk feeds all
+  // nine taps (TW = 8, TH = 16; a tap is a descriptor start offset of whole
+  // rows).  num_kb then counts channel chunks, weights stay resident.
+  int halo;
+  int hx, hy;                     // halo box in pixels (16 x (TH + 2))
+  int halo_bytes;                 // smem bytes of one halo box (1024-aligned)
   // epilogue
   const __half *bias;             // [Np] or null
   int cout;
