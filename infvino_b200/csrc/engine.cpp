@@ -711,19 +711,25 @@ void Engine::lower() {
       // 3x3 stride 1 with resident weights: one 16 x (TH+2) halo box per channel
       // chunk feeds all nine taps (an eighth of the TMA rows of per-tap boxes)
       c.kern_kb = c.num_kb;
-      if (c.ksize == 3 && c.stride == 1 && c.pad == 1 && c.nsrc == 1 && c.n_tiles == 1 && bres <= 96 * 1024 &&
-          !(flags_ & kFlagNoHalo)) {
-        c.halo = 1;
-        c.TW = 8;
-        c.TH = 16;
-        c.hx = 16;
-        c.hy = c.TH + 2;
-        c.kern_kb = c.chunks[0];
+      auto smem_budget = [](int a_tile) { return 232448 - 1024 - 2048 /*static + barriers*/ - 1024 /*align*/ - a_tile; };
+      if (c.ksize == 3 && (c.stride == 1 || c.stride == 2) && c.pad == 1 && c.nsrc == 1 && c.n_tiles == 1 &&
+          bres <= 96 * 1024 && !(flags_ & kFlagNoHalo)) {
+        const int hx = c.stride == 1 ? 16 : 8 + 1;   // stride 2: one phase (every other column)
+        const int hy = c.stride == 1 ? 16 + 2 : 16 + 1;
+        const int a_h = (int)round_up((int64_t)hx * hy * c.BK * 2, 1024) * (c.stride == 2 ? 4 : 1);
+        if (smem_budget(a_h) - bres >= 2 * a_h) {  // resident weights + two stages
+          c.halo = c.stride;
+          c.TW = 8;
+          c.TH = 16;
+          c.hx = hx;
+          c.hy = hy;
+          c.kern_kb = c.chunks[0];
+        }
       }
-      const int a_tile = c.halo ? (int)round_up((int64_t)c.hx * c.hy * c.BK * 2, 1024) : 128 * c.BK * 2;
-      const int budget = 232448 - 1024 - 2048 /*static smem + barriers*/ - 1024 /*align*/ - a_tile /*slack*/;
+      const int64_t halo_box = round_up((int64_t)c.hx * c.hy * c.BK * 2, 1024);
+      const int a_tile = c.halo ? (int)(halo_box * (c.halo == 2 ? 4 : 1)) : 128 * c.BK * 2;
+      const int budget = smem_budget(a_tile);
       c.resident_b = c.halo || (c.n_tiles == 1 && bres <= 96 * 1024 && budget - bres >= 2 * a_tile) ? 1 : 0;
-      if (c.halo && budget - bres < 2 * a_tile) throw std::runtime_error("CudaPlanModel: halo conv does not fit shared memory");
       const int kb_bytes = a_tile + (c.resident_b ? 0 : b_tile);
       const int ring = budget - (c.resident_b ? bres : 0);
       // k-blocks per pipeline stage: one full/empty handshake costs a few
@@ -801,8 +807,8 @@ void Engine::lower() {
             } else {
               const uint64_t dims[4] = {(uint64_t)v.C, (uint64_t)v.W, (uint64_t)v.H, (uint64_t)B};
               const uint64_t strides[3] = {(uint64_t)v.sx * 2, (uint64_t)v.sy * 2, (uint64_t)v.sb * 2};
-              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)(c.halo ? c.hx : c.TW * c.stride),
-                                       (uint32_t)(c.halo ? c.hy : c.TH * c.stride), 1};
+              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)((c.halo ? c.hx : c.TW) * c.stride),
+                                       (uint32_t)((c.halo ? c.hy : c.TH) * c.stride), 1};
               const uint32_t es[4] = {1, (uint32_t)c.stride, (uint32_t)c.stride, 1};
               ok = encode_tiled_f16(&a.mapA[sidx], 4, v.ptr, dims, strides, box, es,
                                     swizzle_for_row_bytes(c.BK * 2), &err);

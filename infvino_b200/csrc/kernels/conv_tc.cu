@@ -246,7 +246,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   const bool halo = a.halo != 0;
-  const uint32_t a_tile = halo ? (uint32_t)a.halo_bytes : 128u * (uint32_t)BK * 2u;  // bytes
+  const int nphase = a.halo == 2 ? 4 : 1;  // stride-2 halo: four phase boxes
+  const uint32_t a_tile = halo ? (uint32_t)(a.halo_bytes * nphase) : 128u * (uint32_t)BK * 2u;  // bytes
   const uint32_t b_tile = (((uint32_t)BN * (uint32_t)BK * 2u) + 1023u) & ~1023u;
   const int b_blocks = halo ? num_kb * 9 : num_kb;  // resident weight blocks
   const uint32_t bres_bytes = resident_b ? b_tile * (uint32_t)b_blocks : 0u;
@@ -304,7 +305,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       // bytes one A box delivers: 128 pixel rows (1x1), TH*TW rows (3x3) or
       // the hx*hy halo
       const uint32_t a_tx =
-          (uint32_t)(halo ? a.hx * a.hy : ksize == 1 ? 128 : a.tile_rows) * (uint32_t)BK * 2u;
+          (uint32_t)(halo ? a.hx * a.hy * nphase : ksize == 1 ? 128 : a.tile_rows) * (uint32_t)BK * 2u;
+      const uint32_t phase_bytes = (uint32_t)a.halo_bytes;
       const uint32_t b_tx = (uint32_t)BN * (uint32_t)BK * 2u;
       const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx);
       if (resident_b) {
@@ -344,8 +346,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             const uint32_t sa = ring_base + stage * stage_bytes + (uint32_t)g * kb_bytes;
             if (ksize == 1)
               tma_load_2d(sa, mapA_ptr(a, src), fb, chunk * BK, p0);
-            else if (halo)  // the whole (hx x hy) window once per chunk; kb counts chunks
+            else if (halo) {  // the whole window once per chunk; kb counts chunks
               tma_load_4d(sa, mapA_ptr(a, src), fb, kb * BK, ix0, iy0, b);
+              if (nphase == 4) {  // odd columns, odd rows, both odd
+                tma_load_4d(sa + phase_bytes, mapA_ptr(a, src), fb, kb * BK, ix0 + 1, iy0, b);
+                tma_load_4d(sa + 2u * phase_bytes, mapA_ptr(a, src), fb, kb * BK, ix0, iy0 + 1, b);
+                tma_load_4d(sa + 3u * phase_bytes, mapA_ptr(a, src), fb, kb * BK, ix0 + 1, iy0 + 1, b);
+              }
+            }
             else
               tma_load_4d(sa, mapA_ptr(a, src), fb, chunk * BK, ix0 + kx, iy0 + ky, b);
             if (!resident_b) tma_load_2d(sa + a_tile, &a.mapB, fb, kb * BK, nt * BN);
@@ -399,10 +407,16 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       const uint32_t stage_step = stage_bytes >> 4, kb_step = kb_bytes >> 4, b_step = b_tile >> 4;
       // halo: tap (dy, dx) starts dy*hx + dx rows into the halo, and its weights
       // are resident block tap * num_kb + chunk
+      // (stride 2: phase (ky & 1, kx & 1), row (ky >> 1) * hx + (kx >> 1))
       uint32_t tap_a[9], tap_b[9];
+      const bool s2 = a.halo == 2;
 #pragma unroll
       for (int tap = 0; tap < 9; ++tap) {
-        tap_a[tap] = ((uint32_t)((tap / 3) * hx + tap % 3) * row_bytes) >> 4;
+        const int ky = tap / 3, kx = tap % 3;
+        const uint32_t off = s2 ? (uint32_t)(((ky & 1) * 2 + (kx & 1)) * a.halo_bytes) +
+                                      (uint32_t)((ky >> 1) * hx + (kx >> 1)) * row_bytes
+                                : (uint32_t)(ky * hx + kx) * row_bytes;
+        tap_a[tap] = off >> 4;
         tap_b[tap] = (uint32_t)(tap * num_kb) * b_step;
       }
       bool ok = true;

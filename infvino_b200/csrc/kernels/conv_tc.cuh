@@ -43,12 +43,16 @@ struct alignas(64) ConvTcArgs {
   int m_tiles;
   int Ho, Wo, TH, TW, tiles_x, tiles_per_img;
   int tile_rows;                  // rows of the A tile actually filled (TH*TW or 128)
-  // 3x3 stride-1 halo mode: one (hx x hy)-pixel box per channel chunk feeds all
-  // nine taps (TW = 8, TH = 16; a tap is a descriptor start offset of whole
-  // rows).  num_kb then counts channel chunks, weights stay resident.
+  // 3x3 halo mode (halo = the stride, 1 or 2; 0 = one box per tap): the input
+  // window of a TW = 8 x TH = 16 output tile is loaded once per channel chunk
+  // and feeds all nine taps, a tap being a descriptor start offset of whole
+  // rows.  Stride 1: one 16 x 18 box.  Stride 2: four phase boxes (even / odd
+  // rows x columns, TMA element stride 2) of 9 x 17 pixels; tap (ky, kx) reads
+  // phase (ky & 1, kx & 1) from row (ky >> 1) * hx + (kx >> 1).  num_kb then
+  // counts channel chunks, and the weights stay resident.
   int halo;
-  int hx, hy;                     // halo box in pixels (16 x (TH + 2))
-  int halo_bytes;                 // smem bytes of one halo box (1024-aligned)
+  int hx, hy;                     // one halo / phase box in pixels
+  int halo_bytes;                 // smem bytes of one box (1024-aligned)
   // epilogue
   const __half *bias;             // [Np] or null
   int cout;
