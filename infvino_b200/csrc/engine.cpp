@@ -12,6 +12,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <functional>
 #include <cstring>
 #include <numeric>
 #include <set>
@@ -43,6 +44,12 @@ uint16_t f32_to_f16_rne_host(float f) {  // host packing of padded weights only 
   return u;
 }
 
+float f16_to_f32_host(uint16_t u) {  // exact widening of an init value (host)
+  __half_raw r;
+  r.x = u;
+  return __half2float(__half(r));
+}
+
 }  // namespace
 
 // ============================================================================ setup
@@ -63,6 +70,7 @@ Engine::Engine(const std::string &plan_path, int device, int max_batch, unsigned
   }
   plan_layouts();
   build_tensors();
+  if (!(flags_ & kFlagNoFusion)) plan_tails();
   allocate();
   upload_weights();
   lower();
@@ -371,6 +379,7 @@ void Engine::allocate() {
     for (const auto &in : nodes[(size_t)i].ins) touch(in, i);
     for (const auto &o : nodes[(size_t)i].outs) touch(o, i);
   }
+  for (const auto &u : tail_uses_) touch(T_[(size_t)u.first].name, u.second);  // fused tails read late
   for (const auto &o : plan_->outputs()) T_[(size_t)T_[(size_t)tid(o)].root].death = N;
 
   std::vector<int> roots;
@@ -522,6 +531,385 @@ int pow2_at_least(int v) {
 
 }  // namespace
 
+// ============================================================================ fused planar tails
+// A region of reshape / slice_axis / concat4 / ew_binary / ew_unary nodes (and
+// the DFL chain permute_0213 -> softmax_axis -> conv1x1) ending in a plan
+// output, whose tensors all keep the anchor axis A innermost, becomes one
+// TailProgram: the node DAG expanded per output row (rows, slices, concats and
+// broadcasts resolved on the host, scalar inits folded to constants, every
+// (tensor, row) value computed once), executed per anchor column on the device.
+void Engine::plan_tails() {
+  Plan &p = *plan_;
+  const auto &nodes = p.nodes();
+  std::map<std::string, int> producer;
+  std::map<std::string, std::vector<int>> consumers;
+  for (size_t ni = 0; ni < nodes.size(); ++ni) {
+    for (const auto &in : nodes[ni].ins)
+      if (in != "-") consumers[in].push_back((int)ni);
+    producer[nodes[ni].outs[0]] = (int)ni;
+  }
+  auto sole_consumer = [&](const std::string &t) -> int {
+    auto it = consumers.find(t);
+    return (it != consumers.end() && it->second.size() == 1) ? it->second[0] : -1;
+  };
+  // DFL chain ending at conv node c: returns the permute's input tensor, or "".
+  auto dfl_source = [&](int c) -> std::string {
+    const PlanNode &cv = nodes[(size_t)c];
+    if (cv.op != "conv1x1" || cv.ins.size() < 2 || (cv.ins.size() > 3 && cv.ins[3] != "-")) return "";
+    auto ps = producer.find(cv.ins[1]);
+    if (ps == producer.end()) return "";
+    const PlanNode &sm = nodes[(size_t)ps->second];
+    if (sm.op != "softmax_axis" || sole_consumer(cv.ins[1]) != c) return "";
+    auto pp = producer.find(sm.ins[0]);
+    if (pp == producer.end()) return "";
+    const PlanNode &pm = nodes[(size_t)pp->second];
+    if (pm.op != "permute_0213" || pm.ai("mode", 0) != 0 || sole_consumer(sm.ins[0]) != ps->second) return "";
+    const int D1 = pm.ai("D1", 1), D2 = pm.ai("D2", 1);
+    const int64_t I = pm.ai("I", 1);
+    if (D2 != 16 || sm.ai("outer", 1) != 1 || sm.ai("axdim", 0) != D2 || sm.ai("inner", 1) != (int64_t)D1 * I)
+      return "";
+    const TensorRt &w = T_[(size_t)tid(cv.ins[0])];
+    if (!w.is_init || w.dims.empty() || w.numel != w.dims[0] * D2 || w.dims[0] > 8) return "";
+    return pm.ins[0];
+  };
+
+  for (const auto &oname : p.outputs()) {
+    auto po = producer.find(oname);
+    if (po == producer.end()) continue;
+    const TensorRt &O = T_[(size_t)tid(oname)];
+    if (O.nhwc || !O.dense || O.dims.empty()) continue;
+    const int64_t A = O.dims.back();
+    if (A < 1 || O.numel % A != 0) continue;
+    auto planar_a = [&](const std::string &t) {
+      const TensorRt &x = T_[(size_t)tid(t)];
+      return !x.nhwc && !x.dims.empty() && x.dims.back() == A && x.numel % A == 0;
+    };
+    auto candidate = [&](int ni) -> bool {
+      const PlanNode &n = nodes[(size_t)ni];
+      if (!planar_a(n.outs[0])) return false;
+      if (n.op == "reshape" || n.op == "flatten" || n.op == "ew_unary") return true;
+      if (n.op == "slice_axis") return n.ai("inner", 1) == A;
+      if (n.op == "concat4") return n.ai("inner", 1) == A;
+      if (n.op == "ew_binary") return true;
+      if (n.op == "conv1x1") return !dfl_source(ni).empty();
+      return false;
+    };
+    if (!candidate(po->second)) continue;
+    std::set<int> region{po->second};
+    auto data_inputs = [&](int ni) {
+      const PlanNode &n = nodes[(size_t)ni];
+      std::vector<std::string> v;
+      if (n.op == "conv1x1") return v;  // the DFL chain is taken whole
+      const size_t k = n.op == "concat4" ? std::min<size_t>(4, n.ins.size()) : n.op == "ew_binary" ? 2 : 1;
+      for (size_t i = 0; i < k && i < n.ins.size(); ++i)
+        if (n.ins[i] != "-") v.push_back(n.ins[i]);
+      return v;
+    };
+    for (bool changed = true; changed;) {
+      changed = false;
+      for (int ni : std::vector<int>(region.begin(), region.end()))
+        for (const auto &x : data_inputs(ni)) {
+          const TensorRt &t = T_[(size_t)tid(x)];
+          auto pr = producer.find(x);
+          if (t.is_init || t.is_input || t.is_output || pr == producer.end() || region.count(pr->second)) continue;
+          bool inside = true;
+          for (int c : consumers[x]) inside = inside && region.count(c);
+          if (inside && candidate(pr->second)) {
+            region.insert(pr->second);
+            changed = true;
+          }
+        }
+    }
+    // ---- expand per output row
+    // values in creation (post-) order; loads and constants become operands
+    enum { vLoad, vConst, vBin, vUn, vDfl };
+    struct Val {
+      int code, a, b, arg;
+    };
+    std::vector<Val> ops;
+    std::vector<std::pair<int, int>> events;  // (value, -1) created; (value, row) stored to output row
+    std::vector<std::pair<int, bool>> leaf_ids;  // (tensor, shared across images)
+    std::map<std::string, int> leaf_of;
+    std::vector<TailDfl> dfls;
+    std::map<std::pair<int, int>, int> dfl_of;  // (conv node, cout row) -> table entry
+    std::map<std::pair<std::string, int64_t>, int> memo;
+    std::set<int> dfl_chain;                    // softmax / permute nodes folded into DFL ops
+    bool ok = true;
+    auto fail = [&]() {
+      ok = false;
+      return -1;
+    };
+    auto leaf = [&](const std::string &x, bool shared) -> int {
+      auto it = leaf_of.find(x);
+      if (it != leaf_of.end()) return it->second;
+      const TensorRt &t = T_[(size_t)tid(x)];
+      if ((int)leaf_ids.size() >= kTailMaxLeaves || (!shared && !t.dense)) return fail();
+      leaf_ids.push_back({tid(x), shared});
+      return leaf_of[x] = (int)leaf_ids.size() - 1;
+    };
+    auto push = [&](int code, int a, int b, int arg) {
+      ops.push_back(Val{code, a, b, arg});
+      events.push_back({(int)ops.size() - 1, -1});
+      return (int)ops.size() - 1;
+    };
+    auto cst = [&](float f) {
+      int bits;
+      std::memcpy(&bits, &f, 4);
+      return push(vConst, -1, -1, bits);
+    };
+    auto init_value = [&](const std::string &x, int64_t flat) -> float {
+      const PlanTensor &pt = p.ref(x);
+      return flat < (int64_t)pt.host.size() ? f16_to_f32_host(pt.host[(size_t)flat]) : 0.0f;
+    };
+    std::function<int(const std::string &, int64_t)> emit = [&](const std::string &x, int64_t row) -> int {
+      if (!ok) return -1;
+      auto key = std::make_pair(x, row);
+      auto it = memo.find(key);
+      if (it != memo.end()) return it->second;
+      const TensorRt &t = T_[(size_t)tid(x)];
+      int v = -1;
+      auto pr = producer.find(x);
+      if (t.is_init) {
+        if (t.numel == 1) v = cst(init_value(x, 0));
+        else if (t.numel % A == 0 && row < t.numel / A) v = push(vLoad, leaf(x, true), -1, (int)row);
+        else v = fail();
+      } else if (pr == producer.end() || !region.count(pr->second)) {
+        if (!planar_a(x) || row >= t.numel / A) v = fail();
+        else v = push(vLoad, leaf(x, false), -1, (int)row);
+      } else {
+        const PlanNode &n = nodes[(size_t)pr->second];
+        if (n.op == "reshape" || n.op == "flatten") {
+          v = emit(n.ins[0], row);
+        } else if (n.op == "slice_axis") {
+          const int64_t len = n.ai("len", 0), axdim = n.ai("axdim", 0), start = n.ai("start", 0);
+          v = len > 0 ? emit(n.ins[0], (row / len) * axdim + start + row % len) : fail();
+        } else if (n.op == "concat4") {
+          const int64_t cnt[4] = {n.ai("ca", 0), n.ai("cb", 0), n.ai("cc", 0), n.ai("cd", 0)};
+          const int64_t S = cnt[0] + cnt[1] + cnt[2] + cnt[3];
+          const int64_t o = row / S;
+          int64_t j = row % S;
+          int k = 0;
+          while (k < 4 && j >= cnt[k]) j -= cnt[k++];
+          v = (k < 4 && (size_t)k < n.ins.size()) ? emit(n.ins[(size_t)k], o * cnt[k] + j) : fail();
+        } else if (n.op == "ew_unary") {
+          const int a = emit(n.ins[0], row);
+          v = ok ? push(vUn, a, -1, n.ai("op", 0)) : -1;
+        } else if (n.op == "ew_binary") {
+          int opv[2] = {-1, -1};
+          const bool bsc = n.ai("b_scalar", 0) != 0;
+          for (int w = 0; w < 2 && ok; ++w) {
+            const std::string &xi = n.ins[(size_t)w];
+            const TensorRt &ti = T_[(size_t)tid(xi)];
+            if (!n.attr.count("bdims")) {
+              if (w == 1 && bsc) opv[w] = ti.is_init ? cst(init_value(xi, 0)) : fail();
+              else opv[w] = emit(xi, row);
+              continue;
+            }
+            const std::vector<int64_t> bd = parse_ints(n.attr.at("bdims"));
+            const int R = (int)bd.size() / 3;
+            if (R < 2 || bd[(size_t)R - 1] != A) {
+              opv[w] = fail();
+              continue;
+            }
+            const int64_t *st = &bd[(size_t)(R * (1 + w))];
+            int64_t rem = row, flat = 0;
+            for (int d = R - 2; d >= 1; --d) {
+              flat += (rem % bd[(size_t)d]) * st[d];
+              rem /= bd[(size_t)d];
+            }
+            if (st[R - 1] == 1 && flat % A == 0) opv[w] = emit(xi, flat / A);
+            else if (st[R - 1] == 0 && ti.is_init) opv[w] = cst(init_value(xi, flat));
+            else opv[w] = fail();
+          }
+          v = ok ? push(vBin, opv[0], opv[1], n.ai("op", 0)) : -1;
+        } else if (n.op == "conv1x1") {
+          const std::string src = dfl_source(pr->second);
+          const PlanNode &pm = nodes[(size_t)producer[nodes[(size_t)producer[n.ins[1]]].ins[0]]];
+          const int D1 = pm.ai("D1", 1);
+          dfl_chain.insert(producer[n.ins[1]]);
+          dfl_chain.insert(producer[nodes[(size_t)producer[n.ins[1]]].ins[0]]);
+          const int co = (int)(row / D1), j = (int)(row % D1);
+          auto key2 = std::make_pair(pr->second, co);
+          if (!dfl_of.count(key2)) {
+            if ((int)dfls.size() >= kTailMaxDfl) {
+              v = fail();
+            } else {
+              TailDfl D{};
+              for (int q = 0; q < 16; ++q) D.w[q] = init_value(n.ins[0], (int64_t)co * 16 + q);
+              D.bias = (n.ins.size() > 2 && n.ins[2] != "-") ? init_value(n.ins[2], co) : 0.0f;
+              D.act = n.ai("act", 0);
+              dfls.push_back(D);
+              dfl_of[key2] = (int)dfls.size() - 1;
+            }
+          }
+          if (ok && T_[(size_t)tid(src)].numel / A < (int64_t)(j + 1) * 16) v = fail();
+          if (ok) v = push(vDfl, leaf(src, false), j * 16, dfl_of[key2]);
+        } else {
+          v = fail();
+        }
+      }
+      if (ok) memo[key] = v;
+      return v;
+    };
+    for (int64_t r = 0; r < O.numel / A && ok; ++r) {
+      const int v = emit(oname, r);
+      if (ok) events.push_back({v, (int)r});
+    }
+    if (!ok || region.size() + dfl_chain.size() < 3) continue;
+    // ---- ops: computed values (loads / constants fold into operands), stores
+    // attached to the op that produced the value just before, else a copy op
+    struct Pending {
+      TailOp op;
+      int val;  // value computed by this op (-1 for copies)
+      int ra, rb;  // slot operands read: value ids, or -1
+    };
+    std::vector<Pending> seq;
+    std::vector<int> op_of(ops.size(), -1);
+    auto operand = [&](int v, int &reads) -> TailOperand {
+      reads = -1;
+      const Val &x = ops[(size_t)v];
+      if (x.code == vLoad) return TailOperand{kTailLeafRow, x.a, x.arg};
+      if (x.code == vConst) return TailOperand{kTailImm, x.arg, 0};
+      reads = v;
+      return TailOperand{kTailSlot, -1, 0};
+    };
+    for (const auto &ev : events) {
+      const int v = ev.first;
+      const Val &x = ops[(size_t)v];
+      if (ev.second < 0) {  // creation
+        if (x.code == vLoad || x.code == vConst) continue;
+        Pending pd{};
+        pd.op.dst = -1;
+        pd.op.store_row = -1;
+        pd.op.arg = x.arg;
+        pd.val = v;
+        pd.ra = pd.rb = -1;
+        if (x.code == vDfl) {
+          pd.op.code = kTailDfl;
+          pd.op.a = TailOperand{kTailLeafRow, x.a, x.b};
+          pd.op.b = TailOperand{kTailImm, 0, 0};
+        } else {
+          pd.op.code = x.code == vBin ? kTailBin : kTailUn;
+          pd.op.a = operand(x.a, pd.ra);
+          pd.op.b = x.code == vBin ? operand(x.b, pd.rb) : TailOperand{kTailImm, 0, 0};
+        }
+        op_of[(size_t)v] = (int)seq.size();
+        seq.push_back(pd);
+      } else {  // store of value v to output row ev.second
+        if (!seq.empty() && seq.back().val == v && seq.back().op.store_row < 0) {
+          seq.back().op.store_row = ev.second;
+          continue;
+        }
+        Pending pd{};
+        pd.op.code = kTailCopy;
+        pd.op.dst = -1;
+        pd.op.store_row = ev.second;
+        pd.op.a = operand(v, pd.ra);
+        pd.op.b = TailOperand{kTailImm, 0, 0};
+        pd.val = -1;
+        pd.rb = -1;
+        seq.push_back(pd);
+      }
+    }
+    if (seq.size() > (size_t)kTailMaxOps) continue;
+    // ---- independent chains (ops linked through slot operands) run on
+    // different threads (blockIdx.y); order inside a chain is kept
+    std::vector<int> uf(seq.size());
+    std::iota(uf.begin(), uf.end(), 0);
+    std::function<int(int)> find = [&](int x) { return uf[(size_t)x] == x ? x : uf[(size_t)x] = find(uf[(size_t)x]); };
+    for (size_t i = 0; i < seq.size(); ++i)
+      for (int r : {seq[i].ra, seq[i].rb})
+        if (r >= 0) uf[(size_t)find((int)i)] = find(op_of[(size_t)r]);
+    std::map<int, std::vector<int>> chains;  // root -> op indices (in order)
+    std::vector<int> chain_order;
+    for (size_t i = 0; i < seq.size(); ++i) {
+      const int r = find((int)i);
+      if (!chains.count(r)) chain_order.push_back(r);
+      chains[r].push_back((int)i);
+    }
+    if ((int)chain_order.size() > kTailMaxComp) continue;
+    std::vector<Pending> ordered;
+    std::vector<int> comp_begin;
+    for (int r : chain_order) {
+      comp_begin.push_back((int)ordered.size());
+      for (int i : chains[r]) ordered.push_back(seq[(size_t)i]);
+    }
+    comp_begin.push_back((int)ordered.size());
+    seq.swap(ordered);
+    // ---- slots by last use within each chain (an op may write the slot its
+    // last operand frees)
+    std::vector<int> last(ops.size(), -1), slot(ops.size(), -1);
+    for (size_t i = 0; i < seq.size(); ++i) {
+      if (seq[i].ra >= 0) last[(size_t)seq[i].ra] = (int)i;
+      if (seq[i].rb >= 0) last[(size_t)seq[i].rb] = (int)i;
+    }
+    std::vector<int> free_slots;
+    int n_slots = 0, chain_slots = 0;
+    TailProgram prog;
+    prog.n_comp = (int)chain_order.size();
+    for (size_t c = 0; c < comp_begin.size(); ++c) prog.comp_begin[c] = comp_begin[c];
+    std::set<int> chain_start(comp_begin.begin(), comp_begin.end() - 1);
+    for (size_t i = 0; i < seq.size(); ++i) {
+      if (chain_start.count((int)i)) {  // a new chain starts with every slot free
+        free_slots.clear();
+        chain_slots = 0;
+      }
+      Pending &pd = seq[i];
+      if (pd.ra >= 0) pd.op.a.idx = slot[(size_t)pd.ra];
+      if (pd.rb >= 0) pd.op.b.idx = slot[(size_t)pd.rb];
+      if (pd.ra >= 0 && last[(size_t)pd.ra] == (int)i) free_slots.push_back(slot[(size_t)pd.ra]);
+      if (pd.rb >= 0 && pd.rb != pd.ra && last[(size_t)pd.rb] == (int)i) free_slots.push_back(slot[(size_t)pd.rb]);
+      if (pd.val >= 0 && last[(size_t)pd.val] >= 0) {
+        int sl;
+        if (!free_slots.empty()) {
+          auto m = std::min_element(free_slots.begin(), free_slots.end());
+          sl = *m;
+          free_slots.erase(m);
+        } else {
+          sl = chain_slots++;
+          n_slots = std::max(n_slots, chain_slots);
+        }
+        slot[(size_t)pd.val] = pd.op.dst = sl;
+      }
+      prog.ops[prog.n_ops++] = pd.op;
+    }
+    if (n_slots > kTailMaxSlots) continue;
+    prog.n_slots = n_slots;
+    prog.n_leaves = (int)leaf_ids.size();
+    prog.n_dfl = (int)dfls.size();
+    for (size_t i = 0; i < dfls.size(); ++i) prog.dfl[i] = dfls[i];
+    prog.A = A;
+    const int out_id = tid(oname);
+    Step st;
+    st.node = po->second;
+    st.name = "tail:" + oname;
+    st.family = "decode_tail";
+    for (const auto &lf : leaf_ids) {
+      const TensorRt &t = T_[(size_t)lf.first];
+      if (t.is_init) st.bytes_fixed += (double)t.numel * 2.0;
+      else st.bytes_img += (double)t.numel * 2.0;
+      if (!t.is_init) tail_uses_.push_back({lf.first, po->second});  // read where the tail runs
+    }
+    st.bytes_img += (double)O.numel * 2.0;
+    auto shared_prog = std::make_shared<TailProgram>(prog);
+    auto leaves_v = std::make_shared<std::vector<std::pair<int, bool>>>(leaf_ids);
+    st.launch = [this, shared_prog, leaves_v, out_id, A](int B, cudaStream_t s) -> cudaError_t {
+      TailProgram &pr = *shared_prog;  // device pointers are known once the arena is placed
+      for (size_t i = 0; i < leaves_v->size(); ++i) {
+        const TensorRt &t = T_[(size_t)(*leaves_v)[i].first];
+        pr.leaves[i] = TailLeaf{t.dptr, (*leaves_v)[i].second ? 0 : t.sb, A};
+      }
+      pr.out = T_[(size_t)out_id].dptr;
+      pr.out_img = T_[(size_t)out_id].sb;
+      return launch_tail_program(pr, B, s);
+    };
+    for (int ni : region) elided_nodes_.insert(ni);
+    for (int ni : dfl_chain) elided_nodes_.insert(ni);
+    elided_nodes_.erase(po->second);
+    tail_steps_[po->second] = std::move(st);
+  }
+}
+
 void Engine::lower() {
   Plan &p = *plan_;
   const auto &nodes = p.nodes();
@@ -563,6 +951,10 @@ void Engine::lower() {
     const std::string &op = n.op;
     if (op == "reshape" || op == "flatten") continue;
     if (elided_nodes_.count((int)ni)) continue;  // folded into an earlier step
+    if (tail_steps_.count((int)ni)) {             // fused planar tail ending here
+      steps_.push_back(tail_steps_[(int)ni]);
+      continue;
+    }
     const int out = tid(n.outs[0]);
     Step st;
     st.node = (int)ni;

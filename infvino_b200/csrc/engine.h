@@ -135,6 +135,9 @@ class Engine {
   std::map<std::string, int> tid_;
   std::set<std::string> nhwc_names_;
   std::set<int> elided_nodes_;       // concat4 nodes whose sources write in place
+  std::map<int, Step> tail_steps_;   // fused planar tails, keyed by the node whose place they take
+  std::vector<std::pair<int, int>> tail_uses_;  // (tensor, node) reads of fused tails, for liveness
+  void plan_tails();
   std::vector<Step> steps_;
   EngineStats stats_;
 

@@ -738,6 +738,106 @@ __global__ void dfl_fused_k(const __half *__restrict__ x, const __half *__restri
   }
 }
 
+// Fused tail program (see TailProgram): one thread per (image, V consecutive
+// anchors) runs the whole op list; control flow is the same for every thread.
+template <int V>
+__device__ __forceinline__ void tail_fetch(const TailProgram &P, const TailOperand &o, const float *my, long long img,
+                                           long long an0, float (&v)[V]) {
+  if (o.kind == kTailSlot) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = my[o.idx * (int)blockDim.x * V + j];
+  } else if (o.kind == kTailLeafRow) {
+    const TailLeaf &L = P.leaves[o.idx];
+    const __half *src = L.ptr + img * L.img_stride + (long long)o.row * L.row_stride + an0;
+    if (V == 4) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(src);
+      const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+      const float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]);
+      v[0] = f0.x;
+      v[1 % V] = f0.y;
+      v[2 % V] = f1.x;
+      v[3 % V] = f1.y;
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) v[j] = __half2float(src[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = __int_as_float(o.idx);
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(128) tail_vm_k(const __grid_constant__ TailProgram P, long long n) {
+  extern __shared__ float tail_slots[];
+  float *my = tail_slots + threadIdx.x * V;  // slot s at my[s * blockDim.x * V + j]
+  const long long AV = P.A / V;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long img = i / AV, an0 = (i - img * AV) * V;
+    const int k_end = P.comp_begin[blockIdx.y + 1];
+    for (int k = P.comp_begin[blockIdx.y]; k < k_end; ++k) {
+      const TailOp &op = P.ops[k];
+      float r[V];
+      if (op.code == kTailDfl) {  // softmax_axis_k over 16 bins, then conv1x1_planar_k's arithmetic
+        const TailLeaf &L = P.leaves[op.a.idx];
+        const TailDfl &D = P.dfl[op.arg];
+        const __half *xp = L.ptr + img * L.img_stride + (long long)op.a.row * L.row_stride + an0;
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          float e[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) e[q] = __half2float(xp[(long long)q * L.row_stride + j]);
+          float m = -3.4e38f;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) m = fmaxf(m, e[q]);
+          float s = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            e[q] = expf(e[q] - m);
+            s += e[q];
+          }
+          float acc = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) acc += __half2float(__float2half_rn(e[q] / s)) * D.w[q];
+          r[j] = __half2float(epilogue(acc, D.bias, D.act, kActGemm));
+        }
+      } else {
+        float a[V];
+        tail_fetch<V>(P, op.a, my, img, an0, a);
+        if (op.code == kTailBin) {
+          float b[V];
+          tail_fetch<V>(P, op.b, my, img, an0, b);
+#pragma unroll
+          for (int j = 0; j < V; ++j) r[j] = __half2float(__float2half_rn(binop(a[j], b[j], op.arg)));
+        } else if (op.code == kTailUn) {
+#pragma unroll
+          for (int j = 0; j < V; ++j) r[j] = __half2float(__float2half_rn(unop(a[j], op.arg)));
+        } else {
+#pragma unroll
+          for (int j = 0; j < V; ++j) r[j] = a[j];
+        }
+      }
+      if (op.dst >= 0) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) my[op.dst * (int)blockDim.x * V + j] = r[j];
+      }
+      if (op.store_row >= 0) {
+        __half *dst = P.out + img * P.out_img + (long long)op.store_row * P.A + an0;
+        if (V == 4) {
+          uint2 u;
+          __half2 *h = reinterpret_cast<__half2 *>(&u);
+          h[0] = __floats2half2_rn(r[0], r[1 % V]);
+          h[1] = __floats2half2_rn(r[2 % V], r[3 % V]);
+          *reinterpret_cast<uint2 *>(dst) = u;
+        } else {
+#pragma unroll
+          for (int j = 0; j < V; ++j) dst[j] = __float2half_rn(r[j]);
+        }
+      }
+    }
+  }
+}
+
 inline bool cfast_of(const View4 &y) { return y.sc == 1; }
 inline long long numel4(const View4 &v, int batch) { return (long long)batch * v.C * v.H * v.W; }
 
@@ -946,6 +1046,32 @@ cudaError_t launch_conv1x1_planar(const __half *x, const __half *w, const __half
   if (Cin > kPlanarMaxCin || Cout > kPlanarMaxCout) return cudaErrorInvalidValue;
   const long long npix = (long long)batch * N;
   conv1x1_planar_k<<<grid_for(npix), kThreads, 0, st>>>(x, w, bias, y, npix, N, Cin, Cout, act);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t st) {
+  if (prog.n_ops <= 0 || prog.n_ops > kTailMaxOps || prog.n_slots > kTailMaxSlots || prog.A < 1 ||
+      prog.n_comp < 1 || prog.n_comp > kTailMaxComp)
+    return cudaErrorInvalidValue;
+  // four anchors per thread (8-byte loads / stores) when every row start is 8-byte aligned
+  bool vec = prog.A % 4 == 0 && (reinterpret_cast<uintptr_t>(prog.out) & 7) == 0 && prog.out_img % 4 == 0;
+  for (int i = 0; i < prog.n_leaves; ++i)
+    vec = vec && (reinterpret_cast<uintptr_t>(prog.leaves[i].ptr) & 7) == 0 && prog.leaves[i].img_stride % 4 == 0 &&
+          prog.leaves[i].row_stride % 4 == 0;
+  const int threads = 128;
+  const int V = vec ? 4 : 1;
+  const size_t smem = (size_t)(prog.n_slots > 0 ? prog.n_slots : 1) * threads * V * sizeof(float);
+  const long long n = (long long)batch * (prog.A / V);
+  if (vec) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(tail_vm_k<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      attr = true;
+    }
+    tail_vm_k<4><<<dim3(grid_for(n, threads), prog.n_comp), threads, smem, st>>>(prog, n);
+  } else {
+    tail_vm_k<1><<<dim3(grid_for(n, threads), prog.n_comp), threads, smem, st>>>(prog, n);
+  }
   return cudaGetLastError();
 }
 

@@ -73,6 +73,53 @@ cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, cons
                               int Cout, int S, int P, int act, cudaStream_t st);
 // 1x1 conv over planar [Cin][N] rows with few outputs (Cin <= 64, Cout <= 8),
 // gemm-family rounding, fp32 accumulation over ci in order.
+// ---- fused planar tail: a region of slice / concat / elementwise / reshape
+// nodes (plus the DFL chain) whose tensors all keep the anchor axis (A) as the
+// innermost dimension, compiled at load time into a straight-line program per
+// anchor column.  Every op's result is rounded to fp16 like the node it
+// replaces.  Operands are slots (earlier results, in shared memory
+// [slot][thread]), rows of leaf tensors read directly, or immediates; an op may
+// also write its result to a row of the output.
+constexpr int kTailMaxOps = 400;
+constexpr int kTailMaxLeaves = 8;
+constexpr int kTailMaxDfl = 2;
+constexpr int kTailMaxSlots = 40;
+constexpr int kTailMaxComp = 64;  // independent op chains (one per blockIdx.y)
+enum TailOpCode : int {
+  kTailBin = 0,   // half(binop(a, b, arg))
+  kTailUn = 1,    // half(unop(a, arg))
+  kTailDfl = 2,   // DFL of leaf a.idx, rows a.row .. +15, table arg
+  kTailCopy = 3,  // a
+};
+enum TailOperandKind : int { kTailSlot = 0, kTailLeafRow = 1, kTailImm = 2 };
+struct TailOperand {
+  int kind, idx, row;  // slot: idx; leaf row: leaf idx, row; immediate: float bits in idx
+};
+struct TailOp {
+  int code, dst, store_row, arg;  // dst: slot or -1; store_row: output row or -1
+  TailOperand a, b;
+};
+struct TailLeaf {
+  const __half *ptr;
+  long long img_stride, row_stride;
+};
+struct TailDfl {
+  float w[16];
+  float bias;
+  int act;
+};
+struct TailProgram {
+  int n_ops = 0, n_slots = 0, n_leaves = 0, n_dfl = 0;
+  int n_comp = 0;
+  int comp_begin[kTailMaxComp + 1];  // ops of chain c: [comp_begin[c], comp_begin[c + 1])
+  long long A = 0, out_img = 0;
+  __half *out = nullptr;
+  TailLeaf leaves[kTailMaxLeaves];
+  TailDfl dfl[kTailMaxDfl];
+  TailOp ops[kTailMaxOps];
+};
+cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t st);
+
 // permute_0213 (mode 0) -> softmax over D2 bins -> 1x1 conv D2 -> Cout, fused
 // (the YOLO DFL head).  Supported for D2 == 16 and Cout <= 8.
 bool dfl_fused_supported(int D2, int Cout);

@@ -151,16 +151,20 @@ def test_fastdiv_formula_exact():
         assert q == [int(x) // d for x in n], d
 
 
-def test_head_concats_in_place_and_dfl_fused(model_plans):
-    """The head's anchor-axis concats are written in place by their convolutions
-    and the DFL chain (permute -> softmax -> 1x1) is one step; NO_FUSION keeps
-    the plan's node-per-step form."""
+def test_head_concats_in_place_and_tail_fused(model_plans):
+    """The head's anchor-axis concats are written in place by their convolutions,
+    and everything after them (DFL softmax + projection, box / keypoint decode,
+    sigmoids, the final concats) is one fused tail step; NO_FUSION keeps the
+    plan's node-per-step form."""
     p = model_plans["yolov8n-pose"]
     fused = ivb.PlanModel(p, device=0, max_batch=2, flags=ivb.FLAG_DRY_RUN)
     plain = ivb.PlanModel(p, device=0, max_batch=2, flags=ivb.FLAG_DRY_RUN | ivb.FLAG_NO_FUSION)
     fam = [s["family"] for s in fused.steps()]
     names = [s["name"] for s in fused.steps()]
-    assert fam.count("dfl_fused") == 1 and "softmax_axis" not in fam and "permute_0213" not in fam
+    assert fam.count("decode_tail") == 1 and names[-1] == "tail:output0"
+    for f in ("softmax_axis", "permute_0213", "slice_axis", "ew_unary", "dfl_fused"):
+        assert f not in fam, f
+    assert len(plain.steps()) - len(fused.steps()) >= 20
     for cat in ("box_cat", "kpt_cat", "cls_cat"):
         assert not any(n.endswith(cat) for n in names), cat
     assert sum(n.endswith(c) for n in (s["name"] for s in plain.steps()) for c in ("box_cat", "kpt_cat", "cls_cat")) == 3
