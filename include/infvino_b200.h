@@ -63,6 +63,8 @@ typedef enum ivc_status {
                                          (reference INFVINO_NO_POOL, src/PlanModel.cpp:887) */
 #define IVC_FLAG_NO_HALO 0x20u        /* diagnostic: 3x3 stride-1 convolutions load one box per tap
                                          instead of one halo box per channel chunk */
+#define IVC_FLAG_NO_PDL 0x40u         /* diagnostic: kernels launched without programmatic dependent
+                                         launch (each waits for the previous grid to finish) */
 
 /* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
 int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);

@@ -1605,6 +1605,7 @@ void Engine::upload_input_f16(const void *src, int batch, bool on_device) {
 }
 
 void Engine::upload_input_f32(const float *src, int batch, bool on_device) {
+  pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
   const int64_t n = input_numel() * batch;
@@ -1617,6 +1618,7 @@ void Engine::upload_input_f32(const float *src, int batch, bool on_device) {
 }
 
 void Engine::capture(int batch) {
+  pdl_scope();
   cudaGraph_t g = nullptr;
   check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
   cudaError_t le = cudaSuccess;
@@ -1648,6 +1650,7 @@ void Engine::capture(int batch) {
 }
 
 void Engine::run(int batch) {
+  pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
   if (flags_ & kFlagNoGraph) {
@@ -1666,6 +1669,7 @@ void Engine::run(int batch) {
 }
 
 void Engine::run_profiled(int batch, std::vector<float> *step_ms) {
+  pdl_scope();
   check(cudaSetDevice(device_), "cudaSetDevice");
   std::vector<cudaEvent_t> ev(steps_.size() + 1);
   for (auto &e : ev) check(cudaEventCreate(&e), "cudaEventCreate");
@@ -1690,6 +1694,7 @@ void Engine::download_output_f16(int i, void *dst, int batch, bool on_device) {
 }
 
 void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
+  pdl_scope();
   const TensorRt &t = T_[(size_t)tid(output_name(i))];
   if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
   const int64_t n = t.numel * batch;
@@ -1709,6 +1714,7 @@ void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
 }
 
 bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {
+  pdl_scope();
   auto it = tid_.find(name);
   if (it == tid_.end()) return false;
   const TensorRt &t = T_[(size_t)it->second];
@@ -1738,6 +1744,7 @@ bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch)
 
 int Engine::read_tensor_f16_staged(const std::string &name, void *host_dst, int batch, void *scratch,
                                    int64_t scratch_bytes, int64_t *need_bytes) {
+  pdl_scope();
   auto it = tid_.find(name);
   if (it == tid_.end()) return 1;
   const TensorRt &t = T_[(size_t)it->second];
@@ -1764,6 +1771,7 @@ int Engine::read_tensor_f16_staged(const std::string &name, void *host_dst, int 
 }
 
 int Engine::graph_kernel_count(int batch) {
+  pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
   cudaGraph_t g = nullptr;
@@ -1782,6 +1790,8 @@ int Engine::graph_kernel_count(int batch) {
   cudaGraphDestroy(g);
   return kernels;
 }
+
+void Engine::pdl_scope() const { g_launch_pdl = (flags_ & kFlagNoPdl) == 0; }
 
 void Engine::synchronize() { check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize"); }
 

@@ -29,7 +29,8 @@ enum EngineFlags : unsigned {
   kFlagDryRun = 1u << 2,      // host-only: plan, layout, allocation; no device work
   kFlagNoTensorCores = 1u << 3,  // route convolutions to the CUDA-core direct kernel
   kFlagNoPool = 1u << 4,      // every tensor keeps its own storage (reference INFVINO_NO_POOL)
-  kFlagNoHalo = 1u << 5,      // 3x3 stride-1 convs with per-tap boxes instead of the halo tile
+  kFlagNoHalo = 1u << 5,      // 3x3 convs with per-tap boxes instead of the halo tile
+  kFlagNoPdl = 1u << 6,       // launches without programmatic dependent launch
 };
 
 struct TensorRt {
@@ -138,6 +139,7 @@ class Engine {
   std::map<int, Step> tail_steps_;   // fused planar tails, keyed by the node whose place they take
   std::vector<std::pair<int, int>> tail_uses_;  // (tensor, node) reads of fused tails, for liveness
   void plan_tails();
+  void pdl_scope() const;  // launches on this thread follow kFlagNoPdl
   std::vector<Step> steps_;
   EngineStats stats_;
 

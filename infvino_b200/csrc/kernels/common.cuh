@@ -3,6 +3,8 @@
 // load) and a bounded wait that reports a timeout instead of spinning forever.
 #pragma once
 
+#include <utility>
+
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -43,6 +45,38 @@ __device__ __forceinline__ __half epilogue(float acc, float bias, int act, int k
   const float v = __half2float(__float2half_rn(acc)) + bias;
   const float a = act_f32(__half2float(__float2half_rn(v)), act, kind);
   return __float2half_rn(a);
+}
+
+// ------------------------------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialization, so a grid can
+// start while the previous one finishes.  Each kernel therefore waits for the
+// grids before it (griddepcontrol.wait) before it touches global memory, and
+// then lets the next grid launch: its CTAs take SMs as ours retire and run
+// their own on-chip prologue in the meantime.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_and_release() {
+  pdl_wait();
+  pdl_release();
+}
+
+// Host side: whether launches on this thread carry the attribute (the engine
+// turns it off for IVC_FLAG_NO_PDL), and the launcher every kernel goes through.
+extern thread_local bool g_launch_pdl;
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_launch_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------ resolved activations

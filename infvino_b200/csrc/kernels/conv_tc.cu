@@ -280,6 +280,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     tmem_alloc(smem_u32(&tmem_base_sh), (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
+  // everything above touched only shared memory, TMEM and the parameter block;
+  // global memory (weights, activations, bias) is read after the previous grid
+  pdl_wait_and_release();
   if (warp >= 2 && n_tiles == 1 && a.bias != nullptr) {
     // bias padded to BN (a multiple of 16), 16 B per thread
     const int i = threadIdx.x - 64;
@@ -557,8 +560,7 @@ cudaError_t launch_conv_tc(const ConvTcArgs &args, int grid, cudaStream_t stream
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  conv_tc_kernel<<<grid, kConvThreads, args.smem_bytes, stream>>>(args);
-  return cudaGetLastError();
+  return launch_kernel(conv_tc_kernel, dim3(grid), dim3(kConvThreads), (size_t)args.smem_bytes, stream, args);
 }
 
 }  // namespace ivb

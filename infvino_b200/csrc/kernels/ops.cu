@@ -15,6 +15,8 @@
 
 namespace ivb {
 
+thread_local bool g_launch_pdl = true;
+
 namespace {
 
 constexpr int kThreads = 256;
@@ -76,6 +78,7 @@ __device__ __forceinline__ long long at(const View4 &v, const Idx4 &i) {
 __global__ void ew_binary_flat_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
                                  long long n, int op, int b_scalar, long long per_img, long long a_bs,
                                  long long b_bs) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long img = i / per_img, r = i - img * per_img;
     const float av = __half2float(a[img * a_bs + r]);
@@ -85,6 +88,7 @@ __global__ void ew_binary_flat_k(const __half *__restrict__ a, const __half *__r
 }
 
 __global__ void ew_binary_v4_k(View4 a, View4 b, View4 y, long long n, int op, bool cfast) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 ix = idx4(i, y, cfast);
     const float av = __half2float(a.ptr[at(a, ix)]);
@@ -95,6 +99,7 @@ __global__ void ew_binary_v4_k(View4 a, View4 b, View4 y, long long n, int op, b
 
 __global__ void ew_binary_bcast_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
                                   BcastArgs g, long long n, int op) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     long long rem = i, ai = 0, bi = 0;
     for (int r = g.rank - 1; r >= 0; --r) {
@@ -108,11 +113,13 @@ __global__ void ew_binary_bcast_k(const __half *__restrict__ a, const __half *__
 }
 
 __global__ void ew_unary_flat_k(const __half *__restrict__ x, __half *__restrict__ y, long long n, int op) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     y[i] = __float2half_rn(unop(__half2float(x[i]), op));
 }
 
 __global__ void ew_unary_v4_k(View4 x, View4 y, long long n, int op, bool cfast) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 ix = idx4(i, y, cfast);
     y.ptr[at(y, ix)] = __float2half_rn(unop(__half2float(x.ptr[at(x, ix)]), op));
@@ -120,6 +127,7 @@ __global__ void ew_unary_v4_k(View4 x, View4 y, long long n, int op, bool cfast)
 }
 
 __global__ void copy_v4_k(View4 x, View4 y, long long n, bool cfast) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 ix = idx4(i, y, cfast);
     y.ptr[at(y, ix)] = x.ptr[at(x, ix)];
@@ -129,6 +137,7 @@ __global__ void copy_v4_k(View4 x, View4 y, long long n, bool cfast) {
 // ------------------------------------------------------------------ layout ops
 __global__ void slice_axis_k(const __half *__restrict__ x, __half *__restrict__ y, long long outer, int axdim,
                              long long inner, int start, int len) {
+  pdl_wait_and_release();
   const long long n = outer * len * inner;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long o = i / ((long long)len * inner), rem = i - o * ((long long)len * inner);
@@ -143,6 +152,7 @@ struct ConcatArgs {
 };
 
 __global__ void maxpool_v4_k(View4 x, View4 y, long long n, int K, int S, int P, bool cfast) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 o = idx4(i, y, cfast);
     float m = -3.4e38f;
@@ -160,6 +170,7 @@ __global__ void maxpool_v4_k(View4 x, View4 y, long long n, int K, int S, int P,
 }
 
 __global__ void resize_nn_v4_k(View4 x, View4 y, long long n, int S, bool cfast) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 o = idx4(i, y, cfast);
     y.ptr[at(y, o)] = x.ptr[o.b * x.sb + (long long)o.c * x.sc + (long long)(o.y / S) * x.sy + (long long)(o.x / S) * x.sx];
@@ -169,6 +180,7 @@ __global__ void resize_nn_v4_k(View4 x, View4 y, long long n, int S, bool cfast)
 // serial softmax over the axis, one thread per (outer, inner) column (ops.cl:181-196)
 __global__ void softmax_axis_k(const __half *__restrict__ x, __half *__restrict__ y, long long outer, int axdim,
                                long long inner) {
+  pdl_wait_and_release();
   const long long n = outer * inner;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long o = i / inner, r = i - o * inner;
@@ -185,6 +197,7 @@ __global__ void softmax_axis_k(const __half *__restrict__ x, __half *__restrict_
 
 __global__ void permute_0213_k(const __half *__restrict__ x, __half *__restrict__ y, long long n, int D1, int D2,
                                long long I, int mode) {
+  pdl_wait_and_release();
   const long long per = (long long)D1 * D2 * I;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long img = i / per, j = i - img * per;
@@ -197,6 +210,7 @@ __global__ void permute_0213_k(const __half *__restrict__ x, __half *__restrict_
 
 // global average pool: grid (batch, ceil(C/32)); 32 channels x 8 pixel lanes
 __global__ void gap_v4_k(View4 x, __half *__restrict__ y) {
+  pdl_wait_and_release();
   __shared__ float part[8][33];
   const int cl = threadIdx.x & 31, pl = threadIdx.x >> 5;
   const long long b = blockIdx.x;
@@ -220,6 +234,7 @@ __global__ void gap_v4_k(View4 x, __half *__restrict__ y) {
 
 __global__ void bmm_k(const __half *__restrict__ A, const __half *__restrict__ B, __half *__restrict__ Y, long long n,
                       int B1, int M, int K, int N, long long a_bs, long long b_bs) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int nn = (int)(i % N);
     long long t = i / N;
@@ -237,6 +252,7 @@ __global__ void bmm_k(const __half *__restrict__ A, const __half *__restrict__ B
 
 __global__ void bias_add_k(const __half *__restrict__ x, const __half *__restrict__ b, __half *__restrict__ y,
                            long long n, long long per_img, int HW) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i % per_img;
     y[i] = __float2half_rn(__half2float(x[i]) + __half2float(b[r / HW]));
@@ -248,6 +264,7 @@ __global__ void bias_add_k(const __half *__restrict__ x, const __half *__restric
 // then half(half(acc) + bias) -> act (depthwise_f16 expressions).
 __global__ void depthwise_v4_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias, View4 y,
                                long long n, int K, int S, int P, int act, bool cfast) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 o = idx4(i, y, cfast);
     float acc = 0.0f;
@@ -269,6 +286,7 @@ __global__ void depthwise_v4_k(View4 x, const __half *__restrict__ w, const __ha
 // NHWC fast path: 8 channels per thread with 16-byte loads/stores.
 __global__ void depthwise_nhwc8_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias, View4 y,
                                   long long n8, int K, int S, int P, int act) {
+  pdl_wait_and_release();
   const int C8 = y.C / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const int c8 = (int)(i % C8);
@@ -307,6 +325,7 @@ __global__ void depthwise_nhwc8_k(View4 x, const __half *__restrict__ w, const _
 __global__ void conv_direct_v4_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias,
                                  const __half *res_ptr, View4 res, View4 y, long long n, int K, int S, int P, int G,
                                  int act, int epi, bool cfast) {
+  pdl_wait_and_release();
   const int cin_g = x.C / G, cout_g = y.C / G;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const Idx4 o = idx4(i, y, cfast);
@@ -344,6 +363,7 @@ __global__ void conv_direct_v4_k(View4 x, const __half *__restrict__ w, const __
 constexpr int kStemMaxCout = 64;
 __global__ void stem3x3_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias, View4 y,
                           long long npix, int Cout, int S, int P, int act) {
+  pdl_wait_and_release();
   __shared__ float ws[kStemMaxCout * 36];
   __shared__ float bs[kStemMaxCout];
   const int cin = x.C, kk = cin * 9;
@@ -400,6 +420,7 @@ struct StemWeights {
 template <int CIN, int COUT, int FN>
 __global__ void __launch_bounds__(128) stem3x3_t(View4 x, const __grid_constant__ StemWeights<CIN, COUT> p,
                                                  View4 y, long long npix, int S, int P, int vec_out) {
+  pdl_wait_and_release();
   constexpr int KK = CIN * 9;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix; i += (long long)gridDim.x * blockDim.x) {
     const int ox = (int)(i % y.W);
@@ -453,9 +474,9 @@ cudaError_t launch_stem_t(View4 x, const float *blob, View4 y, long long npix, i
   std::memcpy(&p, blob, sizeof(p));
   const dim3 g(grid_for(npix, 128)), b(128);
   switch (resolve_act(act, kActConv3x3)) {
-    case kFnSilu: stem3x3_t<CIN, COUT, kFnSilu><<<g, b, 0, st>>>(x, p, y, npix, S, P, vec_out); break;
-    case kFnHswishA: stem3x3_t<CIN, COUT, kFnHswishA><<<g, b, 0, st>>>(x, p, y, npix, S, P, vec_out); break;
-    default: stem3x3_t<CIN, COUT, kFnNone><<<g, b, 0, st>>>(x, p, y, npix, S, P, vec_out); break;
+    case kFnSilu: launch_kernel(stem3x3_t<CIN, COUT, kFnSilu>, dim3(g), dim3(b), 0, st, x, p, y, npix, S, P, vec_out); break;
+    case kFnHswishA: launch_kernel(stem3x3_t<CIN, COUT, kFnHswishA>, dim3(g), dim3(b), 0, st, x, p, y, npix, S, P, vec_out); break;
+    default: launch_kernel(stem3x3_t<CIN, COUT, kFnNone>, dim3(g), dim3(b), 0, st, x, p, y, npix, S, P, vec_out); break;
   }
   return cudaGetLastError();
 }
@@ -464,6 +485,7 @@ cudaError_t launch_stem_t(View4 x, const float *blob, View4 y, long long npix, i
 // include/infvino/Half.hpp:14-24: truncate the mantissa, flush exp <= 0 to +-0,
 // exp >= 31 to +-inf.
 __global__ void f32_to_f16_trunc_k(const float *__restrict__ x, __half *__restrict__ y, long long n) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const uint32_t u = __float_as_uint(x[i]);
     const uint32_t sign = (u >> 16) & 0x8000u;
@@ -478,6 +500,7 @@ __global__ void f32_to_f16_trunc_k(const float *__restrict__ x, __half *__restri
 }
 
 __global__ void f16_to_f32_k(const __half *__restrict__ x, float *__restrict__ y, long long n) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     y[i] = __half2float(x[i]);
 }
@@ -509,6 +532,7 @@ __device__ __forceinline__ long long at8(const View4 &v, int b, int y, int x, in
 }
 
 __global__ void copy_nhwc8_k(View4 x, View4 y, long long n8) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const Pix p = pix8((unsigned long long)i, y);
     *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) =
@@ -517,6 +541,7 @@ __global__ void copy_nhwc8_k(View4 x, View4 y, long long n8) {
 }
 
 __global__ void resize_nhwc8_k(View4 x, View4 y, long long n8, int S) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const Pix p = pix8((unsigned long long)i, y);
     *reinterpret_cast<uint4 *>(y.ptr + at8(y, p.b, p.y, p.x, p.c)) =
@@ -525,6 +550,7 @@ __global__ void resize_nhwc8_k(View4 x, View4 y, long long n8, int S) {
 }
 
 __global__ void maxpool_nhwc8_k(View4 x, View4 y, long long n8, int K, int S, int P) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const Pix p = pix8((unsigned long long)i, y);
     float m[8];
@@ -551,6 +577,7 @@ __global__ void maxpool_nhwc8_k(View4 x, View4 y, long long n8, int K, int S, in
 
 // binary op; `b` may broadcast over pixels (bpix = 0: per-image channel vector)
 __global__ void ew_binary_nhwc8_k(View4 a, View4 b, View4 y, long long n8, int op, int bpix, int bscalar) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const Pix p = pix8((unsigned long long)i, y);
     const uint4 av = *reinterpret_cast<const uint4 *>(a.ptr + at8(a, p.b, p.y, p.x, p.c));
@@ -571,6 +598,7 @@ __global__ void ew_binary_nhwc8_k(View4 a, View4 b, View4 y, long long n8, int o
 }
 
 __global__ void ew_unary_nhwc8_k(View4 x, View4 y, long long n8, int op) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const Pix p = pix8((unsigned long long)i, y);
     const uint4 v = *reinterpret_cast<const uint4 *>(x.ptr + at8(x, p.b, p.y, p.x, p.c));
@@ -587,6 +615,7 @@ __global__ void ew_unary_nhwc8_k(View4 x, View4 y, long long n8, int op) {
 // when the run and both ends are 16-byte aligned.
 __global__ void concat_rows_k(ConcatArgs g, __half *__restrict__ y, long long outer, long long per_img_outer,
                               long long inner) {
+  pdl_wait_and_release();
   const long long rows = outer * g.nsrc;
   for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
     const int s = (int)(r % g.nsrc);
@@ -614,6 +643,7 @@ __host__ __device__ __forceinline__ bool al16(const void *p) { return (reinterpr
 // slice_axis as rows: `outer` rows of len*inner contiguous elements
 __global__ void slice_rows8_k(const __half *__restrict__ x, __half *__restrict__ y, long long outer, int axdim,
                               long long inner, int start, int len) {
+  pdl_wait_and_release();
   const long long row = (long long)len * inner / 8;  // vectors per row
   const long long n = outer * row;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -626,6 +656,7 @@ __global__ void slice_rows8_k(const __half *__restrict__ x, __half *__restrict__
 // permute_0213 mode 0 moves whole I-rows: [D1][D2][I] -> [D2][D1][I]
 __global__ void permute0_rows8_k(const __half *__restrict__ x, __half *__restrict__ y, long long n8, int D1, int D2,
                                  long long I) {
+  pdl_wait_and_release();
   const long long I8 = I / 8;
   const long long per = (long long)D1 * D2 * I;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -644,6 +675,7 @@ __global__ void permute0_rows8_k(const __half *__restrict__ x, __half *__restric
 // or broadcast (stride 0) for both operands and a multiple of 8
 __global__ void ew_bcast_rows8_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
                                  BcastArgs g, long long n8, int op) {
+  pdl_wait_and_release();
   const int r = g.rank - 1;
   const long long last8 = g.dims[r] / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -682,6 +714,7 @@ constexpr int kPlanarMaxCin = 64;
 __global__ void conv1x1_planar_k(const __half *__restrict__ x, const __half *__restrict__ w,
                                  const __half *__restrict__ bias, __half *__restrict__ y, long long npix, long long N,
                                  int Cin, int Cout, int act) {
+  pdl_wait_and_release();
   __shared__ float ws[kPlanarMaxCout * kPlanarMaxCin];
   for (int i = threadIdx.x; i < Cin * Cout; i += blockDim.x) ws[i] = __half2float(w[i]);
   __syncthreads();
@@ -706,6 +739,7 @@ template <int D2>
 __global__ void dfl_fused_k(const __half *__restrict__ x, const __half *__restrict__ w,
                             const __half *__restrict__ bias, __half *__restrict__ y, long long n, int D1, long long I,
                             int Cout, int act) {
+  pdl_wait_and_release();
   __shared__ float ws[kPlanarMaxCout * D2];
   for (int i = threadIdx.x; i < Cout * D2; i += blockDim.x) ws[i] = __half2float(w[i]);
   __syncthreads();
@@ -769,6 +803,7 @@ __device__ __forceinline__ void tail_fetch(const TailProgram &P, const TailOpera
 
 template <int V>
 __global__ void __launch_bounds__(128) tail_vm_k(const __grid_constant__ TailProgram P, long long n) {
+  pdl_wait_and_release();
   extern __shared__ float tail_slots[];
   float *my = tail_slots + threadIdx.x * V;  // slot s at my[s * blockDim.x * V + j]
   const long long AV = P.A / V;
@@ -847,7 +882,7 @@ inline long long numel4(const View4 &v, int batch) { return (long long)batch * v
 cudaError_t launch_ew_binary_flat(const __half *a, const __half *b, __half *y, long long n, int op, int b_scalar,
                                   long long per_img, int batch, long long a_bs, long long b_bs, cudaStream_t st) {
   (void)batch;
-  ew_binary_flat_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, n, op, b_scalar, per_img, a_bs, b_bs);
+  launch_kernel(ew_binary_flat_k, dim3(grid_for(n)), dim3(kThreads), 0, st, a, b, y, n, op, b_scalar, per_img, a_bs, b_bs);
   return cudaGetLastError();
 }
 cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cudaStream_t st) {
@@ -857,12 +892,12 @@ cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cu
     if ((bpix && vec8_ok(b)) || (!bpix && !bscalar && (b.sb % 8) == 0 && (reinterpret_cast<uintptr_t>(b.ptr) & 15) == 0) ||
         bscalar) {
       const long long n8 = numel4(y, batch) / 8;
-      ew_binary_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(a, b, y, n8, op, bpix ? 1 : 0, bscalar ? 1 : 0);
+      launch_kernel(ew_binary_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, a, b, y, n8, op, bpix ? 1 : 0, bscalar ? 1 : 0);
       return cudaGetLastError();
     }
   }
   const long long n = numel4(y, batch);
-  ew_binary_v4_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, n, op, cfast_of(y));
+  launch_kernel(ew_binary_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, a, b, y, n, op, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_ew_binary_bcast(const __half *a, const __half *b, __half *y, const BcastArgs &g, int op,
@@ -876,35 +911,35 @@ cudaError_t launch_ew_binary_bcast(const __half *a, const __half *b, __half *y, 
     for (int d = 0; d < r && rows; ++d)
       rows = (g.as[r] == 0 || g.as[d] % 8 == 0) && (g.bs[r] == 0 || g.bs[d] % 8 == 0);
     if (rows) {
-      ew_bcast_rows8_k<<<grid_for(n / 8), kThreads, 0, st>>>(a, b, y, g, n / 8, op);
+      launch_kernel(ew_bcast_rows8_k, dim3(grid_for(n / 8)), dim3(kThreads), 0, st, a, b, y, g, n / 8, op);
       return cudaGetLastError();
     }
   }
-  ew_binary_bcast_k<<<grid_for(n), kThreads, 0, st>>>(a, b, y, g, n, op);
+  launch_kernel(ew_binary_bcast_k, dim3(grid_for(n)), dim3(kThreads), 0, st, a, b, y, g, n, op);
   return cudaGetLastError();
 }
 cudaError_t launch_ew_unary_flat(const __half *x, __half *y, long long n, int op, cudaStream_t st) {
-  ew_unary_flat_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, op);
+  launch_kernel(ew_unary_flat_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, op);
   return cudaGetLastError();
 }
 cudaError_t launch_ew_unary_v4(View4 x, View4 y, int batch, int op, cudaStream_t st) {
   if (vec8_ok(x) && vec8_ok(y)) {
     const long long n8 = numel4(y, batch) / 8;
-    ew_unary_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, op);
+    launch_kernel(ew_unary_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, n8, op);
     return cudaGetLastError();
   }
   const long long n = numel4(y, batch);
-  ew_unary_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, op, cfast_of(y));
+  launch_kernel(ew_unary_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, op, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_copy_v4(View4 x, View4 y, int batch, cudaStream_t st) {
   if (vec8_ok(x) && vec8_ok(y)) {
     const long long n8 = numel4(y, batch) / 8;
-    copy_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8);
+    launch_kernel(copy_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, n8);
     return cudaGetLastError();
   }
   const long long n = numel4(y, batch);
-  copy_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, cfast_of(y));
+  launch_kernel(copy_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_slice_axis(const __half *x, __half *y, long long outer, int axdim, long long inner, int start,
@@ -912,10 +947,10 @@ cudaError_t launch_slice_axis(const __half *x, __half *y, long long outer, int a
   if (((long long)len * inner) % 8 == 0 && ((long long)axdim * inner) % 8 == 0 && ((long long)start * inner) % 8 == 0 &&
       al16(x) && al16(y)) {
     const long long n8 = outer * len * inner / 8;
-    slice_rows8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, outer, axdim, inner, start, len);
+    launch_kernel(slice_rows8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, outer, axdim, inner, start, len);
     return cudaGetLastError();
   }
-  slice_axis_k<<<grid_for(outer * len * inner), kThreads, 0, st>>>(x, y, outer, axdim, inner, start, len);
+  launch_kernel(slice_axis_k, dim3(grid_for(outer * len * inner)), dim3(kThreads), 0, st, x, y, outer, axdim, inner, start, len);
   return cudaGetLastError();
 }
 cudaError_t launch_concat_planar(const ConcatSrc *src, int nsrc, __half *y, long long outer, long long per_img_outer,
@@ -934,60 +969,60 @@ cudaError_t launch_concat_planar(const ConcatSrc *src, int nsrc, __half *y, long
   const long long rows = outer * g.nsrc;
   dim3 grid((unsigned)std::max<long long>(1, std::min<long long>((maxlen / 8 + kThreads - 1) / kThreads, 64)),
             (unsigned)std::min<long long>(rows, 65535));
-  concat_rows_k<<<grid, kThreads, 0, st>>>(g, y, outer, per_img_outer, inner);
+  launch_kernel(concat_rows_k, dim3(grid), dim3(kThreads), 0, st, g, y, outer, per_img_outer, inner);
   return cudaGetLastError();
 }
 cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, cudaStream_t st) {
   if (vec8_ok(x) && vec8_ok(y)) {
     const long long n8 = numel4(y, batch) / 8;
-    maxpool_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, K, S, P);
+    launch_kernel(maxpool_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, n8, K, S, P);
     return cudaGetLastError();
   }
   const long long n = numel4(y, batch);
-  maxpool_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, K, S, P, cfast_of(y));
+  launch_kernel(maxpool_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, K, S, P, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t st) {
   if (vec8_ok(x) && vec8_ok(y)) {
     const long long n8 = numel4(y, batch) / 8;
-    resize_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, S);
+    launch_kernel(resize_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, n8, S);
     return cudaGetLastError();
   }
   const long long n = numel4(y, batch);
-  resize_nn_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, S, cfast_of(y));
+  launch_kernel(resize_nn_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, S, cfast_of(y));
   return cudaGetLastError();
 }
 cudaError_t launch_softmax_axis(const __half *x, __half *y, long long outer, int axdim, long long inner,
                                 cudaStream_t st) {
-  softmax_axis_k<<<grid_for(outer * inner), kThreads, 0, st>>>(x, y, outer, axdim, inner);
+  launch_kernel(softmax_axis_k, dim3(grid_for(outer * inner)), dim3(kThreads), 0, st, x, y, outer, axdim, inner);
   return cudaGetLastError();
 }
 cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, int D2, long long I, int mode,
                                 cudaStream_t st) {
   if (mode == 0 && I % 8 == 0 && al16(x) && al16(y)) {
     const long long n8 = (long long)batch * D1 * D2 * I / 8;
-    permute0_rows8_k<<<grid_for(n8), kThreads, 0, st>>>(x, y, n8, D1, D2, I);
+    launch_kernel(permute0_rows8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, n8, D1, D2, I);
     return cudaGetLastError();
   }
   const long long n = (long long)batch * D1 * D2 * I;
-  permute_0213_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n, D1, D2, I, mode);
+  launch_kernel(permute_0213_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, D1, D2, I, mode);
   return cudaGetLastError();
 }
 cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st) {
   dim3 grid(batch, (x.C + 31) / 32);
-  gap_v4_k<<<grid, 256, 0, st>>>(x, y);
+  launch_kernel(gap_v4_k, dim3(grid), dim3(256), 0, st, x, y);
   return cudaGetLastError();
 }
 cudaError_t launch_bmm(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
                        long long a_bs, long long b_bs, cudaStream_t st) {
   const long long n = (long long)batch * B1 * M * N;
-  bmm_k<<<grid_for(n), kThreads, 0, st>>>(A, B, Y, n, B1, M, K, N, a_bs, b_bs);
+  launch_kernel(bmm_k, dim3(grid_for(n)), dim3(kThreads), 0, st, A, B, Y, n, B1, M, K, N, a_bs, b_bs);
   return cudaGetLastError();
 }
 cudaError_t launch_bias_add(const __half *x, const __half *b, __half *y, long long per_img, int HW, int batch,
                             cudaStream_t st) {
   const long long n = per_img * batch;
-  bias_add_k<<<grid_for(n), kThreads, 0, st>>>(x, b, y, n, per_img, HW);
+  launch_kernel(bias_add_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, b, y, n, per_img, HW);
   return cudaGetLastError();
 }
 cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, View4 y, int batch, int K, int S, int P,
@@ -998,10 +1033,10 @@ cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, Vi
                    (reinterpret_cast<uintptr_t>(w) & 15) == 0;
   if (vec) {
     const long long n8 = numel4(y, batch) / 8;
-    depthwise_nhwc8_k<<<grid_for(n8), kThreads, 0, st>>>(x, w, bias, y, n8, K, S, P, act);
+    launch_kernel(depthwise_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, w, bias, y, n8, K, S, P, act);
   } else {
     const long long n = numel4(y, batch);
-    depthwise_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, w, bias, y, n, K, S, P, act, cfast_of(y));
+    launch_kernel(depthwise_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, w, bias, y, n, K, S, P, act, cfast_of(y));
   }
   return cudaGetLastError();
 }
@@ -1010,7 +1045,7 @@ cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, 
                                   cudaStream_t st) {
   (void)Cout;
   const long long n = numel4(y, batch);
-  conv_direct_v4_k<<<grid_for(n), kThreads, 0, st>>>(x, w, bias, res_ptr, res, y, n, K, S, P, G, act, epi,
+  launch_kernel(conv_direct_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, w, bias, res_ptr, res, y, n, K, S, P, G, act, epi,
                                                      cfast_of(y));
   return cudaGetLastError();
 }
@@ -1038,14 +1073,14 @@ cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, cons
   const int vec_out = (y.sc == 1 && y.sx % 8 == 0 && y.sy % 8 == 0 && y.sb % 8 == 0 &&
                        (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0) ? 1 : 0;
   if (x.C == 3 && Cout == 16 && blob) return launch_stem_t<3, 16>(x, blob, y, npix, S, P, act, vec_out, st);
-  stem3x3_k<<<grid_for(npix, 128), 128, 0, st>>>(x, w, bias, y, npix, Cout, S, P, act);
+  launch_kernel(stem3x3_k, dim3(grid_for(npix, 128)), dim3(128), 0, st, x, w, bias, y, npix, Cout, S, P, act);
   return cudaGetLastError();
 }
 cudaError_t launch_conv1x1_planar(const __half *x, const __half *w, const __half *bias, __half *y, int batch,
                                   long long N, int Cin, int Cout, int act, cudaStream_t st) {
   if (Cin > kPlanarMaxCin || Cout > kPlanarMaxCout) return cudaErrorInvalidValue;
   const long long npix = (long long)batch * N;
-  conv1x1_planar_k<<<grid_for(npix), kThreads, 0, st>>>(x, w, bias, y, npix, N, Cin, Cout, act);
+  launch_kernel(conv1x1_planar_k, dim3(grid_for(npix)), dim3(kThreads), 0, st, x, w, bias, y, npix, N, Cin, Cout, act);
   return cudaGetLastError();
 }
 
@@ -1068,9 +1103,9 @@ cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t
       cudaFuncSetAttribute(tail_vm_k<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
       attr = true;
     }
-    tail_vm_k<4><<<dim3(grid_for(n, threads), prog.n_comp), threads, smem, st>>>(prog, n);
+    launch_kernel(tail_vm_k<4>, dim3(dim3(grid_for(n, threads), prog.n_comp)), dim3(threads), smem, st, prog, n);
   } else {
-    tail_vm_k<1><<<dim3(grid_for(n, threads), prog.n_comp), threads, smem, st>>>(prog, n);
+    launch_kernel(tail_vm_k<1>, dim3(dim3(grid_for(n, threads), prog.n_comp)), dim3(threads), smem, st, prog, n);
   }
   return cudaGetLastError();
 }
@@ -1081,16 +1116,16 @@ cudaError_t launch_dfl_fused(const __half *x, const __half *w, const __half *bia
                              long long I, int Cout, int act, cudaStream_t st) {
   if (!dfl_fused_supported(D2, Cout)) return cudaErrorInvalidValue;
   const long long n = (long long)batch * D1 * I;
-  dfl_fused_k<16><<<grid_for(n), kThreads, 0, st>>>(x, w, bias, y, n, D1, I, Cout, act);
+  launch_kernel(dfl_fused_k<16>, dim3(grid_for(n)), dim3(kThreads), 0, st, x, w, bias, y, n, D1, I, Cout, act);
   return cudaGetLastError();
 }
 
 cudaError_t launch_f32_to_f16_trunc(const float *x, __half *y, long long n, cudaStream_t st) {
-  f32_to_f16_trunc_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n);
+  launch_kernel(f32_to_f16_trunc_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n);
   return cudaGetLastError();
 }
 cudaError_t launch_f16_to_f32(const __half *x, float *y, long long n, cudaStream_t st) {
-  f16_to_f32_k<<<grid_for(n), kThreads, 0, st>>>(x, y, n);
+  launch_kernel(f16_to_f32_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n);
   return cudaGetLastError();
 }
 
