@@ -197,10 +197,7 @@ int ivc_infer_f32(ivc_model *m, const float *input, size_t numel, int batch, flo
     for (int i = 0; i < m->eng->output_count(); ++i)
       if (!outputs[i]) return fail(m, IVC_ERR_ARGUMENT, "ivc_infer_f32: null output buffer");
     const auto t0 = std::chrono::steady_clock::now();
-    m->eng->upload_input_f32(input, batch, false);
-    m->eng->run(batch);
-    for (int i = 0; i < m->eng->output_count(); ++i) m->eng->download_output_f32(i, outputs[i], batch, false);
-    m->eng->synchronize();
+    m->eng->infer_f32_host(input, batch, outputs);
     m->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     return status_check(m);
   });

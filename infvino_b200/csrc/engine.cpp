@@ -85,6 +85,10 @@ Engine::~Engine() {
   if (arena_) cudaFree(arena_);
   if (status_) cudaFree(status_);
   if (in_f32_) cudaFree(in_f32_);
+  if (out_f32_) cudaFree(out_f32_);
+  for (cudaEvent_t e : chunk_events_) cudaEventDestroy(e);
+  if (copy_in_) cudaStreamDestroy(copy_in_);
+  if (copy_out_) cudaStreamDestroy(copy_out_);
   if (scratch_) cudaFree(scratch_);
   if (own_stream_ && stream_) cudaStreamDestroy(stream_);
 }
@@ -1711,6 +1715,69 @@ void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
   float *tmp = reinterpret_cast<float *>(scratch_);
   check(launch_f16_to_f32(t.dptr, tmp, n, stream_), "output conversion");
   check(cudaMemcpyAsync(dst, tmp, (size_t)n * 4, cudaMemcpyDeviceToHost, stream_), "output copy");
+}
+
+void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
+  pdl_scope();
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  constexpr int kChunk = 16;
+  if (batch < 2 * kChunk) {  // too small to overlap: one pass
+    upload_input_f32(src, batch, false);
+    run(batch);
+    for (int i = 0; i < output_count(); ++i) download_output_f32(i, outs[i], batch, false);
+    synchronize();
+    return;
+  }
+  const int n_out = output_count();
+  std::vector<int64_t> out_numel(n_out), out_off(n_out + 1, 0);
+  for (int i = 0; i < n_out; ++i) {
+    out_numel[i] = T_[(size_t)tid(output_name(i))].numel;
+    if (!T_[(size_t)tid(output_name(i))].dense) throw std::runtime_error("CudaPlanModel: output is not planar");
+    out_off[i + 1] = out_off[i] + out_numel[i] * max_batch_;
+  }
+  if (!out_f32_) {
+    check(cudaMalloc(&out_f32_, (size_t)out_off[n_out] * sizeof(float)), "cudaMalloc(output f32 staging)");
+    check(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking), "cudaStreamCreate");
+  }
+  const int n_chunks = (batch + kChunk - 1) / kChunk;
+  while ((int)chunk_events_.size() < 3 * n_chunks + 1) {  // per chunk: copied in, computed; one spare
+    cudaEvent_t e;
+    check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    chunk_events_.push_back(e);
+  }
+  const int64_t in_numel = input_numel();
+  // the copy streams start after whatever the compute stream already holds
+  check(cudaEventRecord(chunk_events_[3 * n_chunks], stream_), "cudaEventRecord");
+  check(cudaStreamWaitEvent(copy_in_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
+  for (int c = 0; c < n_chunks; ++c) {
+    const int b0 = c * kChunk, nb = std::min(kChunk, batch - b0);
+    check(cudaMemcpyAsync(in_f32_ + b0 * in_numel, src + b0 * in_numel, (size_t)(nb * in_numel) * sizeof(float),
+                          cudaMemcpyHostToDevice, copy_in_),
+          "input copy");
+    check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
+  }
+  for (int c = 0; c < n_chunks; ++c) {
+    const int b0 = c * kChunk, nb = std::min(kChunk, batch - b0);
+    check(cudaStreamWaitEvent(stream_, chunk_events_[3 * c], 0), "cudaStreamWaitEvent");
+    check(launch_f32_to_f16_trunc(in_f32_ + b0 * in_numel, input_device_ptr(), nb * in_numel, stream_),
+          "input conversion");
+    run(nb);  // images 0 .. nb-1 of the arena
+    for (int i = 0; i < n_out; ++i)
+      check(launch_f16_to_f32(T_[(size_t)tid(output_name(i))].dptr, out_f32_ + out_off[i] + b0 * out_numel[i],
+                              nb * out_numel[i], stream_),
+            "output conversion");
+    check(cudaEventRecord(chunk_events_[3 * c + 1], stream_), "cudaEventRecord");
+    check(cudaStreamWaitEvent(copy_out_, chunk_events_[3 * c + 1], 0), "cudaStreamWaitEvent");
+    for (int i = 0; i < n_out; ++i)
+      check(cudaMemcpyAsync(outs[i] + b0 * out_numel[i], out_f32_ + out_off[i] + b0 * out_numel[i],
+                            (size_t)(nb * out_numel[i]) * sizeof(float), cudaMemcpyDeviceToHost, copy_out_),
+            "output copy");
+  }
+  check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
+  check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
+  synchronize();
 }
 
 bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {

@@ -101,6 +101,10 @@ class Engine {
   void run_profiled(int batch, std::vector<float> *step_ms);  // eager, events around each step
   void download_output_f16(int i, void *dst, int batch, bool dst_on_device);
   void download_output_f32(int i, float *dst, int batch, bool dst_on_device);
+  // ClBackend::infer for host buffers: chunks of the batch are copied in,
+  // converted, run and copied out on separate streams so that the host copies
+  // of one chunk overlap the network on another (same results as one batch).
+  void infer_f32_host(const float *src, int batch, float *const *outs);
   // Plan-order (NCHW) copy of any tensor for `batch` images into host memory.
   bool read_tensor_f16(const std::string &name, void *host_dst, int batch);
   // read_tensor_f16 staged through caller-provided device scratch (allocates
@@ -150,6 +154,9 @@ class Engine {
   std::vector<void *> dev_allocs_;  // weights and packed weights
   int *status_ = nullptr;           // device status word
   float *in_f32_ = nullptr;         // device staging for f32 input
+  float *out_f32_ = nullptr;        // device staging for f32 outputs (pipelined infer)
+  cudaStream_t copy_in_ = nullptr, copy_out_ = nullptr;
+  std::vector<cudaEvent_t> chunk_events_;
   __half *scratch_ = nullptr;       // read_tensor staging
   int64_t scratch_elems_ = 0;
   std::map<int, cudaGraphExec_t> graphs_;

@@ -279,3 +279,21 @@ def test_graph_and_eager_agree(model_plans):
     b = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_GRAPH).infer_f32(x, 2)[0]
     c = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_FUSION).infer_f32(x, 2)[0]
     assert np.array_equal(a, b) and np.array_equal(a, c)
+
+
+def test_infer_f32_chunked_equals_device_path(model_plans):
+    """ClBackend::infer on host buffers pipelines chunks of 16 images (copies
+    overlapping the network); the outputs equal one device-resident pass over
+    the whole batch, image for image."""
+    p = model_plans["yolov8n-pose"]
+    m = ivb.PlanModel(p, max_batch=40)
+    n = m.inputNumel()
+    x = np.random.default_rng(23).random(40 * n, dtype=np.float32)
+    y_host = m.infer_f32(x, 40)[0]
+    import torch
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(40 * m.outputNumel(0), dtype=torch.float32, device="cuda")
+    m.infer_f32_device(xd.data_ptr(), 40, [yd.data_ptr()])
+    m.synchronize()
+    assert np.array_equal(y_host, yd.cpu().numpy())
+    m.close()
