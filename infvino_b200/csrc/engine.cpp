@@ -1044,9 +1044,9 @@ void Engine::lower() {
           if (!stem_params(xv0.C, cout, p.ref(T_[(size_t)w].name).host.data(),
                            bias >= 0 ? p.ref(T_[(size_t)bias].name).host.data() : nullptr, blob.get()))
             blob.reset();
-          st.launch = [this, x, out, wptr, bptr, blob, cout, S, P, act](int B, cudaStream_t s) {
+          st.launch = [this, x, out, wptr, bptr, blob, cout, S, P, act, status](int B, cudaStream_t s) {
             return launch_stem3x3_v4(view(x), wptr, bptr, blob ? blob->data() : nullptr, view(out), B, cout, S, P,
-                                     act, s);
+                                     act, status, s);
           };
         } else if (c.ksize == 1 && res < 0 && T_[(size_t)x].dense && T_[(size_t)out].dense && c.cout <= 8 &&
                    c.cin_total <= 64) {

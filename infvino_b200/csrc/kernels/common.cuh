@@ -204,6 +204,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
+// Bounded wait without a suspend hint: a short poll for waits expected to end
+// within microseconds (one waiter per CTA; the others wait at a barrier).
+__device__ __forceinline__ bool mbar_wait_poll(uint32_t bar, uint32_t parity, long long limit_cycles) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > limit_cycles) return false;
+  return true;
+}
+
 // Error codes a kernel writes to its status word (first error wins).
 enum KernelStatus : int {
   kStatusOk = 0,

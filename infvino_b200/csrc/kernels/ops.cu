@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "ops.cuh"
+#include "../tma.h"
 
 namespace ivb {
 
@@ -407,78 +408,232 @@ __global__ void stem3x3_k(View4 x, const __half *__restrict__ w, const __half *_
   }
 }
 
-// Compile-time specialised stem (CIN, COUT and the activation known): weights
-// and bias travel in the kernel parameters (constant bank, read directly by the
-// FMAs), the 9*CIN input taps and COUT accumulators live in registers;
-// accumulation order per output channel is (ci, ky, kx) as in the reference.
-template <int CIN, int COUT>
-struct StemWeights {
-  float w[CIN * 9][COUT];  // [tap][channel]
-  uint4 b8[COUT / 8];      // fp16 bias, 8 channels per uint4
+// Stem 3x3 (Cin 3 -> Cout 16) on the tensor cores.  K = the 27 taps of one
+// output pixel in the reference's (ci, ky, kx) order, zero-padded to 32, forms
+// an A row.  Per 8 x 16-pixel tile the CTA stages the planar input patch in
+// shared memory, each thread builds its pixel's row in two 32-byte-row
+// swizzled K16 slices (the layout TMA writes for the conv kernel: 16-byte chunk
+// c of row r at c ^ ((r >> 2) & 1)), one thread issues two MMAs into a
+// 16-column TMEM accumulator (fp32), and four warps run the conv epilogue.
+struct StemTcParams {
+  uint16_t w[16][32];  // [cout][k], k = ci * 9 + ky * 3 + kx, zero beyond 27
+  uint4 b8[2];         // fp16 bias
 };
+constexpr int kStemTW = 16, kStemTH = 8;
+constexpr int kStemPR = (kStemTH - 1) * 2 + 3, kStemPC = (kStemTW - 1) * 2 + 3;  // patch for stride <= 2
 
-template <int CIN, int COUT, int FN>
-__global__ void __launch_bounds__(128) stem3x3_t(View4 x, const __grid_constant__ StemWeights<CIN, COUT> p,
-                                                 View4 y, long long npix, int S, int P, int vec_out) {
+constexpr int kStemTmaW = 40;  // TMA patch row: 8-aligned start, covers the 33-pixel window
+
+template <int FN, int S, bool TMA>
+__global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant__ StemTcParams p,
+                                                 const __grid_constant__ CUtensorMap pmap, View4 y, int P,
+                                                 int tiles_x, int tiles_per_img, long long n_tiles, int vec_out,
+                                                 int *status) {
+  // TMA: the planar patch of the next tile is fetched into the other buffer
+  // while this tile computes (box {40, rows, 3, 1}, x start rounded down to 8)
+  // each buffer starts on a 128-byte boundary (TMA destination alignment)
+  constexpr int kBufHalves = ((3 * kStemPR * kStemTmaW + 63) / 64) * 64;
+  __shared__ __align__(128) __half patch_t[TMA ? 2 : 1][kBufHalves];
+  __shared__ __align__(8) uint64_t pbar[2];
+  __shared__ __align__(1024) uint8_t a_sm[2][128 * 32];
+  __shared__ __align__(1024) uint8_t b_sm[2][16 * 32];
+  __shared__ __half patch[3][kStemPR][kStemPC + 1];
+  __shared__ __align__(8) uint64_t mma_bar;
+  __shared__ uint32_t tmem_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    mbar_init(smem_u32(&mma_bar), 1);
+    mbar_init(smem_u32(&pbar[0]), 1);
+    mbar_init(smem_u32(&pbar[1]), 1);
+    fence_mbar_init();
+    if (TMA) tma_prefetch_desc(&pmap);
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_sh), 32);  // before the release: a following conv grid never starves us
+    tmem_relinquish();
+  }
+  for (int i = tid; i < 2 * 16 * 2; i += blockDim.x) {  // weights: slice, row, 16-byte chunk
+    const int sl = i >> 5, n = (i >> 1) & 15, c = i & 1;
+    const uint4 v = *reinterpret_cast<const uint4 *>(&p.w[n][sl * 16 + c * 8]);
+    *reinterpret_cast<uint4 *>(&b_sm[sl][n * 32 + ((c ^ ((n >> 2) & 1)) << 4)]) = v;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
   pdl_wait_and_release();
-  constexpr int KK = CIN * 9;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npix; i += (long long)gridDim.x * blockDim.x) {
-    const int ox = (int)(i % y.W);
-    const long long t = i / y.W;
-    const int oy = (int)(t % y.H);
-    const long long b = t / y.H;
-    float in[KK];
-#pragma unroll
-    for (int ci = 0; ci < CIN; ++ci)
-#pragma unroll
-      for (int ky = 0; ky < 3; ++ky) {
-        const int iy = oy * S - P + ky;
-#pragma unroll
-        for (int kx = 0; kx < 3; ++kx) {
-          const int ix = ox * S - P + kx;
-          const bool ok = iy >= 0 && iy < x.H && ix >= 0 && ix < x.W;
-          in[ci * 9 + ky * 3 + kx] =
-              ok ? __half2float(x.ptr[b * x.sb + (long long)ci * x.sc + (long long)iy * x.sy + (long long)ix * x.sx])
-                 : 0.0f;
+  const uint32_t idesc = idesc_f16_f32(128, 16);
+  const int ty = tid / kStemTW, tx = tid - ty * kStemTW;  // this thread's pixel in the tile
+  constexpr int pr = (kStemTH - 1) * S + 3, pc = (kStemTW - 1) * S + 3;
+  constexpr uint32_t kPatchBytes = (uint32_t)(kStemTmaW * pr * 3 * 2);
+  static_assert(kBufHalves * 2 % 128 == 0 && kStemTmaW * pr * 3 <= kBufHalves, "patch buffer");
+  auto issue_patch = [&](long long t, int buf) {  // thread 0
+    const long long img = t / tiles_per_img;
+    const int rem = (int)(t - img * tiles_per_img);
+    const int iy0 = (rem / tiles_x) * kStemTH * S - P, ix0 = (rem % tiles_x) * kStemTW * S - P;
+    mbar_expect_tx(smem_u32(&pbar[buf]), kPatchBytes);
+    tma_load_4d(smem_u32(&patch_t[buf][0]), &pmap, smem_u32(&pbar[buf]), ix0 & ~7, iy0, 0, (int)img);
+  };
+  int pending = 0;  // thread 0: a prefetch for the next iteration is in flight
+  if (TMA && tid == 0 && (long long)blockIdx.x < n_tiles) issue_patch(blockIdx.x, 0);
+  uint32_t phase = 0;
+  int k_iter = 0;
+  for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, phase ^= 1u, ++k_iter) {
+    const long long img = t / tiles_per_img;
+    const int rem = (int)(t - img * tiles_per_img);
+    const int oy0 = (rem / tiles_x) * kStemTH, ox0 = (rem % tiles_x) * kStemTW;
+    const int iy0 = oy0 * S - P, ix0 = ox0 * S - P;
+    const int buf = TMA ? (k_iter & 1) : 0;
+    const int xoff = TMA ? ix0 - (ix0 & ~7) : 0;  // window start inside the TMA row
+    if (TMA) {
+      int bad = 0;
+      if (tid == 0) {
+        if (t + gridDim.x < n_tiles) {
+          issue_patch(t + gridDim.x, buf ^ 1);  // freed by the previous iteration
+          pending = 1;
+        } else {
+          pending = 0;
+        }
+        if (!mbar_wait_poll(smem_u32(&pbar[buf]), (uint32_t)(k_iter >> 1) & 1u, 2000000000LL)) {
+          bad = 1;
+          if (status) atomicCAS(status, 0, (int)kStatusTimeoutFull);
         }
       }
-    float acc[COUT];
+      if (__syncthreads_or(bad)) break;
+    } else {  // patch rows rr = warp + 4 i, lanes along x; every load is issued before any store
+      constexpr int kRows = (3 * pr + 3) / 4, kCols = (pc + 31) / 32;
+      __half v[kRows][kCols];
 #pragma unroll
-    for (int c = 0; c < COUT; ++c) acc[c] = 0.0f;
+      for (int i = 0; i < kRows; ++i) {
+        const int rr = warp + 4 * i;
+        const int c = rr / pr, yy = rr - c * pr;
+        const int iy = iy0 + yy;
+        const bool row_ok = rr < 3 * pr && iy >= 0 && iy < x.H;
+        const __half *src = x.ptr + img * x.sb + (long long)c * x.sc + (long long)iy * x.sy;
 #pragma unroll
-    for (int k = 0; k < KK; ++k)
+        for (int j = 0; j < kCols; ++j) {
+          const int ix = ix0 + lane + 32 * j;
+          v[i][j] = (row_ok && lane + 32 * j < pc && ix >= 0 && ix < x.W) ? src[(long long)ix * x.sx]
+                                                                           : __float2half(0.0f);
+        }
+      }
 #pragma unroll
-      for (int c = 0; c < COUT; ++c) acc[c] += in[k] * p.w[k][c];
-    const long long obase = b * y.sb + (long long)oy * y.sy + (long long)ox * y.sx;
+      for (int i = 0; i < kRows; ++i) {
+        const int rr = warp + 4 * i;
+        const int c = rr / pr, yy = rr - c * pr;
 #pragma unroll
-    for (int c0 = 0; c0 < COUT; c0 += 8) {
-      uint32_t a8[8];
+        for (int j = 0; j < kCols; ++j)
+          if (rr < 3 * pr && lane + 32 * j < pc) patch[c][yy][lane + 32 * j] = v[i][j];
+      }
+      __syncthreads();
+    }
+    {  // this pixel's A row: 27 taps + 5 zeros, packed in pairs
+      uint32_t w32[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) a8[j] = __float_as_uint(acc[c0 + j]);
-      const uint4 out = epilogue8<FN>(a8, p.b8[c0 / 8]);
+      for (int j = 0; j < 16; ++j) {
+        uint16_t lo = 0, hi = 0;
+        const int k0 = 2 * j, k1 = 2 * j + 1;
+        if (TMA) {  // the box lands as [channel][pr rows][40]
+          const __half *pt = &patch_t[buf][0];
+          if (k0 < 27) lo = __half_as_ushort(pt[((k0 / 9) * pr + ty * S + (k0 % 9) / 3) * kStemTmaW + xoff + tx * S + k0 % 3]);
+          if (k1 < 27) hi = __half_as_ushort(pt[((k1 / 9) * pr + ty * S + (k1 % 9) / 3) * kStemTmaW + xoff + tx * S + k1 % 3]);
+        } else {
+          if (k0 < 27) lo = __half_as_ushort(patch[k0 / 9][ty * S + (k0 % 9) / 3][tx * S + k0 % 3]);
+          if (k1 < 27) hi = __half_as_ushort(patch[k1 / 9][ty * S + (k1 % 9) / 3][tx * S + k1 % 3]);
+        }
+        w32[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+      }
+      const int sw = (tid >> 2) & 1;
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          *reinterpret_cast<uint4 *>(&a_sm[sl][tid * 32 + ((c ^ sw) << 4)]) =
+              make_uint4(w32[sl * 8 + c * 4], w32[sl * 8 + c * 4 + 1], w32[sl * 8 + c * 4 + 2], w32[sl * 8 + c * 4 + 3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl)
+        umma_f16(tmem, smem_desc_kmajor(smem_u32(&a_sm[sl][0]), 32), smem_desc_kmajor(smem_u32(&b_sm[sl][0]), 32),
+                 idesc, sl != 0 ? 1u : 0u);
+      umma_commit(smem_u32(&mma_bar));
+    }
+    int bad = 0;
+    if (tid == 0 && !mbar_wait_poll(smem_u32(&mma_bar), phase, 2000000000LL)) {  // ~1 s
+      bad = 1;
+      if (status) atomicCAS(status, 0, (int)kStatusTimeoutAcc);
+    }
+    if (__syncthreads_or(bad)) break;  // every thread leaves together
+    tc_fence_after();
+    uint32_t r[16];
+    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) asm volatile("" : "+r"(r[k]));  // uses stay after the wait
+    const int oy = oy0 + ty, ox = ox0 + tx;
+    const uint32_t(&r0)[8] = *reinterpret_cast<const uint32_t(*)[8]>(&r[0]);
+    const uint32_t(&r1)[8] = *reinterpret_cast<const uint32_t(*)[8]>(&r[8]);
+    const uint4 o0 = epilogue8<FN>(r0, p.b8[0]), o1 = epilogue8<FN>(r1, p.b8[1]);
+    if (oy < y.H && ox < y.W) {
+      const long long ob = img * y.sb + (long long)oy * y.sy + (long long)ox * y.sx;
       if (vec_out) {
-        *reinterpret_cast<uint4 *>(y.ptr + obase + c0) = out;
+        *reinterpret_cast<uint4 *>(y.ptr + ob) = o0;
+        *reinterpret_cast<uint4 *>(y.ptr + ob + 8) = o1;
       } else {
-        const __half *h = reinterpret_cast<const __half *>(&out);
+        const __half *h0 = reinterpret_cast<const __half *>(&o0), *h1 = reinterpret_cast<const __half *>(&o1);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y.ptr[obase + (long long)(c0 + j) * y.sc] = h[j];
+        for (int j = 0; j < 8; ++j) {
+          y.ptr[ob + (long long)j * y.sc] = h0[j];
+          y.ptr[ob + (long long)(j + 8) * y.sc] = h1[j];
+        }
       }
     }
+    tc_fence_before();
+    __syncthreads();  // patch, A tile and accumulator are reused by the next tile
+  }
+  if (TMA && tid == 0 && pending)  // only after an early exit: let the last prefetch land (bounded)
+    mbar_wait_poll(smem_u32(&pbar[(k_iter + 1) & 1]), (uint32_t)((k_iter + 1) >> 1) & 1u, 400000000LL);
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
   }
 }
 
-template <int CIN, int COUT>
-cudaError_t launch_stem_t(View4 x, const float *blob, View4 y, long long npix, int S, int P, int act, int vec_out,
-                          cudaStream_t st) {
-  StemWeights<CIN, COUT> p;
-  std::memcpy(&p, blob, sizeof(p));
-  const dim3 g(grid_for(npix, 128)), b(128);
-  switch (resolve_act(act, kActConv3x3)) {
-    case kFnSilu: launch_kernel(stem3x3_t<CIN, COUT, kFnSilu>, dim3(g), dim3(b), 0, st, x, p, y, npix, S, P, vec_out); break;
-    case kFnHswishA: launch_kernel(stem3x3_t<CIN, COUT, kFnHswishA>, dim3(g), dim3(b), 0, st, x, p, y, npix, S, P, vec_out); break;
-    default: launch_kernel(stem3x3_t<CIN, COUT, kFnNone>, dim3(g), dim3(b), 0, st, x, p, y, npix, S, P, vec_out); break;
+template <int FN>
+cudaError_t launch_stem_tc_fn(View4 x, const StemTcParams &p, View4 y, int batch, int S, int P, int vec_out, int *status,
+                              cudaStream_t st) {
+  const int tiles_x = (y.W + kStemTW - 1) / kStemTW, tiles_y = (y.H + kStemTH - 1) / kStemTH;
+  const long long n_tiles = (long long)batch * tiles_x * tiles_y;
+  const long long grid = std::min<long long>(n_tiles, 148LL * 16);
+  // TMA patches need a planar input whose rows and planes are 16-byte aligned
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  bool tma = x.sx == 1 && x.sy % 8 == 0 && x.sc % 8 == 0 && x.sb % 8 == 0 && x.C == 3 &&
+             (reinterpret_cast<uintptr_t>(x.ptr) & 15) == 0;
+  if (tma) {
+    const int pr = (kStemTH - 1) * S + 3;
+    const uint64_t dims[4] = {(uint64_t)x.W, (uint64_t)x.H, 3, (uint64_t)batch};
+    const uint64_t strides[3] = {(uint64_t)x.sy * 2, (uint64_t)x.sc * 2, (uint64_t)x.sb * 2};
+    const uint32_t box[4] = {(uint32_t)kStemTmaW, (uint32_t)pr, 3, 1};
+    const uint32_t es[4] = {1, 1, 1, 1};
+    std::string err;
+    tma = encode_tiled_f16(&map, 4, x.ptr, dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_NONE, &err);
   }
-  return cudaGetLastError();
+  const dim3 g((unsigned)grid), b(128);
+  if (S == 2)
+    return tma ? launch_kernel(stem_tc_k<FN, 2, true>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y,
+                               n_tiles, vec_out, status)
+               : launch_kernel(stem_tc_k<FN, 2, false>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y,
+                               n_tiles, vec_out, status);
+  return tma ? launch_kernel(stem_tc_k<FN, 1, true>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y, n_tiles,
+                             vec_out, status)
+             : launch_kernel(stem_tc_k<FN, 1, false>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y,
+                             n_tiles, vec_out, status);
 }
 
 // ------------------------------------------------------------------ conversions
@@ -1051,14 +1206,10 @@ cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, 
 }
 bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_host, std::vector<float> *blob) {
   if (!(cin == 3 && cout == 16)) return false;
-  StemWeights<3, 16> p;
+  StemTcParams p;
   std::memset(&p, 0, sizeof(p));
   for (int c = 0; c < cout; ++c) {
-    for (int k = 0; k < cin * 9; ++k) {
-      __half_raw hr;
-      hr.x = w_host[(size_t)c * cin * 9 + k];
-      p.w[k][c] = __half2float(__half(hr));
-    }
+    for (int k = 0; k < cin * 9; ++k) p.w[c][k] = w_host[(size_t)c * cin * 9 + k];  // [cout][ci][ky][kx]
     if (b_host) reinterpret_cast<uint16_t *>(&p.b8[c / 8])[c % 8] = b_host[c];
   }
   blob->assign((sizeof(p) + sizeof(float) - 1) / sizeof(float), 0.0f);
@@ -1067,12 +1218,20 @@ bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_ho
 }
 
 cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, const float *blob, View4 y, int batch,
-                              int Cout, int S, int P, int act, cudaStream_t st) {
+                              int Cout, int S, int P, int act, int *status, cudaStream_t st) {
   if (Cout > kStemMaxCout || x.C > 4) return cudaErrorInvalidValue;
   const long long npix = (long long)batch * y.H * y.W;
   const int vec_out = (y.sc == 1 && y.sx % 8 == 0 && y.sy % 8 == 0 && y.sb % 8 == 0 &&
                        (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0) ? 1 : 0;
-  if (x.C == 3 && Cout == 16 && blob) return launch_stem_t<3, 16>(x, blob, y, npix, S, P, act, vec_out, st);
+  if (x.C == 3 && Cout == 16 && blob && S >= 1 && S <= 2 && P == 1) {
+    StemTcParams p;
+    std::memcpy(&p, blob, sizeof(p));
+    switch (resolve_act(act, kActConv3x3)) {
+      case kFnSilu: return launch_stem_tc_fn<kFnSilu>(x, p, y, batch, S, P, vec_out, status, st);
+      case kFnHswishA: return launch_stem_tc_fn<kFnHswishA>(x, p, y, batch, S, P, vec_out, status, st);
+      default: return launch_stem_tc_fn<kFnNone>(x, p, y, batch, S, P, vec_out, status, st);
+    }
+  }
   launch_kernel(stem3x3_k, dim3(grid_for(npix, 128)), dim3(128), 0, st, x, w, bias, y, npix, Cout, S, P, act);
   return cudaGetLastError();
 }

@@ -66,11 +66,13 @@ cudaError_t launch_conv_direct_v4(View4 x, const __half *w, const __half *bias, 
                                   View4 y, int batch, int Cout, int K, int S, int P, int G, int act, int epi,
                                   cudaStream_t st);
 // Stem: 3x3 conv with Cin <= 4 (tiny K), conv3x3 rounding, NHWC or planar output.
-// `blob` (from stem_params, host memory) selects the register / constant-bank
-// specialisation; without it the generic kernel reads `w` / `bias` on the device.
+// `blob` (from stem_params, host memory: Cin 3 -> Cout 16 weights packed as
+// K-major rows) selects the tensor-core kernel (stride 1 or 2, pad 1; `status`
+// receives a bounded-wait timeout); without it the generic CUDA-core kernel
+// reads `w` / `bias` on the device.
 bool stem_params(int cin, int cout, const uint16_t *w_host, const uint16_t *b_host, std::vector<float> *blob);
 cudaError_t launch_stem3x3_v4(View4 x, const __half *w, const __half *bias, const float *blob, View4 y, int batch,
-                              int Cout, int S, int P, int act, cudaStream_t st);
+                              int Cout, int S, int P, int act, int *status, cudaStream_t st);
 // 1x1 conv over planar [Cin][N] rows with few outputs (Cin <= 64, Cout <= 8),
 // gemm-family rounding, fp32 accumulation over ci in order.
 // ---- fused planar tail: a region of slice / concat / elementwise / reshape
