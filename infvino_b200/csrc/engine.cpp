@@ -514,11 +514,113 @@ struct ConvCfg {
   int Ho = 0, Wo = 0, TH = 0, TW = 0;
   int act = 0, act_kind = kActGemm;
   int out = -1, res = -1;
-  int stages = 2, resident_b = 0, smem = 0, tmem_cols = 32, nbuf = 2, kb_per_stage = 1;
-  int halo = 0, hx = 0, hy = 0, kern_kb = 0;  // 3x3 stride-1 halo mode (kern_kb: kernel k-blocks)
+  int halo = 0, kern_kb = 0;  // 3x3 halo mode (= the stride) and the k-blocks the kernel walks
   __half *wp = nullptr;    // packed [Np][Kp]
   __half *bias = nullptr;  // [Np] padded
 };
+
+// Per-launch tile geometry of a tensor-core conv.  A tile is `mb` M blocks of
+// 128 output pixels (mb accumulators of BN columns side by side in TMEM):
+// 1x1 takes mb * 128 consecutive pixels, 3x3 halo a 16-row x 8*mb-column
+// window.  Larger tiles spread the per-tile pipeline handshakes over more
+// pixels; smaller ones give more tiles to spread over the SMs.
+struct ConvGeom {
+  int mb = 1, TW = 0, TH = 0, hx = 0, hy = 0, halo_bytes = 0;
+  int a_tile = 0, resident_b = 0, kb_per_stage = 1, stages = 0, smem = 0;
+};
+
+constexpr int kConvSmemCap = 232448 - 2048 /*static smem + barriers*/ - 1024 /*1 KB alignment*/;
+
+bool conv_geom(const ConvCfg &c, int mb, ConvGeom *g) {
+  ConvGeom r;
+  r.mb = mb;
+  if (c.ksize == 3 && !c.halo) {
+    if (mb != 1) return false;
+    if (c.Wo % 16 == 0) {
+      r.TW = 16;
+      r.TH = 8;
+    } else {
+      r.TW = std::min(c.Wo, 128);
+      r.TH = std::max(1, 128 / r.TW);
+    }
+  } else if (c.halo) {
+    r.TW = 8 * mb;
+    r.TH = 16;
+    r.hx = c.stride == 1 ? r.TW + 2 : r.TW + 1;  // stride 2: one phase (every other column)
+    r.hy = c.stride == 1 ? 16 + 2 : 16 + 1;
+    if (r.hx * c.stride > 256) return false;      // TMA box extent
+    r.halo_bytes = (int)round_up((int64_t)r.hx * r.hy * c.BK * 2, 1024);
+  }
+  r.a_tile = c.halo ? r.halo_bytes * (c.halo == 2 ? 4 : 1) : 128 * mb * c.BK * 2;
+  const int b_tile = (int)round_up((int64_t)c.BN * c.BK * 2, 1024);
+  const int bres = b_tile * c.num_kb;
+  r.resident_b = c.halo || (c.n_tiles == 1 && bres <= 96 * 1024 && kConvSmemCap - bres >= 2 * r.a_tile) ? 1 : 0;
+  if (c.halo && bres > 96 * 1024) return false;
+  const int kb_bytes = r.a_tile + (r.resident_b ? 0 : b_tile);
+  const int ring = kConvSmemCap - (r.resident_b ? bres : 0);
+  // k-blocks per pipeline stage: one full/empty handshake costs a few hundred
+  // cycles, far more than a 16-channel k-block's MMA, so small k-blocks travel
+  // in groups (a divisor of the k-block count, <= 48 KB, >= 3 stages)
+  r.kb_per_stage = 1;
+  for (int gk = c.kern_kb; gk >= 2; --gk)
+    if (c.kern_kb % gk == 0 && gk * kb_bytes <= 48 * 1024 && ring / (gk * kb_bytes) >= 3) {
+      r.kb_per_stage = gk;
+      break;
+    }
+  const int stage_bytes = r.kb_per_stage * kb_bytes;
+  r.stages = std::min(kConvMaxStages, ring / stage_bytes);
+  if (r.stages < 2) return false;
+  r.smem = (r.resident_b ? bres : 0) + r.stages * stage_bytes + 1024;
+  r.smem = std::max(r.smem, 120 * 1024);  // one CTA per SM (TMEM never contended)
+  *g = r;
+  return true;
+}
+
+// M tiles of one launch at batch B with geometry g.
+long long conv_m_tiles(const ConvCfg &c, const ConvGeom &g, int B) {
+  if (c.ksize == 1) return ((long long)B * c.Ho * c.Wo + 128LL * g.mb - 1) / (128LL * g.mb);
+  return (long long)B * ((c.Wo + g.TW - 1) / g.TW) * ((c.Ho + g.TH - 1) / g.TH);
+}
+
+// Accumulator buffers (= epilogue teams working on different tiles at once)
+// for a launch of `tiles` tiles: with few tiles per CTA each tile wants all 16
+// epilogue warps, with many, tiles overlap in the epilogue.
+int conv_nbuf(const ConvCfg &c, long long tiles, int sms) {
+  const long long per_cta = (tiles + sms - 1) / sms;
+  const int most = c.BN <= 128 ? 4 : 2;
+  return per_cta >= 8 ? most : per_cta >= 2 ? std::min(2, most) : 1;
+}
+
+// Geometry of a launch at batch B: the M blocks per tile minimising
+// ceil(tiles / SMs) * (kTileCost + mb), the per-tile handshakes counted as
+// kTileCost M blocks of work, among the tile sizes that fit shared memory and
+// leave TMEM for the accumulator buffers that tile count asks for.
+constexpr double kTileCost = 2.0;
+ConvGeom conv_pick(const ConvCfg &c, int B, int sms, int *nbuf) {
+  ConvGeom best;
+  double best_cost = 0.0;
+  int best_nbuf = 1;
+  bool have = false;
+  const int max_mb = (c.ksize == 3 && !c.halo) ? 1 : 8;
+  for (int mb = 1; mb <= max_mb; ++mb) {
+    ConvGeom g;
+    if (!conv_geom(c, mb, &g)) continue;
+    if (mb > 1 && g.stages < 3) continue;  // keep loads of two tiles ahead in flight
+    const long long tiles = conv_m_tiles(c, g, B) * c.n_tiles;
+    const int nb = conv_nbuf(c, tiles, sms);
+    if (nb * mb * c.BN > 512) continue;
+    const double cost = (double)((tiles + sms - 1) / sms) * (kTileCost + mb);
+    if (!have || cost < best_cost) {
+      best = g;
+      best_cost = cost;
+      best_nbuf = nb;
+      have = true;
+    }
+  }
+  if (!have) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
+  *nbuf = best_nbuf;
+  return best;
+}
 
 int pick_bk(int c) {
   const int c16 = (int)round_up(c, 16);
@@ -1089,59 +1191,23 @@ void Engine::lower() {
         c.n_tiles = (int)((np16 + 127) / 128);
       }
       c.Np = c.BN * c.n_tiles;
-      // up to 4 accumulator buffers (= epilogue teams working on different
-      // tiles at once) within the 512 TMEM columns
-      c.nbuf = c.BN <= 128 ? 4 : 2;
-      c.tmem_cols = pow2_at_least(c.nbuf * c.BN);
-      if (c.ksize == 3) {
-        if (c.Wo % 16 == 0) {
-          c.TW = 16;
-          c.TH = 8;
-        } else {
-          c.TW = std::min(c.Wo, 128);
-          c.TH = std::max(1, 128 / c.TW);
-        }
-      }
-      const int b_tile = (int)round_up((int64_t)c.BN * c.BK * 2, 1024);
-      const int bres = b_tile * c.num_kb;
-      // 3x3 stride 1 with resident weights: one 16 x (TH+2) halo box per channel
-      // chunk feeds all nine taps (an eighth of the TMA rows of per-tap boxes)
+      // 3x3 stride 1 / 2 with resident weights: one halo window per channel
+      // chunk feeds all nine taps (conv_geom decides whether it fits)
       c.kern_kb = c.num_kb;
-      auto smem_budget = [](int a_tile) { return 232448 - 1024 - 2048 /*static + barriers*/ - 1024 /*align*/ - a_tile; };
       if (c.ksize == 3 && (c.stride == 1 || c.stride == 2) && c.pad == 1 && c.nsrc == 1 && c.n_tiles == 1 &&
-          bres <= 96 * 1024 && !(flags_ & kFlagNoHalo)) {
-        const int hx = c.stride == 1 ? 16 : 8 + 1;   // stride 2: one phase (every other column)
-        const int hy = c.stride == 1 ? 16 + 2 : 16 + 1;
-        const int a_h = (int)round_up((int64_t)hx * hy * c.BK * 2, 1024) * (c.stride == 2 ? 4 : 1);
-        if (smem_budget(a_h) - bres >= 2 * a_h) {  // resident weights + two stages
-          c.halo = c.stride;
-          c.TW = 8;
-          c.TH = 16;
-          c.hx = hx;
-          c.hy = hy;
-          c.kern_kb = c.chunks[0];
+          !(flags_ & kFlagNoHalo)) {
+        c.halo = c.stride;
+        c.kern_kb = c.chunks[0];
+        ConvGeom g1;
+        if (!conv_geom(c, 1, &g1)) {  // weights too large to stay resident beside two stages
+          c.halo = 0;
+          c.kern_kb = c.num_kb;
         }
       }
-      const int64_t halo_box = round_up((int64_t)c.hx * c.hy * c.BK * 2, 1024);
-      const int a_tile = c.halo ? (int)(halo_box * (c.halo == 2 ? 4 : 1)) : 128 * c.BK * 2;
-      const int budget = smem_budget(a_tile);
-      c.resident_b = c.halo || (c.n_tiles == 1 && bres <= 96 * 1024 && budget - bres >= 2 * a_tile) ? 1 : 0;
-      const int kb_bytes = a_tile + (c.resident_b ? 0 : b_tile);
-      const int ring = budget - (c.resident_b ? bres : 0);
-      // k-blocks per pipeline stage: one full/empty handshake costs a few
-      // hundred cycles, far more than a 16-channel k-block's MMA, so small
-      // k-blocks travel in groups (a divisor of num_kb, <= 48 KB, >= 3 stages)
-      c.kb_per_stage = 1;
-      for (int g = c.kern_kb; g >= 2; --g)
-        if (c.kern_kb % g == 0 && g * kb_bytes <= 48 * 1024 && ring / (g * kb_bytes) >= 3) {
-          c.kb_per_stage = g;
-          break;
-        }
-      const int stage_bytes = c.kb_per_stage * kb_bytes;
-      c.stages = std::min(kConvMaxStages, ring / stage_bytes);
-      if (c.stages < 2) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
-      c.smem = (c.resident_b ? bres : 0) + c.stages * stage_bytes + 1024 + a_tile;
-      c.smem = std::max(c.smem, 120 * 1024);  // one CTA per SM (TMEM never contended)
+      {
+        ConvGeom g1;
+        if (!conv_geom(c, 1, &g1)) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
+      }
       // ---- weight repack: Wp[Np][Kp], K order (source, tap, chunk, channel)
       const int Kp = c.num_kb * c.BK;
       std::vector<uint16_t> wp((size_t)c.Np * Kp, 0), bp((size_t)c.Np, 0);
@@ -1182,12 +1248,16 @@ void Engine::lower() {
       }
       st.family = c.ksize == 3 ? "conv3x3_tc" : "conv1x1_tc";
       auto cache = std::make_shared<std::map<int, ConvTcArgs>>();
-      st.launch = [this, c, cache, status, sms](int B, cudaStream_t s) -> cudaError_t {
+      st.geometry = std::make_shared<std::map<int, std::string>>();
+      auto geometry = st.geometry;
+      st.launch = [this, c, cache, geometry, status, sms](int B, cudaStream_t s) -> cudaError_t {
         auto it = cache->find(B);
         if (it == cache->end()) {
           ConvTcArgs a;
           std::memset(&a, 0, sizeof(a));
           std::string err;
+          int nbuf = 1;
+          const ConvGeom g = conv_pick(c, B, sms, &nbuf);
           const int Kp = c.num_kb * c.BK;
           for (int sidx = 0; sidx < c.nsrc; ++sidx) {
             const View4 v = view(c.src[sidx]);
@@ -1203,8 +1273,8 @@ void Engine::lower() {
             } else {
               const uint64_t dims[4] = {(uint64_t)v.C, (uint64_t)v.W, (uint64_t)v.H, (uint64_t)B};
               const uint64_t strides[3] = {(uint64_t)v.sx * 2, (uint64_t)v.sy * 2, (uint64_t)v.sb * 2};
-              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)((c.halo ? c.hx : c.TW) * c.stride),
-                                       (uint32_t)((c.halo ? c.hy : c.TH) * c.stride), 1};
+              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)((c.halo ? g.hx : g.TW) * c.stride),
+                                       (uint32_t)((c.halo ? g.hy : g.TH) * c.stride), 1};
               const uint32_t es[4] = {1, (uint32_t)c.stride, (uint32_t)c.stride, 1};
               ok = encode_tiled_f16(&a.mapA[sidx], 4, v.ptr, dims, strides, box, es,
                                     swizzle_for_row_bytes(c.BK * 2), &err);
@@ -1230,29 +1300,30 @@ void Engine::lower() {
           a.n_tiles = c.n_tiles;
           a.num_kb = c.kern_kb;
           a.halo = c.halo;
-          a.hx = c.hx;
-          a.hy = c.hy;
-          a.halo_bytes = c.halo ? (int)round_up((int64_t)c.hx * c.hy * c.BK * 2, 1024) : 0;
-          a.stages = c.stages;
-          a.kb_per_stage = c.kb_per_stage;
-          a.resident_b = c.resident_b;
+          a.mb = g.mb;
+          a.hx = g.hx;
+          a.hy = g.hy;
+          a.halo_bytes = g.halo_bytes;
+          a.stages = g.stages;
+          a.kb_per_stage = g.kb_per_stage;
+          a.resident_b = g.resident_b;
           a.Ho = c.Ho;
           a.Wo = c.Wo;
+          a.m_total = (long long)B * c.Ho * c.Wo;
+          const long long m_tiles = conv_m_tiles(c, g, B);
+          if (m_tiles * c.n_tiles > INT32_MAX) throw std::runtime_error("CudaPlanModel: conv output too large");
+          a.m_tiles = (int)m_tiles;
           if (c.ksize == 1) {
-            a.m_total = (long long)B * c.Ho * c.Wo;
-            a.m_tiles = (int)((a.m_total + 127) / 128);
             a.tile_rows = 128;
             a.TH = a.TW = 1;
             a.tiles_x = a.tiles_per_img = 1;
           } else {
-            a.TH = c.TH;
-            a.TW = c.TW;
-            a.tiles_x = (c.Wo + c.TW - 1) / c.TW;
-            const int tiles_y = (c.Ho + c.TH - 1) / c.TH;
+            a.TH = g.TH;
+            a.TW = g.TW;
+            a.tiles_x = (c.Wo + g.TW - 1) / g.TW;
+            const int tiles_y = (c.Ho + g.TH - 1) / g.TH;
             a.tiles_per_img = a.tiles_x * tiles_y;
-            a.m_tiles = a.tiles_per_img * B;
-            a.m_total = (long long)B * c.Ho * c.Wo;
-            a.tile_rows = c.TH * c.TW;
+            a.tile_rows = c.halo ? 128 : g.TH * g.TW;  // rows of one M block that hold pixels
           }
           a.bias = c.bias;
           a.cout = c.cout;
@@ -1282,18 +1353,19 @@ void Engine::lower() {
                             ? 1
                             : 0;
           }
-          a.tmem_cols = c.tmem_cols;
-          {
-            // teams per CTA from its tile count: with few tiles each tile wants
-            // all 16 epilogue warps; with many, tiles overlap in the epilogue
-            const long long tiles = (long long)a.m_tiles * a.n_tiles;
-            const long long per_cta = (tiles + sms - 1) / sms;
-            a.nbuf = per_cta >= 8 ? c.nbuf : per_cta >= 2 ? 2 : 1;
-          }
-          a.smem_bytes = c.smem;
+          a.nbuf = nbuf;
+          a.tmem_cols = pow2_at_least(nbuf * g.mb * c.BN);
+          a.smem_bytes = g.smem;
           a.status = status;
           const char *why = nullptr;
           if (!conv_tc_finalize(a, &why)) throw std::runtime_error(std::string("CudaPlanModel: ") + why);
+          {
+            std::ostringstream gs;
+            gs << "mb=" << a.mb << " tile=" << (c.ksize == 1 ? 128 * a.mb : a.TH * a.TW) << " halo=" << a.halo
+               << " hx=" << a.hx << " stages=" << a.stages << " kbs=" << a.kb_per_stage << " nbuf=" << a.nbuf
+               << " tiles=" << a.m_tiles * a.n_tiles << " smem=" << a.smem_bytes;
+            (*geometry)[B] = gs.str();
+          }
           it = cache->emplace(B, a).first;
         }
         const ConvTcArgs &a = it->second;
@@ -1879,7 +1951,12 @@ std::string Engine::describe() const {
       os << " arena=" << t.arena_off << " life=[" << t.birth << "," << t.death << "] bytes/img=" << t.bytes_per_img;
     os << "\n";
   }
-  for (const auto &s : steps_) os << "step " << s.family << " " << s.name << "\n";
+  for (const auto &s : steps_) {
+    os << "step " << s.family << " " << s.name;
+    if (s.geometry)
+      for (const auto &g : *s.geometry) os << " [B=" << g.first << " " << g.second << "]";
+    os << "\n";
+  }
   return os.str();
 }
 

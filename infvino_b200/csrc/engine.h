@@ -59,6 +59,8 @@ struct Step {
   double bytes_img = 0.0;       // algorithmic activation bytes per image (inputs + outputs, once)
   double bytes_fixed = 0.0;     // weights / constants, read once per launch
   std::function<cudaError_t(int, cudaStream_t)> launch;
+  // launch geometry per batch size, recorded at the first launch (tensor-core convs)
+  std::shared_ptr<std::map<int, std::string>> geometry;
 };
 
 struct EngineStats {

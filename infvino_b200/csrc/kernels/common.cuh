@@ -150,6 +150,18 @@ __device__ __forceinline__ uint4 epilogue8(const uint32_t (&acc)[8], uint4 bias8
   return out;
 }
 
+// One lane of the (converged) warp is elected; the others get false.  Roles
+// that issue tcgen05 / TMA work run their loops on the whole warp and issue
+// from the elected lane, so loop values stay warp-uniform (a loop run by one
+// divergent lane issues small MMAs at about half the rate).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.u32 %0, 1, 0, P;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ------------------------------------------------------------------ smem/mbarrier
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -10,13 +10,17 @@
 // strided 4-D view (NHWC or planar NCHW).
 //
 // Persistent, warp-specialised CTA (one per SM):
-//   warp 0      : TMA producer (one elected lane), ring of `stages` A (+B) slots
+//   warp 0      : TMA producer (one lane), ring of `stages` A (+B) slots
 //   warp 1      : TMEM allocator + MMA issuer (one lane), `nbuf` (1, 2 or 4)
-//                 accumulator buffers used round robin
+//                 accumulator buffers used round robin, each mb M blocks of
+//                 128 pixels x BN columns
 //   warps 2..17 : epilogue in `nbuf` teams, team j drains buffer j, so nbuf
 //                 tiles are in the epilogue at once; warp w reads TMEM lanes
 //                 32*(w%4) .. +31 (one output row each), and the team's warps
 //                 of a lane quarter split the columns in 8-column chunks
+// The MMA warp runs its loop on all 32 lanes (waits on every lane, results
+// combined with __all_sync so control flow stays uniform) and issues MMAs and
+// commits from one elected lane.
 // Every wait is bounded; a timeout records a status code, raises a CTA abort
 // flag and all roles drain and exit (TMEM is always released).
 #include <cstdio>
@@ -31,8 +35,11 @@ namespace ivb {
 #ifdef IVB_CONV_TRACE
 constexpr int kTraceSlots = 8;  // wait-empty, wait-full, wait-acc-empty, wait-acc-full, epi-work, total, tiles, kblocks
 __device__ unsigned long long g_conv_trace[256 * kTraceSlots];
-#define CONV_TRACE_ADD(slot, v) \
-  atomicAdd(&g_conv_trace[(blockIdx.x & 255) * kTraceSlots + (slot)], (unsigned long long)(v))
+#define CONV_TRACE_ADD(slot, v)                                                                   \
+  do {                                                                                            \
+    if ((threadIdx.x & 31) == 0)                                                                  \
+      atomicAdd(&g_conv_trace[(blockIdx.x & 255) * kTraceSlots + (slot)], (unsigned long long)(v)); \
+  } while (0)
 #define CONV_TRACE_T0() const long long trace_t0_ = clock64()
 #define CONV_TRACE_SINCE(slot) CONV_TRACE_ADD(slot, clock64() - trace_t0_)
 #else
@@ -75,7 +82,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
   const int row = q * 32 + lane;
   const bool leader = (warp == 2 && lane == 0);    // tracer
   (void)leader;
-  const int ksize = a.ksize, BN = a.BN, n_tiles = a.n_tiles, cout = a.cout;
+  const int ksize = a.ksize, BN = a.BN, n_tiles = a.n_tiles, cout = a.cout, mb = a.mb;
   const int num_tiles = a.m_tiles * n_tiles;
   const uint32_t m_total = (uint32_t)a.m_total;
   const int Ho = a.Ho, Wo = a.Wo, TH = a.TH, TW = a.TW, tiles_x = a.tiles_x, tiles_per_img = a.tiles_per_img;
@@ -91,8 +98,10 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
   const bool bias_in_smem = n_tiles == 1 && bias != nullptr;
   int *status = a.status;
   // 3x3: this thread's pixel inside the tile is fixed
-  const int tyr = ksize == 1 ? 0 : (int)fdiv((uint32_t)row, a.fd_tw);
-  const int txr = ksize == 1 ? 0 : row - tyr * TW;
+  // (halo tiles: M block j holds columns 8j .. 8j+7, so the row splits by 8)
+  const int tw_row = a.halo ? 8 : TW;
+  const int tyr = ksize == 1 ? 0 : a.halo ? row >> 3 : (int)fdiv((uint32_t)row, a.fd_tw);
+  const int txr = ksize == 1 ? 0 : row - tyr * tw_row;
   const bool row_in_tile = row < a.tile_rows;
 
   // bias of chunk cc (tile-relative column) of the current N tile; the bias is
@@ -128,73 +137,75 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
 #endif
     const int mt = (int)fdiv((uint32_t)t, fd_nt);
     const int nt = t - mt * n_tiles;
-    bool valid;
-    long long obase, rbase;
-    if (ksize == 1) {
-      const uint32_t p = (uint32_t)mt * 128u + (uint32_t)row;
-      valid = p < m_total;
-      const uint32_t bimg = valid ? fdiv(p, fd_hw) : 0u;
-      const uint32_t r2 = valid ? p - bimg * hw : 0u;
-      const uint32_t oy = fdiv(r2, fd_wo), ox = r2 - oy * (uint32_t)Wo;
-      obase = (long long)bimg * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
-      rbase = (long long)bimg * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
-    } else {
-      const int b = (int)fdiv((uint32_t)mt, fd_tpi);
-      const int rem = mt - b * tiles_per_img;
-      const int ty = (int)fdiv((uint32_t)rem, fd_tx);
-      const int oy = ty * TH + tyr, ox = (rem - ty * tiles_x) * TW + txr;
-      valid = row_in_tile && oy < Ho && ox < Wo;
-      obase = (long long)b * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
-      rbase = (long long)b * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
-    }
     n0 = nt * BN;
-    const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * (uint32_t)BN;
-    // two chunks per TMEM wait: c0 and c0 + 8 * kq
-    for (int c0 = sub * 8; c0 < BN; c0 += 16 * kq) {
-      const int c1 = c0 + 8 * kq;
-      const bool two = c1 < BN;
-      uint32_t r[2][8];
-      tmem_ld8(taddr + (uint32_t)c0, r[0]);
-      if (two) tmem_ld8(taddr + (uint32_t)c1, r[1]);
-      tmem_ld_wait();
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) asm volatile("" : "+r"(r[h][k]));  // uses stay after the wait
+    for (int j = 0; j < mb; ++j) {
+      bool valid;
+      long long obase, rbase;
+      if (ksize == 1) {
+        const uint32_t p = ((uint32_t)mt * (uint32_t)mb + (uint32_t)j) * 128u + (uint32_t)row;
+        valid = p < m_total;
+        const uint32_t bimg = valid ? fdiv(p, fd_hw) : 0u;
+        const uint32_t r2 = valid ? p - bimg * hw : 0u;
+        const uint32_t oy = fdiv(r2, fd_wo), ox = r2 - oy * (uint32_t)Wo;
+        obase = (long long)bimg * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
+        rbase = (long long)bimg * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
+      } else {
+        const int b = (int)fdiv((uint32_t)mt, fd_tpi);
+        const int rem = mt - b * tiles_per_img;
+        const int ty = (int)fdiv((uint32_t)rem, fd_tx);
+        const int oy = ty * TH + tyr, ox = (rem - ty * tiles_x) * TW + txr + 8 * j;
+        valid = row_in_tile && oy < Ho && ox < Wo;
+        obase = (long long)b * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
+        rbase = (long long)b * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
       }
-      // one epilogue call per chunk (one call over both chunks measured slower)
-      const int nch = (n0 + c0 < cout ? 1 : 0) + (two && n0 + c1 < cout ? 1 : 0);  // warp-uniform
-      if (nch == 0) continue;
-      uint4 packed[2];
-      packed[0] = epilogue8<FN>(r[0], load_bias8(c0));
-      if (nch == 2) packed[1] = epilogue8<FN>(r[1], load_bias8(c1));
-      if (!valid) continue;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (h >= nch) break;
-        const int ch0 = n0 + (h == 0 ? c0 : c1);
-        const bool full = ch0 + 8 <= cout;
-        __half *v = reinterpret_cast<__half *>(&packed[h]);
-        if (has_res) {
-          if (res_vec && full) {
-            const uint4 rv = *reinterpret_cast<const uint4 *>(res + rbase + ch0);
-            __half2 *h2 = reinterpret_cast<__half2 *>(&packed[h]);
-            const __half2 *rr = reinterpret_cast<const __half2 *>(&rv);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) h2[k] = __hadd2(h2[k], rr[k]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              if (ch0 + j < cout)
-                v[j] = __float2half_rn(__half2float(v[j]) + __half2float(res[rbase + (long long)(ch0 + j) * r_sc]));
-          }
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (buf * (uint32_t)mb + (uint32_t)j) * (uint32_t)BN;
+      // two chunks per TMEM wait: c0 and c0 + 8 * kq
+      for (int c0 = sub * 8; c0 < BN; c0 += 16 * kq) {
+        const int c1 = c0 + 8 * kq;
+        const bool two = c1 < BN;
+        uint32_t r[2][8];
+        tmem_ld8(taddr + (uint32_t)c0, r[0]);
+        if (two) tmem_ld8(taddr + (uint32_t)c1, r[1]);
+        tmem_ld_wait();
+  #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+  #pragma unroll
+          for (int k = 0; k < 8; ++k) asm volatile("" : "+r"(r[h][k]));  // uses stay after the wait
         }
-        if (out_vec && full) {
-          *reinterpret_cast<uint4 *>(out + obase + ch0) = packed[h];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (ch0 + j < cout) out[obase + (long long)(ch0 + j) * o_sc] = v[j];
+        // one epilogue call per chunk (one call over both chunks measured slower)
+        const int nch = (n0 + c0 < cout ? 1 : 0) + (two && n0 + c1 < cout ? 1 : 0);  // warp-uniform
+        if (nch == 0) continue;
+        uint4 packed[2];
+        packed[0] = epilogue8<FN>(r[0], load_bias8(c0));
+        if (nch == 2) packed[1] = epilogue8<FN>(r[1], load_bias8(c1));
+        if (!valid) continue;
+  #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (h >= nch) break;
+          const int ch0 = n0 + (h == 0 ? c0 : c1);
+          const bool full = ch0 + 8 <= cout;
+          __half *v = reinterpret_cast<__half *>(&packed[h]);
+          if (has_res) {
+            if (res_vec && full) {
+              const uint4 rv = *reinterpret_cast<const uint4 *>(res + rbase + ch0);
+              __half2 *h2 = reinterpret_cast<__half2 *>(&packed[h]);
+              const __half2 *rr = reinterpret_cast<const __half2 *>(&rv);
+  #pragma unroll
+              for (int k = 0; k < 4; ++k) h2[k] = __hadd2(h2[k], rr[k]);
+            } else {
+  #pragma unroll
+              for (int e = 0; e < 8; ++e)
+                if (ch0 + e < cout)
+                  v[e] = __float2half_rn(__half2float(v[e]) + __half2float(res[rbase + (long long)(ch0 + e) * r_sc]));
+            }
+          }
+          if (out_vec && full) {
+            *reinterpret_cast<uint4 *>(out + obase + ch0) = packed[h];
+          } else {
+  #pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (ch0 + e < cout) out[obase + (long long)(ch0 + e) * o_sc] = v[e];
+          }
         }
       }
     }
@@ -238,7 +249,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // parameters every role uses, read once
-  const int BK = a.BK, BN = a.BN, num_kb = a.num_kb, stages = a.stages, n_tiles = a.n_tiles;
+  const int BK = a.BK, BN = a.BN, num_kb = a.num_kb, stages = a.stages, n_tiles = a.n_tiles, mb = a.mb;
   const bool resident_b = a.resident_b != 0;
   const int num_tiles = a.m_tiles * n_tiles;
   int *const status = a.status;
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   const bool halo = a.halo != 0;
   const int nphase = a.halo == 2 ? 4 : 1;  // stride-2 halo: four phase boxes
-  const uint32_t a_tile = halo ? (uint32_t)(a.halo_bytes * nphase) : 128u * (uint32_t)BK * 2u;  // bytes
+  const uint32_t a_tile = halo ? (uint32_t)(a.halo_bytes * nphase) : 128u * (uint32_t)(mb * BK) * 2u;  // bytes
   const uint32_t b_tile = (((uint32_t)BN * (uint32_t)BK * 2u) + 1023u) & ~1023u;
   const int b_blocks = halo ? num_kb * 9 : num_kb;  // resident weight blocks
   const uint32_t bres_bytes = resident_b ? b_tile * (uint32_t)b_blocks : 0u;
@@ -299,16 +310,18 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
+      // (one lane: a whole-warp loop here needs more registers than the
+      // 576-thread CTA leaves, and one TMA box per k-block is no issue limit)
       const int ksize = a.ksize, stride = a.stride, pad = a.pad, nsrc = a.nsrc, taps = a.taps;
       const int TH = a.TH, TW = a.TW, tiles_x = a.tiles_x, tiles_per_img = a.tiles_per_img;
       const FastDiv fd_nt = a.fd_ntiles, fd_tpi = a.fd_tiles_per_img, fd_tx = a.fd_tiles_x;
       int sc[kConvMaxSrc];
 #pragma unroll
       for (int i = 0; i < kConvMaxSrc; ++i) sc[i] = a.src_chunks[i];
-      // bytes one A box delivers: 128 pixel rows (1x1), TH*TW rows (3x3) or
-      // the hx*hy halo
+      // bytes the A boxes of one k-block deliver: mb * 128 pixel rows (1x1),
+      // TH*TW rows (3x3) or the hx*hy halo (per phase)
       const uint32_t a_tx =
-          (uint32_t)(halo ? a.hx * a.hy * nphase : ksize == 1 ? 128 : a.tile_rows) * (uint32_t)BK * 2u;
+          (uint32_t)(halo ? a.hx * a.hy * nphase : ksize == 1 ? 128 * mb : a.tile_rows) * (uint32_t)BK * 2u;
       const uint32_t phase_bytes = (uint32_t)a.halo_bytes;
       const uint32_t b_tx = (uint32_t)BN * (uint32_t)BK * 2u;
       const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx);
@@ -324,7 +337,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         const int nt = t - mt * n_tiles;
         int p0 = 0, b = 0, iy0 = 0, ix0 = 0;
         if (ksize == 1) {
-          p0 = mt * 128;
+          p0 = mt * 128 * mb;
         } else {
           b = (int)fdiv((uint32_t)mt, fd_tpi);
           const int rem = mt - b * tiles_per_img;
@@ -347,18 +360,19 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
           mbar_expect_tx(fb, tx_bytes * (uint32_t)kbs);
           for (int g = 0; g < kbs; ++g, ++kb) {
             const uint32_t sa = ring_base + stage * stage_bytes + (uint32_t)g * kb_bytes;
-            if (ksize == 1)
-              tma_load_2d(sa, mapA_ptr(a, src), fb, chunk * BK, p0);
-            else if (halo) {  // the whole window once per chunk; kb counts chunks
+            if (ksize == 1) {  // mb boxes of 128 pixel rows
+              for (int j = 0; j < mb; ++j)
+                tma_load_2d(sa + (uint32_t)j * 128u * row_bytes, mapA_ptr(a, src), fb, chunk * BK, p0 + 128 * j);
+            } else if (halo) {  // the whole window once per chunk; kb counts chunks
               tma_load_4d(sa, mapA_ptr(a, src), fb, kb * BK, ix0, iy0, b);
               if (nphase == 4) {  // odd columns, odd rows, both odd
                 tma_load_4d(sa + phase_bytes, mapA_ptr(a, src), fb, kb * BK, ix0 + 1, iy0, b);
                 tma_load_4d(sa + 2u * phase_bytes, mapA_ptr(a, src), fb, kb * BK, ix0, iy0 + 1, b);
                 tma_load_4d(sa + 3u * phase_bytes, mapA_ptr(a, src), fb, kb * BK, ix0 + 1, iy0 + 1, b);
               }
-            }
-            else
+            } else {
               tma_load_4d(sa, mapA_ptr(a, src), fb, chunk * BK, ix0 + kx, iy0 + ky, b);
+            }
             if (!resident_b) tma_load_2d(sa + a_tile, &a.mapB, fb, kb * BK, nt * BN);
             if (++chunk == nc) {
               chunk = 0;
@@ -392,12 +406,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         mbar_wait_bounded(smem_u32(&bres_bar), 0, &no_abort, status, kStatusTimeoutDrain, 400000000LL);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ------------------------------------------------------------ MMA issuer
-      // One thread issues every MMA, so the scalar work between two MMAs is
+      // One lane issues every MMA, so the scalar work between two MMAs is
       // pure latency: descriptors are built once and advanced by 32-bit adds on
       // their low word (start address >> 4), and the tap / k-step loops are
       // unrolled with their offsets fixed before the tile loop.
+      const bool leader = elect_one();
       const uint32_t idesc = idesc_f16_f32(128, BN);
       const int ksteps = BK / 16;
       const int hx = a.hx;
@@ -408,6 +423,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       const uint32_t a_lo0 = (uint32_t)a_desc0, a_hi = (uint32_t)(a_desc0 >> 32);
       const uint32_t b_lo0 = (uint32_t)b_desc0, b_hi = (uint32_t)(b_desc0 >> 32);
       const uint32_t stage_step = stage_bytes >> 4, kb_step = kb_bytes >> 4, b_step = b_tile >> 4;
+      // M block j of a tile: 8 rows further into the halo (its 8 columns), or
+      // the next 128 pixel rows of a 1x1 A tile
+      const uint32_t mblk_step = (halo ? 8u : 128u) * row_bytes >> 4;
       // halo: tap (dy, dx) starts dy*hx + dx rows into the halo, and its weights
       // are resident block tap * num_kb + chunk
       // (stride 2: phase (ky & 1, kx & 1), row (ky >> 1) * hx + (kx >> 1))
@@ -423,22 +441,24 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         tap_b[tap] = (uint32_t)(tap * num_kb) * b_step;
       }
       bool ok = true;
-      if (resident_b) ok = mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull);
+      if (resident_b)
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull));
       const uint32_t nbuf = (uint32_t)a.nbuf;
       uint32_t stage = 0, wrap = 0, buf = 0, use = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         CONV_TRACE_T0();
-        if (use > 0 && !mbar_wait_bounded(smem_u32(&acce_bar[buf]), (use - 1) & 1u, &abort_sh, status,
-                                           kStatusTimeoutAccEmpty)) {
+        if (use > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&acce_bar[buf]), (use - 1) & 1u,
+                                                                  &abort_sh, status, kStatusTimeoutAccEmpty))) {
           ok = false;
           break;
         }
         CONV_TRACE_SINCE(2);
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * (uint32_t)BN;
+        const uint32_t d_tmem = tmem_base + buf * (uint32_t)(mb * BN);
         for (int kb = 0; kb < num_kb;) {
           CONV_TRACE_T0();
-          if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), wrap & 1u, &abort_sh, status, kStatusTimeoutFull)) {
+          if (!__all_sync(0xffffffffu,
+                          mbar_wait_bounded(smem_u32(&full_bar[stage]), wrap & 1u, &abort_sh, status, kStatusTimeoutFull))) {
             ok = false;
             break;
           }
@@ -448,40 +468,50 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             const uint32_t a_lo = a_lo0 + stage * stage_step + (uint32_t)g * kb_step;
             if (halo) {
               const uint32_t b_lo = b_lo0 + (uint32_t)kb * b_step;
+              // M blocks one after another: MMAs into one accumulator back to back
+              for (int j = 0; j < mb; ++j) {
+                const uint32_t d = d_tmem + (uint32_t)(j * BN), aj = a_lo + (uint32_t)j * mblk_step;
 #pragma unroll
-              for (int tap = 0; tap < 9; ++tap) {
+                for (int tap = 0; tap < 9; ++tap) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  if (k < ksteps)
-                    umma_f16_lh(d_tmem, a_lo + tap_a[tap] + 2u * k, a_hi, b_lo + tap_b[tap] + 2u * k, b_hi, idesc,
-                                (kb | tap | k) != 0 ? 1u : 0u);
+                  for (int k = 0; k < 4; ++k) {
+                    if (k < ksteps && leader)
+                      umma_f16_lh(d, aj + tap_a[tap] + 2u * k, a_hi, b_lo + tap_b[tap] + 2u * k, b_hi, idesc,
+                                  (kb | tap | k) != 0 ? 1u : 0u);
+                  }
                 }
               }
               continue;
             }
             const uint32_t b_lo = resident_b ? b_lo0 + (uint32_t)kb * b_step : a_lo + (a_tile >> 4);
+            for (int j = 0; j < mb; ++j) {
+              const uint32_t d = d_tmem + (uint32_t)(j * BN), aj = a_lo + (uint32_t)j * mblk_step;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              if (k < ksteps)
-                umma_f16_lh(d_tmem, a_lo + 2u * k, a_hi, b_lo + 2u * k, b_hi, idesc, (kb | k) != 0 ? 1u : 0u);
+              for (int k = 0; k < 4; ++k) {
+                if (k < ksteps && leader)
+                  umma_f16_lh(d, aj + 2u * k, a_hi, b_lo + 2u * k, b_hi, idesc, (kb | k) != 0 ? 1u : 0u);
+              }
             }
           }
-          umma_commit(smem_u32(&empty_bar[stage]));  // slot free once these MMAs retire
+          if (leader) umma_commit(smem_u32(&empty_bar[stage]));  // slot free once these MMAs retire
+          __syncwarp();
           if (++stage == (uint32_t)stages) {
             stage = 0;
             ++wrap;
           }
         }
         if (!ok) break;
-        umma_commit(smem_u32(&accf_bar[buf]));   // accumulator ready
+        if (leader) umma_commit(smem_u32(&accf_bar[buf]));  // accumulator ready
         if (++buf == nbuf) {
           buf = 0;
           ++use;
         }
       }
-      // every MMA issued by this thread must retire before TMEM is released
+      // every MMA issued by this warp must retire before TMEM is released
       volatile int no_abort = 0;
-      umma_commit(smem_u32(&done_bar));
+      __syncwarp();
+      if (leader) umma_commit(smem_u32(&done_bar));
+      __syncwarp();
       mbar_wait_bounded(smem_u32(&done_bar), 0, &no_abort, status, kStatusTimeoutDrain, 400000000LL);
     }
   } else {
@@ -530,7 +560,7 @@ FastDiv make_fastdiv(uint32_t d) {
 
 bool conv_tc_finalize(ConvTcArgs &a, const char **why) {
   const long long lim = (1ll << 31) - 1;
-  if (a.m_total > lim - 128 || (long long)a.m_tiles * a.n_tiles > lim || (long long)a.Ho * a.Wo > lim) {
+  if (a.mb < 1 || a.mb > 8 || a.m_total > lim - 128LL * a.mb || (long long)a.m_tiles * a.n_tiles > lim || (long long)a.Ho * a.Wo > lim) {
     if (why) *why = "conv output too large for 32-bit tile indexing";
     return false;
   }
@@ -538,7 +568,12 @@ bool conv_tc_finalize(ConvTcArgs &a, const char **why) {
     if (why) *why = "conv k-blocks per stage must divide the k-block count";
     return false;
   }
-  if (a.BN > 256 || (a.nbuf != 1 && a.nbuf != 2 && a.nbuf != 4) || a.nbuf * a.BN > a.tmem_cols || a.tmem_cols > 512) {
+  if (a.mb < 1 || (a.mb > 1 && a.ksize == 3 && !a.halo)) {
+    if (why) *why = "conv M blocks per tile out of range";
+    return false;
+  }
+  if (a.BN > 256 || (a.nbuf != 1 && a.nbuf != 2 && a.nbuf != 4) || a.nbuf * a.mb * a.BN > a.tmem_cols ||
+      a.tmem_cols > 512) {
     if (why) *why = "conv N tile / accumulator buffers out of range";
     return false;
   }

@@ -38,18 +38,21 @@ struct alignas(64) ConvTcArgs {
   int stages;
   int kb_per_stage;               // k-blocks per pipeline stage (divides num_kb)
   int resident_b;                 // 1: all of B stays in smem
-  // M tiling
-  long long m_total;              // 1x1: pixels (B*H*W)
+  // M tiling: a tile is mb M blocks of 128 output pixels, accumulated side by
+  // side in TMEM (columns j*BN .. of the tile's buffer for block j)
+  long long m_total;              // pixels (B*Ho*Wo)
   int m_tiles;
+  int mb;                         // M blocks per tile (1x1 and 3x3 halo; 1 otherwise)
   int Ho, Wo, TH, TW, tiles_x, tiles_per_img;
-  int tile_rows;                  // rows of the A tile actually filled (TH*TW or 128)
+  int tile_rows;                  // rows of an M block that hold pixels (TH*TW or 128)
   // 3x3 halo mode (halo = the stride, 1 or 2; 0 = one box per tap): the input
-  // window of a TW = 8 x TH = 16 output tile is loaded once per channel chunk
-  // and feeds all nine taps, a tap being a descriptor start offset of whole
-  // rows.  Stride 1: one 16 x 18 box.  Stride 2: four phase boxes (even / odd
-  // rows x columns, TMA element stride 2) of 9 x 17 pixels; tap (ky, kx) reads
-  // phase (ky & 1, kx & 1) from row (ky >> 1) * hx + (kx >> 1).  num_kb then
-  // counts channel chunks, and the weights stay resident.
+  // window of a TW = 8*mb x TH = 16 output tile is loaded once per channel
+  // chunk and feeds all nine taps, a tap being a descriptor start offset of
+  // whole rows, and M block j the eight columns 8j .. 8j+7 (an offset of 8j
+  // rows).  Stride 1: one (TW+2) x 18 box.  Stride 2: four phase boxes (even /
+  // odd rows x columns, TMA element stride 2) of (TW+1) x 17 pixels; tap
+  // (ky, kx) reads phase (ky & 1, kx & 1) from row (ky >> 1) * hx + (kx >> 1).
+  // num_kb then counts channel chunks, and the weights stay resident.
   int halo;
   int hx, hy;                     // one halo / phase box in pixels
   int halo_bytes;                 // smem bytes of one box (1024-aligned)

@@ -98,11 +98,46 @@ def test_conv3x3_residual(plan_dir):
     check_op(p, 3)
 
 
-def test_concat_conv1x1_cat4(plan_dir):
+# Larger launches whose tiles span several 128-pixel M blocks (the tile size is
+# picked per batch from the tile count): partial tiles at the right edge and at
+# the end of the pixel range, stride-2 phases, a residual, Cout not a multiple
+# of 16, and many tiles per CTA with four accumulator buffers.
+MULTIBLOCK = [  # cin, cout, input hw, ksize, stride, batch, residual
+    (16, 16, 160, 3, 1, 64, True),
+    (16, 16, 100, 3, 1, 8, False),
+    (16, 32, 100, 3, 2, 16, False),
+    (32, 32, 60, 3, 1, 16, True),
+    (64, 51, 52, 3, 1, 16, False),
+    (48, 32, 90, 1, 1, 8, False),
+    (16, 16, 100, 1, 1, 8, False),
+    (32, 64, 80, 1, 1, 32, False),
+]
+
+
+@pytest.mark.parametrize("cin,cout,hw,k,s,batch,res", MULTIBLOCK)
+def test_conv_multiblock_tiles(plan_dir, cin, cout, hw, k, s, batch, res):
+    p = plangen.op_conv(os.path.join(plan_dir, f"mb_{cin}_{cout}_{hw}_{k}_{s}_{int(res)}"), cin, cout, hw, hw, k, s,
+                        act=1, residual=res, producer=True)
+    o, m = run_both(p, batch)
+    geo = [ln for ln in m.describe().splitlines() if ln.startswith("step conv") and "_tc " in ln]
+    assert geo and all(f"[B={batch} mb=" in ln for ln in geo), geo
+    assert any(f"[B={batch} mb=1 " not in ln for ln in geo), geo  # several M blocks per tile
+    for i in range(m.outputCount()):
+        got = m.readOutput(i, batch)
+        ref = o.read_f16(m.outputName(i))
+        g, r = ivref.f16_to_f32(got), ivref.f16_to_f32(ref)
+        scale = float(np.abs(r).max())
+        assert np.abs(g.astype(np.float64) - r).max() <= 2.0 * 2.0 ** -10 * scale
+        assert float(np.mean(ulp_diff(got, ref) > 0)) <= 0.01
+    m.close()
+
+
+@pytest.mark.parametrize("batch", [4, 48])
+def test_concat_conv1x1_cat4(plan_dir, batch):
     p = plangen.op_cat_conv1x1(os.path.join(plan_dir, "cat"), [16, 16, 32, 64], 64, 40, 40)
     m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
     assert m.pool_stats()["fusions_concat"] == 1
-    check_op(p, 4)
+    check_op(p, batch)
 
 
 @pytest.mark.parametrize("c,k,s,act", [(16, 3, 2, 2), (72, 3, 2, 2), (88, 3, 1, 2), (96, 5, 2, 3), (240, 5, 1, 3),
