@@ -990,6 +990,9 @@ void Engine::plan_tails() {
     st.node = po->second;
     st.name = "tail:" + oname;
     st.family = "decode_tail";
+    st.info = "ops=" + std::to_string(prog.n_ops) + " chains=" + std::to_string(prog.n_comp) +
+              " slots=" + std::to_string(prog.n_slots) + " leaves=" + std::to_string(prog.n_leaves) +
+              " dfl=" + std::to_string(prog.n_dfl);
     for (const auto &lf : leaf_ids) {
       const TensorRt &t = T_[(size_t)lf.first];
       if (t.is_init) st.bytes_fixed += (double)t.numel * 2.0;
@@ -1603,9 +1606,38 @@ void Engine::lower() {
     } else if (op == "maxpool") {
       const int x = tid(n.ins[0]);
       const int K = n.ai("K", 5), S = n.ai("S", 1), P = n.ai("P", 2);
-      st.launch = [this, x, out, K, S, P](int B, cudaStream_t s) {
-        return launch_maxpool_v4(view(x), view(out), B, K, S, P, s);
-      };
+      // SPPF: the next plan nodes pool this pool's output again (same size,
+      // stride 1): up to three levels run as one step
+      std::vector<int> chain{out};
+      if (S == 1 && !(flags_ & kFlagNoFusion)) {
+        for (size_t nj = ni + 1; nj < nodes.size() && chain.size() < 3; ++nj) {
+          const PlanNode &m = nodes[nj];
+          if (m.op != "maxpool" || m.ai("K", 5) != K || m.ai("S", 1) != 1 || m.ai("P", 2) != P ||
+              tid(m.ins[0]) != chain.back())
+            break;
+          chain.push_back(tid(m.outs[0]));
+          elided_nodes_.insert((int)nj);
+        }
+      }
+      // the fused kernel reads x from global memory while it writes the later
+      // levels, so x must stay live (unaliased) until the last pooled node
+      if (chain.size() > 1 && T_[(size_t)T_[(size_t)x].root].death < (int)(ni + chain.size() - 1)) {
+        for (size_t l = 1; l < chain.size(); ++l) elided_nodes_.erase((int)(ni + l));
+        chain.resize(1);
+      }
+      if (chain.size() > 1) {
+        st.family = "maxpool_chain";
+        for (size_t l = 1; l < chain.size(); ++l) st.bytes_img += act_bytes(chain[l]);
+        st.launch = [this, x, chain, K, P](int B, cudaStream_t s) {
+          View4 ys[3];
+          for (size_t l = 0; l < chain.size(); ++l) ys[l] = view(chain[l]);
+          return launch_maxpool_chain_v4(view(x), ys, (int)chain.size(), B, K, P, s);
+        };
+      } else {
+        st.launch = [this, x, out, K, S, P](int B, cudaStream_t s) {
+          return launch_maxpool_v4(view(x), view(out), B, K, S, P, s);
+        };
+      }
     } else if (op == "resize_nn") {
       const int x = tid(n.ins[0]);
       const int S = n.ai("S", 2);
@@ -1953,6 +1985,7 @@ std::string Engine::describe() const {
   }
   for (const auto &s : steps_) {
     os << "step " << s.family << " " << s.name;
+    if (!s.info.empty()) os << " [" << s.info << "]";
     if (s.geometry)
       for (const auto &g : *s.geometry) os << " [B=" << g.first << " " << g.second << "]";
     os << "\n";

@@ -61,6 +61,7 @@ struct Step {
   std::function<cudaError_t(int, cudaStream_t)> launch;
   // launch geometry per batch size, recorded at the first launch (tensor-core convs)
   std::shared_ptr<std::map<int, std::string>> geometry;
+  std::string info;  // load-time facts about the step (describe())
 };
 
 struct EngineStats {

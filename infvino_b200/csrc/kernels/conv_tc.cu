@@ -167,9 +167,9 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
         tmem_ld8(taddr + (uint32_t)c0, r[0]);
         if (two) tmem_ld8(taddr + (uint32_t)c1, r[1]);
         tmem_ld_wait();
-  #pragma unroll
+#pragma unroll
         for (int h = 0; h < 2; ++h) {
-  #pragma unroll
+#pragma unroll
           for (int k = 0; k < 8; ++k) asm volatile("" : "+r"(r[h][k]));  // uses stay after the wait
         }
         // one epilogue call per chunk (one call over both chunks measured slower)
@@ -179,7 +179,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
         packed[0] = epilogue8<FN>(r[0], load_bias8(c0));
         if (nch == 2) packed[1] = epilogue8<FN>(r[1], load_bias8(c1));
         if (!valid) continue;
-  #pragma unroll
+#pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (h >= nch) break;
           const int ch0 = n0 + (h == 0 ? c0 : c1);
@@ -190,10 +190,10 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
               const uint4 rv = *reinterpret_cast<const uint4 *>(res + rbase + ch0);
               __half2 *h2 = reinterpret_cast<__half2 *>(&packed[h]);
               const __half2 *rr = reinterpret_cast<const __half2 *>(&rv);
-  #pragma unroll
+#pragma unroll
               for (int k = 0; k < 4; ++k) h2[k] = __hadd2(h2[k], rr[k]);
             } else {
-  #pragma unroll
+#pragma unroll
               for (int e = 0; e < 8; ++e)
                 if (ch0 + e < cout)
                   v[e] = __float2half_rn(__half2float(v[e]) + __half2float(res[rbase + (long long)(ch0 + e) * r_sc]));
@@ -202,7 +202,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
           if (out_vec && full) {
             *reinterpret_cast<uint4 *>(out + obase + ch0) = packed[h];
           } else {
-  #pragma unroll
+#pragma unroll
             for (int e = 0; e < 8; ++e)
               if (ch0 + e < cout) out[obase + (long long)(ch0 + e) * o_sc] = v[e];
           }

@@ -704,6 +704,85 @@ __global__ void resize_nhwc8_k(View4 x, View4 y, long long n8, int S) {
   }
 }
 
+// Nearest upsample by S, channels-last: one thread per input vector of 8
+// channels (read once, written to its S x S output pixels); blockIdx.y is the
+// input row (image * H + y), so only the column / channel split divides.
+__global__ void resize_up_nhwc8_k(View4 x, View4 y, int S, unsigned row8, unsigned C8) {
+  pdl_wait_and_release();
+  const unsigned r = blockIdx.y;
+  const int b = (int)(r / (unsigned)x.H), iy = (int)(r - (unsigned)b * (unsigned)x.H);
+  for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < row8; j += gridDim.x * blockDim.x) {
+    const unsigned ix = j / C8;
+    const int c = (int)(j - ix * C8) * 8;
+    const uint4 v = *reinterpret_cast<const uint4 *>(x.ptr + at8(x, b, iy, (int)ix, c));
+    for (int dy = 0; dy < S; ++dy)
+      for (int dx = 0; dx < S; ++dx)
+        *reinterpret_cast<uint4 *>(y.ptr + at8(y, b, iy * S + dy, (int)ix * S + dx, c)) = v;
+  }
+}
+
+// Chained KxK stride-1 max pools (pad P, out-of-image taps skipped), one block
+// per (8-channel group, image) with the plane in shared memory: level l pools
+// level l-1's result, like the separate pool nodes, as a row pass then a
+// column pass (max is exact, so the split changes no value).
+constexpr int kPoolChainMax = 3;
+struct PoolChainOut {
+  View4 y[kPoolChainMax];
+};
+__global__ void maxpool_chain_nhwc8_k(View4 x, PoolChainOut outs, int levels, int P) {
+  pdl_wait_and_release();
+  extern __shared__ uint4 pool_sm[];
+  const int H = x.H, W = x.W, HW = H * W;
+  const int b = blockIdx.y, c = blockIdx.x * 8;
+  uint4 *A = pool_sm, *T = pool_sm + HW;
+  for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+    const int yy = p / W, xx = p - yy * W;
+    A[p] = *reinterpret_cast<const uint4 *>(x.ptr + at8(x, b, yy, xx, c));
+  }
+  __syncthreads();
+  for (int l = 0; l < levels; ++l) {
+    for (int p = threadIdx.x; p < HW; p += blockDim.x) {  // row pass A -> T
+      const int yy = p / W, xx = p - yy * W;
+      float m[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m[j] = -3.4e38f;
+      const int x0 = max(0, xx - P), x1 = min(W - 1, xx + P);
+      for (int q = x0; q <= x1; ++q) {
+        const uint4 v = A[yy * W + q];
+        const __half *h = reinterpret_cast<const __half *>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], __half2float(h[j]));
+      }
+      __align__(16) __half o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(m[j]);
+      T[p] = *reinterpret_cast<const uint4 *>(o);
+    }
+    __syncthreads();
+    const View4 &y = outs.y[l == 0 ? 0 : l == 1 ? 1 : 2];
+    for (int p = threadIdx.x; p < HW; p += blockDim.x) {  // column pass T -> A, and out
+      const int yy = p / W, xx = p - yy * W;
+      float m[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m[j] = -3.4e38f;
+      const int y0 = max(0, yy - P), y1 = min(H - 1, yy + P);
+      for (int q = y0; q <= y1; ++q) {
+        const uint4 v = T[q * W + xx];
+        const __half *h = reinterpret_cast<const __half *>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], __half2float(h[j]));
+      }
+      __align__(16) __half o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(m[j]);
+      const uint4 r = *reinterpret_cast<const uint4 *>(o);
+      A[p] = r;
+      *reinterpret_cast<uint4 *>(y.ptr + at8(y, b, yy, xx, c)) = r;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void maxpool_nhwc8_k(View4 x, View4 y, long long n8, int K, int S, int P) {
   pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -1137,7 +1216,35 @@ cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, 
   launch_kernel(maxpool_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, x, y, n, K, S, P, cfast_of(y));
   return cudaGetLastError();
 }
+cudaError_t launch_maxpool_chain_v4(View4 x, const View4 *ys, int levels, int batch, int K, int P,
+                                    cudaStream_t st) {
+  if (levels < 1 || levels > kPoolChainMax) return cudaErrorInvalidValue;
+  bool fused = vec8_ok(x) && 2LL * x.H * x.W * 16 <= 48 * 1024 && batch <= 65535;
+  for (int l = 0; l < levels; ++l) fused = fused && vec8_ok(ys[l]) && ys[l].H == x.H && ys[l].W == x.W && ys[l].C == x.C;
+  if (!fused) {  // one pool per level
+    View4 src = x;
+    for (int l = 0; l < levels; ++l) {
+      const cudaError_t e = launch_maxpool_v4(src, ys[l], batch, K, 1, P, st);
+      if (e != cudaSuccess) return e;
+      src = ys[l];
+    }
+    return cudaSuccess;
+  }
+  PoolChainOut outs{};
+  for (int l = 0; l < levels; ++l) outs.y[l] = ys[l];
+  const size_t smem = 2ull * (size_t)x.H * x.W * 16;
+  launch_kernel(maxpool_chain_nhwc8_k, dim3((unsigned)(x.C / 8), (unsigned)batch), dim3(128), smem, st, x, outs,
+                levels, P);
+  return cudaGetLastError();
+}
 cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t st) {
+  if (vec8_ok(x) && vec8_ok(y) && y.H == x.H * S && y.W == x.W * S && y.C == x.C &&
+      (long long)batch * x.H <= 65535 && (long long)x.W * (x.C / 8) < (1LL << 31)) {
+    const unsigned C8 = (unsigned)(x.C / 8), row8 = (unsigned)x.W * C8;
+    const unsigned gx = (unsigned)std::min<long long>((row8 + 255) / 256, 64);
+    launch_kernel(resize_up_nhwc8_k, dim3(gx, (unsigned)(batch * x.H)), dim3(256), 0, st, x, y, S, row8, C8);
+    return cudaGetLastError();
+  }
   if (vec8_ok(x) && vec8_ok(y)) {
     const long long n8 = numel4(y, batch) / 8;
     launch_kernel(resize_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, y, n8, S);

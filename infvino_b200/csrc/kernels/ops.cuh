@@ -46,6 +46,10 @@ cudaError_t launch_concat_planar(const ConcatSrc *src, int nsrc, __half *y, long
                                  long long inner, cudaStream_t st);
 cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, cudaStream_t st);
 cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t st);
+// `levels` (<= 3) chained KxK stride-1 pools: ys[l] = pool(level l-1), level -1
+// being x (the SPPF chain), fused in one kernel when the plane fits shared memory.
+cudaError_t launch_maxpool_chain_v4(View4 x, const View4 *ys, int levels, int batch, int K, int P,
+                                    cudaStream_t st);
 cudaError_t launch_softmax_axis(const __half *x, __half *y, long long outer, int axdim, long long inner,
                                 cudaStream_t st);
 cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, int D2, long long I, int mode,

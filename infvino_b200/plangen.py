@@ -576,9 +576,11 @@ def mobilenetv3_small(out_dir: str, seed: int = 1234, imgsz: int = 224) -> str:
 # ---------------------------------------------------------------------------
 
 def op_conv(out_dir: str, cin: int, cout: int, h: int, w: int, k: int, s: int = 1, act: int = 1,
-            groups: int = 1, residual: bool = False, seed: int = 7, producer: bool = False) -> str:
+            groups: int = 1, residual: bool = False, seed: int = 7, producer: bool = False,
+            consumer: bool = False) -> str:
     """One convolution node; `producer` puts a 1x1 conv in front so that the
-    measured conv reads a channels-last activation (as inside a network)."""
+    measured conv reads a channels-last activation, `consumer` one behind it
+    so that it writes one (as inside a network)."""
     pw = PlanWriter(seed)
     x = pw.input("x", [1, cin, h, w])
     if producer:
@@ -586,6 +588,32 @@ def op_conv(out_dir: str, cin: int, cout: int, h: int, w: int, k: int, s: int = 
     y = pw.conv(x, cout, k, s, act=act, groups=groups, name="op")
     if residual:
         y = pw.add(y, x, 0, name="res")
+    if consumer:
+        y = pw.conv(y, cout, 1, act=1, name="post")
+    pw.output(y)
+    return pw.save(out_dir)
+
+
+def op_sppf(out_dir: str, c: int, h: int, w: int, levels: int = 3, seed: int = 7) -> str:
+    """conv1x1 -> `levels` chained 5x5 max pools -> concat of all -> conv1x1
+    (the SPPF block with channels-last tensors on both sides)."""
+    pw = PlanWriter(seed)
+    x = pw.input("x", [1, c, h, w])
+    x = pw.conv(x, c, 1, act=1, name="pre")
+    ys = [x]
+    for _ in range(levels):
+        ys.append(pw.maxpool(ys[-1], 5, 1, 2))
+    y = pw.conv(pw.concat(ys, 1), c, 1, act=1, name="post")
+    pw.output(y)
+    return pw.save(out_dir)
+
+
+def op_upsample(out_dir: str, c: int, h: int, w: int, s: int = 2, seed: int = 7) -> str:
+    """conv1x1 -> nearest upsample by s -> conv1x1 (channels-last both sides)."""
+    pw = PlanWriter(seed)
+    x = pw.input("x", [1, c, h, w])
+    x = pw.conv(x, c, 1, act=1, name="pre")
+    y = pw.conv(pw.upsample(x, s), c, 1, act=1, name="post")
     pw.output(y)
     return pw.save(out_dir)
 

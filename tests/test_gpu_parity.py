@@ -132,6 +132,20 @@ def test_conv_multiblock_tiles(plan_dir, cin, cout, hw, k, s, batch, res):
     m.close()
 
 
+@pytest.mark.parametrize("c,hw,levels,batch", [(128, 20, 3, 1), (128, 20, 3, 9), (64, 13, 2, 5), (32, 7, 3, 3)])
+def test_sppf_pool_chain(plan_dir, c, hw, levels, batch):
+    p = plangen.op_sppf(os.path.join(plan_dir, f"sppf_{c}_{hw}_{levels}"), c, hw, hw, levels)
+    m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
+    assert [s["family"] for s in m.steps()].count("maxpool_chain") == 1
+    check_op(p, batch)
+
+
+@pytest.mark.parametrize("c,hw,s,batch", [(128, 20, 2, 1), (256, 20, 2, 6), (64, 9, 3, 4)])
+def test_upsample_nearest(plan_dir, c, hw, s, batch):
+    p = plangen.op_upsample(os.path.join(plan_dir, f"up_{c}_{hw}_{s}"), c, hw, hw, s)
+    check_op(p, batch)
+
+
 @pytest.mark.parametrize("batch", [4, 48])
 def test_concat_conv1x1_cat4(plan_dir, batch):
     p = plangen.op_cat_conv1x1(os.path.join(plan_dir, "cat"), [16, 16, 32, 64], 64, 40, 40)

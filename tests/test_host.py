@@ -151,6 +151,19 @@ def test_fastdiv_formula_exact():
         assert q == [int(x) // d for x in n], d
 
 
+def test_sppf_pool_chain_one_step(model_plans):
+    """The SPPF block's three chained 5x5 pools lower to one step (the plane of
+    each 8-channel group pooled three times in shared memory); NO_FUSION keeps
+    one step per pool."""
+    for name in ("yolov8n-pose", "yolo11n-pose"):
+        p = model_plans[name]
+        fused = [s["family"] for s in ivb.PlanModel(p, device=0, max_batch=2, flags=ivb.FLAG_DRY_RUN).steps()]
+        plain = [s["family"] for s in ivb.PlanModel(p, device=0, max_batch=2,
+                                                    flags=ivb.FLAG_DRY_RUN | ivb.FLAG_NO_FUSION).steps()]
+        assert fused.count("maxpool_chain") == 1 and "maxpool" not in fused, name
+        assert plain.count("maxpool") == 3 and "maxpool_chain" not in plain, name
+
+
 def test_head_concats_in_place_and_tail_fused(model_plans):
     """The head's anchor-axis concats are written in place by their convolutions,
     and everything after them (DFL softmax + projection, box / keypoint decode,
