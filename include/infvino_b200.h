@@ -65,6 +65,8 @@ typedef enum ivc_status {
                                          instead of one halo box per channel chunk */
 #define IVC_FLAG_NO_PDL 0x40u         /* diagnostic: kernels launched without programmatic dependent
                                          launch (each waits for the previous grid to finish) */
+#define IVC_FLAG_NO_JIT 0x80u         /* diagnostic: the fused decode tail runs on the interpreting
+                                         kernel instead of its load-time compiled (NVRTC) form */
 
 /* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
 int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);

@@ -21,6 +21,7 @@
 
 #include "kernels/common.cuh"
 #include "kernels/conv_tc.cuh"
+#include "tail_jit.h"
 #include "tma.h"
 
 namespace ivb {
@@ -1002,14 +1003,47 @@ void Engine::plan_tails() {
     st.bytes_img += (double)O.numel * 2.0;
     auto shared_prog = std::make_shared<TailProgram>(prog);
     auto leaves_v = std::make_shared<std::vector<std::pair<int, bool>>>(leaf_ids);
-    st.launch = [this, shared_prog, leaves_v, out_id, A](int B, cudaStream_t s) -> cudaError_t {
+    // The program compiled at load time into straight-line code (NVRTC); the
+    // interpreting kernel runs when that is unavailable or a pointer is not
+    // aligned to the vector width.
+    std::shared_ptr<TailJit> jit;
+    int jit_v = 1;
+    if (!(flags_ & kFlagNoJit)) {  // dry runs compile without loading
+      TailJitLayout lay;
+      lay.A = A;
+      lay.out_img = T_[(size_t)out_id].sb;
+      bool al4 = A % 4 == 0 && lay.out_img % 4 == 0, al2 = A % 2 == 0 && lay.out_img % 2 == 0;
+      for (size_t i = 0; i < leaf_ids.size(); ++i) {
+        lay.leaf_img[i] = leaf_ids[i].second ? 0 : T_[(size_t)leaf_ids[i].first].sb;
+        lay.leaf_row[i] = A;
+        al4 = al4 && lay.leaf_img[i] % 4 == 0;
+        al2 = al2 && lay.leaf_img[i] % 2 == 0;
+      }
+      lay.V = al4 ? 4 : al2 ? 2 : 1;
+      jit = std::make_shared<TailJit>();
+      std::string err;
+      if (jit->build(prog, lay, !dry_, &err)) {
+        jit_v = lay.V;
+        st.info += " jit=V" + std::to_string(lay.V);
+        if (dry_) jit.reset();
+      } else {
+        jit.reset();
+        const size_t nl = err.find('\n');
+        st.info += " jit=off(" + err.substr(0, std::min<size_t>(nl, 80)) + ")";
+      }
+    }
+    st.launch = [this, shared_prog, leaves_v, out_id, A, jit, jit_v](int B, cudaStream_t s) -> cudaError_t {
       TailProgram &pr = *shared_prog;  // device pointers are known once the arena is placed
+      bool aligned = true;
       for (size_t i = 0; i < leaves_v->size(); ++i) {
         const TensorRt &t = T_[(size_t)(*leaves_v)[i].first];
         pr.leaves[i] = TailLeaf{t.dptr, (*leaves_v)[i].second ? 0 : t.sb, A};
+        aligned = aligned && (reinterpret_cast<uintptr_t>(t.dptr) & (uintptr_t)(2 * jit_v - 1)) == 0;
       }
       pr.out = T_[(size_t)out_id].dptr;
       pr.out_img = T_[(size_t)out_id].sb;
+      aligned = aligned && (reinterpret_cast<uintptr_t>(pr.out) & (uintptr_t)(2 * jit_v - 1)) == 0;
+      if (jit && aligned) return jit->launch(pr, B, g_launch_pdl, s);
       return launch_tail_program(pr, B, s);
     };
     for (int ni : region) elided_nodes_.insert(ni);

@@ -31,6 +31,7 @@ enum EngineFlags : unsigned {
   kFlagNoPool = 1u << 4,      // every tensor keeps its own storage (reference INFVINO_NO_POOL)
   kFlagNoHalo = 1u << 5,      // 3x3 convs with per-tap boxes instead of the halo tile
   kFlagNoPdl = 1u << 6,       // launches without programmatic dependent launch
+  kFlagNoJit = 1u << 7,       // fused tail on the interpreting kernel instead of load-time compiled code
 };
 
 struct TensorRt {

@@ -321,6 +321,25 @@ def test_head_fusions_bit_identical(plan_dir):
     b.close()
 
 
+@pytest.mark.parametrize("model,imgsz,batch", [("y8", 320, 2), ("y8", 640, 3), ("y11", 320, 1)])
+def test_tail_compiled_equals_interpreted(plan_dir, model, imgsz, batch):
+    """The load-time compiled decode tail (NVRTC) is active on the device and
+    gives bit-identical outputs to the interpreting tail kernel (NO_JIT)."""
+    gen = plangen.yolov8n_pose if model == "y8" else plangen.yolo11n_pose
+    p = gen(os.path.join(plan_dir, f"{model}_{imgsz}"), imgsz=imgsz)
+    x = np.random.default_rng(23).random(batch * 3 * imgsz * imgsz, dtype=np.float32)
+    a = ivb.PlanModel(p, max_batch=batch)
+    b = ivb.PlanModel(p, max_batch=batch, flags=ivb.FLAG_NO_JIT)
+    tail_a = [ln for ln in a.describe().splitlines() if ln.startswith("step decode_tail")]
+    tail_b = [ln for ln in b.describe().splitlines() if ln.startswith("step decode_tail")]
+    assert tail_a and "jit=V" in tail_a[0], tail_a
+    assert tail_b and "jit=" not in tail_b[0], tail_b
+    ya, yb = a.infer_f32(x, batch)[0], b.infer_f32(x, batch)[0]
+    assert np.array_equal(ya, yb)
+    a.close()
+    b.close()
+
+
 def test_graph_and_eager_agree(model_plans):
     p = model_plans["mobilenetv3-small"]
     x = np.random.default_rng(9).random(2 * 3 * 224 * 224, dtype=np.float32)

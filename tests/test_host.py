@@ -151,6 +151,20 @@ def test_fastdiv_formula_exact():
         assert q == [int(x) // d for x in n], d
 
 
+def test_tail_program_compiles(model_plans):
+    """The fused decode tail's generated CUDA source compiles with NVRTC for
+    sm_100a (a dry run compiles without loading); NO_JIT keeps the
+    interpreting kernel."""
+    for name in ("yolov8n-pose", "yolo11n-pose"):
+        p = model_plans[name]
+        d = ivb.PlanModel(p, device=0, max_batch=1, flags=ivb.FLAG_DRY_RUN).describe()
+        tail = [ln for ln in d.splitlines() if ln.startswith("step decode_tail")]
+        assert len(tail) == 1 and "jit=V4" in tail[0], tail
+        d = ivb.PlanModel(p, device=0, max_batch=1, flags=ivb.FLAG_DRY_RUN | ivb.FLAG_NO_JIT).describe()
+        tail = [ln for ln in d.splitlines() if ln.startswith("step decode_tail")]
+        assert len(tail) == 1 and "jit=" not in tail[0], tail
+
+
 def test_sppf_pool_chain_one_step(model_plans):
     """The SPPF block's three chained 5x5 pools lower to one step (the plane of
     each 8-channel group pooled three times in shared memory); NO_FUSION keeps
