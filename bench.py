@@ -103,10 +103,14 @@ def make_plan(rank: int, workload: str = MODEL) -> str:
         return plangen.MODELS[workload](d, seed=SEED)
     kind, *v = workload.split(":")
     v = [int(t) for t in v]
+    # a 1x1 conv on each side, so the measured conv reads and writes channels-last
+    # tensors as it does inside the network (its launch is the first conv_tc_kernel
+    # of a run when the producer runs on the CUDA cores)
     if kind == "conv3x3":
-        return plangen.op_conv(d, v[0], v[1], v[2], v[2], 3, v[3] if len(v) > 3 else 1, act=1, producer=True)
+        return plangen.op_conv(d, v[0], v[1], v[2], v[2], 3, v[3] if len(v) > 3 else 1, act=1, producer=True,
+                               consumer=True)
     if kind == "conv1x1":
-        return plangen.op_conv(d, v[0], v[1], v[2], v[2], 1, 1, act=1, producer=True)
+        return plangen.op_conv(d, v[0], v[1], v[2], v[2], 1, 1, act=1, producer=True, consumer=True)
     if kind == "dw":
         return plangen.op_conv(d, v[0], v[0], v[2], v[2], v[1], v[3] if len(v) > 3 else 1, act=3, groups=v[0],
                                producer=True)
@@ -359,10 +363,22 @@ def main() -> int:
     achieved = conv_bytes / (conv_ms / 1e3) / 1e9
     troof_total = sum(t_roof(s) for s in steps)
     net_frac = troof_total / (ms / 1e3)
+    # DRAM bytes of the same launches from the committed ncu capture of this
+    # workload (per network step, summed over the conv launches)
+    traffic = None
+    tpath = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
+                         "conv_tc_dram_yolov8n-pose_b64.json")
+    if B == 64 and args.workload == MODEL and os.path.exists(tpath):
+        with open(tpath) as f:
+            t = json.load(f)
+        if t.get("launches_per_run") == len(conv):
+            traffic = int(t["dram_bytes_read"] + t["dram_bytes_write"])
     roofline = {
         "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM conv, %d launches/step)" % len(conv),
         "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-        "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+        "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+        "algorithmic_bytes": int(conv_bytes),
+        "per": "network step (bytes over all conv launches of one step)",
         "peak_source": pk_src + " (hbm_gbs copy bandwidth)",
         "achieved_tflops": round(conv_flops / (conv_ms / 1e3) / 1e12, 1),
         "share_of_step": round(conv_ms / float(prof.sum()), 3),
