@@ -67,6 +67,8 @@ typedef enum ivc_status {
                                          launch (each waits for the previous grid to finish) */
 #define IVC_FLAG_NO_JIT 0x80u         /* diagnostic: the fused decode tail runs on the interpreting
                                          kernel instead of its load-time compiled (NVRTC) form */
+#define IVC_FLAG_NO_TUNE 0x100u       /* convolution tile geometry from the cost model alone (no timing
+                                         of candidate geometries at the first run of a batch size) */
 
 /* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
 int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);

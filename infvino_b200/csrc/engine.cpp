@@ -583,44 +583,46 @@ long long conv_m_tiles(const ConvCfg &c, const ConvGeom &g, int B) {
   return (long long)B * ((c.Wo + g.TW - 1) / g.TW) * ((c.Ho + g.TH - 1) / g.TH);
 }
 
-// Accumulator buffers (= epilogue teams working on different tiles at once)
-// for a launch of `tiles` tiles: with few tiles per CTA each tile wants all 16
-// epilogue warps, with many, tiles overlap in the epilogue.
-int conv_nbuf(const ConvCfg &c, long long tiles, int sms) {
+// Epilogue teams (tiles in the epilogue at once) for a launch of `tiles`
+// tiles: with few tiles per CTA each tile wants all 16 epilogue warps, with
+// many, tiles overlap in the epilogue.
+int conv_nteams(const ConvCfg &c, long long tiles, int sms) {
   const long long per_cta = (tiles + sms - 1) / sms;
   const int most = c.BN <= 128 ? 4 : 2;
   return per_cta >= 8 ? most : per_cta >= 2 ? std::min(2, most) : 1;
 }
 
-// Geometry of a launch at batch B: the M blocks per tile minimising
-// ceil(tiles / SMs) * (kTileCost + mb), the per-tile handshakes counted as
+// Tile geometries of a launch at batch B, cheapest first by the cost
+// ceil(tiles / SMs) * (kTileCost + mb): the per-tile handshakes counted as
 // kTileCost M blocks of work, among the tile sizes that fit shared memory and
-// leave TMEM for the accumulator buffers that tile count asks for.
+// leave TMEM for the accumulator buffers.  Two buffers per team let the MMA
+// warp fill a team's next tile while the team drains the current one; one
+// buffer per team is charged kSingleBufCost.
 constexpr double kTileCost = 2.0;
-ConvGeom conv_pick(const ConvCfg &c, int B, int sms, int *nbuf) {
-  ConvGeom best;
-  double best_cost = 0.0;
-  int best_nbuf = 1;
-  bool have = false;
+constexpr double kSingleBufCost = 1.25;
+constexpr int kConvTuneCands = 6;  // geometries timed by the load-time tuning
+struct ConvCand {
+  ConvGeom g;
+  int nteams = 1, nbuf = 1;
+  double cost = 0.0;
+};
+std::vector<ConvCand> conv_candidates(const ConvCfg &c, int B, int sms) {
+  std::vector<ConvCand> out;
   const int max_mb = (c.ksize == 3 && !c.halo) ? 1 : 8;
   for (int mb = 1; mb <= max_mb; ++mb) {
     ConvGeom g;
     if (!conv_geom(c, mb, &g)) continue;
     if (mb > 1 && g.stages < 3) continue;  // keep loads of two tiles ahead in flight
     const long long tiles = conv_m_tiles(c, g, B) * c.n_tiles;
-    const int nb = conv_nbuf(c, tiles, sms);
-    if (nb * mb * c.BN > 512) continue;
-    const double cost = (double)((tiles + sms - 1) / sms) * (kTileCost + mb);
-    if (!have || cost < best_cost) {
-      best = g;
-      best_cost = cost;
-      best_nbuf = nb;
-      have = true;
-    }
+    const int nt = conv_nteams(c, tiles, sms);
+    if (nt * mb * c.BN > 512) continue;
+    const double base = (double)((tiles + sms - 1) / sms) * (kTileCost + mb);
+    if (2 * nt * mb * c.BN <= 512 && tiles > (long long)sms * nt) out.push_back({g, nt, 2 * nt, base});
+    out.push_back({g, nt, nt, base * kSingleBufCost});
   }
-  if (!have) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
-  *nbuf = best_nbuf;
-  return best;
+  if (out.empty()) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
+  std::stable_sort(out.begin(), out.end(), [](const ConvCand &x, const ConvCand &y) { return x.cost < y.cost; });
+  return out;
 }
 
 int pick_bk(int c) {
@@ -1284,131 +1286,180 @@ void Engine::lower() {
         c.bias = bias >= 0 ? static_cast<__half *>(db) : nullptr;
       }
       st.family = c.ksize == 3 ? "conv3x3_tc" : "conv1x1_tc";
+      // Launch parameters of one batch size and tile geometry.
+      auto build = std::make_shared<std::function<ConvTcArgs(int, const ConvCand &)>>(
+          [this, c, status](int B, const ConvCand &cand) -> ConvTcArgs {
+        const ConvGeom &g = cand.g;
+        const int nteams = cand.nteams, nbuf = cand.nbuf;
+        ConvTcArgs a;
+        std::memset(&a, 0, sizeof(a));
+        std::string err;
+        const int Kp = c.num_kb * c.BK;
+        for (int sidx = 0; sidx < c.nsrc; ++sidx) {
+          const View4 v = view(c.src[sidx]);
+          bool ok;
+          if (c.ksize == 1) {
+            const int64_t pix = (v.H * v.W == 1) ? v.sb : v.sx;
+            const uint64_t dims[2] = {(uint64_t)v.C, (uint64_t)B * v.H * v.W};
+            const uint64_t strides[1] = {(uint64_t)pix * 2};
+            const uint32_t box[2] = {(uint32_t)c.BK, 128};
+            const uint32_t es[2] = {1, 1};
+            ok = encode_tiled_f16(&a.mapA[sidx], 2, v.ptr, dims, strides, box, es,
+                                  swizzle_for_row_bytes(c.BK * 2), &err);
+          } else {
+            const uint64_t dims[4] = {(uint64_t)v.C, (uint64_t)v.W, (uint64_t)v.H, (uint64_t)B};
+            const uint64_t strides[3] = {(uint64_t)v.sx * 2, (uint64_t)v.sy * 2, (uint64_t)v.sb * 2};
+            const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)((c.halo ? g.hx : g.TW) * c.stride),
+                                     (uint32_t)((c.halo ? g.hy : g.TH) * c.stride), 1};
+            const uint32_t es[4] = {1, (uint32_t)c.stride, (uint32_t)c.stride, 1};
+            ok = encode_tiled_f16(&a.mapA[sidx], 4, v.ptr, dims, strides, box, es,
+                                  swizzle_for_row_bytes(c.BK * 2), &err);
+          }
+          if (!ok) throw std::runtime_error("CudaPlanModel: tensor map (activation) " + err);
+        }
+        {
+          const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)c.Np};
+          const uint64_t strides[1] = {(uint64_t)Kp * 2};
+          const uint32_t box[2] = {(uint32_t)c.BK, (uint32_t)c.BN};
+          const uint32_t es[2] = {1, 1};
+          if (!encode_tiled_f16(&a.mapB, 2, c.wp, dims, strides, box, es, swizzle_for_row_bytes(c.BK * 2), &err))
+            throw std::runtime_error("CudaPlanModel: tensor map (weights) " + err);
+        }
+        a.ksize = c.ksize;
+        a.stride = c.stride;
+        a.pad = c.pad;
+        a.nsrc = c.nsrc;
+        for (int sidx = 0; sidx < c.nsrc; ++sidx) a.src_chunks[sidx] = c.chunks[sidx];
+        a.taps = c.taps;
+        a.BK = c.BK;
+        a.BN = c.BN;
+        a.n_tiles = c.n_tiles;
+        a.num_kb = c.kern_kb;
+        a.halo = c.halo;
+        a.mb = g.mb;
+        a.hx = g.hx;
+        a.hy = g.hy;
+        a.halo_bytes = g.halo_bytes;
+        a.stages = g.stages;
+        a.kb_per_stage = g.kb_per_stage;
+        a.resident_b = g.resident_b;
+        a.Ho = c.Ho;
+        a.Wo = c.Wo;
+        a.m_total = (long long)B * c.Ho * c.Wo;
+        const long long m_tiles = conv_m_tiles(c, g, B);
+        if (m_tiles * c.n_tiles > INT32_MAX) throw std::runtime_error("CudaPlanModel: conv output too large");
+        a.m_tiles = (int)m_tiles;
+        if (c.ksize == 1) {
+          a.tile_rows = 128;
+          a.TH = a.TW = 1;
+          a.tiles_x = a.tiles_per_img = 1;
+        } else {
+          a.TH = g.TH;
+          a.TW = g.TW;
+          a.tiles_x = (c.Wo + g.TW - 1) / g.TW;
+          const int tiles_y = (c.Ho + g.TH - 1) / g.TH;
+          a.tiles_per_img = a.tiles_x * tiles_y;
+          a.tile_rows = c.halo ? 128 : g.TH * g.TW;  // rows of one M block that hold pixels
+        }
+        a.bias = c.bias;
+        a.cout = c.cout;
+        a.act = c.act;
+        a.act_kind = c.act_kind;
+        a.act_fn = resolve_act(c.act, c.act_kind);
+        const View4 ov = view(c.out);
+        a.out = ov.ptr;
+        a.o_sb = ov.sb;
+        a.o_sc = ov.sc;
+        a.o_sy = ov.sy;
+        a.o_sx = ov.sx;
+        if (c.ksize == 1 && (ov.H != c.Ho || ov.W != c.Wo)) throw std::runtime_error("conv1x1 output view mismatch");
+        a.out_vec = (ov.sc == 1 && ov.sx % 8 == 0 && ov.sy % 8 == 0 && ov.sb % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(ov.ptr) & 15) == 0)
+                        ? 1
+                        : 0;
+        if (c.res >= 0) {
+          const View4 rv = view(c.res);
+          a.res = rv.ptr;
+          a.r_sb = rv.sb;
+          a.r_sc = rv.sc;
+          a.r_sy = rv.sy;
+          a.r_sx = rv.sx;
+          a.res_vec = (rv.sc == 1 && rv.sx % 8 == 0 && rv.sy % 8 == 0 && rv.sb % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(rv.ptr) & 15) == 0)
+                          ? 1
+                          : 0;
+        }
+        a.nteams = nteams;
+        a.nbuf = nbuf;
+        a.tmem_cols = pow2_at_least(nbuf * g.mb * c.BN);
+        a.smem_bytes = g.smem;
+        a.status = status;
+        const char *why = nullptr;
+        if (!conv_tc_finalize(a, &why)) throw std::runtime_error(std::string("CudaPlanModel: ") + why);
+        return a;
+      });
       auto cache = std::make_shared<std::map<int, ConvTcArgs>>();
       st.geometry = std::make_shared<std::map<int, std::string>>();
       auto geometry = st.geometry;
-      st.launch = [this, c, cache, geometry, status, sms](int B, cudaStream_t s) -> cudaError_t {
+      auto record = [c, geometry](int B, const ConvTcArgs &a, const char *how) {
+        std::ostringstream gs;
+        gs << "mb=" << a.mb << " tile=" << (c.ksize == 1 ? 128 * a.mb : a.TH * a.TW) << " halo=" << a.halo
+           << " hx=" << a.hx << " stages=" << a.stages << " kbs=" << a.kb_per_stage << " teams=" << a.nteams
+           << " nbuf=" << a.nbuf << " tiles=" << a.m_tiles * a.n_tiles << " smem=" << a.smem_bytes << " " << how;
+        (*geometry)[B] = gs.str();
+      };
+      st.launch = [c, cache, build, record, sms](int B, cudaStream_t s) -> cudaError_t {
         auto it = cache->find(B);
-        if (it == cache->end()) {
-          ConvTcArgs a;
-          std::memset(&a, 0, sizeof(a));
-          std::string err;
-          int nbuf = 1;
-          const ConvGeom g = conv_pick(c, B, sms, &nbuf);
-          const int Kp = c.num_kb * c.BK;
-          for (int sidx = 0; sidx < c.nsrc; ++sidx) {
-            const View4 v = view(c.src[sidx]);
-            bool ok;
-            if (c.ksize == 1) {
-              const int64_t pix = (v.H * v.W == 1) ? v.sb : v.sx;
-              const uint64_t dims[2] = {(uint64_t)v.C, (uint64_t)B * v.H * v.W};
-              const uint64_t strides[1] = {(uint64_t)pix * 2};
-              const uint32_t box[2] = {(uint32_t)c.BK, 128};
-              const uint32_t es[2] = {1, 1};
-              ok = encode_tiled_f16(&a.mapA[sidx], 2, v.ptr, dims, strides, box, es,
-                                    swizzle_for_row_bytes(c.BK * 2), &err);
-            } else {
-              const uint64_t dims[4] = {(uint64_t)v.C, (uint64_t)v.W, (uint64_t)v.H, (uint64_t)B};
-              const uint64_t strides[3] = {(uint64_t)v.sx * 2, (uint64_t)v.sy * 2, (uint64_t)v.sb * 2};
-              const uint32_t box[4] = {(uint32_t)c.BK, (uint32_t)((c.halo ? g.hx : g.TW) * c.stride),
-                                       (uint32_t)((c.halo ? g.hy : g.TH) * c.stride), 1};
-              const uint32_t es[4] = {1, (uint32_t)c.stride, (uint32_t)c.stride, 1};
-              ok = encode_tiled_f16(&a.mapA[sidx], 4, v.ptr, dims, strides, box, es,
-                                    swizzle_for_row_bytes(c.BK * 2), &err);
-            }
-            if (!ok) throw std::runtime_error("CudaPlanModel: tensor map (activation) " + err);
-          }
-          {
-            const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)c.Np};
-            const uint64_t strides[1] = {(uint64_t)Kp * 2};
-            const uint32_t box[2] = {(uint32_t)c.BK, (uint32_t)c.BN};
-            const uint32_t es[2] = {1, 1};
-            if (!encode_tiled_f16(&a.mapB, 2, c.wp, dims, strides, box, es, swizzle_for_row_bytes(c.BK * 2), &err))
-              throw std::runtime_error("CudaPlanModel: tensor map (weights) " + err);
-          }
-          a.ksize = c.ksize;
-          a.stride = c.stride;
-          a.pad = c.pad;
-          a.nsrc = c.nsrc;
-          for (int sidx = 0; sidx < c.nsrc; ++sidx) a.src_chunks[sidx] = c.chunks[sidx];
-          a.taps = c.taps;
-          a.BK = c.BK;
-          a.BN = c.BN;
-          a.n_tiles = c.n_tiles;
-          a.num_kb = c.kern_kb;
-          a.halo = c.halo;
-          a.mb = g.mb;
-          a.hx = g.hx;
-          a.hy = g.hy;
-          a.halo_bytes = g.halo_bytes;
-          a.stages = g.stages;
-          a.kb_per_stage = g.kb_per_stage;
-          a.resident_b = g.resident_b;
-          a.Ho = c.Ho;
-          a.Wo = c.Wo;
-          a.m_total = (long long)B * c.Ho * c.Wo;
-          const long long m_tiles = conv_m_tiles(c, g, B);
-          if (m_tiles * c.n_tiles > INT32_MAX) throw std::runtime_error("CudaPlanModel: conv output too large");
-          a.m_tiles = (int)m_tiles;
-          if (c.ksize == 1) {
-            a.tile_rows = 128;
-            a.TH = a.TW = 1;
-            a.tiles_x = a.tiles_per_img = 1;
-          } else {
-            a.TH = g.TH;
-            a.TW = g.TW;
-            a.tiles_x = (c.Wo + g.TW - 1) / g.TW;
-            const int tiles_y = (c.Ho + g.TH - 1) / g.TH;
-            a.tiles_per_img = a.tiles_x * tiles_y;
-            a.tile_rows = c.halo ? 128 : g.TH * g.TW;  // rows of one M block that hold pixels
-          }
-          a.bias = c.bias;
-          a.cout = c.cout;
-          a.act = c.act;
-          a.act_kind = c.act_kind;
-          a.act_fn = resolve_act(c.act, c.act_kind);
-          const View4 ov = view(c.out);
-          a.out = ov.ptr;
-          a.o_sb = ov.sb;
-          a.o_sc = ov.sc;
-          a.o_sy = ov.sy;
-          a.o_sx = ov.sx;
-          if (c.ksize == 1 && (ov.H != c.Ho || ov.W != c.Wo)) throw std::runtime_error("conv1x1 output view mismatch");
-          a.out_vec = (ov.sc == 1 && ov.sx % 8 == 0 && ov.sy % 8 == 0 && ov.sb % 8 == 0 &&
-                       (reinterpret_cast<uintptr_t>(ov.ptr) & 15) == 0)
-                          ? 1
-                          : 0;
-          if (c.res >= 0) {
-            const View4 rv = view(c.res);
-            a.res = rv.ptr;
-            a.r_sb = rv.sb;
-            a.r_sc = rv.sc;
-            a.r_sy = rv.sy;
-            a.r_sx = rv.sx;
-            a.res_vec = (rv.sc == 1 && rv.sx % 8 == 0 && rv.sy % 8 == 0 && rv.sb % 8 == 0 &&
-                         (reinterpret_cast<uintptr_t>(rv.ptr) & 15) == 0)
-                            ? 1
-                            : 0;
-          }
-          a.nbuf = nbuf;
-          a.tmem_cols = pow2_at_least(nbuf * g.mb * c.BN);
-          a.smem_bytes = g.smem;
-          a.status = status;
-          const char *why = nullptr;
-          if (!conv_tc_finalize(a, &why)) throw std::runtime_error(std::string("CudaPlanModel: ") + why);
-          {
-            std::ostringstream gs;
-            gs << "mb=" << a.mb << " tile=" << (c.ksize == 1 ? 128 * a.mb : a.TH * a.TW) << " halo=" << a.halo
-               << " hx=" << a.hx << " stages=" << a.stages << " kbs=" << a.kb_per_stage << " nbuf=" << a.nbuf
-               << " tiles=" << a.m_tiles * a.n_tiles << " smem=" << a.smem_bytes;
-            (*geometry)[B] = gs.str();
-          }
+        if (it == cache->end()) {  // untuned: the cost model's pick
+          const ConvTcArgs a = (*build)(B, conv_candidates(c, B, sms).front());
+          record(B, a, "model");
           it = cache->emplace(B, a).first;
         }
         const ConvTcArgs &a = it->second;
         const int tiles = a.m_tiles * a.n_tiles;
         const int grid = std::max(1, std::min(tiles, sms));
         return launch_conv_tc(a, grid, s);
+      };
+      // Load-time tuning: the first run of a batch size times the cost model's
+      // best few tile geometries of this conv (each geometry accumulates every
+      // output in the same order, so the choice changes no result) and keeps
+      // the fastest.
+      st.tune = [c, cache, build, record, sms](int B, cudaStream_t s) {
+        const std::vector<ConvCand> cands = conv_candidates(c, B, sms);
+        if (cands.size() < 2) return;
+        float best_ms = 0.0f;
+        ConvTcArgs best{};
+        bool have = false;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) return;
+        for (size_t k = 0; k < cands.size() && k < (size_t)kConvTuneCands; ++k) {
+          ConvTcArgs a;
+          try {
+            a = (*build)(B, cands[k]);
+          } catch (const std::exception &) {
+            continue;
+          }
+          const int grid = std::max(1, std::min(a.m_tiles * a.n_tiles, sms));
+          if (launch_conv_tc(a, grid, s) != cudaSuccess) continue;  // warm-up
+          cudaEventRecord(e0, s);
+          bool ok = true;
+          for (int r = 0; r < 3 && ok; ++r) ok = launch_conv_tc(a, grid, s) == cudaSuccess;
+          cudaEventRecord(e1, s);
+          if (!ok || cudaEventSynchronize(e1) != cudaSuccess) continue;
+          float ms = 0.0f;
+          cudaEventElapsedTime(&ms, e0, e1);
+          if (!have || ms < best_ms) {
+            best_ms = ms;
+            best = a;
+            have = true;
+          }
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        if (have) {
+          (*cache)[B] = best;
+          record(B, best, "tuned");
+        }
       };
       steps_.push_back(std::move(st));
       continue;
@@ -1759,8 +1810,40 @@ void Engine::upload_input_f32(const float *src, int batch, bool on_device) {
   check(launch_f32_to_f16_trunc(d, input_device_ptr(), n, stream_), "input conversion");
 }
 
+// One eager pass over the network in plan order; a step with a tuning hook
+// times its candidates where it runs (its inputs are the values the plan
+// gives it there, and repeating it only rewrites its own output, which no
+// live tensor aliases), every other step just runs.  The activation pool
+// lets later tensors reuse the input's storage, so the input is saved before
+// the pass and put back after it: the caller's run reads what it uploaded.
+void Engine::tune(int batch) {
+  if (dry_ || (flags_ & kFlagNoTune) || tuned_.count(batch)) return;
+  tuned_.insert(batch);
+  const size_t in_bytes = (size_t)input_numel() * batch * 2;
+  void *saved = nullptr;
+  if (cudaMalloc(&saved, in_bytes) != cudaSuccess) {  // no room: the cost model's geometry stays
+    cudaGetLastError();
+    return;
+  }
+  check(cudaMemcpyAsync(saved, input_device_ptr(), in_bytes, cudaMemcpyDeviceToDevice, stream_), "input save");
+  for (auto &s : steps_) {
+    if (s.tune) s.tune(batch, stream_);
+    const cudaError_t e = s.launch(batch, stream_);  // (tuned steps: the kept geometry once more)
+    if (e != cudaSuccess) {
+      cudaStreamSynchronize(stream_);
+      cudaFree(saved);
+      throw std::runtime_error("CudaPlanModel: launch failed at " + s.name + ": " + cudaGetErrorString(e));
+    }
+  }
+  check(cudaMemcpyAsync(input_device_ptr(), saved, in_bytes, cudaMemcpyDeviceToDevice, stream_), "input restore");
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  cudaFree(saved);
+  check(cudaGetLastError(), "tuning");
+}
+
 void Engine::capture(int batch) {
   pdl_scope();
+  tune(batch);
   cudaGraph_t g = nullptr;
   check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
   cudaError_t le = cudaSuccess;
@@ -1796,6 +1879,7 @@ void Engine::run(int batch) {
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
   if (flags_ & kFlagNoGraph) {
+    tune(batch);
     for (auto &s : steps_) {
       const cudaError_t e = s.launch(batch, stream_);
       if (e != cudaSuccess) throw std::runtime_error("CudaPlanModel: launch failed at " + s.name + ": " + cudaGetErrorString(e));
@@ -1813,6 +1897,7 @@ void Engine::run(int batch) {
 void Engine::run_profiled(int batch, std::vector<float> *step_ms) {
   pdl_scope();
   check(cudaSetDevice(device_), "cudaSetDevice");
+  tune(batch);
   std::vector<cudaEvent_t> ev(steps_.size() + 1);
   for (auto &e : ev) check(cudaEventCreate(&e), "cudaEventCreate");
   check(cudaEventRecord(ev[0], stream_), "cudaEventRecord");
@@ -1979,6 +2064,7 @@ int Engine::graph_kernel_count(int batch) {
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
+  tune(batch);
   cudaGraph_t g = nullptr;
   check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
   for (auto &s : steps_) s.launch(batch, stream_);

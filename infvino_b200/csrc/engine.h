@@ -32,6 +32,7 @@ enum EngineFlags : unsigned {
   kFlagNoHalo = 1u << 5,      // 3x3 convs with per-tap boxes instead of the halo tile
   kFlagNoPdl = 1u << 6,       // launches without programmatic dependent launch
   kFlagNoJit = 1u << 7,       // fused tail on the interpreting kernel instead of load-time compiled code
+  kFlagNoTune = 1u << 8,      // convolution tile geometry from the cost model, no timing at load
 };
 
 struct TensorRt {
@@ -63,6 +64,8 @@ struct Step {
   // launch geometry per batch size, recorded at the first launch (tensor-core convs)
   std::shared_ptr<std::map<int, std::string>> geometry;
   std::string info;  // load-time facts about the step (describe())
+  // optional load-time tuning, run once per batch size before the first launch
+  std::function<void(int, cudaStream_t)> tune;
 };
 
 struct EngineStats {
@@ -148,6 +151,8 @@ class Engine {
   std::vector<std::pair<int, int>> tail_uses_;  // (tensor, node) reads of fused tails, for liveness
   void plan_tails();
   void pdl_scope() const;  // launches on this thread follow kFlagNoPdl
+  void tune(int batch);    // per-step load-time tuning for this batch size (once)
+  std::set<int> tuned_;
   std::vector<Step> steps_;
   EngineStats stats_;
 

@@ -11,13 +11,15 @@
 //
 // Persistent, warp-specialised CTA (one per SM):
 //   warp 0      : TMA producer (one lane), ring of `stages` A (+B) slots
-//   warp 1      : TMEM allocator + MMA issuer (one lane), `nbuf` (1, 2 or 4)
-//                 accumulator buffers used round robin, each mb M blocks of
-//                 128 pixels x BN columns
-//   warps 2..17 : epilogue in `nbuf` teams, team j drains buffer j, so nbuf
-//                 tiles are in the epilogue at once; warp w reads TMEM lanes
-//                 32*(w%4) .. +31 (one output row each), and the team's warps
-//                 of a lane quarter split the columns in 8-column chunks
+//   warp 1      : TMEM allocator + MMA issuer, `nbuf` (1 to 8) accumulator
+//                 buffers used round robin, each mb M blocks of 128 pixels x
+//                 BN columns
+//   warps 2..17 : epilogue in `nteams` (1, 2 or 4) teams, team k drains the
+//                 CTA's tiles k, k + nteams, ... (one or two buffers per team),
+//                 so nteams tiles are in the epilogue at once; warp w reads
+//                 TMEM lanes 32*(w%4) .. +31 (one output row each), and the
+//                 team's warps of a lane quarter split the columns in
+//                 8-column chunks
 // The MMA warp runs its loop on all 32 lanes (waits on every lane, results
 // combined with __all_sync so control flow stays uniform) and issues MMAs and
 // commits from one elected lane.
@@ -67,17 +69,20 @@ template <int FN>
 __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int lane, uint32_t tmem_base,
                                               uint64_t *accf_bar, uint64_t *acce_bar, volatile int *abort_sh,
                                               volatile int *epi_go, const uint4 *bias_sh) {
-  // The 16 warps form `nbuf` teams; team j owns accumulator buffer j and the
-  // CTA's tiles j, j + nbuf, ...  so that nbuf tiles are in the epilogue at
-  // once.  Inside a team the (4 / nbuf) warps of a lane quarter split the
-  // columns in 8-column chunks.
-  const int nbuf = a.nbuf;
+  // The 16 warps form `nteams` teams; team k drains the CTA's tiles k,
+  // k + nteams, ... so that nteams tiles are in the epilogue at once.  Tile i
+  // of the CTA sits in accumulator buffer i % nbuf; with nbuf = 2 * nteams a
+  // team alternates between two buffers, so the MMA warp fills its next tile
+  // while it drains the current one.  Inside a team the (4 / nteams) warps of
+  // a lane quarter split the columns in 8-column chunks.
+  const int nteams = a.nteams;
+  const uint32_t nbuf = (uint32_t)a.nbuf;
   const int q = warp & 3;
   const int grp = (warp - 2) >> 2;                 // 0..3: groups of four consecutive warps
-  const int team = grp & (nbuf - 1);
-  const int sub = grp / nbuf;                      // position among the team's warps of this quarter
-  const int kq = 4 / nbuf;                         // team warps per lane quarter
-  const int team_threads = 32 * kConvEpiWarps / nbuf;
+  const int team = grp & (nteams - 1);
+  const int sub = grp / nteams;                    // position among the team's warps of this quarter
+  const int kq = 4 / nteams;                       // team warps per lane quarter
+  const int team_threads = 32 * kConvEpiWarps / nteams;
   const bool team_lead = warp == 2 + 4 * team;     // its lane 0 waits for the accumulator
   const int row = q * 32 + lane;
   const bool leader = (warp == 2 && lane == 0);    // tracer
@@ -112,25 +117,26 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
     if (bias != nullptr) return *reinterpret_cast<const uint4 *>(bias + n0 + cc);
     return make_uint4(0, 0, 0, 0);
   };
-  const uint32_t buf = (uint32_t)team;
   volatile int *go = epi_go + 2 * team;
-  uint32_t use = 0;
-  for (int t = blockIdx.x + team * gridDim.x; t < num_tiles; t += nbuf * gridDim.x, ++use) {
+  uint32_t jt = 0;                                 // the team's tile count
+  for (int t = blockIdx.x + team * gridDim.x; t < num_tiles; t += nteams * gridDim.x, ++jt) {
+    const uint32_t ti = (uint32_t)team + jt * (uint32_t)nteams;  // the CTA's tile index
+    const uint32_t buf = ti % nbuf, use = ti / nbuf;
     // One thread per team waits for the accumulator; the team's other warps
     // block in a hardware barrier (no issue slots).  The go flag is
     // double-buffered so a late reader never sees the next tile's value.
     if (team_lead) {
       if (lane == 0) {
         CONV_TRACE_T0();
-        go[use & 1u] = mbar_wait_bounded(smem_u32(&accf_bar[buf]), use & 1u, abort_sh, status, kStatusTimeoutAcc)
-                           ? 1
-                           : 0;
+        go[jt & 1u] = mbar_wait_bounded(smem_u32(&accf_bar[buf]), use & 1u, abort_sh, status, kStatusTimeoutAcc)
+                          ? 1
+                          : 0;
         CONV_TRACE_SINCE(3);
       }
       __syncwarp();  // reconverge before the warp-aligned barrier
     }
     named_bar_sync(1 + team, team_threads);
-    if (!go[use & 1u]) break;
+    if (!go[jt & 1u]) break;
     tc_fence_after();
 #ifdef IVB_CONV_TRACE
     const long long work_t0 = clock64();
@@ -243,7 +249,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
-  __shared__ volatile int epi_go[2 * kConvMaxBufs];
+  __shared__ volatile int epi_go[2 * kConvMaxTeams];
   __shared__ uint4 bias_sh[256 / 8];  // the bias of the single N tile (n_tiles == 1)
 
   const int warp = threadIdx.x >> 5;
@@ -276,7 +282,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
     for (int j = 0; j < kConvMaxBufs; ++j) {
       mbar_init(smem_u32(&accf_bar[j]), 1);
-      mbar_init(smem_u32(&acce_bar[j]), kConvEpiWarps / a.nbuf);  // one arrival per team warp
+      mbar_init(smem_u32(&acce_bar[j]), kConvEpiWarps / a.nteams);  // one arrival per team warp
     }
     mbar_init(smem_u32(&bres_bar), 1);
     mbar_init(smem_u32(&done_bar), 1);
@@ -572,7 +578,8 @@ bool conv_tc_finalize(ConvTcArgs &a, const char **why) {
     if (why) *why = "conv M blocks per tile out of range";
     return false;
   }
-  if (a.BN > 256 || (a.nbuf != 1 && a.nbuf != 2 && a.nbuf != 4) || a.nbuf * a.mb * a.BN > a.tmem_cols ||
+  if (a.BN > 256 || (a.nteams != 1 && a.nteams != 2 && a.nteams != 4) ||
+      (a.nbuf != a.nteams && a.nbuf != 2 * a.nteams) || a.nbuf > kConvMaxBufs || a.nbuf * a.mb * a.BN > a.tmem_cols ||
       a.tmem_cols > 512) {
     if (why) *why = "conv N tile / accumulator buffers out of range";
     return false;

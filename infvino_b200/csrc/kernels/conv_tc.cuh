@@ -11,7 +11,8 @@ namespace ivb {
 constexpr int kConvMaxSrc = 4;
 constexpr int kConvMaxStages = 12;
 constexpr int kConvEpiWarps = 16;   // four groups of four warps (one per TMEM lane quarter)
-constexpr int kConvMaxBufs = 4;     // TMEM accumulator buffers (= epilogue teams)
+constexpr int kConvMaxTeams = 4;    // epilogue teams (tiles in the epilogue at once)
+constexpr int kConvMaxBufs = 8;     // TMEM accumulator buffers (one or two per team)
 constexpr int kConvThreads = 64 + 32 * kConvEpiWarps;  // warp0 TMA, warp1 MMA, then epilogue
 
 // Division by a launch-invariant divisor as a multiply-high:
@@ -68,7 +69,8 @@ struct alignas(64) ConvTcArgs {
   long long r_sb, r_sc, r_sy, r_sx;
   int res_vec;
   int tmem_cols;
-  int nbuf;                       // accumulator buffers / epilogue teams: 1, 2 or 4
+  int nteams;                     // epilogue teams: 1, 2 or 4
+  int nbuf;                       // accumulator buffers: nteams or 2 * nteams
   int smem_bytes;
   int *status;
   // derived by conv_tc_finalize(): divisors of the per-tile index arithmetic

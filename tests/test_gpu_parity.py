@@ -118,7 +118,8 @@ MULTIBLOCK = [  # cin, cout, input hw, ksize, stride, batch, residual
 def test_conv_multiblock_tiles(plan_dir, cin, cout, hw, k, s, batch, res):
     p = plangen.op_conv(os.path.join(plan_dir, f"mb_{cin}_{cout}_{hw}_{k}_{s}_{int(res)}"), cin, cout, hw, hw, k, s,
                         act=1, residual=res, producer=True)
-    o, m = run_both(p, batch)
+    # the cost model's geometry (load-time tuning could pick one M block)
+    o, m = run_both(p, batch, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_TUNE)
     geo = [ln for ln in m.describe().splitlines() if ln.startswith("step conv") and "_tc " in ln]
     assert geo and all(f"[B={batch} mb=" in ln for ln in geo), geo
     assert any(f"[B={batch} mb=1 " not in ln for ln in geo), geo  # several M blocks per tile
@@ -336,6 +337,22 @@ def test_tail_compiled_equals_interpreted(plan_dir, model, imgsz, batch):
     assert tail_b and "jit=" not in tail_b[0], tail_b
     ya, yb = a.infer_f32(x, batch)[0], b.infer_f32(x, batch)[0]
     assert np.array_equal(ya, yb)
+    a.close()
+    b.close()
+
+
+def test_tuned_geometry_changes_no_bit(plan_dir):
+    """Load-time tuning times several tile geometries per conv and keeps the
+    fastest; every geometry accumulates each output in the same order, so the
+    tuned handle equals the cost-model handle bit for bit."""
+    p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_320"), imgsz=320)
+    x = np.random.default_rng(29).random(6 * 3 * 320 * 320, dtype=np.float32)
+    a = ivb.PlanModel(p, max_batch=6)
+    b = ivb.PlanModel(p, max_batch=6, flags=ivb.FLAG_NO_TUNE)
+    ya, yb = a.infer_f32(x, 6)[0], b.infer_f32(x, 6)[0]
+    assert np.array_equal(ya, yb)
+    da, db = a.describe(), b.describe()
+    assert " tuned" in da and " tuned" not in db and " model" in db
     a.close()
     b.close()
 
