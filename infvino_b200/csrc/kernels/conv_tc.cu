@@ -292,19 +292,27 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < a.nsrc; ++s) tma_prefetch_desc(mapA_ptr(a, s));
     tma_prefetch_desc(&a.mapB);
+    // the resident weights are constants (written once at load), so their
+    // copy starts before the previous grid has finished; the thread that
+    // initialised the barrier issues it
+    if (resident_b) {
+      mbar_expect_tx(smem_u32(&bres_bar), (uint32_t)BN * (uint32_t)BK * 2u * (uint32_t)b_blocks);
+      for (int kb = 0; kb < b_blocks; ++kb)
+        tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * BK, 0);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&tmem_base_sh), (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
-  // everything above touched only shared memory, TMEM and the parameter block;
-  // global memory (weights, activations, bias) is read after the previous grid
-  pdl_wait_and_release();
-  if (warp >= 2 && n_tiles == 1 && a.bias != nullptr) {
+  if (warp >= 2 && n_tiles == 1 && a.bias != nullptr) {  // (a constant too)
     // bias padded to BN (a multiple of 16), 16 B per thread
     const int i = threadIdx.x - 64;
     if (i < BN / 8) bias_sh[i] = reinterpret_cast<const uint4 *>(a.bias)[i];
   }
+  // everything above touched only shared memory, TMEM, the parameter block and
+  // the constant weights and bias; activations are read after the previous grid
+  pdl_wait_and_release();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -331,11 +339,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       const uint32_t phase_bytes = (uint32_t)a.halo_bytes;
       const uint32_t b_tx = (uint32_t)BN * (uint32_t)BK * 2u;
       const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx);
-      if (resident_b) {
-        mbar_expect_tx(smem_u32(&bres_bar), b_tx * (uint32_t)b_blocks);
-        for (int kb = 0; kb < b_blocks; ++kb)
-          tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * BK, 0);
-      }
       uint32_t stage = 0, wrap = 0, issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
