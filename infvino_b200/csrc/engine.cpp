@@ -555,9 +555,10 @@ bool conv_geom(const ConvCfg &c, int mb, ConvGeom *g) {
   r.a_tile = c.halo ? r.halo_bytes * (c.halo == 2 ? 4 : 1) : 128 * mb * c.BK * 2;
   const int b_tile = (int)round_up((int64_t)c.BN * c.BK * 2, 1024);
   const int bres = b_tile * c.num_kb;
-  r.resident_b = c.halo || (c.n_tiles == 1 && bres <= 96 * 1024 && kConvSmemCap - bres >= 2 * r.a_tile) ? 1 : 0;
-  if (c.halo && bres > 96 * 1024) return false;
-  const int kb_bytes = r.a_tile + (r.resident_b ? 0 : b_tile);
+  // weights resident when they fit beside two stages; otherwise they travel
+  // with the A tiles (halo: each stage carries its chunk's nine tap blocks)
+  r.resident_b = (c.n_tiles == 1 && bres <= 96 * 1024 && kConvSmemCap - bres >= 2 * r.a_tile) ? 1 : 0;
+  const int kb_bytes = r.a_tile + (r.resident_b ? 0 : (c.halo ? 9 : 1) * b_tile);
   const int ring = kConvSmemCap - (r.resident_b ? bres : 0);
   // k-blocks per pipeline stage: one full/empty handshake costs a few hundred
   // cycles, far more than a 16-channel k-block's MMA, so small k-blocks travel

@@ -269,7 +269,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   const int b_blocks = halo ? num_kb * 9 : num_kb;  // resident weight blocks
   const uint32_t bres_bytes = resident_b ? b_tile * (uint32_t)b_blocks : 0u;
   const int kbs = a.kb_per_stage;                      // k-blocks per stage
-  const uint32_t kb_bytes = a_tile + (resident_b ? 0u : b_tile);
+  // B in the ring: one block per k-block, or (halo) the chunk's nine tap blocks
+  const uint32_t b_stage = resident_b ? 0u : (halo ? 9u : 1u) * b_tile;
+  const uint32_t kb_bytes = a_tile + b_stage;
   const uint32_t stage_bytes = (uint32_t)kbs * kb_bytes;
   const uint32_t bres_base = base;
   const uint32_t ring_base = base + bres_bytes;
@@ -338,7 +340,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
           (uint32_t)(halo ? a.hx * a.hy * nphase : ksize == 1 ? 128 * mb : a.tile_rows) * (uint32_t)BK * 2u;
       const uint32_t phase_bytes = (uint32_t)a.halo_bytes;
       const uint32_t b_tx = (uint32_t)BN * (uint32_t)BK * 2u;
-      const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx);
+      const uint32_t tx_bytes = a_tx + (resident_b ? 0u : b_tx * (halo ? 9u : 1u));
       uint32_t stage = 0, wrap = 0, issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -382,7 +384,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             } else {
               tma_load_4d(sa, mapA_ptr(a, src), fb, chunk * BK, ix0 + kx, iy0 + ky, b);
             }
-            if (!resident_b) tma_load_2d(sa + a_tile, &a.mapB, fb, kb * BK, nt * BN);
+            if (!resident_b) {
+              if (halo) {  // weights of this chunk for all nine taps (K block tap * chunks + chunk)
+                for (int tp = 0; tp < 9; ++tp)
+                  tma_load_2d(sa + a_tile + (uint32_t)tp * b_tile, &a.mapB, fb, (tp * num_kb + kb) * BK, nt * BN);
+              } else {
+                tma_load_2d(sa + a_tile, &a.mapB, fb, kb * BK, nt * BN);
+              }
+            }
             if (++chunk == nc) {
               chunk = 0;
               if (++kx == ksize) {
@@ -447,7 +456,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
                                       (uint32_t)((ky >> 1) * hx + (kx >> 1)) * row_bytes
                                 : (uint32_t)(ky * hx + kx) * row_bytes;
         tap_a[tap] = off >> 4;
-        tap_b[tap] = (uint32_t)(tap * num_kb) * b_step;
+        tap_b[tap] = (uint32_t)(resident_b ? tap * num_kb : tap) * b_step;  // resident: all blocks; ring: the chunk's nine
       }
       bool ok = true;
       if (resident_b)
@@ -476,7 +485,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
           for (int g = 0; g < kbs; ++g, ++kb) {
             const uint32_t a_lo = a_lo0 + stage * stage_step + (uint32_t)g * kb_step;
             if (halo) {
-              const uint32_t b_lo = b_lo0 + (uint32_t)kb * b_step;
+              const uint32_t b_lo = resident_b ? b_lo0 + (uint32_t)kb * b_step : a_lo + (a_tile >> 4);
               // M blocks one after another: MMAs into one accumulator back to back
               for (int j = 0; j < mb; ++j) {
                 const uint32_t d = d_tmem + (uint32_t)(j * BN), aj = a_lo + (uint32_t)j * mblk_step;

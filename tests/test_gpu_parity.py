@@ -70,7 +70,9 @@ def test_conv1x1(plan_dir, cin, cout, hw, batch):
 
 
 CONV3 = [(16, 16, 40, 1), (32, 32, 20, 1), (64, 64, 40, 2), (16, 32, 80, 2), (64, 51, 20, 1), (51, 51, 40, 1),
-         (128, 128, 10, 1), (128, 256, 20, 2), (64, 64, 7, 1), (256, 64, 20, 1)]
+         (128, 128, 10, 1), (128, 256, 20, 2), (64, 64, 7, 1), (256, 64, 20, 1),
+         # weights too large to stay resident: halo tiles with each chunk's nine tap blocks in the stage
+         (128, 64, 40, 1), (128, 51, 40, 1), (192, 64, 20, 1), (128, 64, 13, 1)]
 
 
 @pytest.mark.parametrize("cin,cout,hw,s", CONV3)
