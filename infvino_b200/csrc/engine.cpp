@@ -601,7 +601,8 @@ int conv_nteams(const ConvCfg &c, long long tiles, int sms) {
 // buffer per team is charged kSingleBufCost.
 constexpr double kTileCost = 2.0;
 constexpr double kSingleBufCost = 1.25;
-constexpr int kConvTuneCands = 6;  // geometries timed by the load-time tuning
+constexpr double kOtherTeamsCost = 1.5;
+constexpr int kConvTuneCands = 10;  // geometries timed by the load-time tuning
 struct ConvCand {
   ConvGeom g;
   int nteams = 1, nbuf = 1;
@@ -615,11 +616,19 @@ std::vector<ConvCand> conv_candidates(const ConvCfg &c, int B, int sms) {
     if (!conv_geom(c, mb, &g)) continue;
     if (mb > 1 && g.stages < 3) continue;  // keep loads of two tiles ahead in flight
     const long long tiles = conv_m_tiles(c, g, B) * c.n_tiles;
-    const int nt = conv_nteams(c, tiles, sms);
-    if (nt * mb * c.BN > 512) continue;
+    const int nt_model = conv_nteams(c, tiles, sms);
     const double base = (double)((tiles + sms - 1) / sms) * (kTileCost + mb);
-    if (2 * nt * mb * c.BN <= 512 && tiles > (long long)sms * nt) out.push_back({g, nt, 2 * nt, base});
-    out.push_back({g, nt, nt, base * kSingleBufCost});
+    // the tile-count rule's team count first; the other counts are kept as
+    // candidates for the load-time tuning (charged kOtherTeamsCost)
+    const int counts[4] = {nt_model, nt_model == 4 ? 2 : 4, nt_model == 1 ? 2 : 1, nt_model == 2 ? 1 : 2};
+    for (int ci = 0; ci < 4; ++ci) {
+      const int nt = counts[ci];
+      if (ci == 3 && (nt == counts[1] || nt == counts[2])) continue;  // {model, the other two} once each
+      if (nt * mb * c.BN > 512 || (nt == 4 && c.BN > 128)) continue;
+      const double cb = base * (nt == nt_model ? 1.0 : kOtherTeamsCost);
+      if (2 * nt * mb * c.BN <= 512 && tiles > (long long)sms * nt) out.push_back({g, nt, 2 * nt, cb});
+      out.push_back({g, nt, nt, cb * kSingleBufCost});
+    }
   }
   if (out.empty()) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
   std::stable_sort(out.begin(), out.end(), [](const ConvCand &x, const ConvCand &y) { return x.cost < y.cost; });
