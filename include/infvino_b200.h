@@ -69,6 +69,8 @@ typedef enum ivc_status {
                                          kernel instead of its load-time compiled (NVRTC) form */
 #define IVC_FLAG_NO_TUNE 0x100u       /* convolution tile geometry from the cost model alone (no timing
                                          of candidate geometries at the first run of a batch size) */
+#define IVC_FLAG_SERIAL 0x200u        /* every step on one stream: the captured graph has no concurrent
+                                         branches (and activations may share more memory) */
 
 /* Loads `plan_path` (+ its init_*.bin files) onto CUDA device `device_ordinal`. */
 int ivc_create(const char *plan_path, int device_ordinal, int max_batch, unsigned flags, ivc_model **out);

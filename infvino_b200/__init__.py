@@ -23,11 +23,11 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 
 from . import _native
-from ._native import (FLAG_DRY_RUN, FLAG_NO_FUSION, FLAG_NO_GRAPH, FLAG_NO_HALO, FLAG_NO_JIT, FLAG_NO_PDL, FLAG_NO_TUNE, FLAG_NO_POOL, FLAG_NO_TENSOR_CORES, NativeError,
+from ._native import (FLAG_DRY_RUN, FLAG_NO_FUSION, FLAG_NO_GRAPH, FLAG_NO_HALO, FLAG_NO_JIT, FLAG_NO_PDL, FLAG_NO_TUNE, FLAG_NO_POOL, FLAG_SERIAL, FLAG_NO_TENSOR_CORES, NativeError,
                       check, lib)
 
 __all__ = ["PlanModel", "CudaBackend", "Tensor", "ModelInfo", "NativeError", "FLAG_DRY_RUN", "FLAG_NO_FUSION",
-           "FLAG_NO_GRAPH", "FLAG_NO_HALO", "FLAG_NO_JIT", "FLAG_NO_PDL", "FLAG_NO_TUNE", "FLAG_NO_POOL", "FLAG_NO_TENSOR_CORES", "f32_to_f16", "f16_to_f32"]
+           "FLAG_NO_GRAPH", "FLAG_NO_HALO", "FLAG_NO_JIT", "FLAG_NO_PDL", "FLAG_NO_TUNE", "FLAG_NO_POOL", "FLAG_SERIAL", "FLAG_NO_TENSOR_CORES", "f32_to_f16", "f16_to_f32"]
 
 
 def f32_to_f16(x: np.ndarray) -> np.ndarray:

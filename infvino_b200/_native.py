@@ -22,6 +22,7 @@ FLAG_NO_HALO = 0x20
 FLAG_NO_PDL = 0x40
 FLAG_NO_JIT = 0x80
 FLAG_NO_TUNE = 0x100
+FLAG_SERIAL = 0x200
 
 # every symbol include/infvino_b200.h declares, with its ctypes signature
 _vp, _cp, _i32, _i64, _u32, _sz, _f64 = (ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int64,

@@ -72,9 +72,12 @@ Engine::Engine(const std::string &plan_path, int device, int max_batch, unsigned
   plan_layouts();
   build_tensors();
   if (!(flags_ & kFlagNoFusion)) plan_tails();
-  allocate();
+  lifetimes();
+  alloc_aux();
   upload_weights();
   lower();
+  plan_streams();
+  allocate();
 }
 
 Engine::~Engine() {
@@ -91,6 +94,13 @@ Engine::~Engine() {
   if (copy_in_) cudaStreamDestroy(copy_in_);
   if (copy_out_) cudaStreamDestroy(copy_out_);
   if (scratch_) cudaFree(scratch_);
+  for (cudaEvent_t e : step_events_)
+    if (e) cudaEventDestroy(e);
+  if (fork_event_) cudaEventDestroy(fork_event_);
+  for (int t = 1; t < kMaxStreams; ++t) {
+    if (join_events_[t]) cudaEventDestroy(join_events_[t]);
+    if (side_[t]) cudaStreamDestroy(side_[t]);
+  }
   if (own_stream_ && stream_) cudaStreamDestroy(stream_);
 }
 
@@ -368,7 +378,7 @@ void Engine::build_tensors() {
 }
 
 // ============================================================================ allocation
-void Engine::allocate() {
+void Engine::lifetimes() {
   const auto &nodes = plan_->nodes();
   const int N = (int)nodes.size();
   auto touch = [&](const std::string &name, int i) {
@@ -386,6 +396,46 @@ void Engine::allocate() {
   }
   for (const auto &u : tail_uses_) touch(T_[(size_t)u.first].name, u.second);  // fused tails read late
   for (const auto &o : plan_->outputs()) T_[(size_t)T_[(size_t)tid(o)].root].death = N;
+}
+
+void Engine::alloc_aux() {
+  if (dry_) return;
+  check(cudaMalloc(&status_, sizeof(int)), "cudaMalloc(status)");
+  check(cudaMemset(status_, 0, sizeof(int)), "cudaMemset(status)");
+  check(cudaMalloc(&in_f32_, (size_t)input_numel() * max_batch_ * sizeof(float)), "cudaMalloc(input f32)");
+}
+
+// Arena placement.  Two roots may share bytes only when every step touching
+// one of them is ordered before every step touching the other, by a
+// dependency or by the order of one stream (plan_streams); the graph input is
+// touched before the first step and the outputs after the last.  With one
+// stream this is the node-order liveness of the serial executor.
+void Engine::allocate() {
+  const int S = (int)steps_.size();
+  const int kSource = -1, kSink = S;
+  std::vector<std::vector<int>> acc(T_.size());
+  for (int j = 0; j < S; ++j) {
+    for (int r : step_reads_[(size_t)j]) acc[(size_t)r].push_back(j);
+    for (int r : step_writes_[(size_t)j]) acc[(size_t)r].push_back(j);
+  }
+  acc[(size_t)T_[(size_t)tid(plan_->input())].root].push_back(kSource);
+  for (const auto &o : plan_->outputs()) acc[(size_t)T_[(size_t)tid(o)].root].push_back(kSink);
+  for (size_t i = 0; i < T_.size(); ++i)  // values passed inside a fused step only
+    if ((int)i == T_[i].root && !T_[i].is_init) T_[i].materialized = !acc[i].empty() || (flags_ & kFlagNoPool);
+  auto reaches = [&](int a, int b) -> bool {  // a finishes before b starts
+    if (a == kSource) return b != kSource;
+    if (b == kSink) return a != kSink;
+    if (a == kSink || b == kSource || a == b) return false;
+    return (reach_[(size_t)a][(size_t)b >> 6] >> (b & 63)) & 1ull;
+  };
+  auto before = [&](int x, int y) -> bool {
+    for (int a : acc[(size_t)x])
+      for (int b : acc[(size_t)y])
+        if (!reaches(a, b)) return false;
+    return true;
+  };
+  const bool no_pool = (flags_ & kFlagNoPool) != 0;  // diagnostics: no reuse, every tensor stays readable
+  auto conflict = [&](int x, int y) { return no_pool || !(before(x, y) || before(y, x)); };
 
   std::vector<int> roots;
   for (size_t i = 0; i < T_.size(); ++i)
@@ -401,12 +451,8 @@ void Engine::allocate() {
     const int64_t sz = bytes_of(r);
     stats_.requested_bytes += sz;
     std::vector<std::pair<int64_t, int64_t>> busy;
-    const bool no_pool = (flags_ & kFlagNoPool) != 0;  // diagnostics: no reuse, every tensor stays readable
-    for (int q : placed) {
-      const TensorRt &a = T_[(size_t)r], &b = T_[(size_t)q];
-      if (no_pool || (a.birth <= b.death && b.birth <= a.death))
-        busy.push_back({b.arena_off, b.arena_off + bytes_of(q)});
-    }
+    for (int q : placed)
+      if (conflict(r, q)) busy.push_back({T_[(size_t)q].arena_off, T_[(size_t)q].arena_off + bytes_of(q)});
     std::sort(busy.begin(), busy.end());
     int64_t cur = 0;
     for (const auto &iv : busy) {
@@ -419,22 +465,18 @@ void Engine::allocate() {
   }
   arena_bytes_ = std::max<int64_t>(top, 256);
   stats_.arena_bytes = arena_bytes_;
-  // self-check: roots with intersecting lifetimes never share bytes
+  // self-check: roots whose accesses are not ordered never share bytes
   for (size_t i = 0; i < placed.size(); ++i)
     for (size_t j = i + 1; j < placed.size(); ++j) {
-      const TensorRt &a = T_[(size_t)placed[i]], &b = T_[(size_t)placed[j]];
-      if (!(a.birth <= b.death && b.birth <= a.death)) continue;
-      const int64_t a0 = a.arena_off, a1 = a0 + bytes_of(placed[i]);
-      const int64_t b0 = b.arena_off, b1 = b0 + bytes_of(placed[j]);
+      if (!conflict(placed[i], placed[j])) continue;
+      const int64_t a0 = T_[(size_t)placed[i]].arena_off, a1 = a0 + bytes_of(placed[i]);
+      const int64_t b0 = T_[(size_t)placed[j]].arena_off, b1 = b0 + bytes_of(placed[j]);
       if (a0 < b1 && b0 < a1) ++stats_.overlap_errors;
     }
   if (stats_.overlap_errors) throw std::runtime_error("CudaPlanModel: activation allocator produced overlaps");
   if (!dry_) {
     check(cudaMalloc(&arena_, (size_t)arena_bytes_), "cudaMalloc(arena)");
     check(cudaMemset(arena_, 0, (size_t)arena_bytes_), "cudaMemset(arena)");
-    check(cudaMalloc(&status_, sizeof(int)), "cudaMalloc(status)");
-    check(cudaMemset(status_, 0, sizeof(int)), "cudaMemset(status)");
-    check(cudaMalloc(&in_f32_, (size_t)input_numel() * max_batch_ * sizeof(float)), "cudaMalloc(input f32)");
   }
   uint8_t *base = dry_ ? nullptr : arena_;
   for (auto &t : T_) {
@@ -1061,6 +1103,9 @@ void Engine::plan_tails() {
     for (int ni : region) elided_nodes_.insert(ni);
     for (int ni : dfl_chain) elided_nodes_.insert(ni);
     elided_nodes_.erase(po->second);
+    st.nodes.assign(region.begin(), region.end());
+    st.nodes.insert(st.nodes.end(), dfl_chain.begin(), dfl_chain.end());
+    if (std::find(st.nodes.begin(), st.nodes.end(), po->second) == st.nodes.end()) st.nodes.push_back(po->second);
     tail_steps_[po->second] = std::move(st);
   }
 }
@@ -1113,6 +1158,7 @@ void Engine::lower() {
     const int out = tid(n.outs[0]);
     Step st;
     st.node = (int)ni;
+    st.nodes = {(int)ni};
     st.name = op + ":" + n.outs[0];
     st.family = op;
 
@@ -1551,6 +1597,8 @@ void Engine::lower() {
         };
         elided_nodes_.insert(sm_node);
         elided_nodes_.insert(cv_node);
+        st.nodes.push_back(sm_node);
+        st.nodes.push_back(cv_node);
         steps_.push_back(std::move(st));
         continue;
       }
@@ -1722,6 +1770,7 @@ void Engine::lower() {
       }
       if (chain.size() > 1) {
         st.family = "maxpool_chain";
+        for (size_t l = 1; l < chain.size(); ++l) st.nodes.push_back((int)(ni + l));
         for (size_t l = 1; l < chain.size(); ++l) st.bytes_img += act_bytes(chain[l]);
         st.launch = [this, x, chain, K, P](int B, cudaStream_t s) {
           View4 ys[3];
@@ -1820,6 +1869,125 @@ void Engine::upload_input_f32(const float *src, int batch, bool on_device) {
   check(launch_f32_to_f16_trunc(d, input_device_ptr(), n, stream_), "input conversion");
 }
 
+// Step dependencies come from the plan nodes each step carries out: two steps
+// touching one storage root, at least one of them writing it, keep their
+// order.  Steps go to streams greedily: a step continues the stream of its
+// latest predecessor when that stream still ends with it, else takes a stream
+// whose last step is already ordered before it, else the least recently used
+// stream.  A step waits (graph edge) for the latest step it depends on in
+// each other stream.  reach_ is the closure of dependencies and stream order:
+// the allocator lets two roots share bytes only along it.
+void Engine::plan_streams() {
+  const auto &nodes = plan_->nodes();
+  const int S = (int)steps_.size();
+  step_reads_.assign((size_t)S, {});
+  step_writes_.assign((size_t)S, {});
+  auto root_of = [&](const std::string &name) -> int {
+    if (name == "-") return -1;
+    const TensorRt &t = T_[(size_t)tid(name)];
+    return t.is_init ? -1 : t.root;
+  };
+  std::vector<std::set<int>> rds((size_t)S), wrs((size_t)S);
+  std::map<int, int> writers;  // root -> steps writing it
+  for (int j = 0; j < S; ++j) {
+    for (int ni : steps_[(size_t)j].nodes) {
+      const PlanNode &n = nodes[(size_t)ni];
+      for (const auto &in : n.ins)
+        if (root_of(in) >= 0) rds[(size_t)j].insert(root_of(in));
+      for (const auto &o : n.outs)
+        if (root_of(o) >= 0) wrs[(size_t)j].insert(root_of(o));
+    }
+    for (int r : wrs[(size_t)j]) ++writers[r];
+  }
+  for (int j = 0; j < S; ++j) {
+    const Step &stp = steps_[(size_t)j];
+    if (stp.family == "decode_tail" || stp.family == "dfl_fused") {
+      // computed in registers: the values the fused nodes pass to each other
+      // (written by this step alone, other than its last node's output) never
+      // reach memory and are no accesses; tensors other steps write (the
+      // in-place concats the region reads) stay reads
+      const int last_node = *std::max_element(stp.nodes.begin(), stp.nodes.end());
+      std::set<int> out;
+      for (const auto &o : nodes[(size_t)last_node].outs)
+        if (root_of(o) >= 0) out.insert(root_of(o));
+      for (int r : wrs[(size_t)j]) {
+        if (out.count(r)) continue;  // the step's own output
+        if (writers[r] > 1)
+          rds[(size_t)j].insert(r);  // another step writes it: a read here
+        else
+          rds[(size_t)j].erase(r);   // a value inside the fused region
+      }
+      wrs[(size_t)j] = out;
+    }
+    step_reads_[(size_t)j].assign(rds[(size_t)j].begin(), rds[(size_t)j].end());
+    step_writes_[(size_t)j].assign(wrs[(size_t)j].begin(), wrs[(size_t)j].end());
+  }
+  auto meets = [](const std::vector<int> &a, const std::vector<int> &b) {
+    size_t i = 0, k = 0;
+    while (i < a.size() && k < b.size()) {
+      if (a[i] == b[k]) return true;
+      if (a[i] < b[k]) ++i;
+      else ++k;
+    }
+    return false;
+  };
+  std::vector<std::vector<int>> preds((size_t)S);
+  for (int j = 0; j < S; ++j)
+    for (int i = 0; i < j; ++i)
+      if (meets(step_writes_[(size_t)i], step_reads_[(size_t)j]) ||
+          meets(step_writes_[(size_t)i], step_writes_[(size_t)j]) ||
+          meets(step_reads_[(size_t)i], step_writes_[(size_t)j]))
+        preds[(size_t)j].push_back(i);
+
+  const int K = (flags_ & kFlagSerial) ? 1 : kMaxStreams;
+  const size_t words = ((size_t)S + 63) / 64;
+  std::vector<std::vector<uint64_t>> anc((size_t)S, std::vector<uint64_t>(words, 0));  // ancestors of j
+  auto is_anc = [&](int a, int j) { return (anc[(size_t)j][(size_t)a >> 6] >> (a & 63)) & 1ull; };
+  auto add_anc = [&](int j, int a) {
+    anc[(size_t)j][(size_t)a >> 6] |= 1ull << (a & 63);
+    for (size_t w = 0; w < words; ++w) anc[(size_t)j][w] |= anc[(size_t)a][w];
+  };
+  stream_of_.assign((size_t)S, 0);
+  waits_.assign((size_t)S, {});
+  signals_.assign((size_t)S, 0);
+  std::vector<int> last((size_t)K, -1), used_at((size_t)K, -1);
+  for (int j = 0; j < S; ++j) {
+    for (int p : preds[(size_t)j]) add_anc(j, p);
+    int st = -1;
+    for (auto it = preds[(size_t)j].rbegin(); it != preds[(size_t)j].rend() && st < 0; ++it)
+      if (last[(size_t)stream_of_[(size_t)*it]] == *it) st = stream_of_[(size_t)*it];
+    if (st < 0)
+      for (int t = 0; t < K && st < 0; ++t)
+        if (last[(size_t)t] < 0 || is_anc(last[(size_t)t], j)) st = t;
+    if (st < 0) {
+      st = 0;
+      for (int t = 1; t < K; ++t)
+        if (used_at[(size_t)t] < used_at[(size_t)st]) st = t;
+    }
+    stream_of_[(size_t)j] = st;
+    if (last[(size_t)st] >= 0) add_anc(j, last[(size_t)st]);  // stream order
+    // waits: the latest predecessor in each other stream, unless already implied
+    std::vector<int> latest((size_t)K, -1);
+    for (int p : preds[(size_t)j])
+      if (stream_of_[(size_t)p] != st) latest[(size_t)stream_of_[(size_t)p]] = std::max(latest[(size_t)stream_of_[(size_t)p]], p);
+    for (int t = 0; t < K; ++t) {
+      const int p = latest[(size_t)t];
+      if (p < 0) continue;
+      if (last[(size_t)st] >= 0 && (last[(size_t)st] == p || is_anc(p, last[(size_t)st]))) continue;
+      waits_[(size_t)j].push_back(p);
+      signals_[(size_t)p] = 1;
+    }
+    last[(size_t)st] = j;
+    used_at[(size_t)st] = j;
+  }
+  n_streams_ = 1;
+  for (int j = 0; j < S; ++j) n_streams_ = std::max(n_streams_, stream_of_[(size_t)j] + 1);
+  reach_.assign((size_t)S, std::vector<uint64_t>(words, 0));
+  for (int j = 0; j < S; ++j)
+    for (int a = 0; a < j; ++a)
+      if (is_anc(a, j)) reach_[(size_t)a][(size_t)j >> 6] |= 1ull << (j & 63);
+}
+
 // One eager pass over the network in plan order; a step with a tuning hook
 // times its candidates where it runs (its inputs are the values the plan
 // gives it there, and repeating it only rewrites its own output, which no
@@ -1854,17 +2022,36 @@ void Engine::tune(int batch) {
 void Engine::capture(int batch) {
   pdl_scope();
   tune(batch);
+  if (n_streams_ > 1 && !side_[1]) {  // side streams and the events that order them, once
+    for (int t = 1; t < n_streams_; ++t) {
+      check(cudaStreamCreateWithFlags(&side_[t], cudaStreamNonBlocking), "cudaStreamCreate");
+      check(cudaEventCreateWithFlags(&join_events_[t], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    check(cudaEventCreateWithFlags(&fork_event_, cudaEventDisableTiming), "cudaEventCreate");
+    step_events_.assign(steps_.size(), nullptr);
+    for (size_t j = 0; j < steps_.size(); ++j)
+      if (signals_[j]) check(cudaEventCreateWithFlags(&step_events_[j], cudaEventDisableTiming), "cudaEventCreate");
+  }
   cudaGraph_t g = nullptr;
   check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
   cudaError_t le = cudaSuccess;
   std::string where;
   try {
-    for (auto &s : steps_) {
-      le = s.launch(batch, stream_);
-      if (le != cudaSuccess) {
-        where = s.name;
-        break;
-      }
+    if (n_streams_ > 1) {  // fork: the side streams start after everything queued before the run
+      le = cudaEventRecord(fork_event_, stream_);
+      for (int t = 1; t < n_streams_ && le == cudaSuccess; ++t) le = cudaStreamWaitEvent(side_[t], fork_event_, 0);
+    }
+    for (size_t j = 0; j < steps_.size() && le == cudaSuccess; ++j) {
+      cudaStream_t st = stream_of_[j] == 0 ? stream_ : side_[stream_of_[j]];
+      for (int p : waits_[j])
+        if (le == cudaSuccess) le = cudaStreamWaitEvent(st, step_events_[(size_t)p], 0);
+      if (le == cudaSuccess) le = steps_[j].launch(batch, st);
+      if (le == cudaSuccess && signals_[j]) le = cudaEventRecord(step_events_[j], st);
+      if (le != cudaSuccess) where = steps_[j].name;
+    }
+    for (int t = 1; t < n_streams_ && le == cudaSuccess; ++t) {  // join
+      le = cudaEventRecord(join_events_[t], side_[t]);
+      if (le == cudaSuccess) le = cudaStreamWaitEvent(stream_, join_events_[t], 0);
     }
   } catch (...) {
     cudaStreamEndCapture(stream_, &g);
@@ -2110,11 +2297,14 @@ std::string Engine::describe() const {
     os << "tensor " << t.name << (t.is_init ? " init" : "") << (t.nhwc ? " nhwc" : " planar") << " root="
        << T_[(size_t)t.root].name << " off=" << t.elem_off;
     if ((int)(&t - &T_[0]) == t.root && !t.is_init)
-      os << " arena=" << t.arena_off << " life=[" << t.birth << "," << t.death << "] bytes/img=" << t.bytes_per_img;
+      os << " arena=" << t.arena_off << " life=[" << t.birth << "," << t.death << "] bytes/img=" << t.bytes_per_img
+         << (t.materialized ? "" : " unmaterialized");
     os << "\n";
   }
   for (const auto &s : steps_) {
     os << "step " << s.family << " " << s.name;
+    const size_t j = (size_t)(&s - &steps_[0]);
+    if (n_streams_ > 1 && j < stream_of_.size()) os << " [stream " << stream_of_[j] << "]";
     if (!s.info.empty()) os << " [" << s.info << "]";
     if (s.geometry)
       for (const auto &g : *s.geometry) os << " [B=" << g.first << " " << g.second << "]";

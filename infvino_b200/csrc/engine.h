@@ -33,6 +33,7 @@ enum EngineFlags : unsigned {
   kFlagNoPdl = 1u << 6,       // launches without programmatic dependent launch
   kFlagNoJit = 1u << 7,       // fused tail on the interpreting kernel instead of load-time compiled code
   kFlagNoTune = 1u << 8,      // convolution tile geometry from the cost model, no timing at load
+  kFlagSerial = 1u << 9,      // every step on one stream (no concurrent branches in the graph)
 };
 
 struct TensorRt {
@@ -50,6 +51,7 @@ struct TensorRt {
   int64_t bytes_per_img = 0;    // roots only
   int64_t arena_off = -1;       // roots only, bytes
   int birth = -1, death = -1;   // roots only, node indices
+  bool materialized = true;     // roots only: some step reads or writes it in memory
   __half *dptr = nullptr;       // element (image 0, offset) on the device
 };
 
@@ -66,6 +68,7 @@ struct Step {
   std::string info;  // load-time facts about the step (describe())
   // optional load-time tuning, run once per batch size before the first launch
   std::function<void(int, cudaStream_t)> tune;
+  std::vector<int> nodes;  // plan nodes this step carries out (its own and the ones fused into it)
 };
 
 struct EngineStats {
@@ -128,9 +131,12 @@ class Engine {
  private:
   void plan_layouts();
   void build_tensors();
-  void allocate();
+  void lifetimes();       // node-order birth / death of every root (fusion checks)
+  void alloc_aux();       // status word and f32 input staging
+  void allocate();        // arena placement over the step DAG, then device pointers
   void upload_weights();
   void lower();
+  void plan_streams();    // step dependencies, stream assignment, reachability
   void check(cudaError_t e, const char *what) const;
   int tid(const std::string &name) const;
   View4 view(int t) const;                 // image-0 view with per-image strides
@@ -154,6 +160,18 @@ class Engine {
   void tune(int batch);    // per-step load-time tuning for this batch size (once)
   std::set<int> tuned_;
   std::vector<Step> steps_;
+  // concurrency: steps run on up to kMaxStreams streams inside the captured
+  // graph; a step waits for the latest step it depends on in every other stream
+  static constexpr int kMaxStreams = 4;
+  std::vector<std::vector<int>> step_reads_, step_writes_;  // roots
+  std::vector<int> stream_of_;                              // per step
+  std::vector<std::vector<int>> waits_;                     // per step: steps on other streams
+  std::vector<char> signals_;                               // per step: another stream waits for it
+  std::vector<std::vector<uint64_t>> reach_;                // step i reaches step j (bitset rows)
+  int n_streams_ = 1;
+  cudaStream_t side_[kMaxStreams] = {};
+  std::vector<cudaEvent_t> step_events_;
+  cudaEvent_t fork_event_ = nullptr, join_events_[kMaxStreams] = {};
   EngineStats stats_;
 
   cudaStream_t stream_ = nullptr;

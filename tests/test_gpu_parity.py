@@ -359,6 +359,24 @@ def test_tuned_geometry_changes_no_bit(plan_dir):
     b.close()
 
 
+@pytest.mark.parametrize("model,batch", [("yolov8n-pose", 3), ("yolo11n-pose", 2), ("mobilenetv3-small", 4)])
+def test_concurrent_branches_equal_serial(model_plans, model, batch):
+    """The graph with the head's branches on side streams gives the same bits
+    as the one-stream graph, and keeps doing so on a second run (no stale or
+    overwritten buffer between concurrent branches)."""
+    p = model_plans[model]
+    a = ivb.PlanModel(p, max_batch=batch)
+    b = ivb.PlanModel(p, max_batch=batch, flags=ivb.FLAG_SERIAL)
+    n = a.inputNumel()
+    for seed in (31, 37):
+        x = np.random.default_rng(seed).random(batch * n, dtype=np.float32)
+        ya, yb = a.infer_f32(x, batch), b.infer_f32(x, batch)
+        for u, v in zip(ya, yb):
+            assert np.array_equal(u, v)
+    a.close()
+    b.close()
+
+
 def test_graph_and_eager_agree(model_plans):
     p = model_plans["mobilenetv3-small"]
     x = np.random.default_rng(9).random(2 * 3 * 224 * 224, dtype=np.float32)

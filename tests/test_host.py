@@ -53,18 +53,24 @@ def test_mobilenet_and_yolo11_plan_facts(model_plans):
 
 
 def test_allocator_reuses_memory_and_views(model_plans):
-    m = dry(model_plans["yolov8n-pose"], 1)
+    m = dry(model_plans["yolov8n-pose"], 1, ivb.FLAG_SERIAL)
     st = m.pool_stats()
     assert st["views"] > 0            # reshape + zero-copy channel splits
     text = m.describe()
-    # every arena placement line has a lifetime; check pairwise disjointness here too
+    # every arena placement line has a lifetime; with one stream, roots whose
+    # node lifetimes intersect never share bytes (values that stay inside a
+    # fused step are not materialized and may)
     roots = []
+    placed = 0
     for line in text.splitlines():
         mm = re.search(r"arena=(\d+) life=\[(-?\d+),(-?\d+)\] bytes/img=(\d+)", line)
         if mm:
+            placed += 1
+            if "unmaterialized" in line:
+                continue
             off, b, d, sz = map(int, mm.groups())
             roots.append((off, off + ((sz + 255) // 256) * 256, b, d))
-    assert len(roots) == st["roots"]
+    assert placed == st["roots"] and len(roots) < placed
     for i in range(len(roots)):
         for j in range(i + 1, len(roots)):
             a, c = roots[i], roots[j]
@@ -149,6 +155,20 @@ def test_fastdiv_formula_exact():
         n = n[(n >= 0) & (n < (1 << 31))].astype(object)
         q = [(int(x) * m) >> (31 + s) for x in n]
         assert q == [int(x) // d for x in n], d
+
+
+def test_head_branches_on_side_streams(model_plans):
+    """The pose head's independent branches are spread over several streams;
+    IVC_FLAG_SERIAL keeps every step on one stream, and then the arena equals
+    the serial liveness packing.  Placement is self-checked (construction
+    throws on an overlap of roots whose accesses are not ordered)."""
+    p = model_plans["yolov8n-pose"]
+    con = ivb.PlanModel(p, device=0, max_batch=8, flags=ivb.FLAG_DRY_RUN)
+    ser = ivb.PlanModel(p, device=0, max_batch=8, flags=ivb.FLAG_DRY_RUN | ivb.FLAG_SERIAL)
+    side = [ln for ln in con.describe().splitlines() if ln.startswith("step") and "[stream " in ln and "[stream 0]" not in ln]
+    assert len(side) >= 9 and all("model.22." in ln or "tail:" in ln for ln in side), side
+    assert not any("[stream " in ln for ln in ser.describe().splitlines())
+    assert ser.pool_stats()["arena_bytes"] <= con.pool_stats()["arena_bytes"]
 
 
 def test_tail_program_compiles(model_plans):
