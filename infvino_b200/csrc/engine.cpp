@@ -2141,6 +2141,10 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
+  // The host->device copy of the f32 input bounds the call; chunks of 16
+  // images keep the network runs ahead of it, and the last chunks shrink
+  // (8, 4) so that what follows the final copy (its run and its results'
+  // copy back) is short.
   constexpr int kChunk = 16;
   if (batch < 2 * kChunk) {  // too small to overlap: one pass
     upload_input_f32(src, batch, false);
@@ -2161,7 +2165,14 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
     check(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking), "cudaStreamCreate");
     check(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking), "cudaStreamCreate");
   }
-  const int n_chunks = (batch + kChunk - 1) / kChunk;
+  std::vector<int> chunk0;  // first image of each chunk (+ the end)
+  for (int b0 = 0; b0 < batch;) {
+    const int rem = batch - b0;
+    chunk0.push_back(b0);
+    b0 += rem >= 2 * kChunk ? kChunk : rem >= kChunk ? kChunk / 2 : rem >= kChunk / 2 ? kChunk / 4 : rem;
+  }
+  chunk0.push_back(batch);
+  const int n_chunks = (int)chunk0.size() - 1;
   while ((int)chunk_events_.size() < 3 * n_chunks + 1) {  // per chunk: copied in, computed; one spare
     cudaEvent_t e;
     check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
@@ -2172,14 +2183,14 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   check(cudaEventRecord(chunk_events_[3 * n_chunks], stream_), "cudaEventRecord");
   check(cudaStreamWaitEvent(copy_in_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   for (int c = 0; c < n_chunks; ++c) {
-    const int b0 = c * kChunk, nb = std::min(kChunk, batch - b0);
+    const int b0 = chunk0[(size_t)c], nb = chunk0[(size_t)c + 1] - b0;
     check(cudaMemcpyAsync(in_f32_ + b0 * in_numel, src + b0 * in_numel, (size_t)(nb * in_numel) * sizeof(float),
                           cudaMemcpyHostToDevice, copy_in_),
           "input copy");
     check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
   }
   for (int c = 0; c < n_chunks; ++c) {
-    const int b0 = c * kChunk, nb = std::min(kChunk, batch - b0);
+    const int b0 = chunk0[(size_t)c], nb = chunk0[(size_t)c + 1] - b0;
     check(cudaStreamWaitEvent(stream_, chunk_events_[3 * c], 0), "cudaStreamWaitEvent");
     check(launch_f32_to_f16_trunc(in_f32_ + b0 * in_numel, input_device_ptr(), nb * in_numel, stream_),
           "input conversion");
