@@ -237,6 +237,39 @@ __device__ __forceinline__ const CUtensorMap *mapA_ptr(const ConvTcArgs &a, int 
   }
 }
 
+// MMAs of one k-block (ksteps k-steps of 16): halo tiles run the nine taps (each a
+// start offset into the window and its weight block), M block after M block
+// so that one accumulator takes its MMAs back to back.  Issued by one lane;
+// tap offsets come from three strides (in 16-byte descriptor units): the
+// window row `hx_u`, the pixel row `ru`, and (stride 2) the phase box
+// `phase_u`; tap t's weights start t * b_tap further.
+__device__ __forceinline__ void issue_kblock(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                             uint32_t b_hi, uint32_t idesc, int ksteps, bool halo, bool s2,
+                                             uint32_t hx_u, uint32_t ru, uint32_t phase_u, uint32_t b_tap, int mb,
+                                             uint32_t mblk_step, int BN, bool first) {
+  for (int j = 0; j < mb; ++j) {
+    const uint32_t d = d_tmem + (uint32_t)(j * BN), aj = a_lo + (uint32_t)j * mblk_step;
+    if (halo) {
+#pragma unroll
+      for (int tap = 0; tap < 9; ++tap) {
+        const int ky = tap / 3, kx = tap % 3;
+        const uint32_t ao = s2 ? (uint32_t)((ky & 1) * 2 + (kx & 1)) * phase_u + (uint32_t)(ky >> 1) * hx_u +
+                                     (uint32_t)(kx >> 1) * ru
+                               : (uint32_t)ky * hx_u + (uint32_t)kx * ru;
+        const uint32_t bo = (uint32_t)tap * b_tap;
+#pragma unroll 1
+        for (int k = 0; k < ksteps; ++k)
+          umma_f16_lh(d, aj + ao + 2u * k, a_hi, b_lo + bo + 2u * k, b_hi, idesc,
+                      (!first || tap != 0 || k != 0) ? 1u : 0u);
+      }
+    } else {
+#pragma unroll 1
+      for (int k = 0; k < ksteps; ++k)
+        umma_f16_lh(d, aj + 2u * k, a_hi, b_lo + 2u * k, b_hi, idesc, (!first || k != 0) ? 1u : 0u);
+    }
+  }
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_constant__ ConvTcArgs a) {
@@ -445,19 +478,11 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       // the next 128 pixel rows of a 1x1 A tile
       const uint32_t mblk_step = (halo ? 8u : 128u) * row_bytes >> 4;
       // halo: tap (dy, dx) starts dy*hx + dx rows into the halo, and its weights
-      // are resident block tap * num_kb + chunk
+      // are resident block tap * num_kb + chunk (streamed: the chunk's nine)
       // (stride 2: phase (ky & 1, kx & 1), row (ky >> 1) * hx + (kx >> 1))
-      uint32_t tap_a[9], tap_b[9];
       const bool s2 = a.halo == 2;
-#pragma unroll
-      for (int tap = 0; tap < 9; ++tap) {
-        const int ky = tap / 3, kx = tap % 3;
-        const uint32_t off = s2 ? (uint32_t)(((ky & 1) * 2 + (kx & 1)) * a.halo_bytes) +
-                                      (uint32_t)((ky >> 1) * hx + (kx >> 1)) * row_bytes
-                                : (uint32_t)(ky * hx + kx) * row_bytes;
-        tap_a[tap] = off >> 4;
-        tap_b[tap] = (uint32_t)(resident_b ? tap * num_kb : tap) * b_step;  // resident: all blocks; ring: the chunk's nine
-      }
+      const uint32_t ru = row_bytes >> 4, hx_u = (uint32_t)hx * ru, phase_u = (uint32_t)a.halo_bytes >> 4;
+      const uint32_t b_tap = (uint32_t)(resident_b ? num_kb : 1) * b_step;
       bool ok = true;
       if (resident_b)
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull));
@@ -482,35 +507,16 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
           }
           CONV_TRACE_SINCE(1);
           tc_fence_after();
-          for (int g = 0; g < kbs; ++g, ++kb) {
-            const uint32_t a_lo = a_lo0 + stage * stage_step + (uint32_t)g * kb_step;
-            if (halo) {
-              const uint32_t b_lo = resident_b ? b_lo0 + (uint32_t)kb * b_step : a_lo + (a_tile >> 4);
-              // M blocks one after another: MMAs into one accumulator back to back
-              for (int j = 0; j < mb; ++j) {
-                const uint32_t d = d_tmem + (uint32_t)(j * BN), aj = a_lo + (uint32_t)j * mblk_step;
-#pragma unroll
-                for (int tap = 0; tap < 9; ++tap) {
-#pragma unroll
-                  for (int k = 0; k < 4; ++k) {
-                    if (k < ksteps && leader)
-                      umma_f16_lh(d, aj + tap_a[tap] + 2u * k, a_hi, b_lo + tap_b[tap] + 2u * k, b_hi, idesc,
-                                  (kb | tap | k) != 0 ? 1u : 0u);
-                  }
-                }
-              }
-              continue;
-            }
-            const uint32_t b_lo = resident_b ? b_lo0 + (uint32_t)kb * b_step : a_lo + (a_tile >> 4);
-            for (int j = 0; j < mb; ++j) {
-              const uint32_t d = d_tmem + (uint32_t)(j * BN), aj = a_lo + (uint32_t)j * mblk_step;
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                if (k < ksteps && leader)
-                  umma_f16_lh(d, aj + 2u * k, a_hi, b_lo + 2u * k, b_hi, idesc, (kb | k) != 0 ? 1u : 0u);
-              }
+          if (leader) {  // one divergent region per stage; the loops inside are exact
+            for (int g = 0; g < kbs; ++g) {
+              const uint32_t a_lo = a_lo0 + stage * stage_step + (uint32_t)g * kb_step;
+              const uint32_t b_lo = resident_b ? b_lo0 + (uint32_t)(kb + g) * b_step : a_lo + (a_tile >> 4);
+              const bool first = kb + g == 0;
+              issue_kblock(d_tmem, a_lo, a_hi, b_lo, b_hi, idesc, ksteps, halo, s2, hx_u, ru, phase_u, b_tap, mb,
+                           mblk_step, BN, first);
             }
           }
+          kb += kbs;
           if (leader) umma_commit(smem_u32(&empty_bar[stage]));  // slot free once these MMAs retire
           __syncwarp();
           if (++stage == (uint32_t)stages) {
