@@ -213,6 +213,9 @@ void Engine::plan_layouts() {
     }
     p.fuse_concat_conv1x1(allowed);
     p.fuse_residual_add();
+    std::vector<std::string> merged;
+    p.fuse_sibling_convs(nhwc_names_, &merged);
+    nhwc_names_.insert(merged.begin(), merged.end());
   }
   stats_.fusions_concat = p.fusions_concat;
   stats_.fusions_res = p.fusions_res;
@@ -578,11 +581,11 @@ bool conv_geom(const ConvCfg &c, int mb, ConvGeom *g) {
   ConvGeom r;
   r.mb = mb;
   if (c.ksize == 3 && !c.halo) {
-    if (mb != 1) return false;
-    if (c.Wo % 16 == 0) {
+    if (c.Wo % 16 == 0) {  // M block j: rows 8j .. 8j+7 of a 16-wide tile
       r.TW = 16;
-      r.TH = 8;
+      r.TH = 8 * mb;
     } else {
+      if (mb != 1) return false;
       r.TW = std::min(c.Wo, 128);
       r.TH = std::max(1, 128 / r.TW);
     }
@@ -652,7 +655,7 @@ struct ConvCand {
 };
 std::vector<ConvCand> conv_candidates(const ConvCfg &c, int B, int sms) {
   std::vector<ConvCand> out;
-  const int max_mb = (c.ksize == 3 && !c.halo) ? 1 : 8;
+  const int max_mb = (c.ksize == 3 && !c.halo && c.Wo % 16 != 0) ? 1 : 8;
   for (int mb = 1; mb <= max_mb; ++mb) {
     ConvGeom g;
     if (!conv_geom(c, mb, &g)) continue;
@@ -1210,7 +1213,8 @@ void Engine::lower() {
       }
       c.taps = c.ksize * c.ksize;
       // FLOPs / bytes (algorithmic, per image) for the roofline
-      st.flops_img = 2.0 * c.cout * c.cin_total * c.taps * (double)c.Ho * c.Wo;
+      // (merged sibling convolutions: the members' channels, not the padding)
+      st.flops_img = 2.0 * n.ai("alg_cout", c.cout) * c.cin_total * c.taps * (double)c.Ho * c.Wo;
       for (int s = 0; s < c.nsrc; ++s) st.bytes_img += act_bytes(c.src[s]);
       st.bytes_img += act_bytes(out) + (c.res >= 0 ? act_bytes(c.res) : 0.0);
       st.bytes_fixed = init_bytes(w) + (bias >= 0 ? init_bytes(bias) : 0.0);

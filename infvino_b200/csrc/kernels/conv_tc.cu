@@ -108,6 +108,9 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
   const int tyr = ksize == 1 ? 0 : a.halo ? row >> 3 : (int)fdiv((uint32_t)row, a.fd_tw);
   const int txr = ksize == 1 ? 0 : row - tyr * tw_row;
   const bool row_in_tile = row < a.tile_rows;
+  // M block j of a 3x3 tile: eight columns further (halo windows) or eight
+  // rows further (one box per tap: 16-pixel-wide tiles of 8 * mb rows)
+  const int jx = a.halo ? 8 : 0, jy = a.halo ? 0 : 8;
 
   // bias of chunk cc (tile-relative column) of the current N tile; the bias is
   // padded to the N tile, so 8 values are always readable
@@ -159,7 +162,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
         const int b = (int)fdiv((uint32_t)mt, fd_tpi);
         const int rem = mt - b * tiles_per_img;
         const int ty = (int)fdiv((uint32_t)rem, fd_tx);
-        const int oy = ty * TH + tyr, ox = (rem - ty * tiles_x) * TW + txr + 8 * j;
+        const int oy = ty * TH + tyr + jy * j, ox = (rem - ty * tiles_x) * TW + txr + jx * j;
         valid = row_in_tile && oy < Ho && ox < Wo;
         obase = (long long)b * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
         rbase = (long long)b * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
@@ -592,7 +595,7 @@ bool conv_tc_finalize(ConvTcArgs &a, const char **why) {
     if (why) *why = "conv k-blocks per stage must divide the k-block count";
     return false;
   }
-  if (a.mb < 1 || (a.mb > 1 && a.ksize == 3 && !a.halo)) {
+  if (a.mb < 1 || (a.mb > 1 && a.ksize == 3 && !a.halo && (a.TW != 16 || a.TH != 8 * a.mb))) {
     if (why) *why = "conv M blocks per tile out of range";
     return false;
   }

@@ -43,7 +43,7 @@ struct alignas(64) ConvTcArgs {
   // side in TMEM (columns j*BN .. of the tile's buffer for block j)
   long long m_total;              // pixels (B*Ho*Wo)
   int m_tiles;
-  int mb;                         // M blocks per tile (1x1 and 3x3 halo; 1 otherwise)
+  int mb;                         // M blocks per tile (3x3 with one box per tap: only 16-wide tiles)
   int Ho, Wo, TH, TW, tiles_x, tiles_per_img;
   int tile_rows;                  // rows of an M block that hold pixels (TH*TW or 128)
   // 3x3 halo mode (halo = the stride, 1 or 2; 0 = one box per tap): the input

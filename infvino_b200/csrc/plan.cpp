@@ -3,6 +3,7 @@
 // `fuseConcatConv1x1` and `fuseResidualAdd` (src/PlanModel.cpp:447-740).
 #include "plan.h"
 
+#include <algorithm>
 #include <cstdlib>
 #include <fstream>
 #include <set>
@@ -219,6 +220,119 @@ int Plan::fuse_residual_add() {
     nodes_ = std::move(kept);
   }
   fusions_res += fused;
+  return fused;
+}
+
+int Plan::fuse_sibling_convs(const std::set<std::string> &channels_last, std::vector<std::string> *merged_outputs) {
+  std::map<std::string, int> uses;
+  for (const auto &n : nodes_)
+    for (const auto &in : n.ins)
+      if (in != "-") ++uses[in];
+  auto opt_in = [](const PlanNode &n, size_t k) { return n.ins.size() > k ? n.ins[k] : std::string("-"); };
+  // members keyed by everything that must agree: op, input, geometry,
+  // activation and the weight shape past the output-channel axis
+  std::map<std::string, std::vector<size_t>> groups;
+  for (size_t i = 0; i < nodes_.size(); ++i) {
+    const PlanNode &n = nodes_[i];
+    const bool c3 = n.op == "conv3x3", c1 = n.op == "conv1x1";
+    if (!(c3 || c1) || n.outs.size() != 1) continue;
+    const std::string x = c3 ? opt_in(n, 0) : opt_in(n, 1), w = c3 ? opt_in(n, 1) : opt_in(n, 0), b = opt_in(n, 2);
+    if (x == "-" || w == "-" || opt_in(n, 3) != "-" || opt_in(n, 4) != "-") continue;  // no residual / scale
+    const PlanTensor &wt = T_.at(w), &ot = T_.at(n.outs[0]);
+    if (!wt.is_init || wt.dims.size() < 2 || (int64_t)wt.host.size() != wt.numel()) continue;
+    if (b != "-" && (!T_.at(b).is_init || T_.at(b).numel() != wt.dims[0] ||
+                     (int64_t)T_.at(b).host.size() != wt.dims[0]))
+      continue;
+    if (ot.is_output || ot.dims.size() != 4 || ot.dims[1] != wt.dims[0] || !channels_last.count(n.outs[0]) ||
+        !channels_last.count(x))
+      continue;
+    std::string key = n.op + "|" + x + "|" + (b == "-" ? "nb" : "b");
+    for (const char *k : {"stride", "pad", "Hout", "Wout", "act"}) key += "|" + std::to_string(n.ai(k, -1));
+    for (size_t d = 1; d < wt.dims.size(); ++d) key += "|" + std::to_string(wt.dims[d]);
+    for (size_t d = 2; d < 4; ++d) key += "|" + std::to_string(ot.dims[d]);
+    groups[key].push_back(i);
+  }
+  std::vector<char> drop(nodes_.size(), 0);
+  std::map<size_t, std::vector<PlanNode>> replace;  // first member -> merged node + views
+  int fused = 0;
+  for (const auto &g : groups) {
+    const std::vector<size_t> &mem = g.second;
+    if (mem.size() < 2) continue;
+    const PlanNode &first = nodes_[mem[0]];
+    const bool c3 = first.op == "conv3x3";
+    const std::string wname = c3 ? first.ins[1] : first.ins[0], bname = opt_in(first, 2);
+    const PlanTensor &w0 = T_.at(wname);
+    const int64_t per = w0.numel() / w0.dims[0];  // weights per output channel
+    int64_t ctot = 0, calg = 0;
+    std::vector<int64_t> off;
+    for (size_t j : mem) {
+      const int64_t co = T_.at(c3 ? nodes_[j].ins[1] : nodes_[j].ins[0]).dims[0];
+      off.push_back(ctot);
+      ctot += (co + 7) / 8 * 8;  // channel views start on 16-byte boundaries
+      calg += co;
+    }
+    const std::string tag = "siblings:" + first.outs[0];
+    if (T_.count(tag) || T_.count(tag + ".weight") || T_.count(tag + ".bias")) continue;
+    PlanTensor mw;
+    mw.name = tag + ".weight";
+    mw.dims = w0.dims;
+    mw.dims[0] = ctot;
+    mw.is_init = true;
+    mw.host.assign((size_t)(ctot * per), 0);
+    PlanTensor mb;
+    mb.name = tag + ".bias";
+    mb.dims = {ctot};
+    mb.is_init = true;
+    mb.host.assign((size_t)ctot, 0);
+    PlanTensor mo = T_.at(first.outs[0]);
+    mo.name = tag;
+    mo.dims[1] = ctot;
+    mo.file.clear();
+    PlanNode m = first;
+    m.ins = c3 ? std::vector<std::string>{first.ins[0], mw.name, bname == "-" ? "-" : mb.name, "-"}
+               : std::vector<std::string>{mw.name, first.ins[1], bname == "-" ? "-" : mb.name, "-"};
+    m.outs = {tag};
+    m.attr["alg_cout"] = std::to_string(calg);
+    std::vector<PlanNode> seq{m};
+    for (size_t k = 0; k < mem.size(); ++k) {
+      const PlanNode &n = nodes_[mem[k]];
+      const PlanTensor &wt = T_.at(c3 ? n.ins[1] : n.ins[0]);
+      std::copy(wt.host.begin(), wt.host.end(), mw.host.begin() + off[k] * per);
+      if (bname != "-") {
+        const PlanTensor &bt = T_.at(n.ins[2]);
+        std::copy(bt.host.begin(), bt.host.end(), mb.host.begin() + off[k]);
+      }
+      const PlanTensor &ot = T_.at(n.outs[0]);
+      PlanNode v;
+      v.op = "copy_c";
+      v.ins = {tag};
+      v.outs = n.outs;
+      v.attr["c0"] = std::to_string(off[k]);
+      v.attr["cnt"] = std::to_string(ot.dims[1]);
+      v.attr["HW"] = std::to_string(ot.dims[2] * ot.dims[3]);
+      v.attr["dst_off"] = "0";
+      seq.push_back(v);
+      drop[mem[k]] = 1;
+    }
+    T_[mw.name] = std::move(mw);
+    if (bname != "-") T_[mb.name] = std::move(mb);
+    T_[tag] = std::move(mo);
+    replace[mem[0]] = std::move(seq);
+    if (merged_outputs) merged_outputs->push_back(tag);
+    ++fused;
+  }
+  if (fused) {
+    std::vector<PlanNode> kept;
+    for (size_t i = 0; i < nodes_.size(); ++i) {
+      auto it = replace.find(i);
+      if (it != replace.end())
+        for (auto &n : it->second) kept.push_back(std::move(n));
+      else if (!drop[i])
+        kept.push_back(std::move(nodes_[i]));
+    }
+    nodes_ = std::move(kept);
+  }
+  fusions_sibling += fused;
   return fused;
 }
 

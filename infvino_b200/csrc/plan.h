@@ -4,6 +4,7 @@
 
 #include <cstdint>
 #include <map>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -53,6 +54,15 @@ class Plan {
   // `allow_cat` filters which concat outputs may be fused (layout constraint).
   int fuse_concat_conv1x1(const std::vector<std::string> &allowed_concat_outputs);
   int fuse_residual_add();
+  //  * sibling convolutions (same op, input, geometry and activation, no
+  //    residual) become one convolution over the members' output channels side
+  //    by side, each member padded to a multiple of 8 channels with zero weight
+  //    rows, and every member output a channel view of it (copy_c at its
+  //    offset, zero-copy for channels-last tensors).  Members and input must be
+  //    in `channels_last`; the merged outputs are appended to `merged_outputs`.
+  //    The merged node carries `alg_cout` (the members' channel total) for the
+  //    algorithmic FLOP count.
+  int fuse_sibling_convs(const std::set<std::string> &channels_last, std::vector<std::string> *merged_outputs);
 
   const std::string &path() const { return path_; }
   const std::string &dir() const { return dir_; }
@@ -66,7 +76,7 @@ class Plan {
   const PlanTensor &ref(const std::string &name) const;
   bool has(const std::string &name) const { return T_.count(name) != 0; }
 
-  int fusions_concat = 0, fusions_res = 0;
+  int fusions_concat = 0, fusions_res = 0, fusions_sibling = 0;
 
  private:
   std::string path_, dir_, input_;

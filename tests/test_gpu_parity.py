@@ -116,12 +116,23 @@ MULTIBLOCK = [  # cin, cout, input hw, ksize, stride, batch, residual
 ]
 
 
-@pytest.mark.parametrize("cin,cout,hw,k,s,batch,res", MULTIBLOCK)
-def test_conv_multiblock_tiles(plan_dir, cin, cout, hw, k, s, batch, res):
+# 3x3 convs with one TMA box per tap (IVC_FLAG_NO_HALO, and the path of
+# convolutions whose weights fit no halo stage): 16-pixel-wide tiles of 8 * mb
+# rows, M block j being rows 8j .. 8j+7; partial tiles at the bottom edge.
+MULTIBLOCK_BOXES = [
+    (32, 32, 64, 3, 1, 16, True),
+    (16, 32, 128, 3, 2, 16, False),
+    (64, 51, 80, 3, 1, 16, False),
+]
+
+
+@pytest.mark.parametrize("cin,cout,hw,k,s,batch,res,boxes",
+                         [c + (False,) for c in MULTIBLOCK] + [c + (True,) for c in MULTIBLOCK_BOXES])
+def test_conv_multiblock_tiles(plan_dir, cin, cout, hw, k, s, batch, res, boxes):
     p = plangen.op_conv(os.path.join(plan_dir, f"mb_{cin}_{cout}_{hw}_{k}_{s}_{int(res)}"), cin, cout, hw, hw, k, s,
                         act=1, residual=res, producer=True)
     # the cost model's geometry (load-time tuning could pick one M block)
-    o, m = run_both(p, batch, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_TUNE)
+    o, m = run_both(p, batch, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_TUNE | (ivb.FLAG_NO_HALO if boxes else 0))
     geo = [ln for ln in m.describe().splitlines() if ln.startswith("step conv") and "_tc " in ln]
     assert geo and all(f"[B={batch} mb=" in ln for ln in geo), geo
     assert any(f"[B={batch} mb=1 " not in ln for ln in geo), geo  # several M blocks per tile
@@ -308,17 +319,23 @@ def test_batched_equals_single(model_plans):
 
 
 def test_head_fusions_bit_identical(plan_dir):
-    """Concat-in-place and the fused DFL step change no output bit: the default
-    handle equals a NO_FUSION handle (the plan run node by node, plus no CAT4/RES
-    rewrites) on the decoded output, and the in-place head tensors read back the same."""
+    """Concat-in-place, the merged sibling convolutions and the fused DFL step
+    change no output bit: the default handle equals a NO_FUSION handle (the plan
+    run node by node, plus no CAT4/RES rewrites) on the decoded output, and the
+    in-place and merged head tensors read back the same.  Both handles use one
+    TMA box per tap for 3x3 convs: a merged head conv's weights fit no halo
+    stage, and the halo tiles sum a multi-chunk conv's k-blocks chunk by chunk
+    where the per-tap boxes go tap by tap."""
     p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_320"), imgsz=320)
     n = 3 * 320 * 320
     x = np.random.default_rng(17).random(2 * n, dtype=np.float32)
-    a = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_POOL)
-    b = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_FUSION)
+    a = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_HALO)
+    b = ivb.PlanModel(p, max_batch=2, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_HALO | ivb.FLAG_NO_FUSION)
+    assert any(ln.startswith("step conv3x3_tc conv3x3:siblings:") for ln in a.describe().splitlines())
     ya, yb = a.infer_f32(x, 2)[0], b.infer_f32(x, 2)[0]
     assert np.array_equal(ya, yb)
-    for name in ("model.22.cv2.1.2.out", "model.22.cv4.2.2.out", "model.22.cv3.0.2.out"):
+    for name in ("model.22.cv2.1.2.out", "model.22.cv4.2.2.out", "model.22.cv3.0.2.out", "model.22.cv4.0.0.out",
+                 "model.22.cv2.1.0.out", "model.22.cv3.2.0.out"):
         assert np.array_equal(a.readTensor(name, 2), b.readTensor(name, 2)), name
     a.close()
     b.close()

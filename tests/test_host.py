@@ -218,3 +218,25 @@ def test_head_concats_in_place_and_tail_fused(model_plans):
     d = fused.describe()
     assert "tensor model.22.cv2.0.2.out planar root=model.22.box_cat off=0" in d
     assert "tensor model.22.cv2.1.2.out planar root=model.22.box_cat off=6400" in d
+
+
+def test_sibling_convs_merged(model_plans):
+    """The pose head's first three convolutions at each scale read one input
+    with one geometry: they become one convolution over their output channels
+    side by side (each member padded to a multiple of 8), the member outputs
+    channel views of it at 16-byte aligned offsets; the merged step counts the
+    members' FLOPs, not the padding.  NO_FUSION keeps them separate."""
+    p = model_plans["yolov8n-pose"]
+    m = dry(p, 2)
+    plain = {s["name"]: s for s in dry(p, 2, ivb.FLAG_NO_FUSION).steps()}
+    d = m.describe()
+    merged = {s["name"]: s for s in m.steps() if ":siblings:" in s["name"]}
+    assert len(merged) == 3
+    assert not any(":siblings:" in n for n in plain)
+    for scale in range(3):
+        root = f"siblings:model.22.cv4.{scale}.0.out"
+        for br, off in (("cv4", 0), ("cv2", 56), ("cv3", 120)):
+            assert f"tensor model.22.{br}.{scale}.0.out nhwc root={root} off={off}" in d, (br, scale)
+            assert f"conv3x3:model.22.{br}.{scale}.0.out" not in {s["name"] for s in m.steps()}
+        want = sum(plain[f"conv3x3:model.22.{br}.{scale}.0.out"]["flops_per_image"] for br in ("cv2", "cv3", "cv4"))
+        assert merged["conv3x3:" + root]["flops_per_image"] == want
