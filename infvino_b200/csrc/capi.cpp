@@ -11,6 +11,7 @@
 
 #include "../../include/infvino_b200.h"
 #include "engine.h"
+#include "host_cast.h"
 
 struct ivc_model {
   std::unique_ptr<ivb::Engine> eng;
@@ -58,16 +59,6 @@ int status_check(ivc_model *m) {
 }
 
 // include/infvino/Half.hpp:14-24 (truncating) and :26-47 (exact widening)
-inline uint16_t f2h_trunc(float f) {
-  uint32_t x;
-  std::memcpy(&x, &f, 4);
-  const uint32_t sign = (x >> 16) & 0x8000u;
-  const int32_t e = (int32_t)((x >> 23) & 0xff) - 112;
-  const uint32_t mant = x & 0x7fffffu;
-  if (e <= 0) return (uint16_t)sign;
-  if (e >= 31) return (uint16_t)(sign | 0x7c00u);
-  return (uint16_t)(sign | ((uint32_t)e << 10) | (mant >> 13));
-}
 inline float h2f(uint16_t h) {
   const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
   uint32_t e = (h >> 10) & 0x1fu, mant = h & 0x3ffu, f;
@@ -405,11 +396,7 @@ int ivc_describe(const ivc_model *m, char *buf, size_t cap) {
   return (int)d.size();
 }
 
-void ivc_f32_to_f16(const float *in, uint16_t *out, size_t n) {
-  parallel_for(n, [&](size_t b, size_t e) {
-    for (size_t i = b; i < e; ++i) out[i] = f2h_trunc(in[i]);
-  });
-}
+void ivc_f32_to_f16(const float *in, uint16_t *out, size_t n) { ivb::f32_to_f16_trunc_host(in, out, n); }
 
 void ivc_f16_to_f32(const uint16_t *in, float *out, size_t n) {
   parallel_for(n, [&](size_t b, size_t e) {

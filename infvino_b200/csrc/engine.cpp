@@ -10,6 +10,7 @@
 //   planBlockedLayout / LayoutSolver .. Engine::plan_layouts (NHWC vs planar)
 //   run() dispatch + capture/replay ... Engine::lower + CUDA graph per batch size
 #include "engine.h"
+#include "host_cast.h"
 
 #include <algorithm>
 #include <functional>
@@ -90,6 +91,7 @@ Engine::~Engine() {
   if (status_) cudaFree(status_);
   if (in_f32_) cudaFree(in_f32_);
   if (out_f32_) cudaFree(out_f32_);
+  if (in_f16_host_) cudaFreeHost(in_f16_host_);
   for (cudaEvent_t e : chunk_events_) cudaEventDestroy(e);
   if (copy_in_) cudaStreamDestroy(copy_in_);
   if (copy_out_) cudaStreamDestroy(copy_out_);
@@ -2145,10 +2147,12 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
-  // The host->device copy of the f32 input bounds the call; chunks of 16
-  // images keep the network runs ahead of it, and the last chunks shrink
-  // (8, 4) so that what follows the final copy (its run and its results'
-  // copy back) is short.
+  // The host->device copy of the input bounds the call.  Large batches cast
+  // the f32 input to fp16 on the host (the reference's truncation, on the
+  // worker pool) into one of two pinned chunk buffers, so the copy carries
+  // half the bytes; chunks of 16 images keep the network runs ahead of the
+  // copies, and the last chunks shrink (8, 4) so that what follows the final
+  // copy (its run and its results' copy back) is short.
   constexpr int kChunk = 16;
   if (batch < 2 * kChunk) {  // too small to overlap: one pass
     upload_input_f32(src, batch, false);
@@ -2164,51 +2168,101 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
     if (!T_[(size_t)tid(output_name(i))].dense) throw std::runtime_error("CudaPlanModel: output is not planar");
     out_off[i + 1] = out_off[i] + out_numel[i] * max_batch_;
   }
+  const int64_t in_numel = input_numel();
   if (!out_f32_) {
     check(cudaMalloc(&out_f32_, (size_t)out_off[n_out] * sizeof(float)), "cudaMalloc(output f32 staging)");
     check(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking), "cudaStreamCreate");
     check(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaHostAlloc(reinterpret_cast<void **>(&in_f16_host_), (size_t)(2 * kChunk * in_numel) * sizeof(uint16_t),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(input fp16 chunks)");
   }
-  std::vector<int> chunk0;  // first image of each chunk (+ the end)
-  for (int b0 = 0; b0 < batch;) {
+  // Split: images [0, n16) are cast on the host and cross as fp16, images
+  // [n16, batch) cross as f32 first (no host work, so the link starts at once)
+  // and are cast on the device.  A host cast moves 8 bytes of host memory per
+  // element (f32 read, fp16 write, fp16 read by the copy) against 4 for an
+  // f32 copy, so on a host whose memory bandwidth the copy engines already
+  // share, casting everything on the host is slower than casting nothing; half
+  // the batch (a multiple of 4, so that chunks take sizes 16, 8, 4, 2 or 1,
+  // each with its graph captured once) was the fastest split measured.
+  const int n16 = batch / 2 / 4 * 4;
+  // the fp16 images [0, n16) travel into the front of the f32 staging (2 bytes
+  // per element), the f32 images [n16, batch) into their own place (4 bytes)
+  uint16_t *in_f16_dev = reinterpret_cast<uint16_t *>(in_f32_);
+  struct Chunk {
+    int b0, nb;
+    bool host;  // cast on the host
+  };
+  std::vector<Chunk> chunks;
+  for (int b0 = n16; b0 < batch;) {
     const int rem = batch - b0;
-    chunk0.push_back(b0);
-    b0 += rem >= 2 * kChunk ? kChunk : rem >= kChunk ? kChunk / 2 : rem >= kChunk / 2 ? kChunk / 4 : rem;
+    const int nb = rem >= kChunk ? kChunk : rem >= 8 ? 8 : rem >= 4 ? 4 : rem >= 2 ? 2 : 1;
+    chunks.push_back({b0, nb, false});
+    b0 += nb;
   }
-  chunk0.push_back(batch);
-  const int n_chunks = (int)chunk0.size() - 1;
+  for (int b0 = 0; b0 < n16;) {  // the last copies shrink (8, 4) so that what follows them is short
+    const int rem = n16 - b0;
+    const int nb = rem >= 2 * kChunk ? kChunk : rem >= kChunk ? kChunk / 2 : 4;
+    chunks.push_back({b0, nb, true});
+    b0 += nb;
+  }
+  const int n_chunks = (int)chunks.size();
   while ((int)chunk_events_.size() < 3 * n_chunks + 1) {  // per chunk: copied in, computed; one spare
     cudaEvent_t e;
     check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
     chunk_events_.push_back(e);
   }
-  const int64_t in_numel = input_numel();
   // the copy streams start after whatever the compute stream already holds
   check(cudaEventRecord(chunk_events_[3 * n_chunks], stream_), "cudaEventRecord");
   check(cudaStreamWaitEvent(copy_in_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
-  for (int c = 0; c < n_chunks; ++c) {
-    const int b0 = chunk0[(size_t)c], nb = chunk0[(size_t)c + 1] - b0;
-    check(cudaMemcpyAsync(in_f32_ + b0 * in_numel, src + b0 * in_numel, (size_t)(nb * in_numel) * sizeof(float),
-                          cudaMemcpyHostToDevice, copy_in_),
-          "input copy");
-    check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
-  }
-  for (int c = 0; c < n_chunks; ++c) {
-    const int b0 = chunk0[(size_t)c], nb = chunk0[(size_t)c + 1] - b0;
+  // compute and results of one chunk, once its input has arrived
+  auto finish = [&](int c) {
+    const Chunk &k = chunks[(size_t)c];
     check(cudaStreamWaitEvent(stream_, chunk_events_[3 * c], 0), "cudaStreamWaitEvent");
-    check(launch_f32_to_f16_trunc(in_f32_ + b0 * in_numel, input_device_ptr(), nb * in_numel, stream_),
-          "input conversion");
-    run(nb);  // images 0 .. nb-1 of the arena
+    if (k.host)
+      check(cudaMemcpyAsync(input_device_ptr(), in_f16_dev + k.b0 * in_numel,
+                            (size_t)(k.nb * in_numel) * sizeof(uint16_t), cudaMemcpyDeviceToDevice, stream_),
+            "input staging copy");
+    else
+      check(launch_f32_to_f16_trunc(in_f32_ + k.b0 * in_numel, input_device_ptr(), k.nb * in_numel, stream_),
+            "input conversion");
+    run(k.nb);  // images 0 .. nb-1 of the arena
     for (int i = 0; i < n_out; ++i)
-      check(launch_f16_to_f32(T_[(size_t)tid(output_name(i))].dptr, out_f32_ + out_off[i] + b0 * out_numel[i],
-                              nb * out_numel[i], stream_),
+      check(launch_f16_to_f32(T_[(size_t)tid(output_name(i))].dptr, out_f32_ + out_off[i] + k.b0 * out_numel[i],
+                              k.nb * out_numel[i], stream_),
             "output conversion");
     check(cudaEventRecord(chunk_events_[3 * c + 1], stream_), "cudaEventRecord");
     check(cudaStreamWaitEvent(copy_out_, chunk_events_[3 * c + 1], 0), "cudaStreamWaitEvent");
     for (int i = 0; i < n_out; ++i)
-      check(cudaMemcpyAsync(outs[i] + b0 * out_numel[i], out_f32_ + out_off[i] + b0 * out_numel[i],
-                            (size_t)(nb * out_numel[i]) * sizeof(float), cudaMemcpyDeviceToHost, copy_out_),
+      check(cudaMemcpyAsync(outs[i] + k.b0 * out_numel[i], out_f32_ + out_off[i] + k.b0 * out_numel[i],
+                            (size_t)(k.nb * out_numel[i]) * sizeof(float), cudaMemcpyDeviceToHost, copy_out_),
             "output copy");
+  };
+  // f32 chunks: every copy queued at once
+  for (int c = 0; c < n_chunks; ++c) {
+    const Chunk &k = chunks[(size_t)c];
+    if (k.host) continue;
+    check(cudaMemcpyAsync(in_f32_ + k.b0 * in_numel, src + k.b0 * in_numel, (size_t)(k.nb * in_numel) * sizeof(float),
+                          cudaMemcpyHostToDevice, copy_in_),
+          "input copy");
+    check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
+  }
+  for (int c = 0; c < n_chunks; ++c)
+    if (!chunks[(size_t)c].host) finish(c);
+  // fp16 chunks: cast on the host into one of two pinned buffers, then copied
+  for (int c = 0, j = 0; c < n_chunks; ++c) {
+    const Chunk &k = chunks[(size_t)c];
+    if (!k.host) continue;
+    uint16_t *pinned = in_f16_host_ + (size_t)(j & 1) * kChunk * in_numel;
+    // the copy that last read this pinned buffer (two fp16 chunks back) must be done
+    if (j >= 2) check(cudaEventSynchronize(chunk_events_[3 * (c - 2)]), "cudaEventSynchronize");
+    f32_to_f16_trunc_host(src + k.b0 * in_numel, pinned, (size_t)(k.nb * in_numel));
+    check(cudaMemcpyAsync(in_f16_dev + k.b0 * in_numel, pinned, (size_t)(k.nb * in_numel) * sizeof(uint16_t),
+                          cudaMemcpyHostToDevice, copy_in_),
+          "input copy");
+    check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
+    finish(c);
+    ++j;
   }
   check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");

@@ -182,6 +182,7 @@ class Engine {
   int *status_ = nullptr;           // device status word
   float *in_f32_ = nullptr;         // device staging for f32 input
   float *out_f32_ = nullptr;        // device staging for f32 outputs (pipelined infer)
+  uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
   cudaStream_t copy_in_ = nullptr, copy_out_ = nullptr;
   std::vector<cudaEvent_t> chunk_events_;
   __half *scratch_ = nullptr;       // read_tensor staging
