@@ -92,7 +92,10 @@ int ivc_max_batch(const ivc_model *m);
 /* ClBackend::infer: `input` holds batch*input_numel f32 values (host memory,
  * pinned or pageable); converted to fp16 with the reference's truncating cast,
  * run, and every output written as f32 to outputs[i] (batch*output_numel(i)
- * values, host memory).  Synchronous. */
+ * values, host memory).  Synchronous.  Batches of 32 or more are pipelined in
+ * chunks, and half of their images are cast on the host by a process-wide
+ * pool of worker threads (up to 16, created at the first such call), so that
+ * fewer bytes cross PCIe; the first call also pins two chunk buffers. */
 int ivc_infer_f32(ivc_model *m, const float *input, size_t numel, int batch, float *const *outputs);
 
 /* PlanModel-style split calls (fp16 host buffers, synchronous). */
