@@ -724,11 +724,21 @@ __global__ void resize_up_nhwc8_k(View4 x, View4 y, int S, unsigned row8, unsign
 // Chained KxK stride-1 max pools (pad P, out-of-image taps skipped), one block
 // per (8-channel group, image) with the plane in shared memory: level l pools
 // level l-1's result, like the separate pool nodes, as a row pass then a
-// column pass (max is exact, so the split changes no value).
+// column pass (max is exact, so the split changes no value), on packed halves.
 constexpr int kPoolChainMax = 3;
 struct PoolChainOut {
   View4 y[kPoolChainMax];
 };
+// max of eight packed halves (exact: the result is one of the inputs)
+__device__ __forceinline__ uint4 hmax8(uint4 a, uint4 b) {
+  uint4 r;
+  const __half2 *pa = reinterpret_cast<const __half2 *>(&a), *pb = reinterpret_cast<const __half2 *>(&b);
+  __half2 *pr = reinterpret_cast<__half2 *>(&r);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) pr[j] = __hmax2(pa[j], pb[j]);
+  return r;
+}
+
 __global__ void maxpool_chain_nhwc8_k(View4 x, PoolChainOut outs, int levels, int P) {
   pdl_wait_and_release();
   extern __shared__ uint4 pool_sm[];
@@ -743,41 +753,20 @@ __global__ void maxpool_chain_nhwc8_k(View4 x, PoolChainOut outs, int levels, in
   for (int l = 0; l < levels; ++l) {
     for (int p = threadIdx.x; p < HW; p += blockDim.x) {  // row pass A -> T
       const int yy = p / W, xx = p - yy * W;
-      float m[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) m[j] = -3.4e38f;
       const int x0 = max(0, xx - P), x1 = min(W - 1, xx + P);
-      for (int q = x0; q <= x1; ++q) {
-        const uint4 v = A[yy * W + q];
-        const __half *h = reinterpret_cast<const __half *>(&v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], __half2float(h[j]));
-      }
-      __align__(16) __half o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(m[j]);
-      T[p] = *reinterpret_cast<const uint4 *>(o);
+      uint4 m = A[yy * W + x0];
+      for (int q = x0 + 1; q <= x1; ++q) m = hmax8(m, A[yy * W + q]);
+      T[p] = m;
     }
     __syncthreads();
     const View4 &y = outs.y[l == 0 ? 0 : l == 1 ? 1 : 2];
     for (int p = threadIdx.x; p < HW; p += blockDim.x) {  // column pass T -> A, and out
       const int yy = p / W, xx = p - yy * W;
-      float m[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) m[j] = -3.4e38f;
       const int y0 = max(0, yy - P), y1 = min(H - 1, yy + P);
-      for (int q = y0; q <= y1; ++q) {
-        const uint4 v = T[q * W + xx];
-        const __half *h = reinterpret_cast<const __half *>(&v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], __half2float(h[j]));
-      }
-      __align__(16) __half o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(m[j]);
-      const uint4 r = *reinterpret_cast<const uint4 *>(o);
-      A[p] = r;
-      *reinterpret_cast<uint4 *>(y.ptr + at8(y, b, yy, xx, c)) = r;
+      uint4 m = T[y0 * W + xx];
+      for (int q = y0 + 1; q <= y1; ++q) m = hmax8(m, T[q * W + xx]);
+      A[p] = m;
+      *reinterpret_cast<uint4 *>(y.ptr + at8(y, b, yy, xx, c)) = m;
     }
     __syncthreads();
   }
