@@ -70,3 +70,38 @@ def test_live_reference_half_random():
     ref = np.empty(x.size, dtype=np.uint16)
     L.ref_f32_to_f16_bulk(x.ctypes.data, ref.ctypes.data, x.size)
     assert np.array_equal(ivref.f32_to_f16_trunc(x), ref)
+
+
+def test_product_host_cast_large_and_concurrent():
+    """The product's host cast is vectorised and spread over a shared worker
+    pool: arrays far above the pool's split threshold, lengths that leave a
+    scalar tail after the 16-wide vector loop, and several calls at once from
+    different threads (ctypes releases the GIL) each give the reference's
+    truncation (oracle/ivref.py) bit for bit."""
+    import threading
+    import infvino_b200 as ivb
+    rng = np.random.default_rng(41)
+    bits = rng.integers(0, 1 << 32, size=(1 << 21) + 13, dtype=np.uint64).astype(np.uint32)
+    specials = np.array([0, 0x80000000, 0x7f800000, 0xff800000, 0x7fc00000, 0x38800000, 0x387fffff, 0x477fe000,
+                         0x477ff000, 0x47800000, 0x33800000, 0xb8800000], dtype=np.uint32)
+    bits[:specials.size] = specials
+    x = bits.view(np.float32)
+    want = ivref.f32_to_f16_trunc(x)
+    assert np.array_equal(ivb.f32_to_f16(x), want)
+    for n in (1, 15, 16, 17, 31, 1000003):
+        assert np.array_equal(ivb.f32_to_f16(x[:n]), want[:n]), n
+    results, errors = {}, []
+
+    def work(k):
+        try:
+            sl = slice(k * 1000, k * 1000 + (1 << 20) + k)
+            results[k] = np.array_equal(ivb.f32_to_f16(x[sl]), want[sl])
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(k,)) for k in range(6)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors and all(results.get(k) for k in range(6)), (errors, results)
