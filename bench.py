@@ -159,9 +159,37 @@ def run_kernels_only(args, local: int) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of one GPU while the timed region runs."""
+    """SM clock, power and clock-event reasons of one GPU while the timed
+    region runs (read-only queries).  NVML from a thread every 5 ms, plus one
+    sample when sampling starts and one when it stops, so that even a short
+    timed region is covered; without NVML, nvidia-smi every 200 ms."""
+
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
     def __init__(self, gpu_id: str):
+        self.rows = []  # (sm MHz, max sm MHz, power W, reason bits)
+        self.p = None
+        self.nv = None
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            try:
+                h = nv.nvmlDeviceGetHandleByPciBusId(gpu_id)
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(int(gpu_id) if gpu_id.isdigit() else 0)
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nv, self.h, self._reasons = nv, h, reasons
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+            self.sample()
+            self.t = threading.Thread(target=self._loop, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nv = None
         self.path = os.path.join(tempfile.gettempdir(), f"ivb_clocks_{os.getpid()}.csv")
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -173,7 +201,31 @@ class ClockSampler:
         except OSError:
             self.p = None
 
+    def sample(self):
+        nv, h = self.nv, self.h
+        self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), self.max_mhz,
+                          nv.nvmlDeviceGetPowerUsage(h) / 1000.0, int(self._reasons(h))))
+
+    def _loop(self):
+        while not self._stop.wait(0.005):
+            try:
+                self.sample()
+            except Exception:
+                return
+
     def stop(self):
+        if self.nv is not None:
+            self._stop.set()
+            self.t.join(timeout=5)
+            try:
+                self.sample()
+            except Exception:
+                pass
+            rows = self.rows
+            load = [r[0] for r in rows if r[2] > 250.0] or [r[0] for r in rows]
+            reasons = sorted({name for r in rows for bit, name in self.REASONS.items() if r[3] & bit})
+            return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                    "samples": len(rows), "source": "nvml"}
         if self.p is not None:
             self.p.terminate()
             try:
@@ -197,7 +249,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 def gpu_pci_id(dev: int) -> str:
