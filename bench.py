@@ -392,6 +392,19 @@ def main() -> int:
     e2e_ms = max_over_ranks(max(e0.elapsed_time(e1) / e2e_steps, wall))
     e2e_val = world * B / (e2e_ms / 1e3)
 
+    # ---- pose decode + NMS on the device (ivc_decode_pose) of the last e2e
+    # batch: random-init class scores are all ~0.5, so every anchor is a
+    # candidate and each image reaches the max_det cut (the worst case)
+    model.decodePose(B)
+    dec_t = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        dets = model.decodePose(B)
+        dec_t.append((time.perf_counter() - t0) * 1e3)
+    pose_decode = {"ms_per_batch": round(float(np.median(dec_t)), 3), "batch": B, "conf": 0.25, "iou": 0.7,
+                   "max_det": 300, "detections_per_image": int(np.median([len(d) for d in dets])),
+                   "includes": "kernel + copy of the detections to host memory (synchronous call)"}
+
     # ---- batch-1 latency (device-resident graph replay and host round trip)
     lat, lat_e2e = [], []
     x1 = x_host.numpy()[:n_in]
@@ -462,6 +475,14 @@ def main() -> int:
             cpu = cpu_baseline(plan)
         except Exception as e:  # reported, not fatal
             cpu = {"value": None, "error": repr(e)}
+        try:  # the CPU restatement of the reference's pose decoder + NMS on one image of the same batch
+            from oracle import decode
+            y0 = outs[0].reshape(B, -1)[0].reshape(56, -1)
+            t0 = time.perf_counter()
+            decode.pose_decode(y0)
+            pose_decode["cpu_port_ms_per_image"] = round((time.perf_counter() - t0) * 1e3, 2)
+        except Exception as e:  # reported, not fatal
+            pose_decode["cpu_port_error"] = repr(e)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "images/s", "n_gpus": world, "steps": args.steps,
@@ -482,6 +503,7 @@ def main() -> int:
             "network_roofline_ms": round(troof_total * 1e3, 4),
             "family_ms": {k: round(v, 4) for k, v in sorted(fam_ms.items(), key=lambda kv: -kv[1])},
             "cpu_baseline": cpu,
+            "pose_decode": pose_decode,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -30,6 +30,8 @@
  *   ivc_pool_stats ......... PlanModel::poolRequestedBytes/poolAllocatedBytes/
  *                            poolBufferCount  PlanModel.hpp:94-97
  *   ivc_infer_f16_device ... (new) zero-copy device-pointer inference on a caller stream
+ *   ivc_decode_pose ........ PoseDecoder::decode + nmsPerClass + nms, on the device
+ *                            src/Decoders.cpp:33-65,127-179, src/Nms.cpp:10-55
  *   ivc_destroy ............ PlanModel::~PlanModel / ClBackend destructor
  */
 #ifndef INFVINO_B200_H_
@@ -107,6 +109,23 @@ int ivc_run_async(ivc_model *m, int batch, void *stream);
 int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch);
 /* Copies tensor `name` for `batch` images in plan (NCHW) order; IVC_ERR_NOT_FOUND if unknown. */
 int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch);
+
+/* Pose decode + greedy NMS of output 0 of the last run, on the device, for
+ * `batch` images (replaces the host-side PoseDecoder::decode with
+ * nmsPerClass, src/Decoders.cpp:127-179 and :33-65, and nms / iou,
+ * src/Nms.cpp:10-55).  Candidates are anchors whose score is not below
+ * `conf`; boxes and keypoints are mapped through the letterbox
+ * (include/infvino/Preprocess.hpp:24-35; `letterbox` is [batch][scale,
+ * pad_left, pad_top] in host memory, or NULL for scale 1 and no padding);
+ * greedy suppression at IoU above `iou` in descending score (ties by anchor
+ * index) keeps at most `max_det` per image.  Results in host memory:
+ * counts[b] detections for image b, detection k at
+ * dets[(b * max_det + k) * (6 + 2 * nk)]: anchor index, score, x, y, w, h,
+ * then x, y of each keypoint.  nk <= 0 infers the keypoint count from the
+ * output's channels as (C - 5) / kdims (kdims <= 0: 3).  The output must be
+ * channel-major [1, 5 + nk * kdims, A] with A <= 16384.  Synchronous. */
+int ivc_decode_pose(ivc_model *m, int batch, float conf, float iou, int max_det, int nk, int kdims,
+                    const float *letterbox, int *counts, float *dets);
 /* ivc_read_tensor_f16 without any allocation (no counterpart in the reference).
  * The NHWC -> NCHW relayout is staged through a static 4 MiB device buffer per
  * device instead of a scratch buffer grown with cudaMalloc; a tensor that needs

@@ -192,6 +192,25 @@ class PlanModel:
         check(st, self._h)
         return out
 
+    def decodePose(self, batch: int = 1, conf: float = 0.25, iou: float = 0.7, max_det: int = 300, nk: int = 17,
+                   kdims: int = 3, letterbox=None):
+        """PoseDecoder::decode + NMS of the last run's output 0 on the device
+        (src/Decoders.cpp:127-179, src/Nms.cpp:10-55).  Returns, per image, an
+        array [n, 6 + 2 * nk]: anchor, score, x, y, w, h, then keypoint x, y
+        pairs, in descending score.  `letterbox`: [batch, 3] of (scale,
+        pad_left, pad_top), or None."""
+        S = 6 + 2 * nk
+        counts = np.zeros(batch, dtype=np.int32)
+        dets = np.zeros(batch * max_det * S, dtype=np.float32)
+        lb = None
+        if letterbox is not None:
+            lb = np.ascontiguousarray(letterbox, dtype=np.float32).reshape(batch, 3)
+        check(lib().ivc_decode_pose(self._h, batch, conf, iou, max_det, nk, kdims,
+                                    None if lb is None else lb.ctypes.data, counts.ctypes.data,
+                                    dets.ctypes.data), self._h)
+        dets = dets.reshape(batch, max_det, S)
+        return [dets[b, :counts[b]].copy() for b in range(batch)]
+
     def lastRunMs(self) -> float:
         return float(lib().ivc_last_infer_ms(self._h))
 

@@ -47,6 +47,7 @@ SIGNATURES = {
     "ivc_run_async": (_i32, [_vp, _i32, _vp]),
     "ivc_read_output_f16": (_i32, [_vp, _i32, _vp, _i32]),
     "ivc_read_tensor_f16": (_i32, [_vp, _cp, _vp, _i32]),
+    "ivc_decode_pose": (_i32, [_vp, _i32, ctypes.c_float, ctypes.c_float, _i32, _i32, _i32, _vp, _vp, _vp]),
     "ivc_read_tensor_f16_noalloc": (_i32, [_vp, _cp, _vp, _i32]),
     "ivc_infer_f16_device": (_i32, [_vp, _vp, _i32, _P(_vp), _vp]),
     "ivc_infer_f32_device": (_i32, [_vp, _vp, _i32, _P(_vp), _vp]),

@@ -242,6 +242,16 @@ int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch
   });
 }
 
+int ivc_decode_pose(ivc_model *m, int batch, float conf, float iou, int max_det, int nk, int kdims,
+                    const float *letterbox, int *counts, float *dets) {
+  return guarded(m, [&]() -> int {
+    if (!counts || !dets || batch < 1 || batch > m->eng->max_batch() || max_det < 1)
+      return fail(m, IVC_ERR_ARGUMENT, "ivc_decode_pose: bad arguments");
+    m->eng->decode_pose(batch, conf, iou, max_det, nk, kdims, letterbox, counts, dets);
+    return status_check(m);
+  });
+}
+
 // ---- ivc_read_tensor_f16_noalloc: the relayout of ivc_read_tensor_f16 staged
 // through one static device buffer per device instead of a cudaMalloc'd one.
 // Overlapping calls on the same device (any handles) share the buffer and race.

@@ -92,6 +92,10 @@ Engine::~Engine() {
   if (in_f32_) cudaFree(in_f32_);
   if (out_f32_) cudaFree(out_f32_);
   if (in_f16_host_) cudaFreeHost(in_f16_host_);
+  if (nms_boxes_) cudaFree(nms_boxes_);
+  if (nms_counts_) cudaFree(nms_counts_);
+  if (nms_dets_) cudaFree(nms_dets_);
+  if (nms_lbox_) cudaFree(nms_lbox_);
   for (cudaEvent_t e : chunk_events_) cudaEventDestroy(e);
   if (copy_in_) cudaStreamDestroy(copy_in_);
   if (copy_out_) cudaStreamDestroy(copy_out_);
@@ -2267,6 +2271,63 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   synchronize();
+}
+
+void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, int kdims, const float *letterbox,
+                         int *counts, float *dets) {
+  pdl_scope();
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  if (output_count() < 1) throw std::runtime_error("PoseDecoder: unexpected output shape");
+  const TensorRt &t = T_[(size_t)tid(output_name(0))];
+  // channel-major [1, C, A] (the reference also accepts anchor-major; the
+  // pose plans emit channel-major)
+  if (t.dims.size() != 3 || !t.dense || t.dims[1] > t.dims[2])
+    throw std::runtime_error("PoseDecoder: unexpected output shape");
+  const int C = (int)t.dims[1], A = (int)t.dims[2];
+  if (kdims <= 0) kdims = 3;
+  if (nk <= 0) nk = (C - 5) / kdims;
+  if (nk < 0 || 5 + nk * kdims > C) throw std::runtime_error("PoseDecoder: keypoints do not fit the output channels");
+  if (A > kPoseNmsMaxAnchors) throw std::runtime_error("PoseDecoder: more anchors than the device decoder sorts");
+  if (max_det < 1) throw std::runtime_error("PoseDecoder: max_det must be positive");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  int P = 2;
+  while (P < A) P <<= 1;
+  const int S = 6 + 2 * nk;
+  if (!nms_boxes_) {
+    check(cudaMalloc(&nms_boxes_, (size_t)max_batch_ * kPoseNmsMaxAnchors * sizeof(float4)), "cudaMalloc(nms boxes)");
+    check(cudaMalloc(&nms_counts_, (size_t)max_batch_ * sizeof(int)), "cudaMalloc(nms counts)");
+    check(cudaMalloc(&nms_lbox_, (size_t)max_batch_ * 3 * sizeof(float)), "cudaMalloc(nms letterbox)");
+  }
+  const int64_t need = (int64_t)batch * max_det * S;
+  if (need > nms_dets_cap_) {
+    if (nms_dets_) check(cudaFree(nms_dets_), "cudaFree(nms dets)");
+    nms_dets_ = nullptr;
+    check(cudaMalloc(&nms_dets_, (size_t)need * sizeof(float)), "cudaMalloc(nms dets)");
+    nms_dets_cap_ = need;
+  }
+  if (letterbox)
+    check(cudaMemcpyAsync(nms_lbox_, letterbox, (size_t)batch * 3 * sizeof(float), cudaMemcpyHostToDevice, stream_),
+          "letterbox copy");
+  PoseNmsArgs a{};
+  a.out = t.dptr;
+  a.img_stride = t.numel;
+  a.A = A;
+  a.P = P;
+  a.nk = nk;
+  a.kdims = kdims;
+  a.conf = conf;
+  a.iou = iou;
+  a.max_det = max_det;
+  a.letterbox = letterbox ? nms_lbox_ : nullptr;
+  a.boxes = nms_boxes_;
+  a.counts = nms_counts_;
+  a.dets = nms_dets_;
+  check(launch_pose_nms(a, batch, stream_), "pose decode + NMS");
+  check(cudaMemcpyAsync(counts, nms_counts_, (size_t)batch * sizeof(int), cudaMemcpyDeviceToHost, stream_),
+        "detection counts copy");
+  check(cudaMemcpyAsync(dets, nms_dets_, (size_t)need * sizeof(float), cudaMemcpyDeviceToHost, stream_),
+        "detections copy");
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
 }
 
 bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {

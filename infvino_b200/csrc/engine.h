@@ -124,6 +124,14 @@ class Engine {
                              int64_t scratch_bytes, int64_t *need_bytes);
   void synchronize();
   int device_status();  // kernel status word (0 = ok), resets it
+  // Pose decode + NMS of output 0 of the last run on the device (reference
+  // PoseDecoder::decode + nmsPerClass): per image, counts[b] detections of
+  // 6 + 2 * nk floats each (anchor, score, x, y, w, h, keypoint x/y pairs) at
+  // dets + b * max_det * (6 + 2 * nk), in host memory.  `letterbox` (host,
+  // [batch][scale, pad_left, pad_top]) may be null.  nk <= 0: inferred from
+  // the output's channels as (C - 5) / kdims.  Synchronous.
+  void decode_pose(int batch, float conf, float iou, int max_det, int nk, int kdims, const float *letterbox,
+                   int *counts, float *dets);
   int graph_kernel_count(int batch);  // kernel nodes in the CUDA graph of `batch`
   __half *input_device_ptr() const;
   float *input_f32_staging() const { return in_f32_; }
@@ -183,6 +191,11 @@ class Engine {
   float *in_f32_ = nullptr;         // device staging for f32 input
   float *out_f32_ = nullptr;        // device staging for f32 outputs (pipelined infer)
   uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
+  // pose decode + NMS: box scratch, results and letterboxes (allocated at the first call)
+  float4 *nms_boxes_ = nullptr;
+  int *nms_counts_ = nullptr;
+  float *nms_dets_ = nullptr, *nms_lbox_ = nullptr;
+  int64_t nms_dets_cap_ = 0;        // floats in nms_dets_
   cudaStream_t copy_in_ = nullptr, copy_out_ = nullptr;
   std::vector<cudaEvent_t> chunk_events_;
   __half *scratch_ = nullptr;       // read_tensor staging

@@ -128,6 +128,25 @@ cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t
 
 // permute_0213 (mode 0) -> softmax over D2 bins -> 1x1 conv D2 -> Cout, fused
 // (the YOLO DFL head).  Supported for D2 == 16 and Cout <= 8.
+// Pose decode + greedy NMS over a batch of channel-major fp16 pose outputs
+// [5 + nk * kdims, A] (pose_nms.cu); one CTA per image.
+constexpr int kPoseNmsThreads = 1024;
+constexpr int kPoseNmsMaxAnchors = 16384;  // P: the sort runs over a power of two >= A, in shared memory
+struct PoseNmsArgs {
+  const __half *out;       // image 0 of the output
+  long long img_stride;    // elements
+  int A;                   // anchors
+  int P;                   // power of two >= A (sort length)
+  int nk, kdims;           // keypoints, values per keypoint
+  float conf, iou;
+  int max_det;
+  const float *letterbox;  // [batch][scale, pad_left, pad_top] or null (scale 1, no padding)
+  float4 *boxes;           // scratch [batch][P]
+  int *counts;             // [batch]
+  float *dets;             // [batch][max_det][6 + 2 * nk]: anchor, score, x, y, w, h, then (x, y) per keypoint
+};
+cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st);
+
 bool dfl_fused_supported(int D2, int Cout);
 cudaError_t launch_dfl_fused(const __half *x, const __half *w, const __half *bias, __half *y, int batch, int D1, int D2,
                              long long I, int Cout, int act, cudaStream_t st);

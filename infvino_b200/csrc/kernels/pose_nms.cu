@@ -1,0 +1,142 @@
+// Pose decode + greedy NMS on the device: the reference's PoseDecoder::decode
+// (src/Decoders.cpp:127-179) with nmsPerClass (:33-65, one class) and nms /
+// iou (src/Nms.cpp:10-55), one CTA per image over the [5 + nk * kdims, A]
+// channel-major fp16 output.
+//
+//   1. candidates: anchors whose score is not below `conf` (`score < conf`
+//      skips, as in the reference);
+//   2. the candidates in descending score, ties by anchor index (the
+//      reference's stable sort): a 30-bit key per anchor (the fp16 score's
+//      order inverted, then the anchor) bitonic-sorted in shared memory;
+//   3. each candidate's box (x, y, w, h) in image coordinates through the
+//      letterbox (rectToImage), into global scratch;
+//   4. greedy suppression in that order (IoU above `iou` removes a later
+//      candidate), stopping once `max_det` are kept: kept boxes come out in
+//      score order, so they are the first `max_det` of the reference's result.
+// All float arithmetic is the reference's, operation by operation, with
+// round-to-nearest intrinsics so that nothing is contracted into an FMA.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace ivb {
+
+namespace {
+
+__device__ __forceinline__ float4 pose_box(const __half *o, long long A, int a, float scale, float pl, float pt) {
+  const float cx = __half2float(o[a]), cy = __half2float(o[A + a]);
+  const float w = __half2float(o[2 * A + a]), h = __half2float(o[3 * A + a]);
+  const float x = __fdiv_rn(__fsub_rn(cx, pl), scale), y = __fdiv_rn(__fsub_rn(cy, pt), scale);
+  const float ws = __fdiv_rn(w, scale), hs = __fdiv_rn(h, scale);
+  return make_float4(__fsub_rn(x, __fdiv_rn(ws, 2.0f)), __fsub_rn(y, __fdiv_rn(hs, 2.0f)), ws, hs);
+}
+
+__device__ __forceinline__ float box_iou(float4 a, float4 b) {
+  const float x1 = fmaxf(a.x, b.x), y1 = fmaxf(a.y, b.y);
+  const float x2 = fminf(__fadd_rn(a.x, a.z), __fadd_rn(b.x, b.z));
+  const float y2 = fminf(__fadd_rn(a.y, a.w), __fadd_rn(b.y, b.w));
+  const float inter = __fmul_rn(fmaxf(0.0f, __fsub_rn(x2, x1)), fmaxf(0.0f, __fsub_rn(y2, y1)));
+  const float area_a = __fmul_rn(fmaxf(0.0f, a.z), fmaxf(0.0f, a.w));
+  const float area_b = __fmul_rn(fmaxf(0.0f, b.z), fmaxf(0.0f, b.w));
+  const float uni = __fsub_rn(__fadd_rn(area_a, area_b), inter);
+  return uni > 1e-9f ? __fdiv_rn(inter, uni) : 0.0f;
+}
+
+__global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
+  pdl_wait_and_release();
+  extern __shared__ uint32_t nms_sm[];
+  uint32_t *key = nms_sm;                                              // P sort keys
+  unsigned char *removed = reinterpret_cast<unsigned char *>(nms_sm + p.P);  // P flags
+  __shared__ int n_cand;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const long long A = p.A;
+  const __half *o = p.out + (long long)b * p.img_stride;
+  const float scale = p.letterbox ? p.letterbox[3 * b] : 1.0f;
+  const float pl = p.letterbox ? p.letterbox[3 * b + 1] : 0.0f, pt = p.letterbox ? p.letterbox[3 * b + 2] : 0.0f;
+  if (tid == 0) n_cand = 0;
+  __syncthreads();
+  // 1. keys: the fp16 score mapped to an unsigned order (+0 and -0 alike),
+  // inverted so that ascending keys run in descending score, then the anchor
+  for (int a = tid; a < p.P; a += blockDim.x) {
+    uint32_t k = 0xffffffffu;
+    if (a < p.A) {
+      const __half hs = o[4 * A + a];
+      if (!(__half2float(hs) < p.conf)) {
+        uint32_t u = __half_as_ushort(hs);
+        if ((u & 0x7fffu) == 0) u = 0;
+        const uint32_t ord = (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u);
+        k = ((0xffffu - ord) << 14) | (uint32_t)a;
+        atomicAdd(&n_cand, 1);
+      }
+    }
+    key[a] = k;
+  }
+  __syncthreads();
+  // 2. bitonic sort, ascending (P is a power of two)
+  for (int size = 2; size <= p.P; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int t = tid; t < p.P / 2; t += blockDim.x) {
+        const int lo = 2 * stride * (t / stride) + (t % stride), hi = lo + stride;
+        const uint32_t x = key[lo], y = key[hi];
+        if ((x > y) == ((lo & size) == 0)) {
+          key[lo] = y;
+          key[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  const int n = n_cand;
+  // 3. boxes of the candidates in sorted order
+  float4 *bx = p.boxes + (long long)b * p.P;
+  for (int i = tid; i < n; i += blockDim.x) {
+    bx[i] = pose_box(o, A, (int)(key[i] & 0x3fffu), scale, pl, pt);
+    removed[i] = 0;
+  }
+  __syncthreads();
+  // 4. greedy suppression; kept detection k: anchor, score, box, keypoints
+  const int S = 6 + 2 * p.nk;
+  float *dets = p.dets + (long long)b * p.max_det * S;
+  int kept = 0;
+  for (int i = 0; i < n && kept < p.max_det; ++i) {
+    if (removed[i]) continue;  // the same for every thread: written before the last barrier
+    const float4 bi = bx[i];
+    const int a = (int)(key[i] & 0x3fffu);
+    for (int f = tid; f < S; f += blockDim.x) {
+      float v;
+      if (f == 0) v = (float)a;
+      else if (f == 1) v = __half2float(o[4 * A + a]);
+      else if (f < 6) v = f == 2 ? bi.x : f == 3 ? bi.y : f == 4 ? bi.z : bi.w;
+      else {
+        const int kk = (f - 6) >> 1, xy = (f - 6) & 1;
+        v = __fdiv_rn(__fsub_rn(__half2float(o[(5 + (long long)kk * p.kdims + xy) * A + a]), xy ? pt : pl), scale);
+      }
+      dets[(long long)kept * S + f] = v;
+    }
+    ++kept;
+    for (int j = i + 1 + tid; j < n; j += blockDim.x)
+      if (!removed[j] && box_iou(bi, bx[j]) > p.iou) removed[j] = 1;
+    __syncthreads();
+  }
+  if (tid == 0) p.counts[b] = kept;
+}
+
+}  // namespace
+
+cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st) {
+  if (args.P < 2 || args.P > kPoseNmsMaxAnchors || (args.P & (args.P - 1)) || args.A > args.P || args.A < 1 ||
+      args.max_det < 1 || batch < 1)
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)args.P * 5;  // keys + flags
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(pose_nms_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)((size_t)kPoseNmsMaxAnchors * 5));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  launch_kernel(pose_nms_k, dim3((unsigned)batch), dim3(kPoseNmsThreads), smem, st, args);
+  return cudaGetLastError();
+}
+
+}  // namespace ivb

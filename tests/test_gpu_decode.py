@@ -1,0 +1,59 @@
+"""Device pose decode + NMS (ivc_decode_pose) against the oracle's restatement
+of the reference's PoseDecoder::decode, nmsPerClass and nms (oracle/decode.py)
+on the same network outputs: the same detections in the same order, with the
+same anchor, score, box and keypoint values bit for bit."""
+import os
+
+import numpy as np
+import pytest
+
+import infvino_b200 as ivb
+from infvino_b200 import plangen
+from oracle import decode
+
+
+def check_against_oracle(m, y, batch, conf, iou, max_det, letterbox):
+    got = m.decodePose(batch, conf=conf, iou=iou, max_det=max_det, letterbox=letterbox)
+    total = 0
+    for b in range(batch):
+        scale, pl, pt = (1.0, 0.0, 0.0) if letterbox is None else (float(v) for v in letterbox[b])
+        ref = decode.pose_decode(y[b], conf=conf, iou=iou, max_det=max_det, scale=scale, pad=(pl, pt))
+        assert got[b].shape == (len(ref), 6 + 2 * 17), (b, got[b].shape, len(ref))
+        for k, (a, s, box, kp) in enumerate(ref):
+            row = got[b][k]
+            assert int(row[0]) == a and row[1] == np.float32(s), (b, k, row[:2], a, s)
+            assert np.array_equal(row[2:6], np.asarray(box, dtype=np.float32)), (b, k)
+            assert np.array_equal(row[6:].reshape(17, 2), np.asarray(kp, dtype=np.float32)), (b, k)
+        total += len(ref)
+    return total
+
+
+@pytest.mark.gpu
+def test_device_pose_decode_peaked(plan_dir):
+    """A class head scaled to give a few dozen detections per image (as with
+    trained weights), three images, per-image letterboxes."""
+    p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_peaked_dec"), cls_gain=100.0, cls_shift=-3.0)
+    m = ivb.PlanModel(p, max_batch=3)
+    x = np.random.default_rng(61).random(3 * m.inputNumel(), dtype=np.float32)
+    y = m.infer_f32(x, 3)[0].reshape(3, 56, -1)
+    lb = np.array([[1.0, 0.0, 0.0], [0.5, 3.0, 7.0], [0.8125, 0.0, 80.0]], dtype=np.float32)
+    n = check_against_oracle(m, y, 3, 0.25, 0.7, 300, lb)
+    assert n >= 30, n
+    assert check_against_oracle(m, y, 3, 0.25, 0.7, 300, None) == n
+    m.close()
+
+
+@pytest.mark.gpu
+def test_device_pose_decode_every_anchor_a_candidate(plan_dir):
+    """Random-init class scores are all ~0.5: every anchor is a candidate, many
+    scores tie in fp16 (ties go by anchor index), and the max_det cut is
+    reached; twice in a row, and with a smaller cut."""
+    p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_320_dec"), imgsz=320)
+    m = ivb.PlanModel(p, max_batch=2)
+    x = np.random.default_rng(62).random(2 * m.inputNumel(), dtype=np.float32)
+    y = m.infer_f32(x, 2)[0].reshape(2, 56, -1)
+    assert (y[:, 4] >= 0.25).all()
+    for _ in range(2):
+        assert check_against_oracle(m, y, 2, 0.25, 0.7, 300, None) == 600
+    assert check_against_oracle(m, y, 2, 0.25, 0.5, 40, None) == 80
+    m.close()
