@@ -96,6 +96,8 @@ Engine::~Engine() {
   if (nms_counts_) cudaFree(nms_counts_);
   if (nms_dets_) cudaFree(nms_dets_);
   if (nms_lbox_) cudaFree(nms_lbox_);
+  if (nms_host_) cudaFreeHost(nms_host_);
+  if (nms_kept_) cudaFree(nms_kept_);
   for (cudaEvent_t e : chunk_events_) cudaEventDestroy(e);
   if (copy_in_) cudaStreamDestroy(copy_in_);
   if (copy_out_) cudaStreamDestroy(copy_out_);
@@ -2290,7 +2292,7 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
   if (A > kPoseNmsMaxAnchors) throw std::runtime_error("PoseDecoder: more anchors than the device decoder sorts");
   if (max_det < 1) throw std::runtime_error("PoseDecoder: max_det must be positive");
   check(cudaSetDevice(device_), "cudaSetDevice");
-  int P = 2;
+  int P = 4;  // (the boxes follow 4 * P bytes of keys in shared memory, 16-byte aligned)
   while (P < A) P <<= 1;
   const int S = 6 + 2 * nk;
   if (!nms_boxes_) {
@@ -2301,8 +2303,12 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
   const int64_t need = (int64_t)batch * max_det * S;
   if (need > nms_dets_cap_) {
     if (nms_dets_) check(cudaFree(nms_dets_), "cudaFree(nms dets)");
+    if (nms_kept_) check(cudaFree(nms_kept_), "cudaFree(nms kept)");
     nms_dets_ = nullptr;
+    nms_kept_ = nullptr;
     check(cudaMalloc(&nms_dets_, (size_t)need * sizeof(float)), "cudaMalloc(nms dets)");
+    // batch * max_det <= need / 6 for any later call the buffers still fit (S >= 6)
+    check(cudaMalloc(&nms_kept_, (size_t)(need / 6 + 1) * sizeof(int)), "cudaMalloc(nms kept)");
     nms_dets_cap_ = need;
   }
   if (letterbox)
@@ -2320,14 +2326,33 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
   a.max_det = max_det;
   a.letterbox = letterbox ? nms_lbox_ : nullptr;
   a.boxes = nms_boxes_;
+  // boxes and the kept list in shared memory where they fit, else in scratch
+  a.kept = nms_kept_;
+  a.boxes_in_smem = pose_nms_smem_bytes(P, A, true, 0) <= (size_t)kPoseNmsSmemMax ? 1 : 0;
+  a.kept_idx_smem = pose_nms_smem_bytes(P, A, a.boxes_in_smem != 0, max_det) <= (size_t)kPoseNmsSmemMax ? 1 : 0;
   a.counts = nms_counts_;
   a.dets = nms_dets_;
   check(launch_pose_nms(a, batch, stream_), "pose decode + NMS");
-  check(cudaMemcpyAsync(counts, nms_counts_, (size_t)batch * sizeof(int), cudaMemcpyDeviceToHost, stream_),
+  // results through pinned staging; each image's used rows go to the caller
+  if (need + batch > nms_host_cap_) {
+    if (nms_host_) check(cudaFreeHost(nms_host_), "cudaFreeHost(nms staging)");
+    nms_host_ = nullptr;
+    check(cudaHostAlloc(reinterpret_cast<void **>(&nms_host_), (size_t)(need + batch) * sizeof(float),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(nms staging)");
+    nms_host_cap_ = need + batch;
+  }
+  int *host_counts = reinterpret_cast<int *>(nms_host_ + need);
+  check(cudaMemcpyAsync(host_counts, nms_counts_, (size_t)batch * sizeof(int), cudaMemcpyDeviceToHost, stream_),
         "detection counts copy");
-  check(cudaMemcpyAsync(dets, nms_dets_, (size_t)need * sizeof(float), cudaMemcpyDeviceToHost, stream_),
+  check(cudaMemcpyAsync(nms_host_, nms_dets_, (size_t)need * sizeof(float), cudaMemcpyDeviceToHost, stream_),
         "detections copy");
   check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  for (int b = 0; b < batch; ++b) {
+    counts[b] = host_counts[b];
+    std::memcpy(dets + (size_t)b * max_det * S, nms_host_ + (size_t)b * max_det * S,
+                (size_t)host_counts[b] * S * sizeof(float));
+  }
 }
 
 bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {

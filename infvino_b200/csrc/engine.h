@@ -193,9 +193,11 @@ class Engine {
   uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
   // pose decode + NMS: box scratch, results and letterboxes (allocated at the first call)
   float4 *nms_boxes_ = nullptr;
-  int *nms_counts_ = nullptr;
+  int *nms_counts_ = nullptr, *nms_kept_ = nullptr;
   float *nms_dets_ = nullptr, *nms_lbox_ = nullptr;
   int64_t nms_dets_cap_ = 0;        // floats in nms_dets_
+  float *nms_host_ = nullptr;       // pinned staging of results and counts
+  int64_t nms_host_cap_ = 0;        // floats in nms_host_
   cudaStream_t copy_in_ = nullptr, copy_out_ = nullptr;
   std::vector<cudaEvent_t> chunk_events_;
   __half *scratch_ = nullptr;       // read_tensor staging

@@ -141,10 +141,17 @@ struct PoseNmsArgs {
   float conf, iou;
   int max_det;
   const float *letterbox;  // [batch][scale, pad_left, pad_top] or null (scale 1, no padding)
-  float4 *boxes;           // scratch [batch][P]
+  float4 *boxes;           // scratch [batch][P] (used when the boxes do not fit in shared memory)
+  int boxes_in_smem;       // 1: boxes in shared memory (pose_nms_smem_bytes(P, A, true) <= kPoseNmsSmemMax)
+  int *kept;               // scratch [batch][max_det] (used when the kept list does not fit in shared memory)
+  int kept_idx_smem;       // 1: kept list in shared memory
   int *counts;             // [batch]
   float *dets;             // [batch][max_det][6 + 2 * nk]: anchor, score, x, y, w, h, then (x, y) per keypoint
 };
+constexpr int kPoseNmsSmemMax = 226 * 1024;  // dynamic; the kernel's own static shared memory fits beside it
+inline size_t pose_nms_smem_bytes(int P, int A, bool boxes_in_smem, int kept_in_smem) {
+  return (size_t)P * 4 + (boxes_in_smem ? (size_t)A * 16 : 0) + (size_t)kept_in_smem * 4;  // keys, boxes, kept list
+}
 cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st);
 
 bool dfl_fused_supported(int D2, int Cout);

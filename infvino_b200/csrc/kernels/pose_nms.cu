@@ -9,10 +9,13 @@
 //      reference's stable sort): a 30-bit key per anchor (the fp16 score's
 //      order inverted, then the anchor) bitonic-sorted in shared memory;
 //   3. each candidate's box (x, y, w, h) in image coordinates through the
-//      letterbox (rectToImage), into global scratch;
+//      letterbox (rectToImage), in shared memory when keys, boxes and flags
+//      fit there (A <= 9,800 or so), else in global scratch;
 //   4. greedy suppression in that order (IoU above `iou` removes a later
 //      candidate), stopping once `max_det` are kept: kept boxes come out in
-//      score order, so they are the first `max_det` of the reference's result.
+//      score order, so they are the first `max_det` of the reference's result;
+//      a candidate is tested against the boxes kept so far, 32 candidates at a
+//      time.
 // All float arithmetic is the reference's, operation by operation, with
 // round-to-nearest intrinsics so that nothing is contracted into an FMA.
 #include <cuda_fp16.h>
@@ -46,8 +49,12 @@ __device__ __forceinline__ float box_iou(float4 a, float4 b) {
 __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   pdl_wait_and_release();
   extern __shared__ uint32_t nms_sm[];
-  uint32_t *key = nms_sm;                                              // P sort keys
-  unsigned char *removed = reinterpret_cast<unsigned char *>(nms_sm + p.P);  // P flags
+  // shared memory: P sort keys, then the boxes (A, when they fit), then the
+  // kept candidates' indices (max_det, when they fit)
+  uint32_t *key = nms_sm;
+  float4 *bx = p.boxes_in_smem ? reinterpret_cast<float4 *>(nms_sm + p.P) : p.boxes + (long long)blockIdx.x * p.P;
+  int *kept_sm = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(nms_sm + p.P) +
+                                         (p.boxes_in_smem ? (size_t)p.A * sizeof(float4) : 0));
   __shared__ int n_cand;
   const int b = blockIdx.x, tid = threadIdx.x;
   const long long A = p.A;
@@ -88,35 +95,70 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
     }
   const int n = n_cand;
   // 3. boxes of the candidates in sorted order
-  float4 *bx = p.boxes + (long long)b * p.P;
-  for (int i = tid; i < n; i += blockDim.x) {
-    bx[i] = pose_box(o, A, (int)(key[i] & 0x3fffu), scale, pl, pt);
-    removed[i] = 0;
-  }
+  for (int i = tid; i < n; i += blockDim.x) bx[i] = pose_box(o, A, (int)(key[i] & 0x3fffu), scale, pl, pt);
   __syncthreads();
-  // 4. greedy suppression; kept detection k: anchor, score, box, keypoints
-  const int S = 6 + 2 * p.nk;
-  float *dets = p.dets + (long long)b * p.max_det * S;
-  int kept = 0;
-  for (int i = 0; i < n && kept < p.max_det; ++i) {
-    if (removed[i]) continue;  // the same for every thread: written before the last barrier
-    const float4 bi = bx[i];
-    const int a = (int)(key[i] & 0x3fffu);
-    for (int f = tid; f < S; f += blockDim.x) {
-      float v;
-      if (f == 0) v = (float)a;
-      else if (f == 1) v = __half2float(o[4 * A + a]);
-      else if (f < 6) v = f == 2 ? bi.x : f == 3 ? bi.y : f == 4 ? bi.z : bi.w;
-      else {
-        const int kk = (f - 6) >> 1, xy = (f - 6) & 1;
-        v = __fdiv_rn(__fsub_rn(__half2float(o[(5 + (long long)kk * p.kdims + xy) * A + a]), xy ? pt : pl), scale);
-      }
-      dets[(long long)kept * S + f] = v;
-    }
-    ++kept;
-    for (int j = i + 1 + tid; j < n; j += blockDim.x)
-      if (!removed[j] && box_iou(bi, bx[j]) > p.iou) removed[j] = 1;
+  // 4. greedy suppression.  A candidate is kept when no earlier kept box
+  // overlaps it above `iou` (the reference's loop, which removes every later
+  // candidate a kept box overlaps, decides the same).  Candidates go in groups
+  // of 32: warp w tests kept boxes w, w + 32, ... against the group (lane =
+  // candidate), warp r tests group candidate r against the later ones; warp 0
+  // then walks the group in order with the two bit masks.
+  __shared__ uint32_t sup_mask, row_mask[32];
+  __shared__ int n_kept;
+  const int warp = tid >> 5, lane = tid & 31;
+  int *kept_idx = p.kept_idx_smem ? kept_sm : p.kept + (long long)b * p.max_det;
+  if (tid == 0) n_kept = 0;
+  __syncthreads();
+  for (int base = 0; base < n && n_kept < p.max_det; base += 32) {
+    const int nk_now = n_kept;
+    const int c = base + lane;
+    const bool valid = c < n;
+    const float4 bc = valid ? bx[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    bool hit = false;
+    for (int k = warp; k < nk_now && valid; k += 32) hit = hit || box_iou(bx[kept_idx[k]], bc) > p.iou;
+    const uint32_t sup = __ballot_sync(0xffffffffu, hit);
+    // row `warp`: group candidate base + warp against the later ones (lanes above it)
+    const int r = base + warp;
+    const bool later = valid && lane > warp && r < n;
+    const bool over = later && box_iou(bx[r], bc) > p.iou;
+    const uint32_t row = __ballot_sync(0xffffffffu, over);
+    if (tid == 0) sup_mask = 0;
     __syncthreads();
+    if (lane == 0) {
+      if (sup) atomicOr(&sup_mask, sup);
+      row_mask[warp] = row;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t m = sup_mask;
+      int nk = n_kept;
+      for (int j = 0; j < 32 && base + j < n && nk < p.max_det; ++j)
+        if (!((m >> j) & 1u)) {
+          kept_idx[nk++] = base + j;
+          m |= row_mask[j];
+        }
+      n_kept = nk;
+    }
+    __syncthreads();
+  }
+  // 5. the kept detections: anchor, score, box, keypoints
+  const int S = 6 + 2 * p.nk, kept = n_kept;
+  float *dets = p.dets + (long long)b * p.max_det * S;
+  for (long long e = tid; e < (long long)kept * S; e += blockDim.x) {
+    const int k = (int)(e / S), f = (int)(e - (long long)k * S);
+    const int i = kept_idx[k];
+    const int a = (int)(key[i] & 0x3fffu);
+    float v;
+    if (f == 0) v = (float)a;
+    else if (f == 1) v = __half2float(o[4 * A + a]);
+    else if (f < 6) {
+      const float4 bi = bx[i];
+      v = f == 2 ? bi.x : f == 3 ? bi.y : f == 4 ? bi.z : bi.w;
+    } else {
+      const int kk = (f - 6) >> 1, xy = (f - 6) & 1;
+      v = __fdiv_rn(__fsub_rn(__half2float(o[(5 + (long long)kk * p.kdims + xy) * A + a]), xy ? pt : pl), scale);
+    }
+    dets[e] = v;
   }
   if (tid == 0) p.counts[b] = kept;
 }
@@ -124,14 +166,15 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
 }  // namespace
 
 cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st) {
-  if (args.P < 2 || args.P > kPoseNmsMaxAnchors || (args.P & (args.P - 1)) || args.A > args.P || args.A < 1 ||
+  if (args.P < 4 || args.P > kPoseNmsMaxAnchors || (args.P & (args.P - 1)) || args.A > args.P || args.A < 1 ||
       args.max_det < 1 || batch < 1)
     return cudaErrorInvalidValue;
-  const size_t smem = (size_t)args.P * 5;  // keys + flags
+  const size_t smem =
+      pose_nms_smem_bytes(args.P, args.A, args.boxes_in_smem != 0, args.kept_idx_smem ? args.max_det : 0);
+  if (smem > (size_t)kPoseNmsSmemMax) return cudaErrorInvalidValue;
   static bool attr = false;
   if (!attr) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(pose_nms_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)((size_t)kPoseNmsMaxAnchors * 5));
+    const cudaError_t e = cudaFuncSetAttribute(pose_nms_k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPoseNmsSmemMax);
     if (e != cudaSuccess) return e;
     attr = true;
   }
