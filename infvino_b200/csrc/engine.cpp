@@ -1861,6 +1861,7 @@ void Engine::set_stream(cudaStream_t s) {
 }
 
 void Engine::upload_input_f16(const void *src, int batch, bool on_device) {
+  require_device();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
   check(cudaMemcpyAsync(input_device_ptr(), src, (size_t)input_numel() * batch * 2,
@@ -1869,6 +1870,7 @@ void Engine::upload_input_f16(const void *src, int batch, bool on_device) {
 }
 
 void Engine::upload_input_f32(const float *src, int batch, bool on_device) {
+  require_device();
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
@@ -2084,6 +2086,7 @@ void Engine::capture(int batch) {
 }
 
 void Engine::run(int batch) {
+  require_device();
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
@@ -2104,6 +2107,7 @@ void Engine::run(int batch) {
 }
 
 void Engine::run_profiled(int batch, std::vector<float> *step_ms) {
+  require_device();
   pdl_scope();
   check(cudaSetDevice(device_), "cudaSetDevice");
   tune(batch);
@@ -2122,6 +2126,7 @@ void Engine::run_profiled(int batch, std::vector<float> *step_ms) {
 }
 
 void Engine::download_output_f16(int i, void *dst, int batch, bool on_device) {
+  require_device();
   const TensorRt &t = T_[(size_t)tid(output_name(i))];
   if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
   check(cudaMemcpyAsync(dst, t.dptr, (size_t)t.numel * batch * 2,
@@ -2130,6 +2135,7 @@ void Engine::download_output_f16(int i, void *dst, int batch, bool on_device) {
 }
 
 void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
+  require_device();
   pdl_scope();
   const TensorRt &t = T_[(size_t)tid(output_name(i))];
   if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
@@ -2150,6 +2156,7 @@ void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
 }
 
 void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
+  require_device();
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
@@ -2277,6 +2284,7 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
 
 void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, int kdims, const float *letterbox,
                          int *counts, float *dets) {
+  require_device();
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   if (output_count() < 1) throw std::runtime_error("PoseDecoder: unexpected output shape");
@@ -2356,6 +2364,7 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
 }
 
 bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {
+  require_device();
   pdl_scope();
   auto it = tid_.find(name);
   if (it == tid_.end()) return false;
@@ -2386,6 +2395,7 @@ bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch)
 
 int Engine::read_tensor_f16_staged(const std::string &name, void *host_dst, int batch, void *scratch,
                                    int64_t scratch_bytes, int64_t *need_bytes) {
+  require_device();
   pdl_scope();
   auto it = tid_.find(name);
   if (it == tid_.end()) return 1;
@@ -2413,6 +2423,7 @@ int Engine::read_tensor_f16_staged(const std::string &name, void *host_dst, int 
 }
 
 int Engine::graph_kernel_count(int batch) {
+  require_device();
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
@@ -2432,6 +2443,10 @@ int Engine::graph_kernel_count(int batch) {
   }
   cudaGraphDestroy(g);
   return kernels;
+}
+
+void Engine::require_device() const {
+  if (dry_) throw std::runtime_error("CudaPlanModel: a dry run handle has no device state (IVC_FLAG_DRY_RUN)");
 }
 
 void Engine::pdl_scope() const { g_launch_pdl = (flags_ & kFlagNoPdl) == 0; }

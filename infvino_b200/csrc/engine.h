@@ -165,6 +165,7 @@ class Engine {
   std::vector<std::pair<int, int>> tail_uses_;  // (tensor, node) reads of fused tails, for liveness
   void plan_tails();
   void pdl_scope() const;  // launches on this thread follow kFlagNoPdl
+  void require_device() const;  // throws for a dry run handle (no device state)
   void tune(int batch);    // per-step load-time tuning for this batch size (once)
   std::set<int> tuned_;
   std::vector<Step> steps_;

@@ -240,3 +240,15 @@ def test_sibling_convs_merged(model_plans):
             assert f"conv3x3:model.22.{br}.{scale}.0.out" not in {s["name"] for s in m.steps()}
         want = sum(plain[f"conv3x3:model.22.{br}.{scale}.0.out"]["flops_per_image"] for br in ("cv2", "cv3", "cv4"))
         assert merged["conv3x3:" + root]["flops_per_image"] == want
+
+
+def test_dry_run_handle_refuses_device_calls(model_plans):
+    """A dry run builds everything but device state: calls that would run,
+    read or decode refuse with a clear error instead of touching the GPU."""
+    m = dry(model_plans["yolov8n-pose"], 2)
+    x = np.zeros(m.inputNumel(), dtype=np.uint16)
+    for call in (lambda: m.setInput(x, 1), lambda: m.run(1), lambda: m.readOutput(0, 1),
+                 lambda: m.decodePose(1)):
+        with pytest.raises(ivb.NativeError) as e:
+            call()
+        assert "dry run handle" in str(e.value), str(e.value)
