@@ -150,10 +150,14 @@ def run_kernels_only(args, local: int) -> int:
         m.run_async(args.batch)
     m.synchronize()
     dt = (time.perf_counter() - t0) / max(1, args.steps)
+    n_dets = None
+    if args.decode:  # pose decode + NMS of the last replay's output, inside the profiled range
+        n_dets = [len(d) for d in m.decodePose(args.batch)]
     if cu is not None:
         cu.cuProfilerStop()
     print(json.dumps({"mode": "kernels", "workload": args.workload, "batch": args.batch,
-                      "launches_per_step": m.launch_count(args.batch), "wall_ms_per_step": round(dt * 1e3, 4)}))
+                      "launches_per_step": m.launch_count(args.batch), "wall_ms_per_step": round(dt * 1e3, 4),
+                      "detections_per_image": n_dets}))
     m.close()
     return 0
 
@@ -319,6 +323,7 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default=MODEL)
     ap.add_argument("--mode", default="full", choices=["full", "kernels"])
+    ap.add_argument("--decode", action="store_true", help="kernels mode: also run the device pose decode + NMS")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":

@@ -84,7 +84,8 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   for (int size = 2; size <= p.P; size <<= 1)
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int t = tid; t < p.P / 2; t += blockDim.x) {
-        const int lo = 2 * stride * (t / stride) + (t % stride), hi = lo + stride;
+        // lo = 2 * stride * (t / stride) + t % stride, stride a power of two
+        const int lo = 2 * t - (t & (stride - 1)), hi = lo + stride;
         const uint32_t x = key[lo], y = key[hi];
         if ((x > y) == ((lo & size) == 0)) {
           key[lo] = y;
