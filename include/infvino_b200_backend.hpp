@@ -36,6 +36,16 @@ struct DeviceInfo {
   int ordinal = 0;
 };
 
+// One pose detection of decodePose(): the reference's Detection for a pose
+// model (include/infvino/Types.hpp:38-45: box, score, class 0, keypoints)
+// without OpenCV types, plus the anchor it came from.
+struct PoseDetection {
+  int anchor = 0;
+  float score = 0.f;
+  float x = 0.f, y = 0.f, w = 0.f, h = 0.f;  // box in image coordinates
+  std::vector<float> keypoints;             // x, y per keypoint
+};
+
 template <class TensorT, class ModelInfoT>
 class CudaBackendT {
  public:
@@ -81,6 +91,36 @@ class CudaBackendT {
     }
     if (ivc_infer_f32(m_, input_f32, numel, batch, ptrs.data()) != IVC_OK) throw std::runtime_error(ivc_last_error(m_));
     return outs;
+  }
+
+  // Pose decode + greedy NMS of the last infer() on the device, in place of
+  // PoseDecoder::decode with nmsPerClass (src/Decoders.cpp:127-179, :33-65):
+  // per image, the detections in descending score.  `letterbox` (host):
+  // [batch][scale, pad_left, pad_top], or null for scale 1 and no padding.
+  std::vector<std::vector<PoseDetection>> decodePose(int batch = 1, float conf = 0.25f, float iou = 0.7f,
+                                                     int max_det = 300, int nk = 17, int kdims = 3,
+                                                     const float *letterbox = nullptr) {
+    std::lock_guard<std::mutex> lock(mutex_);
+    const size_t S = 6 + 2 * (size_t)nk;
+    std::vector<int> counts((size_t)batch);
+    std::vector<float> dets((size_t)batch * (size_t)max_det * S);
+    if (ivc_decode_pose(m_, batch, conf, iou, max_det, nk, kdims, letterbox, counts.data(), dets.data()) != IVC_OK)
+      throw std::runtime_error(ivc_last_error(m_));
+    std::vector<std::vector<PoseDetection>> out((size_t)batch);
+    for (int b = 0; b < batch; ++b)
+      for (int k = 0; k < counts[(size_t)b]; ++k) {
+        const float *r = &dets[((size_t)b * (size_t)max_det + (size_t)k) * S];
+        PoseDetection d;
+        d.anchor = (int)r[0];
+        d.score = r[1];
+        d.x = r[2];
+        d.y = r[3];
+        d.w = r[4];
+        d.h = r[5];
+        d.keypoints.assign(r + 6, r + S);
+        out[(size_t)b].push_back(std::move(d));
+      }
+    return out;
   }
 
   ivc_model *handle() const { return m_; }

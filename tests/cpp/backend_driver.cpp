@@ -3,6 +3,9 @@
 // infer twice (A then B), dump the last outputs as raw f32.
 //   backend_driver <plan> <input_a.f32> <input_b.f32> <out.f32>
 //   backend_driver --empty-plan     (checks the empty-plan error message)
+//   backend_driver --pose <plan> <input.f32> <dets.f32>
+//                                   (infer one image, decodePose on the device,
+//                                    dump anchor, score, box, keypoints per detection)
 #include <cstdio>
 #include <fstream>
 #include <iostream>
@@ -42,6 +45,22 @@ int main(int argc, char **argv) {
       return std::string(e.what()).find("ModelInfo.plan is empty") != std::string::npos ? 0 : 1;
     }
     return 1;
+  }
+  if (argc == 5 && std::string(argv[1]) == "--pose") {
+    Backend b(ModelInfo{argv[2]});
+    size_t n = 1;
+    for (auto d : b.inputDims()) n *= (size_t)d;
+    const auto x = read_f32(argv[3]);
+    b.infer(x.data(), n);
+    const auto dets = b.decodePose();
+    std::ofstream o(argv[4], std::ios::binary);
+    for (const auto &d : dets[0]) {
+      const float head[6] = {(float)d.anchor, d.score, d.x, d.y, d.w, d.h};
+      o.write(reinterpret_cast<const char *>(head), sizeof(head));
+      o.write(reinterpret_cast<const char *>(d.keypoints.data()), (std::streamsize)(d.keypoints.size() * 4));
+    }
+    std::cout << "ok " << dets[0].size() << " detections\n";
+    return 0;
   }
   if (argc != 5) return 2;
   Backend b(ModelInfo{argv[1]});

@@ -52,3 +52,22 @@ def test_cpp_backend_matches_python_path(tmp_path, model_plans):
     m = ivb.PlanModel(plan)
     ref = m.infer_f32(b, 1)[0]
     assert np.array_equal(got, ref)
+
+
+@pytest.mark.gpu
+def test_cpp_backend_decode_pose_matches_python_path(tmp_path, plan_dir):
+    """decodePose() of the C++ drop-in returns the detections of the Python
+    path's decodePose (both over ivc_decode_pose) for the same image."""
+    from infvino_b200 import plangen
+    exe = compile_driver(str(tmp_path))
+    plan = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_peaked_cpp"), cls_gain=100.0, cls_shift=-3.0)
+    x = np.random.default_rng(7).random(3 * 640 * 640, dtype=np.float32)
+    x.tofile(tmp_path / "x.f32")
+    r = subprocess.run([exe, "--pose", plan, str(tmp_path / "x.f32"), str(tmp_path / "d.f32")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    got = np.fromfile(tmp_path / "d.f32", dtype=np.float32).reshape(-1, 6 + 34)
+    m = ivb.PlanModel(plan)
+    m.infer_f32(x, 1)
+    ref = m.decodePose(1)[0]
+    assert got.shape[0] > 0 and np.array_equal(got, ref)
