@@ -14,7 +14,7 @@
 //   4. greedy suppression in that order (IoU above `iou` removes a later
 //      candidate), stopping once `max_det` are kept: kept boxes come out in
 //      score order, so they are the first `max_det` of the reference's result;
-//      a candidate is tested against the boxes kept so far, 32 candidates at a
+//      a candidate is tested against the boxes kept so far, 64 candidates at a
 //      time.
 // All float arithmetic is the reference's, operation by operation, with
 // round-to-nearest intrinsics so that nothing is contracted into an FMA.
@@ -101,44 +101,60 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   // 4. greedy suppression.  A candidate is kept when no earlier kept box
   // overlaps it above `iou` (the reference's loop, which removes every later
   // candidate a kept box overlaps, decides the same).  Candidates go in groups
-  // of 32: warp w tests kept boxes w, w + 32, ... against the group (lane =
-  // candidate), warp r tests group candidate r against the later ones; warp 0
-  // then walks the group in order with the two bit masks.
-  __shared__ uint32_t sup_mask, row_mask[32];
+  // of 64, lane l holding group candidates l and l + 32: warp w tests kept
+  // boxes w, w + 32, ... against the group, and group rows w and w + 32 (one
+  // candidate against the later ones in the group); thread 0 then walks the
+  // group in order with 64-bit masks.  Two barriers per group.
+  __shared__ unsigned long long sup_mask, row_mask[64];
   __shared__ int n_kept;
   const int warp = tid >> 5, lane = tid & 31;
   int *kept_idx = p.kept_idx_smem ? kept_sm : p.kept + (long long)b * p.max_det;
-  if (tid == 0) n_kept = 0;
+  if (tid == 0) {
+    n_kept = 0;
+    sup_mask = 0ull;
+  }
   __syncthreads();
-  for (int base = 0; base < n && n_kept < p.max_det; base += 32) {
+  for (int base = 0; base < n && n_kept < p.max_det; base += 64) {
     const int nk_now = n_kept;
-    const int c = base + lane;
-    const bool valid = c < n;
-    const float4 bc = valid ? bx[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    bool hit = false;
-    for (int k = warp; k < nk_now && valid; k += 32) hit = hit || box_iou(bx[kept_idx[k]], bc) > p.iou;
-    const uint32_t sup = __ballot_sync(0xffffffffu, hit);
-    // row `warp`: group candidate base + warp against the later ones (lanes above it)
-    const int r = base + warp;
-    const bool later = valid && lane > warp && r < n;
-    const bool over = later && box_iou(bx[r], bc) > p.iou;
-    const uint32_t row = __ballot_sync(0xffffffffu, over);
-    if (tid == 0) sup_mask = 0;
-    __syncthreads();
+    const int c0 = base + lane, c1 = base + 32 + lane;
+    const bool v0 = c0 < n, v1 = c1 < n;
+    const float4 b0 = v0 ? bx[c0] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 b1 = v1 ? bx[c1] : make_float4(0.f, 0.f, 0.f, 0.f);
+    bool h0 = false, h1 = false;
+    for (int k = warp; k < nk_now && (v0 || v1); k += 32) {
+      const float4 bk = bx[kept_idx[k]];
+      h0 = h0 || (v0 && box_iou(bk, b0) > p.iou);
+      h1 = h1 || (v1 && box_iou(bk, b1) > p.iou);
+    }
+    const unsigned long long sup = (unsigned long long)__ballot_sync(0xffffffffu, h0) |
+                                   ((unsigned long long)__ballot_sync(0xffffffffu, h1) << 32);
+    unsigned long long rows[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {  // group row r = warp + 32 q against group columns lane, lane + 32
+      const int r = warp + 32 * q;
+      const bool rv = base + r < n;
+      const float4 br = rv ? bx[base + r] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool o0 = rv && v0 && lane > r && box_iou(br, b0) > p.iou;
+      const bool o1 = rv && v1 && 32 + lane > r && box_iou(br, b1) > p.iou;
+      rows[q] = (unsigned long long)__ballot_sync(0xffffffffu, o0) |
+                ((unsigned long long)__ballot_sync(0xffffffffu, o1) << 32);
+    }
     if (lane == 0) {
       if (sup) atomicOr(&sup_mask, sup);
-      row_mask[warp] = row;
+      row_mask[warp] = rows[0];
+      row_mask[warp + 32] = rows[1];
     }
     __syncthreads();
     if (tid == 0) {
-      uint32_t m = sup_mask;
+      unsigned long long m = sup_mask;
       int nk = n_kept;
-      for (int j = 0; j < 32 && base + j < n && nk < p.max_det; ++j)
-        if (!((m >> j) & 1u)) {
+      for (int j = 0; j < 64 && base + j < n && nk < p.max_det; ++j)
+        if (!((m >> j) & 1ull)) {
           kept_idx[nk++] = base + j;
           m |= row_mask[j];
         }
       n_kept = nk;
+      sup_mask = 0ull;  // for the next group (its ORs come after the next barrier)
     }
     __syncthreads();
   }
