@@ -57,3 +57,50 @@ def test_device_pose_decode_every_anchor_a_candidate(plan_dir):
         assert check_against_oracle(m, y, 2, 0.25, 0.7, 300, None) == 600
     assert check_against_oracle(m, y, 2, 0.25, 0.5, 40, None) == 80
     m.close()
+
+
+def identity_plan(out_dir, A):
+    """A plan whose output is its input ([1, 56, A] plus a zero initializer,
+    exact in fp16): the decoder's input can be set value by value."""
+    pw = plangen.PlanWriter(5)
+    x = pw.input("x", [1, 56, A])
+    z = pw.init("zero", np.zeros((1, 56, A), dtype=np.float16))
+    pw.output(pw.add(x, z, name="y"))
+    return pw.save(out_dir)
+
+
+def adversarial_outputs(rng, batch, A):
+    """Pose outputs built to stress the decoder: scores from a handful of fp16
+    values (exact ties everywhere, one of them exactly `conf` and one just
+    below it), clusters of identical boxes, boxes of zero and negative size,
+    small random shifts that put many IoUs near the threshold, and random
+    keypoints."""
+    y = np.zeros((batch, 56, A), dtype=np.float32)
+    levels = np.array([0.25, 0.2499, 0.5, 0.75, 0.875, 1.0, 0.0], dtype=np.float16).astype(np.float32)
+    for b in range(batch):
+        y[b, 4] = rng.choice(levels, A)
+        centers = rng.uniform(0, 640, (A // 16, 2))
+        k = rng.integers(0, len(centers), A)
+        y[b, 0] = centers[k, 0] + rng.choice([0.0, 0.0, 1.5, -3.0, 8.0], A)
+        y[b, 1] = centers[k, 1] + rng.choice([0.0, 2.0, -4.0], A)
+        y[b, 2] = rng.choice([40.0, 48.0, 0.0, -5.0, 64.0, 20.0], A)
+        y[b, 3] = rng.choice([40.0, 32.0, 56.0, 0.0], A)
+        y[b, 5:] = rng.uniform(-50, 700, (51, A))
+    return y.astype(np.float16)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("conf,iou,max_det", [(0.25, 0.7, 300), (0.5, 0.45, 50), (0.0, 0.0, 2048)])
+def test_device_pose_decode_adversarial(plan_dir, conf, iou, max_det):
+    A, B = 2048, 3
+    p = identity_plan(os.path.join(plan_dir, "pose_identity"), A)
+    m = ivb.PlanModel(p, max_batch=B)
+    y16 = adversarial_outputs(np.random.default_rng(63), B, A)
+    m.setInput(y16.view(np.uint16).ravel(), B)
+    m.run(B)
+    y = y16.astype(np.float32)
+    assert np.array_equal(ivb.f16_to_f32(m.readOutput(0, B)).reshape(B, 56, A), y)
+    lb = np.array([[0.75, 16.0, 0.0], [1.0, 0.0, 0.0], [0.5, 0.0, 140.0]], dtype=np.float32)
+    n = check_against_oracle(m, y, B, conf, iou, max_det, lb)
+    assert n > 0
+    m.close()
