@@ -148,7 +148,7 @@ struct PoseNmsArgs {
   int *counts;             // [batch]
   float *dets;             // [batch][max_det][6 + 2 * nk]: anchor, score, x, y, w, h, then (x, y) per keypoint
 };
-constexpr int kPoseNmsSmemMax = 226 * 1024;  // dynamic; the kernel's own static shared memory fits beside it
+constexpr int kPoseNmsSmemMax = 225 * 1024;  // dynamic; the kernel's static shared memory (~1 KB) fits beside it
 inline size_t pose_nms_smem_bytes(int P, int A, bool boxes_in_smem, int kept_in_smem) {
   return (size_t)P * 4 + (boxes_in_smem ? (size_t)A * 16 : 0) + (size_t)kept_in_smem * 4;  // keys, boxes, kept list
 }

@@ -192,7 +192,10 @@ cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st)
   static bool attr = false;
   if (!attr) {
     const cudaError_t e = cudaFuncSetAttribute(pose_nms_k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPoseNmsSmemMax);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();  // a later launch's error check must not report this one
+      return e;
+    }
     attr = true;
   }
   launch_kernel(pose_nms_k, dim3((unsigned)batch), dim3(kPoseNmsThreads), smem, st, args);
