@@ -620,7 +620,10 @@ cudaError_t launch_conv_tc(const ConvTcArgs &args, int grid, cudaStream_t stream
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();  // a later launch's error check must not report this one
+      return e;
+    }
     attr_set[dev] = true;
   }
   return launch_kernel(conv_tc_kernel, dim3(grid), dim3(kConvThreads), (size_t)args.smem_bytes, stream, args);

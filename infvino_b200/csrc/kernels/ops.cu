@@ -1355,7 +1355,11 @@ cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t
   if (vec) {
     static bool attr = false;
     if (!attr) {
-      cudaFuncSetAttribute(tail_vm_k<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      const cudaError_t e = cudaFuncSetAttribute(tail_vm_k<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      if (e != cudaSuccess) {
+        (void)cudaGetLastError();  // a later launch's error check must not report this one
+        return e;
+      }
       attr = true;
     }
     launch_kernel(tail_vm_k<4>, dim3(dim3(grid_for(n, threads), prog.n_comp)), dim3(threads), smem, st, prog, n);
