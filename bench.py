@@ -265,9 +265,18 @@ def gpu_pci_id(dev: int) -> str:
         return str(dev)
 
 
+def host_cores() -> int:
+    """Threads this process may run on (its CPU affinity), not the OpenMP
+    default, which torchrun sets to 1."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(plan: str, budget_s: float = 12.0):
     from oracle import ivref
-    cores = ivref.set_threads(0)
+    cores = ivref.set_threads(host_cores())
     o = ivref.OraclePlan(plan)
     x = np.random.default_rng(SEED).random(o.input_numel, dtype=np.float32)
     o.run(x, 1)  # warm
@@ -287,7 +296,7 @@ def run_reference(args, rank: int, world: int) -> int:
         return 0
     from oracle import ivref
     plan = make_plan(0)
-    cores = ivref.set_threads(0)
+    cores = ivref.set_threads(host_cores())
     o = ivref.OraclePlan(plan)
     x = np.random.default_rng(SEED).random(o.input_numel, dtype=np.float32)
     for _ in range(max(0, args.warmup)):
@@ -313,6 +322,58 @@ def run_reference(args, rank: int, world: int) -> int:
     return 0
 
 
+def bind_rank_cpus(local: int, local_world: int):
+    """Multi-GPU runs: binds this rank to CPUs of its GPU's NUMA node, split
+    evenly among the local ranks whose GPUs share that node, so that its
+    host-cast threads and the pinned buffers it touches first sit next to its
+    GPU and no two ranks share cores.  Without NUMA information the allowed
+    CPUs are split evenly by local rank.  Returns the CPUs bound (or None)."""
+    try:
+        allowed = sorted(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return None
+
+    def node_of(dev):
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(dev)
+            path = f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/numa_node"
+            with open(path) as f:
+                return int(f.read().strip())
+        except Exception:
+            return -1
+
+    def node_cpus(node):
+        try:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                spec = f.read().strip()
+        except OSError:
+            return []
+        cpus = []
+        for part in spec.split(","):
+            if "-" in part:
+                a, b = part.split("-")
+                cpus.extend(range(int(a), int(b) + 1))
+            elif part:
+                cpus.append(int(part))
+        return [c for c in cpus if c in set(allowed)]
+
+    nodes = [node_of(d) for d in range(local_world)]
+    pool, peers = allowed, list(range(local_world))
+    if nodes[local] >= 0:
+        cand = node_cpus(nodes[local])
+        if len(cand) >= sum(1 for n in nodes if n == nodes[local]):
+            pool, peers = cand, [d for d in range(local_world) if nodes[d] == nodes[local]]
+    k = peers.index(local)
+    per = max(1, len(pool) // len(peers))
+    mine = pool[k * per:(k + 1) * per] or pool
+    try:
+        os.sched_setaffinity(0, mine)
+    except OSError:
+        return None
+    return mine
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -324,6 +385,9 @@ def main() -> int:
     ap.add_argument("--workload", default=MODEL)
     ap.add_argument("--mode", default="full", choices=["full", "kernels"])
     ap.add_argument("--decode", action="store_true", help="kernels mode: also run the device pose decode + NMS")
+    ap.add_argument("--min-replays", type=int, default=200,
+                    help="device-resident timing: each step repeats the graph replay so that at least this many "
+                         "replays are timed")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
@@ -336,6 +400,8 @@ def main() -> int:
 
     group = RankGroup(world)
     torch.cuda.set_device(local)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    bound_cpus = bind_rank_cpus(local, local_world) if world > 1 else None
     B = args.batch
     plan = make_plan(rank)
     model = ivb.PlanModel(plan, device=local, max_batch=B)
@@ -353,7 +419,8 @@ def main() -> int:
     barrier = group.barrier
     max_over_ranks = group.max
 
-    # ---- device-resident throughput: input converted once, K graph replays
+    # ---- device-resident throughput: input converted once, then steps of R
+    # graph replays each (R such that at least --min-replays are timed)
     y_dev = torch.empty(B * n_out, dtype=torch.float32, device=f"cuda:{local}")
     model.infer_f32_device(x_dev.data_ptr(), B, [y_dev.data_ptr()], stream.cuda_stream)
     for _ in range(max(3, args.warmup)):
@@ -361,45 +428,85 @@ def main() -> int:
     stream.synchronize()
     model.synchronize()
     launches = model.launch_count(B)
+    reps = max(1, -(-args.min_replays // max(1, args.steps)))
     sampler = ClockSampler(gpu_pci_id(local))
     barrier()
     torch.cuda.synchronize(local)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
-        model.run_async(B, stream.cuda_stream)
+        for _ in range(reps):
+            model.run_async(B, stream.cuda_stream)
     ev1.record(stream)
     ev1.synchronize()
     torch.cuda.synchronize(local)
     barrier()
     clocks = sampler.stop()
     model.synchronize()  # raises if a kernel reported a bounded-wait timeout
-    ms = ev0.elapsed_time(ev1) / args.steps
+    timed_replays = args.steps * reps
+    region_ms = ev0.elapsed_time(ev1)
+    ms = region_ms / timed_replays
     ms_max = max_over_ranks(ms)
     value = world * B / (ms_max / 1e3)
 
-    # ---- end to end through the public API (ClBackend::infer equivalent)
+    # ---- end to end through the public API (ClBackend::infer equivalent),
+    # from pinned host memory (the headline e2e) and from pageable memory
+    # (what a std::vector / cv::Mat caller passes)
     outs = [y_host.numpy()]
     for _ in range(2):
         model.infer_f32(x_host.numpy(), B, outs)
     e2e_steps = max(3, min(args.steps, 20))
-    barrier()
-    torch.cuda.synchronize(local)
-    t0 = time.perf_counter()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        model.infer_f32(x_host.numpy(), B, outs)
-    e1.record(stream)
-    e1.synchronize()
-    wall = (time.perf_counter() - t0) / e2e_steps * 1e3
-    e2e_ms = max_over_ranks(max(e0.elapsed_time(e1) / e2e_steps, wall))
+
+    def time_e2e(src, dst, steps):
+        barrier()
+        torch.cuda.synchronize(local)
+        t0 = time.perf_counter()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            model.infer_f32(src, B, dst)
+        e1.record(stream)
+        e1.synchronize()
+        wall = (time.perf_counter() - t0) / steps * 1e3
+        return max_over_ranks(max(e0.elapsed_time(e1) / steps, wall))
+
+    e2e_ms = time_e2e(x_host.numpy(), outs, e2e_steps)
     e2e_val = world * B / (e2e_ms / 1e3)
+    x_page = np.array(x_host.numpy(), copy=True)
+    y_page = [np.empty(B * n_out, dtype=np.float32)]
+    model.infer_f32(x_page, B, y_page)
+    e2e_page_ms = time_e2e(x_page, y_page, max(3, e2e_steps // 2))
+    del x_page, y_page
+
+    # ---- the host link alone: the same bytes per step as the e2e path, as
+    # plain pinned copies (H2D and D2H on two streams, all ranks at once); the
+    # bound the e2e figure is measured against
+    hb, db = h2d_bytes(B, n_in), B * n_out * 4
+    src_h = x_host.view(torch.uint8)[:hb]
+    dst_d = torch.empty(hb, dtype=torch.uint8, device=f"cuda:{local}")
+    src_d = torch.empty(db, dtype=torch.uint8, device=f"cuda:{local}")
+    dst_h = y_host.view(torch.uint8)[:db]
+    s_in, s_out = torch.cuda.Stream(device=local), torch.cuda.Stream(device=local)
+    for _ in range(2):
+        dst_d.copy_(src_h, non_blocking=True)
+        dst_h.copy_(src_d, non_blocking=True)
+    torch.cuda.synchronize(local)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(s_in):
+            dst_d.copy_(src_h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            dst_h.copy_(src_d, non_blocking=True)
+    torch.cuda.synchronize(local)
+    link_ms = max_over_ranks((time.perf_counter() - t0) / e2e_steps * 1e3)
+    del src_h, dst_d, src_d, dst_h
 
     # ---- pose decode + NMS on the device (ivc_decode_pose) of the last e2e
     # batch: random-init class scores are all ~0.5, so every anchor is a
     # candidate and each image reaches the max_det cut (the worst case)
+    model.infer_f32(x_host.numpy(), B, outs)
     model.decodePose(B)
     dec_t = []
     for _ in range(5):
@@ -415,7 +522,7 @@ def main() -> int:
     x1 = x_host.numpy()[:n_in]
     y1 = [np.empty(n_out, dtype=np.float32)]
     model.infer_f32(x1, 1, y1)
-    for _ in range(10):
+    for _ in range(20):
         model.run_async(1, stream.cuda_stream)
     stream.synchronize()
     for _ in range(200):
@@ -434,12 +541,13 @@ def main() -> int:
     pk, pk_src = peaks()
     steps = model.steps()
     prof = np.zeros(len(steps))
-    reps = 3
-    for _ in range(reps):
+    nprof = 3
+    for _ in range(nprof):
         prof += np.array(model.profile(B))
-    prof /= reps
+    prof /= nprof
     bw = pk["hbm_gbs"] * 1e9
-    tc = pk["bf16_tflops_sustained"] * 1e12
+    # the step is milliseconds long, not seconds: the burst tensor peak applies
+    tc = pk["bf16_tflops"] * 1e12
 
     def t_roof(s):
         return max(s["flops_per_image"] * B / tc, (s["act_bytes_per_image"] * B + s["fixed_bytes"]) / bw)
@@ -451,7 +559,9 @@ def main() -> int:
     conv_ms = float(sum(prof[i] for i in conv))
     conv_bytes = float(sum(steps[i]["act_bytes_per_image"] * B + steps[i]["fixed_bytes"] for i in conv))
     conv_flops = float(sum(steps[i]["flops_per_image"] * B for i in conv))
+    conv_troof = float(sum(t_roof(steps[i]) for i in conv))
     achieved = conv_bytes / (conv_ms / 1e3) / 1e9
+    share = conv_ms / float(prof.sum())
     troof_total = sum(t_roof(s) for s in steps)
     net_frac = troof_total / (ms / 1e3)
     # DRAM bytes of the same launches from the committed ncu capture of this
@@ -464,18 +574,23 @@ def main() -> int:
             t = json.load(f)
         if t.get("launches_per_run") == len(conv):
             traffic = int(t["dram_bytes_read"] + t["dram_bytes_write"])
+    # the conv share of the graph step (eager launch shares applied to the
+    # measured graph replay time): an upper bound on the conv time inside the graph
+    graph_conv_ms = share * ms
     roofline = {
         "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM conv, %d launches/step)" % len(conv),
         "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
         "algorithmic_bytes": int(conv_bytes),
-        "per": "network step (bytes over all conv launches of one step)",
+        "per": "network step (bytes over all conv launches of one step); launch times from CUDA events per launch",
         "peak_source": pk_src + " (hbm_gbs copy bandwidth)",
         "achieved_tflops": round(conv_flops / (conv_ms / 1e3) / 1e12, 1),
-        "share_of_step": round(conv_ms / float(prof.sum()), 3),
+        "share_of_step": round(share, 3),
+        "frac_graph_share": round(conv_bytes / (graph_conv_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+        "frac_of_layer_roofline": round(conv_troof / (conv_ms / 1e3), 4),
     }
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cpu = cpu_baseline(plan)
         except Exception as e:  # reported, not fatal
@@ -498,14 +613,29 @@ def main() -> int:
                        "batch_per_gpu": B, "parallelism": f"batch sharding x{world}, no collectives",
                        "l2": "inputs larger than L2 (157 MB fp16 input + >300 MB activations per step)",
                        "compute": "fp16 storage, fp32 accumulation"},
-            "gpu_launches": launches * args.steps,
+            "timed_replays": timed_replays, "replays_per_step": reps,
+            "timed_region_ms": round(region_ms, 2),
+            "step_definition": "one CUDA-graph replay of the network over one batch of 64 images; ms_per_step is per "
+                               "replay (each of the K timed steps repeats the replay replays_per_step times)",
+            "gpu_launches": launches * timed_replays,
             "e2e": {"value": round(e2e_val, 1), "unit": "images/s", "h2d_bytes_per_step": h2d_bytes(B, n_in),
-                    "d2h_bytes_per_step": B * n_out * 4, "ms_per_step": round(e2e_ms, 3)},
+                    "d2h_bytes_per_step": B * n_out * 4, "ms_per_step": round(e2e_ms, 3),
+                    "host_memory": "pinned",
+                    "h2d_gbs_per_rank": round(hb / (e2e_ms / 1e3) / 1e9, 2),
+                    "d2h_gbs_per_rank": round(db / (e2e_ms / 1e3) / 1e9, 2),
+                    "pageable": {"value": round(world * B / (e2e_page_ms / 1e3), 1), "ms_per_step": round(e2e_page_ms, 3)},
+                    "link_bound": {"ms_per_step": round(link_ms, 3),
+                                   "value": round(world * B / (link_ms / 1e3), 1),
+                                   "what": "the same H2D and D2H bytes as plain pinned copies on two streams, all "
+                                           "ranks at once (max over ranks)",
+                                   "frac_achieved": round(link_ms / e2e_ms, 4)},
+                    "rank_cpus": len(bound_cpus) if bound_cpus else host_cores()},
             "b1_p50_ms": round(float(np.median(lat)), 4), "b1_p99_ms": round(float(np.percentile(lat, 99)), 4),
             "b1_e2e_p50_ms": round(float(np.median(lat_e2e)), 4),
             "roofline": roofline,
             "network_roofline_frac": round(net_frac, 4),
             "network_roofline_ms": round(troof_total * 1e3, 4),
+            "network_roofline_peaks": f"{pk_src}: hbm_gbs {pk['hbm_gbs']}, bf16_tflops {pk['bf16_tflops']} (burst)",
             "family_ms": {k: round(v, 4) for k, v in sorted(fam_ms.items(), key=lambda kv: -kv[1])},
             "cpu_baseline": cpu,
             "pose_decode": pose_decode,

@@ -96,8 +96,9 @@ int ivc_max_batch(const ivc_model *m);
  * run, and every output written as f32 to outputs[i] (batch*output_numel(i)
  * values, host memory).  Synchronous.  Batches of 32 or more are pipelined in
  * chunks, and half of their images are cast on the host by a process-wide
- * pool of worker threads (up to 16, created at the first such call), so that
- * fewer bytes cross PCIe; the first call also pins two chunk buffers. */
+ * pool of worker threads (one per CPU of the process's affinity mask, up to
+ * 16, created at the first such call), so that fewer bytes cross PCIe; the
+ * first call also pins two chunk buffers. */
 int ivc_infer_f32(ivc_model *m, const float *input, size_t numel, int batch, float *const *outputs);
 
 /* PlanModel-style split calls (fp16 host buffers, synchronous). */
@@ -155,6 +156,16 @@ int ivc_step_info(const ivc_model *m, int i, const char **name, const char **fam
 int ivc_profile(ivc_model *m, int batch, float *step_ms, int n);
 /* Number of kernel launches one ivc_run(batch) performs (kernel nodes of its CUDA graph). */
 int ivc_launch_count(ivc_model *m, int batch, int *count);
+
+/* Diagnostic (no counterpart in the reference): settings of the convolution
+ * kernels' bounded waits.  `limit_cycles` is the limit of every working wait
+ * in SM clocks (the default is about 2 s); with `probe` nonzero each conv CTA
+ * first waits on a barrier that nothing arrives on, so that wait runs out, the
+ * kernel drains its copies and MMAs, releases TMEM and reports its status, and
+ * the next synchronising call returns IVC_ERR_KERNEL.  Lets a test exercise the
+ * timeout path without any GPU fault; the handle stays usable.  Takes effect
+ * from the next run (captured graphs are captured again). */
+int ivc_debug_conv_wait(ivc_model *m, long long limit_cycles, int probe);
 
 /* Activation pool statistics (bytes at max_batch). */
 int ivc_pool_stats(const ivc_model *m, int64_t *requested_bytes, int64_t *arena_bytes, int64_t *weight_bytes,

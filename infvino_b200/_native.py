@@ -58,6 +58,7 @@ SIGNATURES = {
     "ivc_step_info": (_i32, [_vp, _i32, _P(_cp), _P(_cp), _P(_f64), _P(_f64), _P(_f64)]),
     "ivc_profile": (_i32, [_vp, _i32, _P(ctypes.c_float), _i32]),
     "ivc_launch_count": (_i32, [_vp, _i32, _P(_i32)]),
+    "ivc_debug_conv_wait": (_i32, [_vp, ctypes.c_longlong, _i32]),
     "ivc_pool_stats": (_i32, [_vp, _P(_i64), _P(_i64), _P(_i64), _P(_i32), _P(_i32), _P(_i32), _P(_i32),
                               _P(_i32)]),
     "ivc_describe": (_i32, [_vp, _cp, _sz]),

@@ -266,6 +266,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 int ivc_read_tensor_f16_noalloc(ivc_model *m, const char *name, uint16_t *dst, int batch) {
   return guarded(m, [&]() -> int {
     if (!name || !dst || batch < 1 || batch > m->eng->max_batch()) return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
+    m->eng->require_device();  // a dry run handle fails here, before any CUDA call
     const int dev = m->eng->device();
     if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(m, IVC_ERR_ARGUMENT, "read_tensor_f16_noalloc: device ordinal out of range");
     void *scratch = nullptr;
@@ -376,6 +377,14 @@ int ivc_launch_count(ivc_model *m, int batch, int *count) {
   return guarded(m, [&]() -> int {
     if (!count) return fail(m, IVC_ERR_ARGUMENT, "bad arguments");
     *count = m->eng->graph_kernel_count(batch);
+    return IVC_OK;
+  });
+}
+
+int ivc_debug_conv_wait(ivc_model *m, long long limit_cycles, int probe) {
+  return guarded(m, [&]() -> int {
+    if (limit_cycles < 1) return fail(m, IVC_ERR_ARGUMENT, "ivc_debug_conv_wait: limit must be positive");
+    m->eng->set_conv_wait(limit_cycles, probe);
     return IVC_OK;
   });
 }

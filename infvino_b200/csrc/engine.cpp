@@ -1462,6 +1462,8 @@ void Engine::lower() {
         a.tmem_cols = pow2_at_least(nbuf * g.mb * c.BN);
         a.smem_bytes = g.smem;
         a.status = status;
+        a.wait_limit = kConvWaitLimitDefault;
+        a.wait_probe = 0;
         const char *why = nullptr;
         if (!conv_tc_finalize(a, &why)) throw std::runtime_error(std::string("CudaPlanModel: ") + why);
         return a;
@@ -1476,7 +1478,8 @@ void Engine::lower() {
            << " nbuf=" << a.nbuf << " tiles=" << a.m_tiles * a.n_tiles << " smem=" << a.smem_bytes << " " << how;
         (*geometry)[B] = gs.str();
       };
-      st.launch = [c, cache, build, record, sms](int B, cudaStream_t s) -> cudaError_t {
+      auto wait = wait_;
+      st.launch = [c, cache, build, record, sms, wait](int B, cudaStream_t s) -> cudaError_t {
         auto it = cache->find(B);
         if (it == cache->end()) {  // untuned: the cost model's pick
           const ConvTcArgs a = (*build)(B, conv_candidates(c, B, sms).front());
@@ -1486,6 +1489,12 @@ void Engine::lower() {
         const ConvTcArgs &a = it->second;
         const int tiles = a.m_tiles * a.n_tiles;
         const int grid = std::max(1, std::min(tiles, sms));
+        if (wait->probe || wait->limit != kConvWaitLimitDefault) {  // test settings of the bounded waits
+          ConvTcArgs b = a;
+          b.wait_limit = wait->limit;
+          b.wait_probe = wait->probe;
+          return launch_conv_tc(b, grid, s);
+        }
         return launch_conv_tc(a, grid, s);
       };
       // Load-time tuning: the first run of a batch size times the cost model's
@@ -2127,6 +2136,7 @@ void Engine::run_profiled(int batch, std::vector<float> *step_ms) {
 
 void Engine::download_output_f16(int i, void *dst, int batch, bool on_device) {
   require_device();
+  check(cudaSetDevice(device_), "cudaSetDevice");
   const TensorRt &t = T_[(size_t)tid(output_name(i))];
   if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
   check(cudaMemcpyAsync(dst, t.dptr, (size_t)t.numel * batch * 2,
@@ -2137,6 +2147,7 @@ void Engine::download_output_f16(int i, void *dst, int batch, bool on_device) {
 void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
   require_device();
   pdl_scope();
+  check(cudaSetDevice(device_), "cudaSetDevice");
   const TensorRt &t = T_[(size_t)tid(output_name(i))];
   if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
   const int64_t n = t.numel * batch;
@@ -2366,6 +2377,7 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
 bool Engine::read_tensor_f16(const std::string &name, void *host_dst, int batch) {
   require_device();
   pdl_scope();
+  check(cudaSetDevice(device_), "cudaSetDevice");
   auto it = tid_.find(name);
   if (it == tid_.end()) return false;
   const TensorRt &t = T_[(size_t)it->second];
@@ -2397,6 +2409,7 @@ int Engine::read_tensor_f16_staged(const std::string &name, void *host_dst, int 
                                    int64_t scratch_bytes, int64_t *need_bytes) {
   require_device();
   pdl_scope();
+  check(cudaSetDevice(device_), "cudaSetDevice");
   auto it = tid_.find(name);
   if (it == tid_.end()) return 1;
   const TensorRt &t = T_[(size_t)it->second];
@@ -2445,6 +2458,18 @@ int Engine::graph_kernel_count(int batch) {
   return kernels;
 }
 
+void Engine::set_conv_wait(long long limit_cycles, int probe) {
+  require_device();
+  if (limit_cycles < 1) throw std::runtime_error("CudaPlanModel: conv wait limit must be positive");
+  wait_->limit = limit_cycles;
+  wait_->probe = probe ? 1 : 0;
+  // captured graphs hold the launch parameters of their capture: capture again
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  for (auto &g : graphs_) cudaGraphExecDestroy(g.second);
+  graphs_.clear();
+}
+
 void Engine::require_device() const {
   if (dry_) throw std::runtime_error("CudaPlanModel: a dry run handle has no device state (IVC_FLAG_DRY_RUN)");
 }
@@ -2455,6 +2480,7 @@ void Engine::synchronize() { check(cudaStreamSynchronize(stream_), "cudaStreamSy
 
 int Engine::device_status() {
   int v = 0;
+  check(cudaSetDevice(device_), "cudaSetDevice");
   check(cudaMemcpyAsync(&v, status_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "status read");
   check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
   if (v) check(cudaMemsetAsync(status_, 0, sizeof(int), stream_), "status reset");

@@ -133,6 +133,12 @@ class Engine {
   void decode_pose(int batch, float conf, float iou, int max_det, int nk, int kdims, const float *letterbox,
                    int *counts, float *dets);
   int graph_kernel_count(int batch);  // kernel nodes in the CUDA graph of `batch`
+  void require_device() const;  // throws for a dry run handle (no device state)
+  // Test settings of the convolutions' bounded waits: the limit of every
+  // working wait in SM clocks, and a probe that makes the first wait of every
+  // conv CTA run out (the kernel then reports a timeout status).  Takes effect
+  // from the next run (captured graphs are dropped).
+  void set_conv_wait(long long limit_cycles, int probe);
   __half *input_device_ptr() const;
   float *input_f32_staging() const { return in_f32_; }
 
@@ -165,7 +171,6 @@ class Engine {
   std::vector<std::pair<int, int>> tail_uses_;  // (tensor, node) reads of fused tails, for liveness
   void plan_tails();
   void pdl_scope() const;  // launches on this thread follow kFlagNoPdl
-  void require_device() const;  // throws for a dry run handle (no device state)
   void tune(int batch);    // per-step load-time tuning for this batch size (once)
   std::set<int> tuned_;
   std::vector<Step> steps_;
@@ -204,6 +209,11 @@ class Engine {
   __half *scratch_ = nullptr;       // read_tensor staging
   int64_t scratch_elems_ = 0;
   std::map<int, cudaGraphExec_t> graphs_;
+  struct ConvWait {
+    long long limit = 4000000000LL;  // kConvWaitLimitDefault
+    int probe = 0;
+  };
+  std::shared_ptr<ConvWait> wait_ = std::make_shared<ConvWait>();  // read by the conv launch closures
 };
 
 }  // namespace ivb

@@ -2,6 +2,7 @@
 #include "host_cast.h"
 
 #include <immintrin.h>
+#include <sched.h>
 
 #include <algorithm>
 #include <condition_variable>
@@ -58,6 +59,13 @@ __attribute__((target("avx2"))) void span_avx2(const float *in, uint16_t *out, s
   span_scalar(in + i, out + i, n - i);
 }
 
+unsigned process_cpus() {
+  cpu_set_t set;
+  CPU_ZERO(&set);
+  if (sched_getaffinity(0, sizeof(set), &set) == 0) return (unsigned)CPU_COUNT(&set);
+  return std::thread::hardware_concurrency();
+}
+
 bool have_avx2() {
   static const bool yes = __builtin_cpu_supports("avx2") != 0;
   return yes;
@@ -68,8 +76,12 @@ bool have_avx2() {
 class Pool {
  public:
   Pool() {
-    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const unsigned workers = std::min(hw, 16u) - 1;  // the caller works too
+    // sized from the CPUs this process may run on (its affinity mask, which a
+    // multi-GPU launcher may have narrowed to the cores near the rank's GPU),
+    // not from the machine's core count: ranks sharing a host must not
+    // oversubscribe it
+    const unsigned cpus = std::max(1u, process_cpus());
+    const unsigned workers = std::min(cpus, 16u) - 1;  // the caller works too
     for (unsigned t = 0; t < workers; ++t) th_.emplace_back([this] { loop(); });
   }
   ~Pool() {

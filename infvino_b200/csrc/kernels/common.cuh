@@ -3,6 +3,7 @@
 // load) and a bounded wait that reports a timeout instead of spinning forever.
 #pragma once
 
+#include <atomic>
 #include <utility>
 
 #include <cstdint>
@@ -77,6 +78,29 @@ inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block
   cfg.attrs = attr;
   cfg.numAttrs = g_launch_pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// A kernel's dynamic shared-memory ceiling is a per-device attribute: it is set
+// on the current device once, and `done` (one flag per device ordinal, shared
+// by the threads of the process) remembers which devices have it.  Two threads
+// may both set it the first time; setting it twice is harmless.  A failed call
+// returns its error and clears the runtime's last error, so a later launch
+// check does not report it.
+constexpr int kAttrMaxDevices = 64;
+template <typename... KArgs>
+inline cudaError_t ensure_dynamic_smem(void (*kernel)(KArgs...), int bytes, std::atomic<bool> (&done)[kAttrMaxDevices]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < kAttrMaxDevices;
+  if (tracked && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return e;
+  }
+  if (tracked) done[dev].store(true, std::memory_order_release);
+  return cudaSuccess;
 }
 
 // ------------------------------------------------------------------ resolved activations
@@ -234,7 +258,11 @@ enum KernelStatus : int {
   kStatusTimeoutAccEmpty = 4,
   kStatusTimeoutDrain = 5,
   kStatusBadConfig = 6,
+  kStatusTimeoutProbe = 7,  // the test probe's wait (a barrier nothing arrives on) ran out
 };
+
+// Default limit of a conv kernel's working waits, in SM clocks (about 2 s).
+constexpr long long kConvWaitLimitDefault = 4000000000LL;
 
 // Bounded wait: gives up after ~`limit_cycles` SM clocks, records `code` in the
 // global status word and raises the CTA-wide abort flag so the other roles stop.

@@ -102,6 +102,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
   const bool out_vec = a.out_vec != 0, res_vec = a.res_vec != 0, has_res = res != nullptr;
   const bool bias_in_smem = n_tiles == 1 && bias != nullptr;
   int *status = a.status;
+  const long long wait_limit = a.wait_limit;
   // 3x3: this thread's pixel inside the tile is fixed
   // (halo tiles: M block j holds columns 8j .. 8j+7, so the row splits by 8)
   const int tw_row = a.halo ? 8 : TW;
@@ -131,7 +132,8 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
     if (team_lead) {
       if (lane == 0) {
         CONV_TRACE_T0();
-        go[jt & 1u] = mbar_wait_bounded(smem_u32(&accf_bar[buf]), use & 1u, abort_sh, status, kStatusTimeoutAcc)
+        go[jt & 1u] = mbar_wait_bounded(smem_u32(&accf_bar[buf]), use & 1u, abort_sh, status, kStatusTimeoutAcc,
+                                        wait_limit)
                           ? 1
                           : 0;
         CONV_TRACE_SINCE(3);
@@ -283,6 +285,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   __shared__ __align__(8) uint64_t acce_bar[kConvMaxBufs];
   __shared__ __align__(8) uint64_t bres_bar;
   __shared__ __align__(8) uint64_t done_bar;
+  __shared__ __align__(8) uint64_t probe_bar;  // nothing arrives on it (test probe)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
   __shared__ volatile int epi_go[2 * kConvMaxTeams];
@@ -295,6 +298,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   const bool resident_b = a.resident_b != 0;
   const int num_tiles = a.m_tiles * n_tiles;
   int *const status = a.status;
+  const long long wait_limit = a.wait_limit;
   // 1024-byte aligned operand area (128B-swizzle atoms repeat every 1024 B)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -324,6 +328,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
     mbar_init(smem_u32(&bres_bar), 1);
     mbar_init(smem_u32(&done_bar), 1);
+    mbar_init(smem_u32(&probe_bar), 1);
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -397,7 +402,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         for (int kb = 0; kb < num_kb;) {
           CONV_TRACE_T0();
           if (wrap > 0 && !mbar_wait_bounded(smem_u32(&empty_bar[stage]), (wrap - 1u) & 1u, &abort_sh, status,
-                                             kStatusTimeoutEmpty)) {
+                                             kStatusTimeoutEmpty, wait_limit)) {
             ok = false;
             break;
           }
@@ -487,14 +492,19 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
       const uint32_t ru = row_bytes >> 4, hx_u = (uint32_t)hx * ru, phase_u = (uint32_t)a.halo_bytes >> 4;
       const uint32_t b_tap = (uint32_t)(resident_b ? num_kb : 1) * b_step;
       bool ok = true;
-      if (resident_b)
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull));
+      if (a.wait_probe)  // test probe: this wait runs out, and the CTA takes its abort path
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait_bounded(smem_u32(&probe_bar), 0, &abort_sh, status, kStatusTimeoutProbe, wait_limit));
+      if (resident_b && ok)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait_bounded(smem_u32(&bres_bar), 0, &abort_sh, status, kStatusTimeoutFull, wait_limit));
       const uint32_t nbuf = (uint32_t)a.nbuf;
       uint32_t stage = 0, wrap = 0, buf = 0, use = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         CONV_TRACE_T0();
         if (use > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&acce_bar[buf]), (use - 1) & 1u,
-                                                                  &abort_sh, status, kStatusTimeoutAccEmpty))) {
+                                                                  &abort_sh, status, kStatusTimeoutAccEmpty,
+                                                                  wait_limit))) {
           ok = false;
           break;
         }
@@ -504,7 +514,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         for (int kb = 0; kb < num_kb;) {
           CONV_TRACE_T0();
           if (!__all_sync(0xffffffffu,
-                          mbar_wait_bounded(smem_u32(&full_bar[stage]), wrap & 1u, &abort_sh, status, kStatusTimeoutFull))) {
+                          mbar_wait_bounded(smem_u32(&full_bar[stage]), wrap & 1u, &abort_sh, status, kStatusTimeoutFull,
+                                            wait_limit))) {
             ok = false;
             break;
           }
@@ -615,17 +626,9 @@ bool conv_tc_finalize(ConvTcArgs &a, const char **why) {
 }
 
 cudaError_t launch_conv_tc(const ConvTcArgs &args, int grid, cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024);
-    if (e != cudaSuccess) {
-      (void)cudaGetLastError();  // a later launch's error check must not report this one
-      return e;
-    }
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[kAttrMaxDevices];
+  const cudaError_t e = ensure_dynamic_smem(conv_tc_kernel, 232448 - 1024, attr_set);
+  if (e != cudaSuccess) return e;
   return launch_kernel(conv_tc_kernel, dim3(grid), dim3(kConvThreads), (size_t)args.smem_bytes, stream, args);
 }
 

@@ -73,6 +73,12 @@ struct alignas(64) ConvTcArgs {
   int nbuf;                       // accumulator buffers: nteams or 2 * nteams
   int smem_bytes;
   int *status;
+  // bounded waits: the limit of every working wait in SM clocks (drains keep
+  // their own), and a test probe: when nonzero the MMA warp first waits on a
+  // barrier that nothing arrives on, so the wait runs out and the kernel takes
+  // its abort path and reports kStatusTimeoutProbe
+  long long wait_limit;
+  int wait_probe;
   // derived by conv_tc_finalize(): divisors of the per-tile index arithmetic
   FastDiv fd_ntiles, fd_tiles_per_img, fd_tiles_x, fd_tw, fd_hw, fd_wo;
 };

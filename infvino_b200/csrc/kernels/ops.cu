@@ -1353,15 +1353,9 @@ cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t
   const size_t smem = (size_t)(prog.n_slots > 0 ? prog.n_slots : 1) * threads * V * sizeof(float);
   const long long n = (long long)batch * (prog.A / V);
   if (vec) {
-    static bool attr = false;
-    if (!attr) {
-      const cudaError_t e = cudaFuncSetAttribute(tail_vm_k<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (e != cudaSuccess) {
-        (void)cudaGetLastError();  // a later launch's error check must not report this one
-        return e;
-      }
-      attr = true;
-    }
+    static std::atomic<bool> attr_set[kAttrMaxDevices];
+    const cudaError_t e = ensure_dynamic_smem(tail_vm_k<4>, 96 * 1024, attr_set);
+    if (e != cudaSuccess) return e;
     launch_kernel(tail_vm_k<4>, dim3(dim3(grid_for(n, threads), prog.n_comp)), dim3(threads), smem, st, prog, n);
   } else {
     launch_kernel(tail_vm_k<1>, dim3(dim3(grid_for(n, threads), prog.n_comp)), dim3(threads), smem, st, prog, n);

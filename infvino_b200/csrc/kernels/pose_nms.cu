@@ -189,15 +189,9 @@ cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st)
   const size_t smem =
       pose_nms_smem_bytes(args.P, args.A, args.boxes_in_smem != 0, args.kept_idx_smem ? args.max_det : 0);
   if (smem > (size_t)kPoseNmsSmemMax) return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(pose_nms_k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPoseNmsSmemMax);
-    if (e != cudaSuccess) {
-      (void)cudaGetLastError();  // a later launch's error check must not report this one
-      return e;
-    }
-    attr = true;
-  }
+  static std::atomic<bool> attr_set[kAttrMaxDevices];
+  const cudaError_t e = ensure_dynamic_smem(pose_nms_k, kPoseNmsSmemMax, attr_set);
+  if (e != cudaSuccess) return e;
   launch_kernel(pose_nms_k, dim3((unsigned)batch), dim3(kPoseNmsThreads), smem, st, args);
   return cudaGetLastError();
 }

@@ -9,7 +9,7 @@ import pytest
 import infvino_b200 as ivb
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REFERENCE_INCLUDE = "/root/reference/include"
+REFERENCE_INCLUDE = os.path.join(os.environ.get("INFVINO_REFERENCE", "/root/reference"), "include")
 
 
 def compile_driver(tmp, extra=()):

@@ -1,0 +1,87 @@
+"""Parity at the benchmark's own configuration: YOLOv8n-pose 640x640, the
+bench plan (seed 1234), a handle for 64 images with the default flags (tuned
+tile geometry for batch 64, CUDA graph, load-time fusions, concurrent head
+branches), batch 64.
+
+Images spread over the batch are compared with the oracle run on each image
+alone (batch invariance is tested elsewhere): the nine raw head tensors
+(max-abs <= 2e-2, rel-L2 <= max(1e-3, 2x the oracle's own fp32 reordering
+floor)), the decoded coordinates (0.5 px) and the post-NMS detection set.  The
+ClBackend::infer path on host buffers (chunked, half the batch cast on the
+host) must equal the device-resident run bit for bit.
+
+With IVB_PARITY_REPORT=<file> set, the achieved figures are appended to that
+file as JSON lines.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import infvino_b200 as ivb
+from oracle import decode, ivref
+
+pytestmark = pytest.mark.gpu
+
+B = 64
+SEED = 1234
+IMAGES = (0, 15, 16, 31, 32, 47, 63)  # chunk edges of the host-cast and device-cast halves
+HEADS = [f"model.22.cv{b}.{i}.2.out" for b in (2, 3, 4) for i in range(3)]
+COORD = [0, 1, 2, 3] + [5 + 3 * k for k in range(17)] + [6 + 3 * k for k in range(17)]
+
+
+def _report(rec):
+    path = os.environ.get("IVB_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(rec) + "\n")
+
+
+def test_yolov8n_pose_b64_headline(model_plans):
+    p = model_plans["yolov8n-pose"]
+    m = ivb.PlanModel(p, device=0, max_batch=B)
+    n = m.inputNumel()
+    x = np.random.default_rng(SEED).random(B * n, dtype=np.float32)
+    x16 = ivref.f32_to_f16_trunc(x)
+    m.setInput(x16, B)
+    m.run(B)
+    geo = [ln for ln in m.describe().splitlines() if ln.startswith("step conv") and f"[B={B} " in ln]
+    assert geo and all(" tuned" in ln or " model" in ln for ln in geo)
+    out = m.readOutput(0, B)
+    heads = {h: m.readTensor(h, B).reshape(B, -1) for h in HEADS}
+    o = ivref.OraclePlan(p)
+    o_rev = ivref.OraclePlan(p, acc_order=1)
+    worst = {"maxabs": 0.0, "rel": 0.0}
+    for b in IMAGES:
+        xb = x16[b * n:(b + 1) * n]
+        o.run_f16(xb, 1)
+        o_rev.run_f16(xb, 1)
+        for h in HEADS:
+            g = ivref.f16_to_f32(heads[h][b]).astype(np.float64)
+            r = ivref.f16_to_f32(o.read_f16(h)).astype(np.float64)
+            r2 = ivref.f16_to_f32(o_rev.read_f16(h)).astype(np.float64)
+            maxabs = float(np.abs(g - r).max())
+            rel = float(np.linalg.norm(g - r) / max(1e-30, np.linalg.norm(r)))
+            floor = float(np.linalg.norm(r2 - r) / max(1e-30, np.linalg.norm(r)))
+            _report({"test": "b64_headline", "image": b, "tensor": h, "maxabs": maxabs, "rel_l2": rel,
+                     "oracle_reorder_floor": floor})
+            worst["maxabs"] = max(worst["maxabs"], maxabs)
+            worst["rel"] = max(worst["rel"], rel)
+            assert maxabs <= 2e-2 and rel <= max(1e-3, 2.0 * floor), (b, h, maxabs, rel, floor)
+        got = ivref.f16_to_f32(out.reshape(B, -1)[b]).reshape(56, 8400)
+        ref = ivref.f16_to_f32(o.read_f16("output0")).reshape(56, 8400)
+        d = np.abs(got[COORD].astype(np.float64) - ref[COORD])
+        assert d.max() <= 0.5, (b, float(d.max()))
+        und, _, _ = decode.undecided_anchors(ref, got)
+        sg = {a for a, *_ in decode.pose_decode(got)}
+        sr = {a for a, *_ in decode.pose_decode(ref)}
+        assert (sg ^ sr) <= und, (b, sorted((sg ^ sr) - und)[:8])
+        _report({"test": "b64_headline", "image": b, "coord_maxabs_px": float(d.max()),
+                 "nms_identical": sg == sr, "undecided": len(und), "detections": len(sg)})
+    _report({"test": "b64_headline", "worst": worst})
+    # ClBackend::infer on host buffers at the same batch: bit-identical to the
+    # device-resident run
+    y = m.infer_f32(x, B)[0]
+    assert np.array_equal(y, ivref.f16_to_f32(out))
+    m.close()

@@ -252,3 +252,13 @@ def test_dry_run_handle_refuses_device_calls(model_plans):
         with pytest.raises(ivb.NativeError) as e:
             call()
         assert "dry run handle" in str(e.value), str(e.value)
+    # the allocation-free read refuses the same way, before it resolves any
+    # device address (no CUDA call on a dry run handle)
+    L = _native.lib()
+    buf = np.zeros(m.tensorNumel(m.outputName(0)), dtype=np.uint16)
+    st = L.ivc_read_tensor_f16_noalloc(m.handle, m.outputName(0).encode(), buf.ctypes.data, 1)
+    assert st != 0
+    assert "dry run handle" in L.ivc_last_error(m.handle).decode()
+    # so does the conv wait diagnostic
+    assert L.ivc_debug_conv_wait(m.handle, 1000, 1) != 0
+    assert "dry run handle" in L.ivc_last_error(m.handle).decode()
