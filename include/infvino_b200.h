@@ -119,7 +119,10 @@ int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch
  * (include/infvino/Preprocess.hpp:24-35; `letterbox` is [batch][scale,
  * pad_left, pad_top] in host memory, or NULL for scale 1 and no padding);
  * greedy suppression at IoU above `iou` in descending score (ties by anchor
- * index) keeps at most `max_det` per image.  Results in host memory:
+ * index, the reference's stable sort); the keep list is then re-sorted by
+ * score with std::sort and cut at `max_det`, as the reference does, so equal
+ * scores come out in the order that (unstable) sort leaves them.  Results in
+ * host memory:
  * counts[b] detections for image b, detection k at
  * dets[(b * max_det + k) * (6 + 2 * nk)]: anchor index, score, x, y, w, h,
  * then x, y of each keypoint.  nk <= 0 infers the keypoint count from the

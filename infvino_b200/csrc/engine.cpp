@@ -98,6 +98,9 @@ Engine::~Engine() {
   if (nms_lbox_) cudaFree(nms_lbox_);
   if (nms_host_) cudaFreeHost(nms_host_);
   if (nms_kept_) cudaFree(nms_kept_);
+  if (nms_pairs_) cudaFree(nms_pairs_);
+  if (nms_chosen_) cudaFree(nms_chosen_);
+  if (nms_pairs_host_) cudaFreeHost(nms_pairs_host_);
   for (cudaEvent_t e : chunk_events_) cudaEventDestroy(e);
   if (copy_in_) cudaStreamDestroy(copy_in_);
   if (copy_out_) cudaStreamDestroy(copy_out_);
@@ -2315,24 +2318,39 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
   while (P < A) P <<= 1;
   const int S = 6 + 2 * nk;
   if (!nms_boxes_) {
-    check(cudaMalloc(&nms_boxes_, (size_t)max_batch_ * kPoseNmsMaxAnchors * sizeof(float4)), "cudaMalloc(nms boxes)");
-    check(cudaMalloc(&nms_counts_, (size_t)max_batch_ * sizeof(int)), "cudaMalloc(nms counts)");
+    const size_t cap = (size_t)max_batch_ * kPoseNmsMaxAnchors;
+    check(cudaMalloc(&nms_boxes_, cap * sizeof(float4)), "cudaMalloc(nms boxes)");
+    check(cudaMalloc(&nms_kept_, cap * sizeof(int)), "cudaMalloc(nms kept)");
+    check(cudaMalloc(&nms_pairs_, cap * sizeof(int2)), "cudaMalloc(nms keep lists)");
+    check(cudaMalloc(&nms_counts_, (size_t)max_batch_ * 2 * sizeof(int)), "cudaMalloc(nms counts)");
     check(cudaMalloc(&nms_lbox_, (size_t)max_batch_ * 3 * sizeof(float)), "cudaMalloc(nms letterbox)");
+    check(cudaHostAlloc(reinterpret_cast<void **>(&nms_pairs_host_), cap * sizeof(int2), cudaHostAllocDefault),
+          "cudaHostAlloc(nms keep lists)");
   }
-  const int64_t need = (int64_t)batch * max_det * S;
-  if (need > nms_dets_cap_) {
+  const int64_t need = (int64_t)batch * max_det * S;  // floats of the result rows
+  const int64_t idx = (int64_t)batch * (max_det + 2);  // ints: chosen anchors, then chosen and kept counts
+  if (need > nms_dets_cap_ || idx > nms_idx_cap_) {
     if (nms_dets_) check(cudaFree(nms_dets_), "cudaFree(nms dets)");
-    if (nms_kept_) check(cudaFree(nms_kept_), "cudaFree(nms kept)");
+    if (nms_chosen_) check(cudaFree(nms_chosen_), "cudaFree(nms chosen)");
     nms_dets_ = nullptr;
-    nms_kept_ = nullptr;
+    nms_chosen_ = nullptr;
     check(cudaMalloc(&nms_dets_, (size_t)need * sizeof(float)), "cudaMalloc(nms dets)");
-    // batch * max_det <= need / 6 for any later call the buffers still fit (S >= 6)
-    check(cudaMalloc(&nms_kept_, (size_t)(need / 6 + 1) * sizeof(int)), "cudaMalloc(nms kept)");
+    check(cudaMalloc(&nms_chosen_, (size_t)idx * sizeof(int)), "cudaMalloc(nms chosen)");
     nms_dets_cap_ = need;
+    nms_idx_cap_ = idx;
+  }
+  if (need + idx > nms_host_cap_) {
+    if (nms_host_) check(cudaFreeHost(nms_host_), "cudaFreeHost(nms staging)");
+    nms_host_ = nullptr;
+    check(cudaHostAlloc(reinterpret_cast<void **>(&nms_host_), (size_t)(need + idx) * sizeof(float),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(nms staging)");
+    nms_host_cap_ = need + idx;
   }
   if (letterbox)
     check(cudaMemcpyAsync(nms_lbox_, letterbox, (size_t)batch * 3 * sizeof(float), cudaMemcpyHostToDevice, stream_),
           "letterbox copy");
+  // 1. candidates, stable score order, greedy suppression: each image's keep list
   PoseNmsArgs a{};
   a.out = t.dptr;
   a.img_stride = t.numel;
@@ -2342,35 +2360,71 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
   a.kdims = kdims;
   a.conf = conf;
   a.iou = iou;
-  a.max_det = max_det;
   a.letterbox = letterbox ? nms_lbox_ : nullptr;
   a.boxes = nms_boxes_;
   // boxes and the kept list in shared memory where they fit, else in scratch
   a.kept = nms_kept_;
   a.boxes_in_smem = pose_nms_smem_bytes(P, A, true, 0) <= (size_t)kPoseNmsSmemMax ? 1 : 0;
-  a.kept_idx_smem = pose_nms_smem_bytes(P, A, a.boxes_in_smem != 0, max_det) <= (size_t)kPoseNmsSmemMax ? 1 : 0;
+  a.kept_idx_smem = pose_nms_smem_bytes(P, A, a.boxes_in_smem != 0, A) <= (size_t)kPoseNmsSmemMax ? 1 : 0;
   a.counts = nms_counts_;
-  a.dets = nms_dets_;
+  a.pairs = nms_pairs_;
   check(launch_pose_nms(a, batch, stream_), "pose decode + NMS");
-  // results through pinned staging; each image's used rows go to the caller
-  if (need + batch > nms_host_cap_) {
-    if (nms_host_) check(cudaFreeHost(nms_host_), "cudaFreeHost(nms staging)");
-    nms_host_ = nullptr;
-    check(cudaHostAlloc(reinterpret_cast<void **>(&nms_host_), (size_t)(need + batch) * sizeof(float),
-                        cudaHostAllocDefault),
-          "cudaHostAlloc(nms staging)");
-    nms_host_cap_ = need + batch;
+  int *host_idx = reinterpret_cast<int *>(nms_host_ + need);  // chosen anchors [batch][max_det], counts
+  int *host_chosen = host_idx + (size_t)batch * max_det, *host_kept = host_chosen + batch;
+  check(cudaMemcpyAsync(host_kept, nms_counts_, (size_t)batch * sizeof(int), cudaMemcpyDeviceToHost, stream_),
+        "keep counts copy");
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  int longest = 0;
+  for (int b = 0; b < batch; ++b) longest = std::max(longest, host_kept[b]);
+  if (longest > 0)
+    check(cudaMemcpy2DAsync(nms_pairs_host_, (size_t)longest * sizeof(int2), nms_pairs_, (size_t)P * sizeof(int2),
+                            (size_t)longest * sizeof(int2), (size_t)batch, cudaMemcpyDeviceToHost, stream_),
+          "keep lists copy");
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  // 2. the reference's last step (src/Decoders.cpp:58-63): the keep list, in
+  // keep order, sorted by descending score with std::sort - not a stable
+  // sort, so equal scores end up where std::sort leaves them, which depends on
+  // the whole list - then cut at max_det.  std::sort's moves depend only on its
+  // comparisons, so (score, anchor) pairs under a score-only comparator take
+  // the permutation the reference's Detection objects take.
+  std::vector<std::pair<float, int>> v;
+  for (int b = 0; b < batch; ++b) {
+    const int2 *pl = nms_pairs_host_ + (size_t)b * longest;
+    v.resize((size_t)host_kept[b]);
+    for (int k = 0; k < host_kept[b]; ++k) {
+      float sc;
+      std::memcpy(&sc, &pl[k].y, sizeof(float));
+      v[(size_t)k] = {sc, pl[k].x};
+    }
+    std::sort(v.begin(), v.end(),
+              [](const std::pair<float, int> &x, const std::pair<float, int> &y) { return x.first > y.first; });
+    const int c = std::min(host_kept[b], max_det);
+    host_chosen[b] = c;
+    for (int k = 0; k < c; ++k) host_idx[(size_t)b * max_det + k] = v[(size_t)k].second;
   }
-  int *host_counts = reinterpret_cast<int *>(nms_host_ + need);
-  check(cudaMemcpyAsync(host_counts, nms_counts_, (size_t)batch * sizeof(int), cudaMemcpyDeviceToHost, stream_),
-        "detection counts copy");
+  // 3. the chosen detections' rows, through pinned staging to the caller
+  check(cudaMemcpyAsync(nms_chosen_, host_idx, (size_t)batch * (max_det + 1) * sizeof(int), cudaMemcpyHostToDevice,
+                        stream_),
+        "chosen detections copy");
+  PoseGatherArgs g{};
+  g.out = t.dptr;
+  g.img_stride = t.numel;
+  g.A = A;
+  g.nk = nk;
+  g.kdims = kdims;
+  g.max_det = max_det;
+  g.letterbox = a.letterbox;
+  g.anchors = nms_chosen_;
+  g.counts = nms_chosen_ + (size_t)batch * max_det;
+  g.dets = nms_dets_;
+  check(launch_pose_gather(g, batch, stream_), "pose detections gather");
   check(cudaMemcpyAsync(nms_host_, nms_dets_, (size_t)need * sizeof(float), cudaMemcpyDeviceToHost, stream_),
         "detections copy");
   check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
   for (int b = 0; b < batch; ++b) {
-    counts[b] = host_counts[b];
+    counts[b] = host_chosen[b];
     std::memcpy(dets + (size_t)b * max_det * S, nms_host_ + (size_t)b * max_det * S,
-                (size_t)host_counts[b] * S * sizeof(float));
+                (size_t)host_chosen[b] * S * sizeof(float));
   }
 }
 

@@ -200,6 +200,10 @@ class Engine {
   // pose decode + NMS: box scratch, results and letterboxes (allocated at the first call)
   float4 *nms_boxes_ = nullptr;
   int *nms_counts_ = nullptr, *nms_kept_ = nullptr;
+  int2 *nms_pairs_ = nullptr;       // keep lists (anchor, score) per image
+  int2 *nms_pairs_host_ = nullptr;  // their pinned staging
+  int *nms_chosen_ = nullptr;       // chosen anchors [batch][max_det], then their counts
+  int64_t nms_idx_cap_ = 0;         // ints in nms_chosen_
   float *nms_dets_ = nullptr, *nms_lbox_ = nullptr;
   int64_t nms_dets_cap_ = 0;        // floats in nms_dets_
   float *nms_host_ = nullptr;       // pinned staging of results and counts

@@ -129,7 +129,9 @@ cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t
 // permute_0213 (mode 0) -> softmax over D2 bins -> 1x1 conv D2 -> Cout, fused
 // (the YOLO DFL head).  Supported for D2 == 16 and Cout <= 8.
 // Pose decode + greedy NMS over a batch of channel-major fp16 pose outputs
-// [5 + nk * kdims, A] (pose_nms.cu); one CTA per image.
+// [5 + nk * kdims, A] (pose_nms.cu); one CTA per image.  pose_nms_k writes each
+// image's keep list; the host orders and cuts it like the reference, and
+// pose_gather_k writes the chosen detections' rows.
 constexpr int kPoseNmsThreads = 1024;
 constexpr int kPoseNmsMaxAnchors = 16384;  // P: the sort runs over a power of two >= A, in shared memory
 struct PoseNmsArgs {
@@ -139,13 +141,21 @@ struct PoseNmsArgs {
   int P;                   // power of two >= A (sort length)
   int nk, kdims;           // keypoints, values per keypoint
   float conf, iou;
-  int max_det;
   const float *letterbox;  // [batch][scale, pad_left, pad_top] or null (scale 1, no padding)
   float4 *boxes;           // scratch [batch][P] (used when the boxes do not fit in shared memory)
   int boxes_in_smem;       // 1: boxes in shared memory (pose_nms_smem_bytes(P, A, true) <= kPoseNmsSmemMax)
-  int *kept;               // scratch [batch][max_det] (used when the kept list does not fit in shared memory)
+  int *kept;               // scratch [batch][P] (used when the kept list does not fit in shared memory)
   int kept_idx_smem;       // 1: kept list in shared memory
-  int *counts;             // [batch]
+  int *counts;             // [batch]: kept candidates
+  int2 *pairs;             // [batch][P]: the keep list in keep order, (anchor, score as f32 bits)
+};
+struct PoseGatherArgs {
+  const __half *out;
+  long long img_stride;
+  int A, nk, kdims, max_det;
+  const float *letterbox;  // as PoseNmsArgs
+  const int *counts;       // [batch]: detections chosen per image (<= max_det)
+  const int *anchors;      // [batch][max_det]: their anchors, in output order
   float *dets;             // [batch][max_det][6 + 2 * nk]: anchor, score, x, y, w, h, then (x, y) per keypoint
 };
 constexpr int kPoseNmsSmemMax = 225 * 1024;  // dynamic; the kernel's static shared memory (~1 KB) fits beside it
@@ -153,6 +163,7 @@ inline size_t pose_nms_smem_bytes(int P, int A, bool boxes_in_smem, int kept_in_
   return (size_t)P * 4 + (boxes_in_smem ? (size_t)A * 16 : 0) + (size_t)kept_in_smem * 4;  // keys, boxes, kept list
 }
 cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st);
+cudaError_t launch_pose_gather(const PoseGatherArgs &args, int batch, cudaStream_t st);
 
 bool dfl_fused_supported(int D2, int Cout);
 cudaError_t launch_dfl_fused(const __half *x, const __half *w, const __half *bias, __half *y, int batch, int D1, int D2,

@@ -3,6 +3,7 @@
 // iou (src/Nms.cpp:10-55), one CTA per image over the [5 + nk * kdims, A]
 // channel-major fp16 output.
 //
+// pose_nms_k, per image:
 //   1. candidates: anchors whose score is not below `conf` (`score < conf`
 //      skips, as in the reference);
 //   2. the candidates in descending score, ties by anchor index (the
@@ -12,10 +13,13 @@
 //      letterbox (rectToImage), in shared memory when keys, boxes and flags
 //      fit there (A <= 9,800 or so), else in global scratch;
 //   4. greedy suppression in that order (IoU above `iou` removes a later
-//      candidate), stopping once `max_det` are kept: kept boxes come out in
-//      score order, so they are the first `max_det` of the reference's result;
-//      a candidate is tested against the boxes kept so far, 64 candidates at a
-//      time.
+//      candidate) over every candidate: a candidate is tested against the
+//      boxes kept so far, 64 candidates at a time;
+//   5. the keep list (anchor, score) in keep order.
+// The reference then re-sorts the keep list by score with std::sort, which is
+// not stable, and cuts it at max_det; the host does that step with the same
+// std::sort on the same sequence (Engine::decode_pose), and pose_gather_k
+// writes the chosen detections' rows.
 // All float arithmetic is the reference's, operation by operation, with
 // round-to-nearest intrinsics so that nothing is contracted into an FMA.
 #include <cuda_fp16.h>
@@ -50,7 +54,7 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   pdl_wait_and_release();
   extern __shared__ uint32_t nms_sm[];
   // shared memory: P sort keys, then the boxes (A, when they fit), then the
-  // kept candidates' indices (max_det, when they fit)
+  // kept candidates' indices (up to A, when they fit)
   uint32_t *key = nms_sm;
   float4 *bx = p.boxes_in_smem ? reinterpret_cast<float4 *>(nms_sm + p.P) : p.boxes + (long long)blockIdx.x * p.P;
   int *kept_sm = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(nms_sm + p.P) +
@@ -108,13 +112,13 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   __shared__ unsigned long long sup_mask, row_mask[64];
   __shared__ int n_kept;
   const int warp = tid >> 5, lane = tid & 31;
-  int *kept_idx = p.kept_idx_smem ? kept_sm : p.kept + (long long)b * p.max_det;
+  int *kept_idx = p.kept_idx_smem ? kept_sm : p.kept + (long long)b * p.P;
   if (tid == 0) {
     n_kept = 0;
     sup_mask = 0ull;
   }
   __syncthreads();
-  for (int base = 0; base < n && n_kept < p.max_det; base += 64) {
+  for (int base = 0; base < n; base += 64) {
     const int nk_now = n_kept;
     const int c0 = base + lane, c1 = base + 32 + lane;
     const bool v0 = c0 < n, v1 = c1 < n;
@@ -148,7 +152,7 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
     if (tid == 0) {
       unsigned long long m = sup_mask;
       int nk = n_kept;
-      for (int j = 0; j < 64 && base + j < n && nk < p.max_det; ++j)
+      for (int j = 0; j < 64 && base + j < n; ++j)
         if (!((m >> j) & 1ull)) {
           kept_idx[nk++] = base + j;
           m |= row_mask[j];
@@ -158,18 +162,37 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
     }
     __syncthreads();
   }
-  // 5. the kept detections: anchor, score, box, keypoints
-  const int S = 6 + 2 * p.nk, kept = n_kept;
+  // 5. the keep list in keep order: anchor and score (the score as the f32
+  // value the reference's Detection holds)
+  const int kept = n_kept;
+  int2 *pairs = p.pairs + (long long)b * p.P;
+  for (int k = tid; k < kept; k += blockDim.x) {
+    const int a = (int)(key[kept_idx[k]] & 0x3fffu);
+    pairs[k] = make_int2(a, __float_as_int(__half2float(o[4 * A + a])));
+  }
+  if (tid == 0) p.counts[b] = kept;
+}
+
+// The rows of the detections the host chose (std::sort of the keep list by
+// score, cut at max_det): anchor, score, box through the letterbox, keypoints.
+__global__ void __launch_bounds__(256) pose_gather_k(PoseGatherArgs p) {
+  pdl_wait_and_release();
+  const int b = blockIdx.x;
+  const long long A = p.A;
+  const __half *o = p.out + (long long)b * p.img_stride;
+  const float scale = p.letterbox ? p.letterbox[3 * b] : 1.0f;
+  const float pl = p.letterbox ? p.letterbox[3 * b + 1] : 0.0f, pt = p.letterbox ? p.letterbox[3 * b + 2] : 0.0f;
+  const int S = 6 + 2 * p.nk, count = p.counts[b];
+  const int *anchors = p.anchors + (long long)b * p.max_det;
   float *dets = p.dets + (long long)b * p.max_det * S;
-  for (long long e = tid; e < (long long)kept * S; e += blockDim.x) {
+  for (long long e = threadIdx.x; e < (long long)count * S; e += blockDim.x) {
     const int k = (int)(e / S), f = (int)(e - (long long)k * S);
-    const int i = kept_idx[k];
-    const int a = (int)(key[i] & 0x3fffu);
+    const int a = anchors[k];
     float v;
     if (f == 0) v = (float)a;
     else if (f == 1) v = __half2float(o[4 * A + a]);
     else if (f < 6) {
-      const float4 bi = bx[i];
+      const float4 bi = pose_box(o, A, a, scale, pl, pt);
       v = f == 2 ? bi.x : f == 3 ? bi.y : f == 4 ? bi.z : bi.w;
     } else {
       const int kk = (f - 6) >> 1, xy = (f - 6) & 1;
@@ -177,22 +200,26 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
     }
     dets[e] = v;
   }
-  if (tid == 0) p.counts[b] = kept;
 }
 
 }  // namespace
 
 cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st) {
   if (args.P < 4 || args.P > kPoseNmsMaxAnchors || (args.P & (args.P - 1)) || args.A > args.P || args.A < 1 ||
-      args.max_det < 1 || batch < 1)
+      batch < 1)
     return cudaErrorInvalidValue;
-  const size_t smem =
-      pose_nms_smem_bytes(args.P, args.A, args.boxes_in_smem != 0, args.kept_idx_smem ? args.max_det : 0);
+  const size_t smem = pose_nms_smem_bytes(args.P, args.A, args.boxes_in_smem != 0, args.kept_idx_smem ? args.A : 0);
   if (smem > (size_t)kPoseNmsSmemMax) return cudaErrorInvalidValue;
   static std::atomic<bool> attr_set[kAttrMaxDevices];
   const cudaError_t e = ensure_dynamic_smem(pose_nms_k, kPoseNmsSmemMax, attr_set);
   if (e != cudaSuccess) return e;
   launch_kernel(pose_nms_k, dim3((unsigned)batch), dim3(kPoseNmsThreads), smem, st, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pose_gather(const PoseGatherArgs &args, int batch, cudaStream_t st) {
+  if (args.A < 1 || args.max_det < 1 || batch < 1) return cudaErrorInvalidValue;
+  launch_kernel(pose_gather_k, dim3((unsigned)batch), dim3(256), 0, st, args);
   return cudaGetLastError();
 }
 

@@ -100,6 +100,33 @@ size_t get_num_groups(uint d) { return d < 3 ? wi.ngrp[d] : 1; }
 void barrier(int) {
   if (g_bar) g_bar->wait();
 }
+}  // extern "C"
+
+// ---- sub-groups: consecutive linear local ids, g_sub_group lanes each
+namespace {
+int g_sub_group = 16;
+size_t linear_local_id() { return wi.lid[0] + wi.lid[1] * wi.lsz[0] + wi.lid[2] * wi.lsz[0] * wi.lsz[1]; }
+half g_bcast_slot[1024];
+}  // namespace
+uint get_sub_group_local_id() { return (uint)(linear_local_id() % (size_t)g_sub_group); }
+uint get_sub_group_id() { return (uint)(linear_local_id() / (size_t)g_sub_group); }
+half sub_group_broadcast(half v, uint lane) {
+  const size_t lin = linear_local_id();
+  g_bcast_slot[lin] = v;
+  barrier(0);
+  const half r = g_bcast_slot[lin / (size_t)g_sub_group * (size_t)g_sub_group + lane];
+  barrier(0);
+  return r;
+}
+ushort2 intel_sub_group_block_read_us2(const ushort *p) {
+  const uint lane = get_sub_group_local_id();
+  ushort2 r;
+  r[0] = p[lane];
+  r[1] = p[lane + (uint)g_sub_group];
+  return r;
+}
+
+extern "C" {
 
 // ---- kernels compiled from the reference sources (kernels/ops.cl)
 void ew_binary(const half *, const half *, half *, const int, const int, const int);
@@ -127,6 +154,27 @@ void conv_general(const half *, const half *, const half *, half *, const int, c
                              const int, const int);
 DW_DECL(3, 1, 0) DW_DECL(3, 1, 2) DW_DECL(3, 2, 2) DW_DECL(3, 1, 3) DW_DECL(3, 2, 3) DW_DECL(5, 1, 3)
 DW_DECL(5, 2, 3) DW_DECL(3, 1, 1) DW_DECL(5, 1, 4)
+
+// kernels/gemm.cl (gemm_f16, default tiles BM=128 BN=64 BK=16 TM=8 TN=4 DBUF=1,
+// SG=0), EPI=1 with activation a and RES r; the CAT4 builds take the staged B
+// rows from four sources.  One build per (a, r[, CAT4]), kernel renamed.
+#define GEMM_DECL(a, r)                                                                                \
+  void gemm_a##a##_r##r(const half *, const half *, half *, const int, const int, const int, const half *, \
+                        const half *);
+#define GEMMCAT_DECL(a, r)                                                                                   \
+  void gemmcat_a##a##_r##r(const half *, const half *, half *, const int, const int, const int, const half *,   \
+                           const half *, const half *, const half *, const half *, const int, const int, const int, \
+                           const int, const int, const int, const int);
+GEMM_DECL(0, 0) GEMM_DECL(1, 0) GEMM_DECL(2, 0) GEMM_DECL(3, 0) GEMM_DECL(4, 0) GEMM_DECL(5, 0)
+GEMM_DECL(0, 1) GEMM_DECL(1, 1) GEMM_DECL(3, 1)
+GEMMCAT_DECL(0, 0) GEMMCAT_DECL(1, 0) GEMMCAT_DECL(1, 1)
+// kernels/conv_ov.cl (conv3x3_ov), SG=16 OSV=32, the executor's default blocks
+// (stride 1: OBW=8 OBH=2; stride 2: OBW=5 OBH=4), activation a, RES r.
+#define OV_DECL(s, a, r)                                                                                      \
+  void ov_s##s##_a##a##_r##r(const half *, const half *, const half *, const half *, half *, const int, const int, \
+                             const int, const int, const int, const int);
+OV_DECL(1, 0, 0) OV_DECL(1, 1, 0) OV_DECL(1, 3, 0) OV_DECL(1, 1, 1) OV_DECL(2, 0, 0) OV_DECL(2, 1, 0)
+OV_DECL(2, 3, 0) OV_DECL(2, 1, 1)
 
 // ---- ctypes entry points (fp16 buffers as void*)
 #define H(p) static_cast<const half *>(p)
@@ -211,6 +259,69 @@ int clref_depthwise(const void *x, const void *w, const void *b, void *y, int C,
   if (!fn) return 1;
   const size_t g[1] = {(size_t)C * Ho * Wo};
   ndrange(1, g, nullptr, false, [&] { fn(H(x), H(w), H(b), HM(y), C, H, W, Ho, Wo); });
+  return 0;
+}
+
+// C[M][N] = act(half(A[M][K] B[K][N]) + bias) (+ res), A = weights [Cout][Cin],
+// B = activations [Cin][HW].  cat: B rows from b0..b3 (channel counts ca, cb,
+// cc, rest; row offsets o0..o3 inside each source).  Returns 1 for a variant
+// that is not built.
+int clref_gemm(const void *A, const void *B, void *C, int M, int N, int K, const void *bias, const void *res, int act,
+               int cat, const void *b1, const void *b2, const void *b3, int ca, int cb, int cc, int o0, int o1, int o2,
+               int o3) {
+  constexpr int kBM = 128, kBN = 64, kTM = 8, kTN = 4;
+  const size_t l[2] = {kBN / kTN, kBM / kTM};
+  const size_t g[2] = {(size_t)((N + kBN - 1) / kBN) * l[0], (size_t)((M + kBM - 1) / kBM) * l[1]};
+  const bool r = res != nullptr;
+  if (!cat) {
+    void (*fn)(const half *, const half *, half *, const int, const int, const int, const half *, const half *) = nullptr;
+#define GEMM_PICK(aa, rr) \
+  if (act == aa && r == (rr != 0)) fn = gemm_a##aa##_r##rr;
+    GEMM_PICK(0, 0) GEMM_PICK(1, 0) GEMM_PICK(2, 0) GEMM_PICK(3, 0) GEMM_PICK(4, 0) GEMM_PICK(5, 0)
+    GEMM_PICK(0, 1) GEMM_PICK(1, 1) GEMM_PICK(3, 1)
+    if (!fn) return 1;
+    ndrange(2, g, l, true, [&] { fn(H(A), H(B), HM(C), M, N, K, H(bias), H(res)); });
+    return 0;
+  }
+  void (*fc)(const half *, const half *, half *, const int, const int, const int, const half *, const half *,
+             const half *, const half *, const half *, const int, const int, const int, const int, const int,
+             const int, const int) = nullptr;
+#define GEMMCAT_PICK(aa, rr) \
+  if (act == aa && r == (rr != 0)) fc = gemmcat_a##aa##_r##rr;
+  GEMMCAT_PICK(0, 0) GEMMCAT_PICK(1, 0) GEMMCAT_PICK(1, 1)
+  if (!fc) return 1;
+  ndrange(2, g, l, true, [&] {
+    fc(H(A), H(B), HM(C), M, N, K, H(bias), H(res), H(b1), H(b2), H(b3), ca, cb, cc, o0, o1, o2, o3);
+  });
+  return 0;
+}
+
+// conv3x3_ov over [Cin][H][W] with pad 1; weights in the reference's [Cout][Cin][3][3]
+// order, swizzled here into the kernel's OSV layout [ceil(Cout/32)][Cin][9][32]
+// (zero rows past Cout).
+int clref_conv3x3_ov(const void *x, const void *w, const void *bias, const void *res, void *y, int Cin, int H, int W,
+                     int Cout, int Ho, int Wo, int stride, int act) {
+  void (*fn)(const half *, const half *, const half *, const half *, half *, const int, const int, const int,
+             const int, const int, const int) = nullptr;
+  const bool r = res != nullptr;
+#define OV_PICK(ss, aa, rr) \
+  if (stride == ss && act == aa && r == (rr != 0)) fn = ov_s##ss##_a##aa##_r##rr;
+  OV_PICK(1, 0, 0) OV_PICK(1, 1, 0) OV_PICK(1, 3, 0) OV_PICK(1, 1, 1) OV_PICK(2, 0, 0) OV_PICK(2, 1, 0)
+  OV_PICK(2, 3, 0) OV_PICK(2, 1, 1)
+  if (!fn) return 1;
+  const int groups = (Cout + 31) / 32;
+  std::vector<half> osv((size_t)groups * Cin * 9 * 32, (half)0);
+  const half *wh = H(w);
+  for (int co = 0; co < Cout; ++co)
+    for (int ci = 0; ci < Cin; ++ci)
+      for (int t = 0; t < 9; ++t)
+        osv[(((size_t)(co / 32) * Cin + ci) * 9 + t) * 32 + co % 32] = wh[((size_t)co * Cin + ci) * 9 + t];
+  const int obw = stride == 2 ? 5 : 8, obh = stride == 2 ? 4 : 2;
+  const size_t l[3] = {1, 1, 16};
+  const size_t g[3] = {(size_t)((Wo + obw - 1) / obw), (size_t)((Ho + obh - 1) / obh),
+                       (size_t)((((Cout + 1) / 2) + 15) / 16) * 16};
+  g_sub_group = 16;
+  ndrange(3, g, l, true, [&] { fn(H(x), osv.data(), H(bias), H(res), HM(y), Cin, H, W, Cout, Ho, Wo); });
   return 0;
 }
 }  // extern "C"

@@ -48,3 +48,29 @@ void barrier(int flags);
 static inline half mad(half a, half b, half c) { return (half)((float)a * (float)b + (float)c); }
 static inline float mad(float a, float b, float c) { return a * b + c; }
 static inline float clamp(float x, float lo, float hi) { return std::fmin(std::fmax(x, lo), hi); }
+
+// ---- additions for kernels/gemm.cl and kernels/conv_ov.cl (compiled after the
+// source pre-pass clref/prepass.sed, which turns `(half2)(a, b)` literals into
+// brace initialisers, `.s0` / `.s1` into subscripts, work-group arrays into
+// IVB_GROUP_ARRAY statics and drops `__local` from pointer declarations and casts)
+#define IVB_GROUP_ARRAY static __attribute__((aligned(64)))
+typedef ushort ushort2 __attribute__((vector_size(4)));
+
+static inline half2 mad(half2 a, half2 b, half2 c) {
+  half2 r;
+  r[0] = mad(a[0], b[0], c[0]);
+  r[1] = mad(a[1], b[1], c[1]);
+  return r;
+}
+static inline half2 as_half2(ushort2 u) {
+  half2 h;
+  __builtin_memcpy(&h, &u, sizeof(h));
+  return h;
+}
+// Sub-groups (harness.cpp): the work-items of a work-group form sub-groups of
+// clref_set_sub_group_size() consecutive linear local ids; a broadcast is an
+// exchange through a group-shared slot between two barriers.
+uint get_sub_group_local_id();
+uint get_sub_group_id();
+half sub_group_broadcast(half v, uint lane);
+ushort2 intel_sub_group_block_read_us2(const ushort *p);

@@ -35,6 +35,7 @@
 // Batch: every plan tensor declares batch 1 in dim 0.  The oracle runs the plan
 // for B images by running each node once per image with per-image offsets for
 // activations (initializers are shared).
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -312,20 +313,37 @@ struct Model {
 };
 
 // ---------------------------------------------------------------- kernels
+// The reference's fp16 accumulation step `acc = mad(a, b, acc)` with half
+// operands (kernels/gemm.cl:538, kernels/conv_ov.cl:234): the product of two
+// halves is exact in f32, the sum is rounded to f32 and then to half.
+static inline uint16_t hmad(float a, float b, uint16_t acc) { return f2h(a * b + h2f(acc)); }
+
 static void conv3x3(const uint16_t *x, const uint16_t *w, const uint16_t *bias, const uint16_t *res,
                     uint16_t *y, int Cin, int H, int W, int Cout, int Ho, int Wo, int S, int P, int act,
                     int order) {
-  // fp32 accumulation; one output row per (co, oy); order (ci, ky, kx) or reversed.
+  // fp32 accumulation; one output row per (co, oy); order (ci, ky, kx) or
+  // reversed.  order 2: the reference conv3x3_ov's fp16 accumulator, one mad
+  // per (ci, ky, kx) in that order, taps outside the image contributing
+  // mad(w, 0, acc) (kernels/conv_ov.cl:190-239).
 #pragma omp parallel for collapse(2) schedule(static)
   for (int co = 0; co < Cout; ++co)
     for (int oy = 0; oy < Ho; ++oy) {
       std::vector<float> acc((size_t)Wo, 0.0f);
+      std::vector<uint16_t> hacc((size_t)Wo, 0);
       for (int t = 0; t < Cin * 9; ++t) {
         const int tt = (order == 1) ? (Cin * 9 - 1 - t) : t;
         const int ci = tt / 9, ky = (tt % 9) / 3, kx = tt % 3;
         const int iy = oy * S - P + ky;
-        if (iy < 0 || iy >= H) continue;
         const float wv = h2f(w[((size_t)co * Cin + ci) * 9 + ky * 3 + kx]);
+        if (order == 2) {
+          for (int ox = 0; ox < Wo; ++ox) {
+            const int ix = ox * S - P + kx;
+            const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+            hacc[ox] = hmad(wv, in ? h2f(x[((size_t)ci * H + iy) * W + ix]) : 0.0f, hacc[ox]);
+          }
+          continue;
+        }
+        if (iy < 0 || iy >= H) continue;
         const uint16_t *xr = x + ((size_t)ci * H + iy) * W;
         for (int ox = 0; ox < Wo; ++ox) {
           const int ix = ox * S - P + kx;
@@ -336,7 +354,7 @@ static void conv3x3(const uint16_t *x, const uint16_t *w, const uint16_t *bias, 
       const uint16_t b = bias ? bias[co] : 0;
       for (int ox = 0; ox < Wo; ++ox) {
         const size_t o = ((size_t)co * Ho + oy) * Wo + ox;
-        uint16_t v = act_conv3x3(hadd(f2h(acc[ox]), b), act);
+        uint16_t v = act_conv3x3(hadd(order == 2 ? hacc[ox] : f2h(acc[ox]), b), act);
         if (res) v = hadd(v, res[o]);
         y[o] = v;
       }
@@ -345,19 +363,27 @@ static void conv3x3(const uint16_t *x, const uint16_t *w, const uint16_t *bias, 
 
 static void conv1x1(const uint16_t *w, const uint16_t *x, const uint16_t *bias, const uint16_t *res,
                     uint16_t *y, int Cout, int Cin, int64_t N, int act, int order) {
+  // order 2 with N > 1: the reference gemm_f16's fp16 accumulator, one mad per
+  // input channel in order (kernels/gemm.cl:528-540, 585-602); N == 1 goes to the
+  // reference's fp32 GEMV (kernels/conv1x1.cl:172-198), kept in fp32 here.
+  const bool half_acc = order == 2 && N > 1;
 #pragma omp parallel for schedule(static)
   for (int co = 0; co < Cout; ++co) {
     std::vector<float> acc((size_t)N, 0.0f);
+    std::vector<uint16_t> hacc(half_acc ? (size_t)N : 0, 0);
     for (int t = 0; t < Cin; ++t) {
       const int ci = (order == 1) ? (Cin - 1 - t) : t;
       const float wv = h2f(w[(size_t)co * Cin + ci]);
       const uint16_t *xr = x + (size_t)ci * N;
-      for (int64_t n = 0; n < N; ++n) acc[(size_t)n] += h2f(xr[n]) * wv;
+      if (half_acc)
+        for (int64_t n = 0; n < N; ++n) hacc[(size_t)n] = hmad(wv, h2f(xr[n]), hacc[(size_t)n]);
+      else
+        for (int64_t n = 0; n < N; ++n) acc[(size_t)n] += h2f(xr[n]) * wv;
     }
     const uint16_t b = bias ? bias[co] : 0;
     for (int64_t n = 0; n < N; ++n) {
       const size_t o = (size_t)co * N + n;
-      uint16_t v = act_gemm(hadd(f2h(acc[(size_t)n]), b), act);
+      uint16_t v = act_gemm(hadd(half_acc ? hacc[(size_t)n] : f2h(acc[(size_t)n]), b), act);
       if (res) v = hadd(v, res[o]);
       y[o] = v;
     }
@@ -718,6 +744,21 @@ int ivref_read_tensor(void *h, const char *name, uint16_t *dst) {
     g_err = e.what();
     return 1;
   }
+}
+
+// The reference's final ordering of the kept detections (src/Decoders.cpp:58-62):
+// std::sort by descending score, an unstable sort, applied to the NMS keep list
+// in its order.  Equal scores come out in the order std::sort (libstdc++'s
+// introsort here) leaves them, which depends only on the sequence of
+// comparisons, so sorting (score, position) pairs with a score-only comparator
+// gives the permutation the reference applies to its Detection objects.
+// perm[k] = position (in the input sequence) of the k-th detection afterwards.
+void ivref_std_sort_desc(const float *scores, int n, int *perm) {
+  std::vector<std::pair<float, int>> v((size_t)n);
+  for (int i = 0; i < n; ++i) v[(size_t)i] = {scores[i], i};
+  std::sort(v.begin(), v.end(),
+            [](const std::pair<float, int> &a, const std::pair<float, int> &b) { return a.first > b.first; });
+  for (int i = 0; i < n; ++i) perm[i] = v[(size_t)i].second;
 }
 
 void ivref_f32_to_f16_trunc(const float *in, uint16_t *out, size_t n) {

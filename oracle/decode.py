@@ -1,9 +1,12 @@
 """Restatement of the reference's pose decoder and NMS - test infrastructure.
 
 Follows src/Decoders.cpp:127-179 (`PoseDecoder::decode`), :33-65
-(`nmsPerClass`) and src/Nms.cpp:10-55 (`iou`, greedy `nms` with a stable sort
-by descending score), with the letterbox mapping of
-include/infvino/Preprocess.hpp:24-35.  Used by the parity tests to check that
+(`nmsPerClass`: per-class greedy NMS, then the kept list re-sorted by score
+with std::sort - unstable, reproduced by calling the same std::sort through the
+oracle library - and cut at max_det) and src/Nms.cpp:10-55 (`iou`, greedy
+`nms` with a stable sort by descending score), with the letterbox mapping of
+include/infvino/Preprocess.hpp:24-35.  Pinned bit for bit to the reference's
+own Decoders.cpp / Nms.cpp compiled here (tests/test_decode_pinned.py).  Used by the parity tests to check that
 the CUDA path and the CPU oracle produce the same post-NMS detection set.
 """
 from __future__ import annotations
@@ -43,8 +46,10 @@ def nms(boxes: np.ndarray, scores: np.ndarray, iou_thr: float) -> List[int]:
 
 
 def pose_decode(out: np.ndarray, conf: float = 0.25, iou: float = 0.7, max_det: int = 300, nk: int = 17,
-                kdims: int = 3, scale: float = 1.0, pad: Tuple[int, int] = (0, 0)):
-    """out: [56, A] channel-major f32 -> list of (anchor, score, box[4], kpts[nk, 2])."""
+                kdims: int = 3, scale: float = 1.0, pad: Tuple[int, int] = (0, 0), tie_order: str = "reference"):
+    """out: [56, A] channel-major f32 -> list of (anchor, score, box[4], kpts[nk, 2]).
+    tie_order "reference": equal scores in the order of the reference's final
+    std::sort; "stable": in keep order (anchor order among equal scores)."""
     out = np.asarray(out, dtype=np.float32)
     scores = out[4]
     idx = np.nonzero(scores >= conf)[0]
@@ -59,7 +64,14 @@ def pose_decode(out: np.ndarray, conf: float = 0.25, iou: float = 0.7, max_det: 
         kp = np.stack([(out[5 + j * kdims, a] - pad[0]) / scale for j in range(nk)]), \
             np.stack([(out[5 + j * kdims + 1, a] - pad[1]) / scale for j in range(nk)])
         dets.append((a, float(scores[a]), boxes[k], np.stack(kp, 1)))
-    dets.sort(key=lambda d: -d[1])
+    # src/Decoders.cpp:58-63: the keep list re-sorted by descending score with
+    # std::sort (not stable: equal scores take the order std::sort leaves them
+    # in, which depends on the whole list), then cut at max_det
+    if tie_order == "reference":
+        from . import ivref
+        dets = [dets[i] for i in ivref.std_sort_desc(np.array([d[1] for d in dets], dtype=np.float32))]
+    else:
+        dets.sort(key=lambda d: -d[1])
     return dets[:max_det]
 
 

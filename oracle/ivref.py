@@ -49,12 +49,24 @@ def lib():
         for f in ("ivref_f32_to_f16_trunc", "ivref_f32_to_f16_rne"):
             getattr(L, f).argtypes = [vp, vp, ctypes.c_size_t]
         L.ivref_f16_to_f32.argtypes = [vp, vp, ctypes.c_size_t]
+        L.ivref_std_sort_desc.argtypes = [vp, ctypes.c_int, vp]
+        L.ivref_std_sort_desc.restype = None
         _lib = L
     return _lib
 
 
 def set_threads(n: int) -> int:
     return lib().ivref_set_threads(n)
+
+
+def std_sort_desc(scores: np.ndarray) -> np.ndarray:
+    """Permutation std::sort applies to a sequence sorted by descending score
+    (the reference's final, unstable ordering of the kept detections)."""
+    s = np.ascontiguousarray(scores, dtype=np.float32)
+    perm = np.empty(s.size, dtype=np.int32)
+    if s.size:
+        lib().ivref_std_sort_desc(s.ctypes.data, s.size, perm.ctypes.data)
+    return perm
 
 
 def f32_to_f16_trunc(x: np.ndarray) -> np.ndarray:

@@ -1,6 +1,7 @@
 """Generates tests/golden/ref_kernels.npz by running the reference's OpenCL
-kernels themselves (kernels/ops.cl, kernels/conv_general.cl), compiled on the CPU
-into oracle/_ref/libclref.so by `make -C oracle ref` (see oracle/clref/).
+kernels themselves (kernels/ops.cl, kernels/conv_general.cl, kernels/gemm.cl,
+kernels/conv_ov.cl), compiled on the CPU into oracle/_ref/libclref.so by
+`make -C oracle ref` (see oracle/clref/).
 
 Every case stores its seeded fp16 inputs, the node attributes the plan would
 carry, and the reference kernel's fp16 output.  tests/test_oracle_pinned.py
@@ -27,6 +28,10 @@ def main():
     if not os.path.exists(LIB):
         raise SystemExit("oracle/_ref/libclref.so missing: run `make -C oracle ref` first")
     L = ctypes.CDLL(LIB)
+    VPT = ctypes.c_void_p
+    L.clref_gemm.argtypes = [VPT, VPT, VPT] + [ctypes.c_int] * 3 + [VPT, VPT] + [ctypes.c_int] * 2 + [VPT] * 3 + \
+        [ctypes.c_int] * 7
+    L.clref_conv3x3_ov.argtypes = [VPT] * 5 + [ctypes.c_int] * 8
     rng = np.random.default_rng(99)
     cases = {}
 
@@ -166,6 +171,82 @@ def main():
             [("x", x, [1, Cc, H, W]), ("w", w, [Cc, 1, K, K]), ("bias", bias, [Cc])],
             dict(K=K, S=S, P=P_, G=Cc, Hout=Ho, Wout=Wo, act=act), y, [1, Cc, Ho, Wo])
 
+    # ---- the contractions, fp16 accumulation as in the reference: gemm_f16
+    # (conv1x1 with N > 1, plain and CAT4) and conv3x3_ov.  These cases carry
+    # their whole plan: the CAT4 one is concat4 + conv1x1 (the executor's
+    # load-time rewrite turns it into conv1x1_cat4, which the reference runs as
+    # gemm_f16 with CAT4 staging); residuals and extra sources are inits.
+
+    def plan_case(name, plan_input, tensors, lines, y, ydims):
+        cases[name] = dict(op="plan", inputs=tensors, attrs={}, out=y, dims=ydims, plan_input=plan_input,
+                           plan_text="\n".join(lines) + "\n")
+
+    def decl(kind, n, d):
+        return f"{kind} {n} " + ("" if kind == "input" else f"init_{n}.bin ") + " ".join(map(str, d))
+
+    for (Cin, Cout, Hh, Ww, act, res) in [(40, 32, 10, 10, 1, 0), (16, 16, 8, 9, 0, 0), (32, 70, 5, 13, 3, 0),
+                                          (64, 40, 6, 6, 1, 1), (24, 20, 7, 7, 2, 0), (36, 24, 5, 5, 4, 0),
+                                          (20, 12, 4, 4, 5, 0), (72, 130, 9, 9, 1, 0), (33, 16, 6, 6, 3, 1)]:
+        N = Hh * Ww
+        x = h(rng.uniform(-1, 1, Cin * N))
+        w = normal(Cout * Cin, np.sqrt(2.0 / Cin))
+        bias = normal(Cout, 0.05)
+        rr = normal(Cout * N) if res else None
+        y = np.zeros(Cout * N, np.uint16)
+        r = L.clref_gemm(P(w), P(x), P(y), Cout, N, Cin, P(bias), P(rr) if res else None, act, 0, None, None, None,
+                         0, 0, 0, 0, 0, 0, 0)
+        assert r == 0, (act, res)
+        t = [("x", x, [1, Cin, Hh, Ww]), ("w", w, [Cout, Cin]), ("bias", bias, [Cout])]
+        if res:
+            t.append(("res", rr, [1, Cout, Hh, Ww]))
+        lines = [decl("input", "x", [1, Cin, Hh, Ww])] + [decl("init", n, d) for n, _, d in t[1:]]
+        lines += [f"tensor y 1 {Cout} {Hh} {Ww}",
+                  f"node conv1x1 w,x,bias,{'res' if res else '-'} y act={act}", "output y"]
+        plan_case(f"gemm_{Cin}_{Cout}_{N}_a{act}_r{res}", "x", t, lines, y, [1, Cout, Hh, Ww])
+    for (cs, Cout, Hh, Ww, act, res) in [((16, 16, 16, 0), 32, 10, 10, 1, 0), ((8, 24, 16, 8), 40, 9, 7, 0, 0),
+                                         ((16, 8, 0, 0), 24, 6, 8, 1, 1)]:
+        N = Hh * Ww
+        Cin = sum(cs)
+        srcs = [h(rng.uniform(-1, 1, c * N)) if c else np.zeros(1, np.uint16) for c in cs]
+        w = normal(Cout * Cin, np.sqrt(2.0 / Cin))
+        bias = normal(Cout, 0.05)
+        rr = normal(Cout * N) if res else None
+        y = np.zeros(Cout * N, np.uint16)
+        r = L.clref_gemm(P(w), P(srcs[0]), P(y), Cout, N, Cin, P(bias), P(rr) if res else None, act, 1,
+                         P(srcs[1]), P(srcs[2]), P(srcs[3]), cs[0], cs[1], cs[2], 0, 0, 0, 0)
+        assert r == 0, (act, res)
+        names = [f"s{i}" for i in range(4)]
+        t = [("s0", srcs[0], [1, cs[0], Hh, Ww])] + [(names[i], srcs[i], [1, cs[i], Hh, Ww]) for i in (1, 2, 3) if cs[i]]
+        t += [("w", w, [Cout, Cin]), ("bias", bias, [Cout])]
+        if res:
+            t.append(("res", rr, [1, Cout, Hh, Ww]))
+        lines = [decl("input", "s0", [1, cs[0], Hh, Ww])] + [decl("init", n, d) for n, _, d in t[1:]]
+        cat_ins = ",".join(names[i] if cs[i] else "-" for i in range(4))
+        lines += [f"tensor cat 1 {Cin} {Hh} {Ww}", f"tensor y 1 {Cout} {Hh} {Ww}",
+                  f"node concat4 {cat_ins} cat ca={cs[0]} cb={cs[1]} cc={cs[2]} cd={cs[3]} outer=1 inner={N}",
+                  f"node conv1x1 w,cat,bias,{'res' if res else '-'} y act={act}", "output y"]
+        plan_case(f"gemmcat_{'_'.join(map(str, cs))}_{Cout}_a{act}_r{res}", "s0", t, lines, y, [1, Cout, Hh, Ww])
+    for (Cin, Cout, Hh, Ww, S, act, res) in [(8, 32, 12, 12, 1, 1, 0), (8, 16, 12, 12, 2, 1, 0), (16, 51, 10, 10, 1, 1, 0),
+                                             (3, 16, 20, 20, 2, 1, 0), (8, 8, 9, 9, 1, 1, 1), (12, 24, 16, 16, 2, 0, 0),
+                                             (16, 40, 8, 8, 1, 3, 0), (6, 33, 11, 13, 2, 3, 0), (10, 20, 10, 10, 2, 1, 1),
+                                             (7, 9, 8, 11, 1, 0, 0)]:
+        Ho, Wo = (Hh - 1) // S + 1, (Ww - 1) // S + 1
+        x = h(rng.uniform(-1, 1, Cin * Hh * Ww))
+        w = normal(Cout * Cin * 9, np.sqrt(2.0 / (Cin * 9)))
+        bias = normal(Cout, 0.05)
+        rr = normal(Cout * Ho * Wo) if res else None
+        y = np.zeros(Cout * Ho * Wo, np.uint16)
+        r = L.clref_conv3x3_ov(P(x), P(w), P(bias), P(rr) if res else None, P(y), Cin, Hh, Ww, Cout, Ho, Wo, S, act)
+        assert r == 0, (S, act, res)
+        t = [("x", x, [1, Cin, Hh, Ww]), ("w", w, [Cout, Cin, 3, 3]), ("bias", bias, [Cout])]
+        if res:
+            t.append(("res", rr, [1, Cout, Ho, Wo]))
+        lines = [decl("input", "x", [1, Cin, Hh, Ww])] + [decl("init", n, d) for n, _, d in t[1:]]
+        lines += [f"tensor y 1 {Cout} {Ho} {Wo}",
+                  f"node conv3x3 x,w,bias,{'res' if res else '-'} y stride={S} pad=1 Hout={Ho} Wout={Wo} act={act}",
+                  "output y"]
+        plan_case(f"conv3x3ov_{Cin}_{Cout}_{Hh}x{Ww}_s{S}_a{act}_r{res}", "x", t, lines, y, [1, Cout, Ho, Wo])
+
     flat = {}
     for name, c in cases.items():
         flat[f"{name}/op"] = np.array(c["op"])
@@ -173,6 +254,9 @@ def main():
         flat[f"{name}/out"] = c["out"]
         flat[f"{name}/out_dims"] = np.array(c["dims"], dtype=np.int64)
         flat[f"{name}/inputs"] = np.array(",".join(n for n, _, _ in c["inputs"]))
+        if "plan_text" in c:
+            flat[f"{name}/plan_text"] = np.array(c["plan_text"])
+            flat[f"{name}/plan_input"] = np.array(c["plan_input"])
         for n, arr, d in c["inputs"]:
             flat[f"{name}/in/{n}"] = arr
             flat[f"{name}/dims/{n}"] = np.array(d, dtype=np.int64)

@@ -46,7 +46,8 @@ def test_device_pose_decode_peaked(plan_dir):
 @pytest.mark.gpu
 def test_device_pose_decode_every_anchor_a_candidate(plan_dir):
     """Random-init class scores are all ~0.5: every anchor is a candidate, many
-    scores tie in fp16 (ties go by anchor index), and the max_det cut is
+    scores tie in fp16 (equal scores in the order of the reference's final
+    std::sort, which decides the max_det cut among them), and the cut is
     reached; twice in a row, and with a smaller cut."""
     p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_320_dec"), imgsz=320)
     m = ivb.PlanModel(p, max_batch=2)

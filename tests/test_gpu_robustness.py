@@ -3,6 +3,8 @@ bounded waits.  A probe makes each conv CTA first wait on a barrier that
 nothing arrives on; with a short limit that wait runs out, the kernel drains
 its copies and MMAs, releases TMEM and reports its status word, and the call
 returns IVC_ERR_KERNEL.  The handle must then run correctly again."""
+import re
+
 import numpy as np
 import pytest
 
@@ -10,7 +12,10 @@ import infvino_b200 as ivb
 from infvino_b200 import _native, plangen
 
 IVC_ERR_KERNEL = 5
-STATUS_PROBE = 7         # kStatusTimeoutProbe
+# kernel status words of a bounded wait that ran out: the probe's own (7), or
+# that of another role whose wait, as short, ran out first (1-4: full, empty,
+# accumulator full, accumulator empty); first one wins
+TIMEOUT_STATUS = {1, 2, 3, 4, 7}
 SHORT_LIMIT = 2_000_000  # SM clocks, about 1 ms
 DEFAULT_LIMIT = 4_000_000_000
 
@@ -31,7 +36,8 @@ def test_conv_wait_timeout_reported_and_handle_recovers(tmp_path, flags):
         with pytest.raises(ivb.NativeError) as e:
             m.run(2)
         assert e.value.status == IVC_ERR_KERNEL, str(e.value)
-        assert f"status {STATUS_PROBE}" in e.value.message, e.value.message
+        code = re.search(r"status (\d+)", e.value.message)
+        assert code and int(code.group(1)) in TIMEOUT_STATUS, e.value.message
     # a short limit without the probe: the waits complete well inside it
     assert L.ivc_debug_conv_wait(m.handle, 200_000_000, 0) == 0
     m.run(2)

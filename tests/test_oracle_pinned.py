@@ -1,14 +1,18 @@
 """The CPU oracle pinned to the reference's own kernel code.
 
 tests/golden/ref_kernels.npz holds outputs of the reference's OpenCL kernels
-(kernels/ops.cl, kernels/conv_general.cl) executed on the CPU (generator:
+(kernels/ops.cl, kernels/conv_general.cl, kernels/gemm.cl, kernels/conv_ov.cl)
+executed on the CPU (generator:
 tests/golden/make_kernel_golden.py; build recipe: `make -C oracle ref`).  Each
 case is replayed here through the oracle as a one-node plan.
 
 * elementwise / layout / pooling / softmax / gap / bmm / generic conv: bit-exact;
-* depthwise_f16 accumulates in fp16: bit-exact against the oracle's fp16
-  accumulation mode; the oracle's fp32 mode (the build's contract) stays within
-  2 fp16 ulps of the output scale (max |d| <= 2 * 2^-10 * max |ref|).
+* depthwise_f16, gemm_f16 (conv1x1 and its CAT4 form) and conv3x3_ov
+  accumulate in fp16: bit-exact against the oracle's fp16 accumulation mode,
+  which pins the oracle's indexing (taps, strides, padding, concat channel
+  order, weight layout) and its epilogue (half(acc) + bias, activation,
+  residual after activation); the oracle's fp32 mode (the build's contract)
+  shares all of that and stays within the fp16 accumulator's drift of it.
 """
 import os
 
@@ -30,6 +34,15 @@ def ulp(a, b):
 
 
 def build_plan(tmp, name):
+    if f"{name}/plan_text" in _g.files:  # a whole plan (contractions, CAT4)
+        first = str(_g[f"{name}/plan_input"])
+        for n in str(_g[f"{name}/inputs"]).split(","):
+            if n != first:
+                _g[f"{name}/in/{n}"].astype("<u2").tofile(os.path.join(tmp, f"init_{n}.bin"))
+        path = os.path.join(tmp, "model.plan")
+        with open(path, "w") as f:
+            f.write(str(_g[f"{name}/plan_text"]))
+        return path, _g[f"{name}/in/{first}"]
     op = str(_g[f"{name}/op"])
     attrs = str(_g[f"{name}/attrs"])
     names = str(_g[f"{name}/inputs"]).split(",")
@@ -56,19 +69,33 @@ def build_plan(tmp, name):
     return path, _g[f"{name}/in/{first}"]
 
 
+FP16_ACC = ("depthwise_", "gemm_", "gemmcat_", "conv3x3ov_")
+
+
 @pytest.mark.parametrize("name", CASES)
 def test_oracle_matches_reference_kernel(tmp_path, name):
     plan, x = build_plan(str(tmp_path), name)
     ref = _g[f"{name}/out"]
-    depthwise = name.startswith("depthwise_")
-    o = ivref.OraclePlan(plan, acc_order=2 if depthwise else 0)
+    half_acc = name.startswith(FP16_ACC)
+    o = ivref.OraclePlan(plan, acc_order=2 if half_acc else 0)
     o.run_f16(x, 1)
     got = o.read_f16("y")
     assert got.shape == ref.shape
     d = ulp(got, ref)
     assert d.max() == 0, (name, int(d.max()), int((d > 0).sum()))
-    if depthwise:  # the contract's fp32 accumulation stays close to the reference's fp16 one
+    if half_acc:
+        # The contract's fp32 accumulation (the oracle's default mode, which
+        # shares every index and epilogue step checked bit-exactly above) stays
+        # close to the reference's fp16 accumulation: depthwise (9 or 25 terms)
+        # within 2 fp16 ulps of the output scale; the convolutions (16 to 144
+        # terms) within the fp16 accumulator's own drift (measured on these
+        # cases: rel-L2 up to 2.0e-3, 4.6 ulps of the output scale), bounded at
+        # rel-L2 3e-3 and 6 ulps.
         o32 = ivref.OraclePlan(plan, acc_order=0)
         o32.run_f16(x, 1)
-        g, r = ivref.f16_to_f32(o32.read_f16("y")), ivref.f16_to_f32(ref)
-        assert np.abs(g - r).max() <= 2 * 2.0 ** -10 * np.abs(r).max()
+        g, r = ivref.f16_to_f32(o32.read_f16("y")).astype(np.float64), ivref.f16_to_f32(ref).astype(np.float64)
+        if name.startswith("depthwise_"):
+            assert np.abs(g - r).max() <= 2 * 2.0 ** -10 * np.abs(r).max()
+        else:
+            assert np.linalg.norm(g - r) <= 3e-3 * np.linalg.norm(r), (name, np.linalg.norm(g - r) / np.linalg.norm(r))
+            assert np.abs(g - r).max() <= 6 * 2.0 ** -10 * np.abs(r).max(), (name, np.abs(g - r).max())
