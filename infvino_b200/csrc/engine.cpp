@@ -92,6 +92,7 @@ Engine::~Engine() {
   if (in_f32_) cudaFree(in_f32_);
   if (out_f32_) cudaFree(out_f32_);
   if (in_f16_host_) cudaFreeHost(in_f16_host_);
+  if (out_host_) cudaFreeHost(out_host_);
   if (nms_boxes_) cudaFree(nms_boxes_);
   if (nms_counts_) cudaFree(nms_counts_);
   if (nms_dets_) cudaFree(nms_dets_);
@@ -2169,11 +2170,31 @@ void Engine::download_output_f32(int i, float *dst, int batch, bool on_device) {
   check(cudaMemcpyAsync(dst, tmp, (size_t)n * 4, cudaMemcpyDeviceToHost, stream_), "output copy");
 }
 
+namespace {
+// Host memory the copy engines can read directly (page-locked or registered);
+// for pageable memory the driver would stage every copy through its own small
+// bounce buffers.
+bool copy_ready(const void *p) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeHost;
+}
+}  // namespace
+
 void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   require_device();
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
+  bool staged = !copy_ready(src);
+  for (int i = 0; i < output_count() && !staged; ++i) staged = !copy_ready(outs[i]);
+  if (staged) {  // pageable caller memory (a std::vector, a cv::Mat)
+    infer_f32_host_staged(src, batch, outs);
+    return;
+  }
   // The host->device copy of the input bounds the call.  Large batches cast
   // the f32 input to fp16 on the host (the reference's truncation, on the
   // worker pool) into one of two pinned chunk buffers, so the copy carries
@@ -2291,6 +2312,102 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
     finish(c);
     ++j;
   }
+  check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
+  check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
+  synchronize();
+}
+
+void Engine::infer_f32_host_staged(const float *src, int batch, float *const *outs) {
+  // Every image is cast on the host (the reference's truncation, on the
+  // worker pool) straight from the caller's memory into one of two pinned
+  // fp16 chunk buffers, so the copy engines read pinned memory at half the
+  // bytes; results come back into two pinned f32 chunk buffers and the pool
+  // copies them out.  The host casts chunk c while the device runs chunk c-1,
+  // and copies chunk c-1 out while the device runs chunk c.
+  constexpr int kChunk = 16;
+  const int n_out = output_count();
+  std::vector<int64_t> out_numel(n_out), out_off(n_out + 1, 0), host_off(n_out + 1, 0);
+  for (int i = 0; i < n_out; ++i) {
+    const TensorRt &t = T_[(size_t)tid(output_name(i))];
+    if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
+    out_numel[i] = t.numel;
+    out_off[i + 1] = out_off[i] + out_numel[i] * max_batch_;
+    host_off[i + 1] = host_off[i] + out_numel[i] * kChunk;
+  }
+  const int64_t in_numel = input_numel();
+  if (!out_f32_) {
+    check(cudaMalloc(&out_f32_, (size_t)out_off[n_out] * sizeof(float)), "cudaMalloc(output f32 staging)");
+    check(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaHostAlloc(reinterpret_cast<void **>(&in_f16_host_), (size_t)(2 * kChunk * in_numel) * sizeof(uint16_t),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(input fp16 chunks)");
+  }
+  if (!out_host_) {
+    check(cudaHostAlloc(reinterpret_cast<void **>(&out_host_), (size_t)(2 * host_off[n_out]) * sizeof(float),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(output f32 chunks)");
+  }
+  std::vector<std::pair<int, int>> chunks;  // (first image, images); sizes 16, 8, 4, 2, 1 (one graph each)
+  for (int b0 = 0; b0 < batch;) {
+    const int rem = batch - b0;
+    const int nb = rem >= kChunk ? kChunk : rem >= 8 ? 8 : rem >= 4 ? 4 : rem >= 2 ? 2 : 1;
+    chunks.emplace_back(b0, nb);
+    b0 += nb;
+  }
+  const int n_chunks = (int)chunks.size();
+  while ((int)chunk_events_.size() < 3 * n_chunks + 1) {  // per chunk: copied in, computed, copied out
+    cudaEvent_t e;
+    check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    chunk_events_.push_back(e);
+  }
+  uint16_t *in_f16_dev = reinterpret_cast<uint16_t *>(in_f32_);
+  check(cudaEventRecord(chunk_events_[3 * n_chunks], stream_), "cudaEventRecord");
+  check(cudaStreamWaitEvent(copy_in_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
+  auto drain = [&](int c) {  // chunk c's results from pinned staging into the caller's buffers
+    const int b0 = chunks[(size_t)c].first, nb = chunks[(size_t)c].second;
+    const float *staged = out_host_ + (size_t)(c & 1) * host_off[n_out];
+    check(cudaEventSynchronize(chunk_events_[3 * c + 2]), "cudaEventSynchronize");
+    for (int i = 0; i < n_out; ++i) {
+      const float *from = staged + host_off[i];
+      float *to = outs[i] + (size_t)b0 * out_numel[i];
+      host_parallel_for((size_t)(nb * out_numel[i]), 1 << 16, [&](size_t b, size_t e) {
+        std::memcpy(to + b, from + b, (e - b) * sizeof(float));
+      });
+    }
+  };
+  for (int c = 0; c < n_chunks; ++c) {
+    const int b0 = chunks[(size_t)c].first, nb = chunks[(size_t)c].second;
+    uint16_t *pinned = in_f16_host_ + (size_t)(c & 1) * kChunk * in_numel;
+    // the copy that last read this pinned buffer (two chunks back) must be done
+    if (c >= 2) check(cudaEventSynchronize(chunk_events_[3 * (c - 2)]), "cudaEventSynchronize");
+    f32_to_f16_trunc_host(src + (size_t)b0 * in_numel, pinned, (size_t)(nb * in_numel));
+    check(cudaMemcpyAsync(in_f16_dev + (size_t)b0 * in_numel, pinned, (size_t)(nb * in_numel) * sizeof(uint16_t),
+                          cudaMemcpyHostToDevice, copy_in_),
+          "input copy");
+    check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
+    check(cudaStreamWaitEvent(stream_, chunk_events_[3 * c], 0), "cudaStreamWaitEvent");
+    check(cudaMemcpyAsync(input_device_ptr(), in_f16_dev + (size_t)b0 * in_numel,
+                          (size_t)(nb * in_numel) * sizeof(uint16_t), cudaMemcpyDeviceToDevice, stream_),
+          "input staging copy");
+    run(nb);
+    for (int i = 0; i < n_out; ++i)
+      check(launch_f16_to_f32(T_[(size_t)tid(output_name(i))].dptr, out_f32_ + out_off[i] + (size_t)b0 * out_numel[i],
+                              nb * out_numel[i], stream_),
+            "output conversion");
+    check(cudaEventRecord(chunk_events_[3 * c + 1], stream_), "cudaEventRecord");
+    // the pinned output buffer this chunk uses was drained (chunk c-2) in the
+    // previous iteration, before this copy is enqueued
+    check(cudaStreamWaitEvent(copy_out_, chunk_events_[3 * c + 1], 0), "cudaStreamWaitEvent");
+    float *staged = out_host_ + (size_t)(c & 1) * host_off[n_out];
+    for (int i = 0; i < n_out; ++i)
+      check(cudaMemcpyAsync(staged + host_off[i], out_f32_ + out_off[i] + (size_t)b0 * out_numel[i],
+                            (size_t)(nb * out_numel[i]) * sizeof(float), cudaMemcpyDeviceToHost, copy_out_),
+            "output copy");
+    check(cudaEventRecord(chunk_events_[3 * c + 2], copy_out_), "cudaEventRecord");
+    if (c >= 1) drain(c - 1);
+  }
+  drain(n_chunks - 1);
   check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   synchronize();

@@ -115,6 +115,9 @@ class Engine {
   // converted, run and copied out on separate streams so that the host copies
   // of one chunk overlap the network on another (same results as one batch).
   void infer_f32_host(const float *src, int batch, float *const *outs);
+  // infer_f32_host for pageable caller memory: every image cast on the host
+  // into pinned chunks, results staged through pinned chunks (same results).
+  void infer_f32_host_staged(const float *src, int batch, float *const *outs);
   // Plan-order (NCHW) copy of any tensor for `batch` images into host memory.
   bool read_tensor_f16(const std::string &name, void *host_dst, int batch);
   // read_tensor_f16 staged through caller-provided device scratch (allocates
@@ -197,6 +200,7 @@ class Engine {
   float *in_f32_ = nullptr;         // device staging for f32 input
   float *out_f32_ = nullptr;        // device staging for f32 outputs (pipelined infer)
   uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
+  float *out_host_ = nullptr;       // pinned f32 outputs, two chunks (pageable callers)
   // pose decode + NMS: box scratch, results and letterboxes (allocated at the first call)
   float4 *nms_boxes_ = nullptr;
   int *nms_counts_ = nullptr, *nms_kept_ = nullptr;

@@ -419,3 +419,25 @@ def test_infer_f32_chunked_equals_device_path(model_plans):
     m.synchronize()
     assert np.array_equal(y_host, yd.cpu().numpy())
     m.close()
+
+
+@pytest.mark.parametrize("batch", [1, 3, 40])
+def test_infer_f32_pinned_and_pageable_agree(model_plans, batch):
+    """ClBackend::infer from page-locked buffers (copied directly, half the
+    batch cast on the host) and from pageable ones (every image cast on the
+    host into pinned chunks, results staged back through pinned chunks) give
+    the same bits, and so does a pinned input with a pageable output."""
+    import torch
+    p = model_plans["yolov8n-pose"]
+    m = ivb.PlanModel(p, max_batch=batch)
+    n, no = m.inputNumel(), m.outputNumel(0)
+    x = np.random.default_rng(41).random(batch * n, dtype=np.float32)
+    xp = torch.from_numpy(x).pin_memory()
+    yp = torch.empty(batch * no, dtype=torch.float32).pin_memory()
+    m.infer_f32(xp.numpy(), batch, [yp.numpy()])
+    y_page = m.infer_f32(x, batch)[0]
+    assert np.array_equal(y_page, yp.numpy())
+    y_mixed = np.empty(batch * no, dtype=np.float32)
+    m.infer_f32(xp.numpy(), batch, [y_mixed])
+    assert np.array_equal(y_mixed, y_page)
+    m.close()
