@@ -411,6 +411,7 @@ void Engine::lifetimes() {
   }
   for (const auto &u : tail_uses_) touch(T_[(size_t)u.first].name, u.second);  // fused tails read late
   for (const auto &o : plan_->outputs()) T_[(size_t)T_[(size_t)tid(o)].root].death = N;
+  T_[(size_t)T_[(size_t)tid(plan_->input())].root].death = N;  // the input outlives the run
 }
 
 void Engine::alloc_aux() {
@@ -433,7 +434,12 @@ void Engine::allocate() {
     for (int r : step_reads_[(size_t)j]) acc[(size_t)r].push_back(j);
     for (int r : step_writes_[(size_t)j]) acc[(size_t)r].push_back(j);
   }
+  // The graph input keeps its own bytes for the whole run (touched before the
+  // first step and after the last), as the reference's input buffer does
+  // (only `tensor` lines enter its pool, src/PlanModel.cpp:505-510): run()
+  // repeated after one setInput() reads the same input every time.
   acc[(size_t)T_[(size_t)tid(plan_->input())].root].push_back(kSource);
+  acc[(size_t)T_[(size_t)tid(plan_->input())].root].push_back(kSink);
   for (const auto &o : plan_->outputs()) acc[(size_t)T_[(size_t)tid(o)].root].push_back(kSink);
   for (size_t i = 0; i < T_.size(); ++i)  // values passed inside a fused step only
     if ((int)i == T_[i].root && !T_[i].is_init) T_[i].materialized = !acc[i].empty() || (flags_ & kFlagNoPool);
@@ -2103,6 +2109,7 @@ void Engine::run(int batch) {
   pdl_scope();
   if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
   check(cudaSetDevice(device_), "cudaSetDevice");
+  last_f32_batch_ = 0;  // the output tensors hold this run's images
   if (flags_ & kFlagNoGraph) {
     tune(batch);
     for (auto &s : steps_) {
@@ -2191,7 +2198,7 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   check(cudaSetDevice(device_), "cudaSetDevice");
   bool staged = !copy_ready(src);
   for (int i = 0; i < output_count() && !staged; ++i) staged = !copy_ready(outs[i]);
-  if (staged) {  // pageable caller memory (a std::vector, a cv::Mat)
+  if (staged && batch > 2) {  // pageable caller memory (a std::vector, a cv::Mat)
     infer_f32_host_staged(src, batch, outs);
     return;
   }
@@ -2202,7 +2209,7 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   // copies, and the last chunks shrink (8, 4) so that what follows the final
   // copy (its run and its results' copy back) is short.
   constexpr int kChunk = 16;
-  if (batch < 2 * kChunk) {  // too small to overlap: one pass
+  if (batch < 2 * kChunk || staged) {  // too small to overlap (or one or two pageable images): one pass
     upload_input_f32(src, batch, false);
     run(batch);
     for (int i = 0; i < output_count(); ++i) download_output_f32(i, outs[i], batch, false);
@@ -2315,6 +2322,7 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   synchronize();
+  last_f32_batch_ = batch;  // the whole batch's outputs are in the f32 staging
 }
 
 void Engine::infer_f32_host_staged(const float *src, int batch, float *const *outs) {
@@ -2411,6 +2419,7 @@ void Engine::infer_f32_host_staged(const float *src, int batch, float *const *ou
   check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   synchronize();
+  last_f32_batch_ = batch;  // the whole batch's outputs are in the f32 staging
 }
 
 void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, int kdims, const float *letterbox,
@@ -2468,8 +2477,12 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
     check(cudaMemcpyAsync(nms_lbox_, letterbox, (size_t)batch * 3 * sizeof(float), cudaMemcpyHostToDevice, stream_),
           "letterbox copy");
   // 1. candidates, stable score order, greedy suppression: each image's keep list
+  // after a chunked ClBackend::infer the output tensor holds only the last
+  // chunk; the f32 staging holds the whole batch (exact copies of the fp16 values)
+  const bool from_f32 = last_f32_batch_ >= batch;
   PoseNmsArgs a{};
-  a.out = t.dptr;
+  a.out = from_f32 ? (const void *)out_f32_ : (const void *)t.dptr;
+  a.out_f32 = from_f32 ? 1 : 0;
   a.img_stride = t.numel;
   a.A = A;
   a.P = P;
@@ -2524,7 +2537,8 @@ void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, 
                         stream_),
         "chosen detections copy");
   PoseGatherArgs g{};
-  g.out = t.dptr;
+  g.out = a.out;
+  g.out_f32 = a.out_f32;
   g.img_stride = t.numel;
   g.A = A;
   g.nk = nk;

@@ -201,6 +201,7 @@ class Engine {
   float *out_f32_ = nullptr;        // device staging for f32 outputs (pipelined infer)
   uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
   float *out_host_ = nullptr;       // pinned f32 outputs, two chunks (pageable callers)
+  int last_f32_batch_ = 0;          // images of the last chunked infer whose outputs are all in out_f32_
   // pose decode + NMS: box scratch, results and letterboxes (allocated at the first call)
   float4 *nms_boxes_ = nullptr;
   int *nms_counts_ = nullptr, *nms_kept_ = nullptr;

@@ -135,7 +135,8 @@ cudaError_t launch_tail_program(const TailProgram &prog, int batch, cudaStream_t
 constexpr int kPoseNmsThreads = 1024;
 constexpr int kPoseNmsMaxAnchors = 16384;  // P: the sort runs over a power of two >= A, in shared memory
 struct PoseNmsArgs {
-  const __half *out;       // image 0 of the output
+  const void *out;         // image 0 of the output: fp16, or its exact f32 copy (out_f32)
+  int out_f32;
   long long img_stride;    // elements
   int A;                   // anchors
   int P;                   // power of two >= A (sort length)
@@ -150,7 +151,8 @@ struct PoseNmsArgs {
   int2 *pairs;             // [batch][P]: the keep list in keep order, (anchor, score as f32 bits)
 };
 struct PoseGatherArgs {
-  const __half *out;
+  const void *out;         // as PoseNmsArgs
+  int out_f32;
   long long img_stride;
   int A, nk, kdims, max_det;
   const float *letterbox;  // as PoseNmsArgs

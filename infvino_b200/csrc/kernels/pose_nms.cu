@@ -31,9 +31,25 @@ namespace ivb {
 
 namespace {
 
-__device__ __forceinline__ float4 pose_box(const __half *o, long long A, int a, float scale, float pl, float pt) {
-  const float cx = __half2float(o[a]), cy = __half2float(o[A + a]);
-  const float w = __half2float(o[2 * A + a]), h = __half2float(o[3 * A + a]);
+// One output value as f32: the fp16 output tensor, or its exact f32 copy that
+// ClBackend::infer's chunked paths leave for the whole batch.
+struct PoseOut {
+  const void *p;
+  int f32;
+  __device__ __forceinline__ float operator[](long long i) const {
+    return f32 ? static_cast<const float *>(p)[i] : __half2float(static_cast<const __half *>(p)[i]);
+  }
+  __device__ __forceinline__ PoseOut image(long long b, long long stride) const {
+    PoseOut r = *this;
+    r.p = f32 ? (const void *)(static_cast<const float *>(p) + b * stride)
+              : (const void *)(static_cast<const __half *>(p) + b * stride);
+    return r;
+  }
+};
+
+__device__ __forceinline__ float4 pose_box(const PoseOut &o, long long A, int a, float scale, float pl, float pt) {
+  const float cx = o[a], cy = o[A + a];
+  const float w = o[2 * A + a], h = o[3 * A + a];
   const float x = __fdiv_rn(__fsub_rn(cx, pl), scale), y = __fdiv_rn(__fsub_rn(cy, pt), scale);
   const float ws = __fdiv_rn(w, scale), hs = __fdiv_rn(h, scale);
   return make_float4(__fsub_rn(x, __fdiv_rn(ws, 2.0f)), __fsub_rn(y, __fdiv_rn(hs, 2.0f)), ws, hs);
@@ -62,7 +78,7 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   __shared__ int n_cand;
   const int b = blockIdx.x, tid = threadIdx.x;
   const long long A = p.A;
-  const __half *o = p.out + (long long)b * p.img_stride;
+  const PoseOut o = PoseOut{p.out, p.out_f32}.image(b, p.img_stride);
   const float scale = p.letterbox ? p.letterbox[3 * b] : 1.0f;
   const float pl = p.letterbox ? p.letterbox[3 * b + 1] : 0.0f, pt = p.letterbox ? p.letterbox[3 * b + 2] : 0.0f;
   if (tid == 0) n_cand = 0;
@@ -72,9 +88,10 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   for (int a = tid; a < p.P; a += blockDim.x) {
     uint32_t k = 0xffffffffu;
     if (a < p.A) {
-      const __half hs = o[4 * A + a];
-      if (!(__half2float(hs) < p.conf)) {
-        uint32_t u = __half_as_ushort(hs);
+      const float fs = o[4 * A + a];
+      if (!(fs < p.conf)) {
+        // every output value is an fp16 value, so the score is exact in fp16
+        uint32_t u = __half_as_ushort(__float2half_rn(fs));
         if ((u & 0x7fffu) == 0) u = 0;
         const uint32_t ord = (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u);
         k = ((0xffffu - ord) << 14) | (uint32_t)a;
@@ -168,7 +185,7 @@ __global__ void __launch_bounds__(kPoseNmsThreads) pose_nms_k(PoseNmsArgs p) {
   int2 *pairs = p.pairs + (long long)b * p.P;
   for (int k = tid; k < kept; k += blockDim.x) {
     const int a = (int)(key[kept_idx[k]] & 0x3fffu);
-    pairs[k] = make_int2(a, __float_as_int(__half2float(o[4 * A + a])));
+    pairs[k] = make_int2(a, __float_as_int(o[4 * A + a]));
   }
   if (tid == 0) p.counts[b] = kept;
 }
@@ -179,7 +196,7 @@ __global__ void __launch_bounds__(256) pose_gather_k(PoseGatherArgs p) {
   pdl_wait_and_release();
   const int b = blockIdx.x;
   const long long A = p.A;
-  const __half *o = p.out + (long long)b * p.img_stride;
+  const PoseOut o = PoseOut{p.out, p.out_f32}.image(b, p.img_stride);
   const float scale = p.letterbox ? p.letterbox[3 * b] : 1.0f;
   const float pl = p.letterbox ? p.letterbox[3 * b + 1] : 0.0f, pt = p.letterbox ? p.letterbox[3 * b + 2] : 0.0f;
   const int S = 6 + 2 * p.nk, count = p.counts[b];
@@ -190,13 +207,13 @@ __global__ void __launch_bounds__(256) pose_gather_k(PoseGatherArgs p) {
     const int a = anchors[k];
     float v;
     if (f == 0) v = (float)a;
-    else if (f == 1) v = __half2float(o[4 * A + a]);
+    else if (f == 1) v = o[4 * A + a];
     else if (f < 6) {
       const float4 bi = pose_box(o, A, a, scale, pl, pt);
       v = f == 2 ? bi.x : f == 3 ? bi.y : f == 4 ? bi.z : bi.w;
     } else {
       const int kk = (f - 6) >> 1, xy = (f - 6) & 1;
-      v = __fdiv_rn(__fsub_rn(__half2float(o[(5 + (long long)kk * p.kdims + xy) * A + a]), xy ? pt : pl), scale);
+      v = __fdiv_rn(__fsub_rn(o[(5 + (long long)kk * p.kdims + xy) * A + a], xy ? pt : pl), scale);
     }
     dets[e] = v;
   }

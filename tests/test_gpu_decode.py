@@ -105,3 +105,27 @@ def test_device_pose_decode_adversarial(plan_dir, conf, iou, max_det):
     n = check_against_oracle(m, y, B, conf, iou, max_det, lb)
     assert n > 0
     m.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pinned", [False, True])
+def test_device_pose_decode_after_chunked_infer(plan_dir, pinned):
+    """ClBackend::infer on a large batch runs the network chunk by chunk; the
+    device decode afterwards still sees every image of the batch (the same
+    detections as after one device-resident run of the whole batch)."""
+    import torch
+    B = 40
+    p = plangen.yolov8n_pose(os.path.join(plan_dir, "y8_320_chunk"), imgsz=320, cls_gain=100.0, cls_shift=-3.0)
+    m = ivb.PlanModel(p, max_batch=B)
+    x = np.random.default_rng(64).random(B * m.inputNumel(), dtype=np.float32)
+    m.setInput(ivb.f32_to_f16(x), B)
+    m.run(B)
+    ref = m.decodePose(B)
+    xs = torch.from_numpy(x).pin_memory().numpy() if pinned else x
+    y = m.infer_f32(xs, B)[0].reshape(B, 56, -1)
+    got = m.decodePose(B)
+    assert sum(len(d) for d in ref) > 0
+    for b in range(B):
+        assert np.array_equal(got[b], ref[b]), b
+    assert check_against_oracle(m, y, B, 0.25, 0.7, 300, None) == sum(len(d) for d in ref)
+    m.close()

@@ -305,6 +305,22 @@ def test_backend_reuse_two_inputs(model_plans):
     assert "numel mismatch" in str(e.value)
 
 
+def test_run_repeats_without_set_input(model_plans):
+    """PlanModel::run() called again after one setInput() reads the same input
+    (the graph input keeps its own memory, as the reference's input buffer
+    does): the output is the same every time."""
+    p = model_plans["yolov8n-pose"]
+    m = ivb.PlanModel(p, max_batch=2)
+    x = np.random.default_rng(6).random(2 * m.inputNumel(), dtype=np.float32)
+    m.setInput(ivb.f32_to_f16(x), 2)
+    m.run(2)
+    y0 = m.readOutput(0, 2)
+    for _ in range(3):
+        m.run(2)
+        assert np.array_equal(m.readOutput(0, 2), y0)
+    m.close()
+
+
 def test_batched_equals_single(model_plans):
     """Image b of a batch-3 run equals the same image run alone (batch sharding is exact)."""
     p = model_plans["yolov8n-pose"]

@@ -37,7 +37,9 @@ def test_yolov8n_pose_plan_facts(model_plans):
     assert abs(gflop - 9.178) < 0.002, gflop
     st = m.pool_stats()
     assert st["fusions_concat"] == 13 and st["fusions_res"] == 6
-    assert 0 < st["arena_bytes"] < st["requested_bytes"] / 4
+    # liveness packing (the graph input keeps its own bytes for the whole run,
+    # as the reference's input buffer does)
+    assert 0 < st["arena_bytes"] < st["requested_bytes"] / 3
     fam = {s["family"] for s in steps}
     assert {"conv3x3_tc", "conv1x1_tc", "stem3x3"} <= fam
 
