@@ -30,6 +30,8 @@
  *   ivc_pool_stats ......... PlanModel::poolRequestedBytes/poolAllocatedBytes/
  *                            poolBufferCount  PlanModel.hpp:94-97
  *   ivc_infer_f16_device ... (new) zero-copy device-pointer inference on a caller stream
+ *   ivc_set_input_bgr_u8 / ivc_infer_bgr_u8
+ *                            Preprocessor::operator() src/Preprocess.cpp:13-77 (+ ClBackend::infer), on the device
  *   ivc_decode_pose ........ PoseDecoder::decode + nmsPerClass + nms, on the device
  *                            src/Decoders.cpp:33-65,127-179, src/Nms.cpp:10-55
  *   ivc_destroy ............ PlanModel::~PlanModel / ClBackend destructor
@@ -110,6 +112,35 @@ int ivc_run_async(ivc_model *m, int batch, void *stream);
 int ivc_read_output_f16(ivc_model *m, int i, uint16_t *dst, int batch);
 /* Copies tensor `name` for `batch` images in plan (NCHW) order; IVC_ERR_NOT_FOUND if unknown. */
 int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch);
+
+/* Image preprocessing on the device (replaces the host-side
+ * Preprocessor::operator(), src/Preprocess.cpp:13-77, and the truncating cast
+ * of ClBackend::infer).  Settings as infvino::PreprocessConfig
+ * (include/infvino/Preprocess.hpp:40-48); the input size is the plan's input. */
+typedef struct ivc_preprocess {
+  int letterbox;        /* 1: keep the aspect ratio and pad with 114 (the default); 0: plain resize */
+  int to_rgb;           /* 1: BGR -> RGB (the default) */
+  int normalize;        /* 1: x 1/255 (the default) */
+  int n_mean, n_std;    /* entries of mean / std in use (0: none), applied after /255 */
+  float mean[3], std[3];
+} ivc_preprocess;
+
+/* `batch` 8-bit BGR frames (height x width x 3, rows `row_stride` bytes apart,
+ * frames height * row_stride bytes apart) in host memory (pinned or pageable),
+ * or in device memory when frames_on_device is nonzero, become the network
+ * input: letterbox + cv::resize INTER_LINEAR (OpenCV's 8-bit arithmetic,
+ * bit-exact) + 114 border + blobFromImage + mean / std + the reference's
+ * truncating f32 -> f16 cast, in one kernel.  cfg NULL: the defaults above.
+ * letterbox (host, [batch][scale, pad_left, pad_top]) or NULL receives what
+ * Preprocessor reports in LetterboxInfo.  Synchronous. */
+int ivc_set_input_bgr_u8(ivc_model *m, const uint8_t *frames, int batch, int height, int width, size_t row_stride,
+                         int frames_on_device, const ivc_preprocess *cfg, float *letterbox);
+/* End to end from 8-bit BGR frames in host memory to f32 outputs in host
+ * memory (Preprocessor + ClBackend::infer in one call): large batches are
+ * pipelined in chunks (frames copied in, preprocessed, run, results copied
+ * out, overlapped).  Synchronous. */
+int ivc_infer_bgr_u8(ivc_model *m, const uint8_t *frames, int batch, int height, int width, size_t row_stride,
+                     const ivc_preprocess *cfg, float *const *outputs, float *letterbox);
 
 /* Pose decode + greedy NMS of output 0 of the last run, on the device, for
  * `batch` images (replaces the host-side PoseDecoder::decode with

@@ -211,6 +211,52 @@ class PlanModel:
         dets = dets.reshape(batch, max_det, S)
         return [dets[b, :counts[b]].copy() for b in range(batch)]
 
+    # ---- device preprocessing (src/Preprocess.cpp:13-77 on the device)
+    @staticmethod
+    def _preprocess_cfg(letterbox=True, to_rgb=True, normalize=True, mean=(), std=()):
+        c = _native.Preprocess()
+        c.letterbox, c.to_rgb, c.normalize = int(bool(letterbox)), int(bool(to_rgb)), int(bool(normalize))
+        c.n_mean, c.n_std = len(mean), len(std)
+        for i, v in enumerate(mean):
+            c.mean[i] = float(v)
+        for i, v in enumerate(std):
+            c.std[i] = float(v)
+        return c
+
+    def setInputBgr(self, frames: np.ndarray, **cfg) -> np.ndarray:
+        """Preprocessor::operator() on the device for a batch of 8-bit BGR
+        frames [batch, H, W, 3] (host memory, or a device pointer with
+        `device_shape=(batch, H, W)`), written to the network input.  Returns
+        the letterbox [batch, 3] (scale, pad_left, pad_top).  Keyword
+        settings: letterbox, to_rgb, normalize, mean, std."""
+        device_shape = cfg.pop("device_shape", None)
+        c = self._preprocess_cfg(**cfg)
+        if device_shape is not None:
+            batch, h, w = device_shape
+            ptr, on_dev = int(frames), 1
+        else:
+            frames = np.ascontiguousarray(frames, dtype=np.uint8)
+            batch, h, w = frames.shape[0], frames.shape[1], frames.shape[2]
+            ptr, on_dev = frames.ctypes.data, 0
+        lb = np.zeros((batch, 3), dtype=np.float32)
+        check(lib().ivc_set_input_bgr_u8(self._h, ptr, batch, h, w, w * 3, on_dev, ctypes.byref(c), lb.ctypes.data),
+              self._h)
+        return lb
+
+    def inferBgr(self, frames: np.ndarray, outs: Optional[List[np.ndarray]] = None, **cfg):
+        """Frames [batch, H, W, 3] uint8 in host memory -> f32 outputs in host
+        memory, preprocessing on the device; returns (outputs, letterbox)."""
+        frames = np.ascontiguousarray(frames, dtype=np.uint8)
+        batch, h, w = frames.shape[0], frames.shape[1], frames.shape[2]
+        c = self._preprocess_cfg(**cfg)
+        if outs is None:
+            outs = [np.empty(self.outputNumel(i) * batch, dtype=np.float32) for i in range(self.outputCount())]
+        arr = (ctypes.c_void_p * len(outs))(*[o.ctypes.data for o in outs])
+        lb = np.zeros((batch, 3), dtype=np.float32)
+        check(lib().ivc_infer_bgr_u8(self._h, frames.ctypes.data, batch, h, w, w * 3, ctypes.byref(c), arr,
+                                     lb.ctypes.data), self._h)
+        return outs, lb
+
     def lastRunMs(self) -> float:
         return float(lib().ivc_last_infer_ms(self._h))
 

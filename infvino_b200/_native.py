@@ -47,6 +47,8 @@ SIGNATURES = {
     "ivc_run_async": (_i32, [_vp, _i32, _vp]),
     "ivc_read_output_f16": (_i32, [_vp, _i32, _vp, _i32]),
     "ivc_read_tensor_f16": (_i32, [_vp, _cp, _vp, _i32]),
+    "ivc_set_input_bgr_u8": (_i32, [_vp, _vp, _i32, _i32, _i32, _sz, _i32, _vp, _vp]),
+    "ivc_infer_bgr_u8": (_i32, [_vp, _vp, _i32, _i32, _i32, _sz, _vp, _P(_vp), _vp]),
     "ivc_decode_pose": (_i32, [_vp, _i32, ctypes.c_float, ctypes.c_float, _i32, _i32, _i32, _vp, _vp, _vp]),
     "ivc_read_tensor_f16_noalloc": (_i32, [_vp, _cp, _vp, _i32]),
     "ivc_infer_f16_device": (_i32, [_vp, _vp, _i32, _P(_vp), _vp]),
@@ -65,6 +67,13 @@ SIGNATURES = {
     "ivc_f32_to_f16": (None, [_vp, _vp, _sz]),
     "ivc_f16_to_f32": (None, [_vp, _vp, _sz]),
 }
+
+class Preprocess(ctypes.Structure):
+    """ivc_preprocess (include/infvino_b200.h): infvino::PreprocessConfig."""
+    _fields_ = [("letterbox", ctypes.c_int), ("to_rgb", ctypes.c_int), ("normalize", ctypes.c_int),
+                ("n_mean", ctypes.c_int), ("n_std", ctypes.c_int), ("mean", ctypes.c_float * 3),
+                ("std", ctypes.c_float * 3)]
+
 
 _lib = None
 _lock = threading.Lock()

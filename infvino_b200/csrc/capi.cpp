@@ -1,5 +1,6 @@
 // C ABI over the engine (include/infvino_b200.h).  Exceptions never cross the
 // boundary: every entry point maps them to an ivc_status and keeps the message.
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <memory>
@@ -239,6 +240,52 @@ int ivc_read_tensor_f16(ivc_model *m, const char *name, uint16_t *dst, int batch
     if (!m->eng->read_tensor_f16(name, dst, batch))
       return fail(m, IVC_ERR_NOT_FOUND, std::string("PlanModel: no tensor ") + name);
     return IVC_OK;
+  });
+}
+
+namespace {
+ivb::PreprocessCfg preprocess_cfg(const ivc_preprocess *c) {
+  ivb::PreprocessCfg p;
+  if (!c) return p;
+  p.letterbox = c->letterbox ? 1 : 0;
+  p.to_rgb = c->to_rgb ? 1 : 0;
+  p.normalize = c->normalize ? 1 : 0;
+  p.n_mean = std::min(std::max(c->n_mean, 0), 3);
+  p.n_std = std::min(std::max(c->n_std, 0), 3);
+  for (int i = 0; i < 3; ++i) {
+    p.mean[i] = c->mean[i];
+    p.std[i] = c->std[i];
+  }
+  return p;
+}
+}  // namespace
+
+int ivc_set_input_bgr_u8(ivc_model *m, const uint8_t *frames, int batch, int height, int width, size_t row_stride,
+                         int frames_on_device, const ivc_preprocess *cfg, float *letterbox) {
+  return guarded(m, [&]() -> int {
+    if (!frames || batch < 1 || batch > m->eng->max_batch() || height < 1 || width < 1 ||
+        row_stride < (size_t)width * 3)
+      return fail(m, IVC_ERR_ARGUMENT, "ivc_set_input_bgr_u8: bad arguments");
+    m->eng->upload_input_bgr_u8(frames, batch, height, width, (int64_t)row_stride, frames_on_device != 0,
+                                preprocess_cfg(cfg), letterbox);
+    m->eng->synchronize();
+    return IVC_OK;
+  });
+}
+
+int ivc_infer_bgr_u8(ivc_model *m, const uint8_t *frames, int batch, int height, int width, size_t row_stride,
+                     const ivc_preprocess *cfg, float *const *outputs, float *letterbox) {
+  return guarded(m, [&]() -> int {
+    if (!frames || !outputs || batch < 1 || batch > m->eng->max_batch() || height < 1 || width < 1 ||
+        row_stride < (size_t)width * 3)
+      return fail(m, IVC_ERR_ARGUMENT, "ivc_infer_bgr_u8: bad arguments");
+    for (int i = 0; i < m->eng->output_count(); ++i)
+      if (!outputs[i]) return fail(m, IVC_ERR_ARGUMENT, "ivc_infer_bgr_u8: null output buffer");
+    const auto t0 = std::chrono::steady_clock::now();
+    m->eng->infer_bgr_u8_host(frames, batch, height, width, (int64_t)row_stride, preprocess_cfg(cfg), outputs,
+                              letterbox);
+    m->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return status_check(m);
   });
 }
 

@@ -13,6 +13,7 @@
 #include "host_cast.h"
 
 #include <algorithm>
+#include <cmath>
 #include <functional>
 #include <cstring>
 #include <numeric>
@@ -93,6 +94,9 @@ Engine::~Engine() {
   if (out_f32_) cudaFree(out_f32_);
   if (in_f16_host_) cudaFreeHost(in_f16_host_);
   if (out_host_) cudaFreeHost(out_host_);
+  if (lbt_.xtab) cudaFree(lbt_.xtab);
+  if (lbt_.ytab) cudaFree(lbt_.ytab);
+  if (frames_dev_) cudaFree(frames_dev_);
   if (nms_boxes_) cudaFree(nms_boxes_);
   if (nms_counts_) cudaFree(nms_counts_);
   if (nms_dets_) cudaFree(nms_dets_);
@@ -2420,6 +2424,254 @@ void Engine::infer_f32_host_staged(const float *src, int batch, float *const *ou
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   synchronize();
   last_f32_batch_ = batch;  // the whole batch's outputs are in the f32 staging
+}
+
+// ---- device preprocessing (src/Preprocess.cpp:13-77 on the device)
+
+namespace {
+// OpenCV's INTER_LINEAR source coordinates for one axis (the published
+// algorithm of cv::resize for 8-bit images): scale = 1 / (dst / src) in
+// double; f = float((d + 0.5) * scale - 0.5), s = floor(f), weight f - s; on
+// the x axis a coordinate left of the image or at / past its last column is
+// clamped with weight 0, on the y axis only the row index is clamped; weights
+// in 11-bit fixed point, rounded to nearest even.  x entries carry byte
+// offsets of the two taps (3 bytes per pixel), y entries row indices.
+void linear_coords(int src, int dst, bool x_axis, std::vector<int4> &tab) {
+  tab.resize((size_t)dst);
+  const double scale = 1.0 / ((double)dst / (double)src);
+  for (int d = 0; d < dst; ++d) {
+    float f = (float)((d + 0.5) * scale - 0.5);
+    int s = (int)std::floor(f);
+    f -= (float)s;
+    if (x_axis) {
+      if (s < 0) {
+        f = 0.f;
+        s = 0;
+      }
+      if (s >= src - 1) {
+        f = 0.f;
+        s = src - 1;
+      }
+    }
+    const int w1 = (int)std::nearbyint(f * 2048.0f);
+    const int w0 = (int)std::nearbyint((1.0f - f) * 2048.0f);
+    const int s0 = std::min(std::max(s, 0), src - 1), s1 = std::min(std::max(s + 1, 0), src - 1);
+    tab[(size_t)d] = x_axis ? make_int4(3 * s0, 3 * s1, w0, w1) : make_int4(s0, s1, w0, w1);
+  }
+}
+}  // namespace
+
+void Engine::letterbox_tables(int h, int w, int letterbox) {
+  if (lbt_.h == h && lbt_.w == w && lbt_.letterbox == letterbox) return;
+  const auto &d = input_dims();
+  const int in_h = (int)d[2], in_w = (int)d[3];
+  LetterboxTables t;
+  t.h = h;
+  t.w = w;
+  t.letterbox = letterbox;
+  if (letterbox) {  // Preprocess.cpp:20-27
+    t.scale = std::min((float)in_w / (float)w, (float)in_h / (float)h);
+    t.rw = (int)std::round((float)w * t.scale);
+    t.rh = (int)std::round((float)h * t.scale);
+    t.pad_left = (in_w - t.rw) / 2;
+    t.pad_top = (in_h - t.rh) / 2;
+  } else {
+    t.rw = in_w;
+    t.rh = in_h;
+  }
+  if (t.rw < 1 || t.rh < 1) throw std::runtime_error("Preprocessor: the frame letterboxes to an empty image");
+  std::vector<int4> xt, yt;
+  linear_coords(w, t.rw, true, xt);
+  linear_coords(h, t.rh, false, yt);
+  check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");  // earlier launches may still read the old tables
+  if (lbt_.xtab) check(cudaFree(lbt_.xtab), "cudaFree(letterbox tables)");
+  if (lbt_.ytab) check(cudaFree(lbt_.ytab), "cudaFree(letterbox tables)");
+  lbt_.xtab = lbt_.ytab = nullptr;
+  check(cudaMalloc(&t.xtab, xt.size() * sizeof(int4)), "cudaMalloc(letterbox tables)");
+  check(cudaMalloc(&t.ytab, yt.size() * sizeof(int4)), "cudaMalloc(letterbox tables)");
+  check(cudaMemcpy(t.xtab, xt.data(), xt.size() * sizeof(int4), cudaMemcpyHostToDevice), "letterbox tables copy");
+  check(cudaMemcpy(t.ytab, yt.data(), yt.size() * sizeof(int4), cudaMemcpyHostToDevice), "letterbox tables copy");
+  lbt_ = t;
+}
+
+void Engine::launch_letterbox(const uint8_t *dframes, int64_t img_bytes, int64_t row_stride, int first, int n,
+                              const PreprocessCfg &cfg, cudaStream_t st) {
+  const auto &d = input_dims();
+  LetterboxArgs a{};
+  a.src = dframes;
+  a.img_stride = img_bytes;
+  a.row_stride = row_stride;
+  a.xtab = lbt_.xtab;
+  a.ytab = lbt_.ytab;
+  a.in_h = (int)d[2];
+  a.in_w = (int)d[3];
+  a.dst = input_device_ptr() + (int64_t)first * input_numel();
+  a.dst_img_stride = input_numel();
+  a.rw = lbt_.rw;
+  a.rh = lbt_.rh;
+  a.pad_left = lbt_.pad_left;
+  a.pad_top = lbt_.pad_top;
+  a.to_rgb = cfg.to_rgb;
+  a.normalize = cfg.normalize;
+  a.has_mean_std = (cfg.n_mean > 0 || cfg.n_std > 0) ? 1 : 0;
+  for (int c = 0; c < 3; ++c) {  // Preprocess.cpp:64-74
+    a.mean[c] = c < cfg.n_mean ? cfg.mean[c] : 0.f;
+    float sd = c < cfg.n_std ? cfg.std[c] : 1.f;
+    a.std[c] = sd == 0.f ? 1.f : sd;
+  }
+  a.vec_store = (a.in_w % 4 == 0 && (reinterpret_cast<uintptr_t>(a.dst) & 7) == 0) ? 1 : 0;
+  check(launch_letterbox_bgr(a, n, st), "letterbox preprocessing");
+}
+
+void Engine::upload_input_bgr_u8(const uint8_t *frames, int batch, int h, int w, int64_t row_stride, bool on_device,
+                                 const PreprocessCfg &cfg, float *letterbox_out) {
+  require_device();
+  pdl_scope();
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  const auto &d = input_dims();
+  if (d.size() != 4 || d[1] != 3) throw std::runtime_error("Preprocessor: the plan's input is not [1, 3, H, W]");
+  if (h < 1 || w < 1 || row_stride < 3 * (int64_t)w) throw std::runtime_error("Preprocessor: bad frame geometry");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  letterbox_tables(h, w, cfg.letterbox);
+  const int64_t img_bytes = row_stride * h;
+  const uint8_t *src = frames;
+  if (!on_device) {
+    const int64_t need = img_bytes * batch;
+    if (need > frames_cap_) {
+      check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+      if (frames_dev_) check(cudaFree(frames_dev_), "cudaFree(frame staging)");
+      frames_dev_ = nullptr;
+      check(cudaMalloc(&frames_dev_, (size_t)need), "cudaMalloc(frame staging)");
+      frames_cap_ = need;
+    }
+    check(cudaMemcpyAsync(frames_dev_, frames, (size_t)(img_bytes * batch), cudaMemcpyHostToDevice, stream_),
+          "frame copy");
+    src = frames_dev_;
+  }
+  launch_letterbox(src, img_bytes, row_stride, 0, batch, cfg, stream_);
+  if (letterbox_out)
+    for (int b = 0; b < batch; ++b) {
+      letterbox_out[3 * b] = cfg.letterbox ? lbt_.scale : 1.f;
+      letterbox_out[3 * b + 1] = (float)lbt_.pad_left;
+      letterbox_out[3 * b + 2] = (float)lbt_.pad_top;
+    }
+}
+
+void Engine::infer_bgr_u8_host(const uint8_t *frames, int batch, int h, int w, int64_t row_stride,
+                               const PreprocessCfg &cfg, float *const *outs, float *letterbox_out) {
+  require_device();
+  pdl_scope();
+  if (batch < 1 || batch > max_batch_) throw std::runtime_error("CudaPlanModel: batch out of range");
+  check(cudaSetDevice(device_), "cudaSetDevice");
+  constexpr int kChunk = 16;
+  bool out_pinned = true;
+  for (int i = 0; i < output_count(); ++i) out_pinned = out_pinned && copy_ready(outs[i]);
+  if (batch < 2 * kChunk) {  // one pass
+    upload_input_bgr_u8(frames, batch, h, w, row_stride, false, cfg, letterbox_out);
+    run(batch);
+    for (int i = 0; i < output_count(); ++i) download_output_f32(i, outs[i], batch, false);
+    synchronize();
+    return;
+  }
+  const auto &d = input_dims();
+  if (d.size() != 4 || d[1] != 3) throw std::runtime_error("Preprocessor: the plan's input is not [1, 3, H, W]");
+  if (h < 1 || w < 1 || row_stride < 3 * (int64_t)w) throw std::runtime_error("Preprocessor: bad frame geometry");
+  letterbox_tables(h, w, cfg.letterbox);
+  const int n_out = output_count();
+  std::vector<int64_t> out_numel(n_out), out_off(n_out + 1, 0), host_off(n_out + 1, 0);
+  for (int i = 0; i < n_out; ++i) {
+    const TensorRt &t = T_[(size_t)tid(output_name(i))];
+    if (!t.dense) throw std::runtime_error("CudaPlanModel: output is not planar");
+    out_numel[i] = t.numel;
+    out_off[i + 1] = out_off[i] + out_numel[i] * max_batch_;
+    host_off[i + 1] = host_off[i] + out_numel[i] * kChunk;
+  }
+  if (!out_f32_) {
+    check(cudaMalloc(&out_f32_, (size_t)out_off[n_out] * sizeof(float)), "cudaMalloc(output f32 staging)");
+    check(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaHostAlloc(reinterpret_cast<void **>(&in_f16_host_), (size_t)(2 * kChunk * input_numel()) * sizeof(uint16_t),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(input fp16 chunks)");
+  }
+  if (!out_pinned && !out_host_)
+    check(cudaHostAlloc(reinterpret_cast<void **>(&out_host_), (size_t)(2 * host_off[n_out]) * sizeof(float),
+                        cudaHostAllocDefault),
+          "cudaHostAlloc(output f32 chunks)");
+  const int64_t img_bytes = row_stride * h;
+  if (img_bytes * batch > frames_cap_) {
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    if (frames_dev_) check(cudaFree(frames_dev_), "cudaFree(frame staging)");
+    frames_dev_ = nullptr;
+    check(cudaMalloc(&frames_dev_, (size_t)(img_bytes * batch)), "cudaMalloc(frame staging)");
+    frames_cap_ = img_bytes * batch;
+  }
+  std::vector<std::pair<int, int>> chunks;
+  for (int b0 = 0; b0 < batch;) {
+    const int rem = batch - b0;
+    const int nb = rem >= kChunk ? kChunk : rem >= 8 ? 8 : rem >= 4 ? 4 : rem >= 2 ? 2 : 1;
+    chunks.emplace_back(b0, nb);
+    b0 += nb;
+  }
+  const int n_chunks = (int)chunks.size();
+  while ((int)chunk_events_.size() < 3 * n_chunks + 1) {
+    cudaEvent_t e;
+    check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    chunk_events_.push_back(e);
+  }
+  check(cudaEventRecord(chunk_events_[3 * n_chunks], stream_), "cudaEventRecord");
+  check(cudaStreamWaitEvent(copy_in_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
+  // every chunk's frames queued at once (each into its own staging range)
+  for (int c = 0; c < n_chunks; ++c) {
+    const int b0 = chunks[(size_t)c].first, nb = chunks[(size_t)c].second;
+    check(cudaMemcpyAsync(frames_dev_ + b0 * img_bytes, frames + b0 * img_bytes, (size_t)(nb * img_bytes),
+                          cudaMemcpyHostToDevice, copy_in_),
+          "frame copy");
+    check(cudaEventRecord(chunk_events_[3 * c], copy_in_), "cudaEventRecord");
+  }
+  auto drain = [&](int c) {
+    const int b0 = chunks[(size_t)c].first, nb = chunks[(size_t)c].second;
+    const float *staged = out_host_ + (size_t)(c & 1) * host_off[n_out];
+    check(cudaEventSynchronize(chunk_events_[3 * c + 2]), "cudaEventSynchronize");
+    for (int i = 0; i < n_out; ++i) {
+      const float *from = staged + host_off[i];
+      float *to = outs[i] + (size_t)b0 * out_numel[i];
+      host_parallel_for((size_t)(nb * out_numel[i]), 1 << 16,
+                        [&](size_t b, size_t e) { std::memcpy(to + b, from + b, (e - b) * sizeof(float)); });
+    }
+  };
+  for (int c = 0; c < n_chunks; ++c) {
+    const int b0 = chunks[(size_t)c].first, nb = chunks[(size_t)c].second;
+    check(cudaStreamWaitEvent(stream_, chunk_events_[3 * c], 0), "cudaStreamWaitEvent");
+    launch_letterbox(frames_dev_ + b0 * img_bytes, img_bytes, row_stride, 0, nb, cfg, stream_);
+    run(nb);
+    for (int i = 0; i < n_out; ++i)
+      check(launch_f16_to_f32(T_[(size_t)tid(output_name(i))].dptr, out_f32_ + out_off[i] + (size_t)b0 * out_numel[i],
+                              nb * out_numel[i], stream_),
+            "output conversion");
+    check(cudaEventRecord(chunk_events_[3 * c + 1], stream_), "cudaEventRecord");
+    check(cudaStreamWaitEvent(copy_out_, chunk_events_[3 * c + 1], 0), "cudaStreamWaitEvent");
+    for (int i = 0; i < n_out; ++i) {
+      float *dst = out_pinned ? outs[i] + (size_t)b0 * out_numel[i]
+                              : out_host_ + (size_t)(c & 1) * host_off[n_out] + host_off[i];
+      check(cudaMemcpyAsync(dst, out_f32_ + out_off[i] + (size_t)b0 * out_numel[i],
+                            (size_t)(nb * out_numel[i]) * sizeof(float), cudaMemcpyDeviceToHost, copy_out_),
+            "output copy");
+    }
+    check(cudaEventRecord(chunk_events_[3 * c + 2], copy_out_), "cudaEventRecord");
+    if (!out_pinned && c >= 1) drain(c - 1);
+  }
+  if (!out_pinned) drain(n_chunks - 1);
+  check(cudaEventRecord(chunk_events_[3 * n_chunks], copy_out_), "cudaEventRecord");
+  check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
+  synchronize();
+  last_f32_batch_ = batch;
+  if (letterbox_out)
+    for (int b = 0; b < batch; ++b) {
+      letterbox_out[3 * b] = cfg.letterbox ? lbt_.scale : 1.f;
+      letterbox_out[3 * b + 1] = (float)lbt_.pad_left;
+      letterbox_out[3 * b + 2] = (float)lbt_.pad_top;
+    }
 }
 
 void Engine::decode_pose(int batch, float conf, float iou, int max_det, int nk, int kdims, const float *letterbox,

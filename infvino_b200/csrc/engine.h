@@ -71,6 +71,16 @@ struct Step {
   std::vector<int> nodes;  // plan nodes this step carries out (its own and the ones fused into it)
 };
 
+// Preprocessor settings (include/infvino/Preprocess.hpp:40-48 PreprocessConfig;
+// the input size is the plan's input).
+struct PreprocessCfg {
+  int letterbox = 1;   // letterbox (aspect kept, 114 border) or plain resize
+  int to_rgb = 1;      // BGR -> RGB
+  int normalize = 1;   // x 1/255
+  int n_mean = 0, n_std = 0;
+  float mean[3] = {0.f, 0.f, 0.f}, std[3] = {1.f, 1.f, 1.f};
+};
+
 struct EngineStats {
   int64_t requested_bytes = 0;  // sum of per-tensor storage at max_batch
   int64_t arena_bytes = 0;      // liveness-packed arena
@@ -115,6 +125,17 @@ class Engine {
   // converted, run and copied out on separate streams so that the host copies
   // of one chunk overlap the network on another (same results as one batch).
   void infer_f32_host(const float *src, int batch, float *const *outs);
+  // Device preprocessing of `batch` 8-bit BGR frames (HWC, rows `row_stride`
+  // bytes apart, frames h * row_stride bytes apart) into the network input:
+  // Preprocessor::operator() + the truncating cast, on the device.  Frames in
+  // host (pinned or pageable) or device memory.  letterbox_out: [batch][scale,
+  // pad_left, pad_top] (host) or null.  Asynchronous on the engine stream.
+  void upload_input_bgr_u8(const uint8_t *frames, int batch, int h, int w, int64_t row_stride, bool on_device,
+                           const PreprocessCfg &cfg, float *letterbox_out);
+  // End to end from 8-bit frames in host memory: chunks of frames copied in,
+  // preprocessed, run and their f32 outputs copied out, overlapped.  Synchronous.
+  void infer_bgr_u8_host(const uint8_t *frames, int batch, int h, int w, int64_t row_stride, const PreprocessCfg &cfg,
+                         float *const *outs, float *letterbox_out);
   // infer_f32_host for pageable caller memory: every image cast on the host
   // into pinned chunks, results staged through pinned chunks (same results).
   void infer_f32_host_staged(const float *src, int batch, float *const *outs);
@@ -202,6 +223,19 @@ class Engine {
   uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
   float *out_host_ = nullptr;       // pinned f32 outputs, two chunks (pageable callers)
   int last_f32_batch_ = 0;          // images of the last chunked infer whose outputs are all in out_f32_
+  // device preprocessing: OpenCV coordinate tables of the last frame size, frame staging
+  struct LetterboxTables {
+    int h = 0, w = 0, letterbox = -1;
+    int rw = 0, rh = 0, pad_left = 0, pad_top = 0;
+    float scale = 1.f;
+    int4 *xtab = nullptr, *ytab = nullptr;
+  };
+  LetterboxTables lbt_;
+  uint8_t *frames_dev_ = nullptr;
+  int64_t frames_cap_ = 0;          // bytes
+  void letterbox_tables(int h, int w, int letterbox);
+  void launch_letterbox(const uint8_t *dframes, int64_t img_bytes, int64_t row_stride, int first, int n,
+                        const PreprocessCfg &cfg, cudaStream_t st);
   // pose decode + NMS: box scratch, results and letterboxes (allocated at the first call)
   float4 *nms_boxes_ = nullptr;
   int *nms_counts_ = nullptr, *nms_kept_ = nullptr;

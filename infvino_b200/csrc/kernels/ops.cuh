@@ -167,6 +167,27 @@ inline size_t pose_nms_smem_bytes(int P, int A, bool boxes_in_smem, int kept_in_
 cudaError_t launch_pose_nms(const PoseNmsArgs &args, int batch, cudaStream_t st);
 cudaError_t launch_pose_gather(const PoseGatherArgs &args, int batch, cudaStream_t st);
 
+// Letterbox preprocessing of 8-bit BGR frames into the planar fp16 network
+// input (preprocess.cu; the reference's Preprocessor::operator() + the
+// truncating cast of ClBackend::infer).  The coordinate tables come from the
+// host (OpenCV's INTER_LINEAR rules): xtab[dx] = {byte offset of tap 0, of
+// tap 1, weight 0, weight 1}, ytab[dy] = {row 0, row 1, weight 0, weight 1},
+// weights in 11-bit fixed point.
+struct LetterboxArgs {
+  const uint8_t *src;          // image 0 of the frames (HWC BGR)
+  long long img_stride;        // bytes between frames
+  long long row_stride;        // bytes between rows
+  const int4 *xtab, *ytab;     // [rw], [rh]
+  void *dst;                   // image 0 of the network input (fp16, [3][in_h][in_w])
+  long long dst_img_stride;    // elements between images
+  int in_h, in_w;              // the canvas (network input) size
+  int rw, rh, pad_left, pad_top;  // the resized image inside the canvas
+  int to_rgb, normalize, has_mean_std;
+  float mean[3], std[3];
+  int vec_store;               // destination rows 8-byte aligned (in_w % 4 == 0, aligned base)
+};
+cudaError_t launch_letterbox_bgr(const LetterboxArgs &args, int batch, cudaStream_t st);
+
 bool dfl_fused_supported(int D2, int Cout);
 cudaError_t launch_dfl_fused(const __half *x, const __half *w, const __half *bias, __half *y, int batch, int D1, int D2,
                              long long I, int Cout, int act, cudaStream_t st);
