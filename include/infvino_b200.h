@@ -207,6 +207,21 @@ int ivc_pool_stats(const ivc_model *m, int64_t *requested_bytes, int64_t *arena_
 /* Human-readable dump of tensors (layout, arena offset, lifetime) and launches. */
 int ivc_describe(const ivc_model *m, char *buf, size_t cap);
 
+/* Properties of CUDA device `device_ordinal`, for the reference's DeviceInfo
+ * (include/infvino/Device.hpp:16-26, describeDevice): name, multiprocessor
+ * count (DeviceInfo::eu), clock (DeviceInfo::clock_mhz), compute capability,
+ * memory, and the number of devices (DeviceInfo::available). */
+typedef struct ivc_device_props {
+  char name[256];
+  int multiprocessors;
+  int clock_mhz;
+  int cc_major, cc_minor;
+  int64_t total_mem_bytes;
+  int device_count;
+  int runtime_version;  /* CUDA runtime, e.g. 12090 */
+} ivc_device_props;
+int ivc_device_properties(int device_ordinal, ivc_device_props *out);
+
 /* Host conversions with the reference's semantics (include/infvino/Half.hpp:14-49). */
 void ivc_f32_to_f16(const float *in, uint16_t *out, size_t n);
 void ivc_f16_to_f32(const uint16_t *in, float *out, size_t n);

@@ -64,6 +64,7 @@ SIGNATURES = {
     "ivc_pool_stats": (_i32, [_vp, _P(_i64), _P(_i64), _P(_i64), _P(_i32), _P(_i32), _P(_i32), _P(_i32),
                               _P(_i32)]),
     "ivc_describe": (_i32, [_vp, _cp, _sz]),
+    "ivc_device_properties": (_i32, [_i32, _vp]),
     "ivc_f32_to_f16": (None, [_vp, _vp, _sz]),
     "ivc_f16_to_f32": (None, [_vp, _vp, _sz]),
 }

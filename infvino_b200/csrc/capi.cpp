@@ -2,6 +2,7 @@
 // boundary: every entry point maps them to an ivc_status and keeps the message.
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -460,6 +461,33 @@ int ivc_describe(const ivc_model *m, char *buf, size_t cap) {
     buf[n] = '\0';
   }
   return (int)d.size();
+}
+
+int ivc_device_properties(int device_ordinal, ivc_device_props *out) {
+  if (!out) return IVC_ERR_ARGUMENT;
+  std::memset(out, 0, sizeof(*out));
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return IVC_ERR_CUDA;
+  }
+  out->device_count = n;
+  if (device_ordinal < 0 || device_ordinal >= n) return IVC_ERR_ARGUMENT;
+  cudaDeviceProp p{};
+  if (cudaGetDeviceProperties(&p, device_ordinal) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return IVC_ERR_CUDA;
+  }
+  std::snprintf(out->name, sizeof(out->name), "%s", p.name);
+  out->multiprocessors = p.multiProcessorCount;
+  int khz = 0;
+  if (cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device_ordinal) != cudaSuccess) (void)cudaGetLastError();
+  out->clock_mhz = khz / 1000;
+  out->cc_major = p.major;
+  out->cc_minor = p.minor;
+  out->total_mem_bytes = (int64_t)p.totalGlobalMem;
+  cudaRuntimeGetVersion(&out->runtime_version);
+  return IVC_OK;
 }
 
 void ivc_f32_to_f16(const float *in, uint16_t *out, size_t n) { ivb::f32_to_f16_trunc_host(in, out, n); }

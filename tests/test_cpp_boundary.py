@@ -30,10 +30,19 @@ def test_cpp_backend_compiles_and_reports_empty_plan(tmp_path):
     assert "ModelInfo.plan is empty" in r.stdout
 
 
+REFERENCE_TYPES = ["-DWITH_REFERENCE_TYPES", "-I" + REFERENCE_INCLUDE,
+                   "-I" + os.path.join(ROOT, "oracle", "cvshim"), "-I" + os.path.join(ROOT, "tests", "cpp", "refshim")]
+
+
 @pytest.mark.skipif(not os.path.isdir(REFERENCE_INCLUDE), reason="reference headers not present here")
-def test_cpp_backend_compiles_with_reference_tensor(tmp_path):
-    # the wrapper instantiates with the reference's own infvino::Tensor type
-    compile_driver(str(tmp_path), ["-DWITH_REFERENCE_TENSOR", "-I" + REFERENCE_INCLUDE])
+def test_cpp_backend_compiles_with_reference_types(tmp_path):
+    """The drop-in instantiates with the reference's own infvino::Tensor,
+    infvino::ModelInfo and infvino::DeviceInfo (device() returns the caller's
+    DeviceInfo, so InferenceEngine::device() forwards it unchanged), and
+    reports the reference's empty-plan error."""
+    exe = compile_driver(str(tmp_path), REFERENCE_TYPES)
+    r = subprocess.run([exe, "--empty-plan"], capture_output=True, text=True)
+    assert r.returncode == 0 and "ModelInfo.plan is empty" in r.stdout, r.stdout + r.stderr
 
 
 @pytest.mark.gpu
@@ -71,3 +80,32 @@ def test_cpp_backend_decode_pose_matches_python_path(tmp_path, plan_dir):
     m.infer_f32(x, 1)
     ref = m.decodePose(1)[0]
     assert got.shape[0] > 0 and np.array_equal(got, ref)
+
+
+@pytest.mark.gpu
+def test_cpp_plan_model_drives_like_the_tools(tmp_path, model_plans):
+    """The C++ PlanModel (setInput once, run twice under profiling, readOutput,
+    readTensor, profile(), pool statistics) gives the Python path's output."""
+    exe = compile_driver(str(tmp_path))
+    plan = model_plans["mobilenetv3-small"]
+    x = np.random.default_rng(4).random(3 * 224 * 224, dtype=np.float32)
+    x.tofile(tmp_path / "x.f32")
+    r = subprocess.run([exe, "--planmodel", plan, str(tmp_path / "x.f32"), str(tmp_path / "y.f16")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    got = np.fromfile(tmp_path / "y.f16", dtype=np.uint16)
+    m = ivb.PlanModel(plan)
+    m.setInput(ivb.f32_to_f16(x), 1)
+    m.run(1)
+    assert np.array_equal(got, m.readOutput(0, 1))
+
+
+@pytest.mark.gpu
+def test_cpp_device_info(tmp_path, model_plans):
+    """device() fills the DeviceInfo fields from the CUDA device, with the
+    reference's own DeviceInfo type when its headers are present."""
+    extra = REFERENCE_TYPES if os.path.isdir(REFERENCE_INCLUDE) else []
+    exe = compile_driver(str(tmp_path), extra)
+    r = subprocess.run([exe, "--device", model_plans["mobilenetv3-small"]], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "CUDA:0" in r.stdout
