@@ -127,6 +127,136 @@ def h2d_bytes(B: int, n_in: int) -> int:
     return n16 * n_in * 2 + (B - n16) * n_in * 4
 
 
+def _t_roof(s, B, pk):
+    """Per-step roofline time: max(FLOPs / tensor peak (burst), bytes / HBM)."""
+    return max(s["flops_per_image"] * B / (pk["bf16_tflops"] * 1e12),
+               (s["act_bytes_per_image"] * B + s["fixed_bytes"]) / (pk["hbm_gbs"] * 1e9))
+
+
+def _graph_ms(m, B, reps):
+    """CUDA-event time per graph replay (after warm-up), on the handle's stream."""
+    import torch
+    s = torch.cuda.Stream()
+    m.set_stream(s.cuda_stream)
+    for _ in range(5):
+        m.run_async(B, s.cuda_stream)
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        m.run_async(B, s.cuda_stream)
+    e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def run_model(args, local: int) -> int:
+    """Any model of the plan emitter (3, 4): batch-1 graph
+    latency (p50 / p99 over 200 replays) and batch-B throughput (CUDA events
+    around >= 200 replays, inputs resident), the summed per-layer roofline
+    and the per-family launch times of an eager profile.  One JSON line."""
+    import torch
+    import infvino_b200 as ivb
+    torch.cuda.set_device(local)
+    pk, pk_src = peaks()
+    B = args.batch
+    m = ivb.PlanModel(make_plan(0, args.workload), device=local, max_batch=B)
+    x = np.random.default_rng(SEED).random(B * m.inputNumel(), dtype=np.float32)
+    m.setInput(ivb.f32_to_f16(x), B)
+    m.run(B)
+    m.run(1)
+    s = torch.cuda.Stream()
+    m.set_stream(s.cuda_stream)
+    for _ in range(20):
+        m.run_async(1, s.cuda_stream)
+    s.synchronize()
+    lat = []
+    for _ in range(200):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        m.run_async(1, s.cuda_stream)
+        b.record(s)
+        b.synchronize()
+        lat.append(a.elapsed_time(b))
+    reps = max(args.min_replays, 20)
+    ms = _graph_ms(m, B, reps)
+    steps = m.steps()
+    troof = sum(_t_roof(st, B, pk) for st in steps)
+    troof1 = sum(_t_roof(st, 1, pk) for st in steps)
+    prof = np.mean([np.array(m.profile(B)) for _ in range(3)], axis=0)
+    fam = {}
+    for st, t in zip(steps, prof):
+        fam[st["family"]] = fam.get(st["family"], 0.0) + float(t)
+    line = {"mode": "model", "workload": args.workload, "batch": B, "images_per_s": round(B / (ms / 1e3), 1),
+            "ms_per_batch": round(ms, 4), "timed_replays": reps, "b1_p50_ms": round(float(np.median(lat)), 4),
+            "b1_p99_ms": round(float(np.percentile(lat, 99)), 4),
+            "gflop_per_image": round(sum(st["flops_per_image"] for st in steps) / 1e9, 4),
+            "network_roofline_ms": round(troof * 1e3, 4), "network_roofline_frac": round(troof / (ms / 1e3), 4),
+            "b1_roofline_us": round(troof1 * 1e6, 2), "launches_per_run": m.launch_count(B),
+            "family_ms_eager": {k: round(v, 4) for k, v in sorted(fam.items(), key=lambda kv: -kv[1])},
+            "peaks": f"{pk_src}: hbm_gbs {pk['hbm_gbs']}, bf16_tflops {pk['bf16_tflops']} (burst)"}
+    print(json.dumps(line), flush=True)
+    m.close()
+    return 0
+
+
+def sweep_shapes():
+    """1x1 convs as GEMMs (M = H*W in {6400, 1600, 400},
+    K, N in {16 .. 256}), 3x3 s1 / s2 at 160..20 with Cin = Cout in
+    {16 .. 128}, depthwise 3x3 / 5x5 s1 / s2 at 112..7 with C in
+    {16, 72, 96, 240, 576}; each with fused bias + SiLU (depthwise: HardSwish,
+    its MobileNet activation)."""
+    out = []
+    for hw in (80, 40, 20):
+        for k in (16, 32, 64, 128, 256):
+            for n in (16, 32, 64, 128, 256):
+                out.append(f"conv1x1:{k}:{n}:{hw}")
+    for hw in (160, 80, 40, 20):
+        for c in (16, 32, 64, 128):
+            for s in (1, 2):
+                out.append(f"conv3x3:{c}:{c}:{hw}:{s}")
+    for hw in (112, 56, 28, 14, 7):
+        for c in (16, 72, 96, 240, 576):
+            for k in (3, 5):
+                for s in (1, 2):
+                    out.append(f"dw:{c}:{k}:{hw}:{s}")
+    return out
+
+
+def run_sweep(args, local: int) -> int:
+    """Config 2 op sweep: per op and batch (1 and 64) the op's own launch time
+    (CUDA events around its launch in an eager profile, median of 5), its
+    roofline time and the fraction; one JSON line per (op, batch)."""
+    import torch
+    import infvino_b200 as ivb
+    torch.cuda.set_device(local)
+    pk, pk_src = peaks()
+    shapes = sweep_shapes() if args.workload in (MODEL, "sweep") else args.workload.split(",")
+    for wl in shapes:
+        plan = make_plan(0, wl)
+        for B in (1, 64):
+            m = ivb.PlanModel(plan, device=local, max_batch=B)
+            x = np.random.default_rng(SEED).random(B * m.inputNumel(), dtype=np.float32)
+            m.setInput(ivb.f32_to_f16(x), B)
+            m.run(B)
+            steps = m.steps()
+            prof = np.median(np.array([m.profile(B) for _ in range(5)]), axis=0)
+            # the measured op is the node named "op" (producer / consumer convs around it)
+            i = next(j for j, st in enumerate(steps) if ":op" in st["name"] or st["name"].endswith("op.out"))
+            t = float(prof[i]) / 1e3
+            r = _t_roof(steps[i], B, pk)
+            st = steps[i]
+            print(json.dumps({"mode": "sweep", "op": wl, "batch": B, "family": st["family"], "us": round(t * 1e6, 2),
+                              "roofline_us": round(r * 1e6, 2), "frac": round(r / t, 4),
+                              "gflops": round(st["flops_per_image"] * B / 1e9, 4),
+                              "mbytes": round((st["act_bytes_per_image"] * B + st["fixed_bytes"]) / 1e6, 3),
+                              "bound": "tensor" if st["flops_per_image"] * B / (pk["bf16_tflops"] * 1e12) >
+                              (st["act_bytes_per_image"] * B + st["fixed_bytes"]) / (pk["hbm_gbs"] * 1e9) else "hbm"}),
+                  flush=True)
+            m.close()
+    return 0
+
+
 def run_kernels_only(args, local: int) -> int:
     """Warm-up + K graph replays and nothing else (for launch lists and ncu captures)."""
     import infvino_b200 as ivb
@@ -383,7 +513,9 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default=MODEL)
-    ap.add_argument("--mode", default="full", choices=["full", "kernels"])
+    ap.add_argument("--mode", default="full", choices=["full", "kernels", "model", "sweep"],
+                    help="full: the headline bench line; kernels: graph replays only (for launch lists and ncu); "
+                         "model: latency / throughput of --workload (any emitted model); sweep: the config-2 op sweep")
     ap.add_argument("--decode", action="store_true", help="kernels mode: also run the device pose decode + NMS")
     ap.add_argument("--min-replays", type=int, default=200,
                     help="device-resident timing: each step repeats the graph replay so that at least this many "
@@ -394,6 +526,10 @@ def main() -> int:
         return run_reference(args, rank, world)
     if args.mode == "kernels":
         return run_kernels_only(args, local)
+    if args.mode == "model":
+        return run_model(args, local)
+    if args.mode == "sweep":
+        return run_sweep(args, local)
 
     import torch
     import infvino_b200 as ivb
