@@ -113,9 +113,9 @@ def make_plan(rank: int, workload: str = MODEL) -> str:
                                consumer=True)
     if kind == "conv1x1":
         return plangen.op_conv(d, v[0], v[1], v[2], v[2], 1, 1, act=1, producer=True, consumer=True)
-    if kind == "dw":
+    if kind == "dw":  # channels-last in and out, as inside MobileNet
         return plangen.op_conv(d, v[0], v[0], v[2], v[2], v[1], v[3] if len(v) > 3 else 1, act=3, groups=v[0],
-                               producer=True)
+                               producer=True, consumer=True)
     raise SystemExit(f"unknown workload {workload}")
 
 
@@ -196,6 +196,16 @@ def run_model(args, local: int) -> int:
             "family_ms_eager": {k: round(v, 4) for k, v in sorted(fam.items(), key=lambda kv: -kv[1])},
             "peaks": f"{pk_src}: hbm_gbs {pk['hbm_gbs']}, bf16_tflops {pk['bf16_tflops']} (burst)"}
     print(json.dumps(line), flush=True)
+    if args.layers:  # one line per step: its eager launch time against its own roofline
+        import re
+        geo = {ln.split()[2]: ln for ln in m.describe().splitlines() if ln.startswith("step ")}
+        for st, t in zip(steps, prof):
+            r = _t_roof(st, B, pk)
+            print(json.dumps({"mode": "layer", "workload": args.workload, "batch": B, "step": st["name"],
+                              "family": st["family"], "us": round(float(t) * 1e3, 2), "roofline_us": round(r * 1e6, 2),
+                              "frac": round(r / (float(t) / 1e3), 4) if t > 0 else None,
+                              "geometry": next(iter(re.findall(rf"\[(B={B} [^\]]*)\]", geo.get(st["name"], ""))),
+                                               None)}), flush=True)
     m.close()
     return 0
 
@@ -516,6 +526,7 @@ def main() -> int:
     ap.add_argument("--mode", default="full", choices=["full", "kernels", "model", "sweep"],
                     help="full: the headline bench line; kernels: graph replays only (for launch lists and ncu); "
                          "model: latency / throughput of --workload (any emitted model); sweep: the config-2 op sweep")
+    ap.add_argument("--layers", action="store_true", help="model mode: also one JSON line per step")
     ap.add_argument("--decode", action="store_true", help="kernels mode: also run the device pose decode + NMS")
     ap.add_argument("--min-replays", type=int, default=200,
                     help="device-resident timing: each step repeats the graph replay so that at least this many "

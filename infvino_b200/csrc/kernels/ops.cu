@@ -322,6 +322,90 @@ __global__ void depthwise_nhwc8_k(View4 x, const __half *__restrict__ w, const _
   }
 }
 
+// Depthwise in row blocks: blockIdx.y is one output row of one image (b * Ho
+// + oy, grid-strided beyond the grid), threads run over that row's (ox,
+// channel) positions, so every index comes from 32-bit arithmetic and the
+// divisions by the row's channel count are multiply-highs.  The activation is
+// a template parameter (the depthwise_f16 expressions, resolved on the host).
+// Same fp32 accumulation order (ky, kx) and epilogue as above.
+struct DwDiv {
+  uint32_t m, s;  // q = (n * m) >> (31 + s), exact for n < 2^31
+};
+__device__ __forceinline__ uint32_t dw_div(uint32_t n, DwDiv d) { return (uint32_t)(((uint64_t)n * d.m) >> (31u + d.s)); }
+
+template <int FN>
+__device__ __forceinline__ __half dw_epilogue(float acc, float bias) {
+  const float v = __half2float(__float2half_rn(acc)) + bias;
+  return __float2half_rn(act_exact<FN>(__half2float(__float2half_rn(v))));
+}
+
+template <int FN>
+__global__ void __launch_bounds__(256) depthwise_nhwc8_rows_k(View4 x, const __half *__restrict__ w,
+                                                             const __half *__restrict__ bias, View4 y, int rows,
+                                                             int K, int S, int P, DwDiv dc8) {
+  pdl_wait_and_release();
+  const int C8 = y.C / 8, per_row = y.W * C8;
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int b = r / y.H, oy = r - b * y.H;
+    const __half *xb = x.ptr + (long long)b * x.sb;
+    __half *yrow = y.ptr + (long long)b * y.sb + (long long)oy * y.sy;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < per_row; t += gridDim.x * blockDim.x) {
+      const int ox = (int)dw_div((uint32_t)t, dc8), c = (t - ox * C8) * 8;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+      for (int ky = 0; ky < K; ++ky) {
+        const int iy = oy * S - P + ky;
+        if (iy < 0 || iy >= x.H) continue;
+        const __half *xr = xb + (long long)iy * x.sy + c;
+        for (int kx = 0; kx < K; ++kx) {
+          const int ix = ox * S - P + kx;
+          if (ix < 0 || ix >= x.W) continue;
+          const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(xr + (long long)ix * x.sx));
+          const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(w + (ky * K + kx) * y.C + c));
+          const __half *xh = reinterpret_cast<const __half *>(&xv);
+          const __half *wh = reinterpret_cast<const __half *>(&wv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += __half2float(xh[j]) * __half2float(wh[j]);
+        }
+      }
+      __align__(16) __half out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = dw_epilogue<FN>(acc[j], bias ? __half2float(__ldg(bias + c + j)) : 0.0f);
+      *reinterpret_cast<uint4 *>(yrow + (long long)ox * y.sx + c) = *reinterpret_cast<const uint4 *>(out);
+    }
+  }
+}
+
+// Planar depthwise in plane rows: blockIdx.y is one (image, channel, output
+// row), threads run over the row's output columns (coalesced stores).
+template <int FN>
+__global__ void __launch_bounds__(256) depthwise_planar_rows_k(View4 x, const __half *__restrict__ w,
+                                                              const __half *__restrict__ bias, View4 y, int rows,
+                                                              int K, int S, int P) {
+  pdl_wait_and_release();
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int oy = r % y.H, bc = r / y.H, c = bc % y.C, b = bc / y.C;
+    const __half *xp = x.ptr + (long long)b * x.sb + (long long)c * x.sc;
+    __half *yr = y.ptr + (long long)b * y.sb + (long long)c * y.sc + (long long)oy * y.sy;
+    const float bv = bias ? __half2float(bias[c]) : 0.0f;
+    for (int ox = blockIdx.x * blockDim.x + threadIdx.x; ox < y.W; ox += gridDim.x * blockDim.x) {
+      float acc = 0.0f;
+      for (int ky = 0; ky < K; ++ky) {
+        const int iy = oy * S - P + ky;
+        if (iy < 0 || iy >= x.H) continue;
+        const __half *xr = xp + (long long)iy * x.sy;
+        for (int kx = 0; kx < K; ++kx) {
+          const int ix = ox * S - P + kx;
+          if (ix < 0 || ix >= x.W) continue;
+          acc += __half2float(xr[(long long)ix * x.sx]) * __half2float(__ldg(w + (ky * K + kx) * y.C + c));
+        }
+      }
+      yr[(long long)ox * y.sx] = dw_epilogue<FN>(acc, bv);
+    }
+  }
+}
+
 // generic direct convolution, weights in the plan layout [Cout][Cin/G][K][K]
 __global__ void conv_direct_v4_k(View4 x, const __half *__restrict__ w, const __half *__restrict__ bias,
                                  const __half *res_ptr, View4 res, View4 y, long long n, int K, int S, int P, int G,
@@ -1282,7 +1366,43 @@ cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, Vi
                    (x.sb % 8) == 0 && (y.sx % 8) == 0 && (y.sy % 8) == 0 && (y.sb % 8) == 0 &&
                    (reinterpret_cast<uintptr_t>(x.ptr) & 15) == 0 && (reinterpret_cast<uintptr_t>(y.ptr) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(w) & 15) == 0;
-  if (vec) {
+  const long long rows_nhwc = (long long)batch * y.H, rows_planar = rows_nhwc * y.C;
+  const int fn = resolve_act(act, kActDepthwise);
+  const bool known = fn == kFnNone || fn == kFnSilu || fn == kFnRelu || fn == kFnHswishB || fn == kFnHsigmoid;
+  if (vec && known && rows_nhwc < (1LL << 31) && (long long)y.W * (y.C / 8) < (1LL << 30)) {
+    // one block row per output row; blocks of 256 threads over its (ox, 8-channel) positions
+    const int per_row = y.W * (y.C / 8);
+    DwDiv d{0u, 0u};
+    {
+      const uint32_t dv = (uint32_t)(y.C / 8);
+      uint32_t sh = 0;
+      while ((1ull << sh) < dv) ++sh;
+      d.s = sh;
+      d.m = (uint32_t)(((1ull << (31 + sh)) / dv) + 1ull);
+    }
+    const dim3 grid((unsigned)((per_row + 255) / 256), (unsigned)std::min<long long>(rows_nhwc, 65535));
+#define IVB_DW_NHWC(F) launch_kernel(depthwise_nhwc8_rows_k<F>, grid, dim3(256), 0, st, x, w, bias, y, (int)rows_nhwc, K, S, P, d)
+    switch (fn) {
+      case kFnSilu: IVB_DW_NHWC(kFnSilu); break;
+      case kFnRelu: IVB_DW_NHWC(kFnRelu); break;
+      case kFnHswishB: IVB_DW_NHWC(kFnHswishB); break;
+      case kFnHsigmoid: IVB_DW_NHWC(kFnHsigmoid); break;
+      default: IVB_DW_NHWC(kFnNone); break;
+    }
+#undef IVB_DW_NHWC
+  } else if (!vec && known && rows_planar < (1LL << 31)) {
+    const dim3 grid((unsigned)((y.W + 255) / 256), (unsigned)std::min<long long>(rows_planar, 65535));
+    const int threads = y.W >= 256 ? 256 : ((y.W + 31) / 32) * 32;
+#define IVB_DW_PLANAR(F) launch_kernel(depthwise_planar_rows_k<F>, grid, dim3(threads), 0, st, x, w, bias, y, (int)rows_planar, K, S, P)
+    switch (fn) {
+      case kFnSilu: IVB_DW_PLANAR(kFnSilu); break;
+      case kFnRelu: IVB_DW_PLANAR(kFnRelu); break;
+      case kFnHswishB: IVB_DW_PLANAR(kFnHswishB); break;
+      case kFnHsigmoid: IVB_DW_PLANAR(kFnHsigmoid); break;
+      default: IVB_DW_PLANAR(kFnNone); break;
+    }
+#undef IVB_DW_PLANAR
+  } else if (vec) {
     const long long n8 = numel4(y, batch) / 8;
     launch_kernel(depthwise_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, x, w, bias, y, n8, K, S, P, act);
   } else {

@@ -176,6 +176,23 @@ def test_depthwise(plan_dir, c, k, s, act):
     check_op(p, 3)
 
 
+# BASELINE config 2's depthwise resolutions (112..7) with MobileNet's channel
+# counts; `producer` puts a 1x1 conv in front and one behind (channels-last
+# input and output, the 8-channel kernel), without them the depthwise reads
+# the planar plan input and writes the planar output
+@pytest.mark.parametrize("c,k,s,hw,act,producer", [
+    (16, 3, 2, 112, 2, True), (72, 3, 2, 56, 2, True), (96, 5, 2, 28, 3, True), (240, 5, 1, 14, 3, True),
+    (576, 5, 1, 7, 3, True), (88, 3, 1, 56, 2, True), (16, 3, 1, 112, 1, False), (72, 5, 2, 28, 4, False),
+    (24, 3, 2, 7, 3, False)])
+def test_depthwise_resolutions(plan_dir, c, k, s, hw, act, producer):
+    p = plangen.op_conv(os.path.join(plan_dir, f"dwr_{c}_{k}_{s}_{hw}_{int(producer)}"), c, c, hw, hw, k, s, act=act,
+                        groups=c, producer=producer, consumer=producer)
+    m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
+    lay = {ln.split()[1]: " nhwc " in ln for ln in m.describe().splitlines() if ln.startswith("tensor")}
+    assert lay["op.out"] == producer
+    check_op(p, 3)
+
+
 def test_generic_grouped_conv(plan_dir):
     # conv_general with groups != Cin: the reference's generic kernel (act code 2 = HardSwish there)
     p = plangen.op_conv(os.path.join(plan_dir, "grp"), 32, 32, 12, 12, 3, 1, act=2, groups=4)
