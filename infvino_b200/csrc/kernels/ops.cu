@@ -233,6 +233,78 @@ __global__ void gap_v4_k(View4 x, __half *__restrict__ y) {
   }
 }
 
+// Global average pool of a channels-last tensor in the reference's summation
+// order (kernels/ops.cl gap_r, GAP_WGS = 128): lane l of 128 sums pixels l,
+// l + 128, ... in sequence, then a tree adds lane l + off into lane l for off =
+// 64, 32, ..., 1, and the sum is divided by H*W.  One block of 128 threads per
+// (image, 8-channel group); each lane keeps the 8 channels' sums.
+__global__ void __launch_bounds__(128) gap_nhwc8_k(View4 x, __half *__restrict__ y, int nq) {
+  pdl_wait_and_release();
+  __shared__ float part[64][8];
+  const int l = threadIdx.x;
+  const int b = blockIdx.x / nq, q = blockIdx.x - b * nq;
+  const int W = x.W, HW = x.H * x.W;
+  const __half *base = x.ptr + (long long)b * x.sb + q * 8;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+  int p = l;
+  // four loads in flight, added in pixel order
+  for (; p + 3 * 128 < HW; p += 4 * 128) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int pp = p + u * 128, yy = pp / W, xx = pp - yy * W;
+      v[u] = __ldg(reinterpret_cast<const uint4 *>(base + (long long)yy * x.sy + (long long)xx * x.sx));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const __half *h = reinterpret_cast<const __half *>(&v[u]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += __half2float(h[e]);
+    }
+  }
+  for (; p < HW; p += 128) {
+    const int yy = p / W, xx = p - yy * W;
+    const uint4 v = __ldg(reinterpret_cast<const uint4 *>(base + (long long)yy * x.sy + (long long)xx * x.sx));
+    const __half *h = reinterpret_cast<const __half *>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += __half2float(h[e]);
+  }
+  // tree: off = 64 (lanes 64..127 into 0..63), off = 32 (through shared memory),
+  // then 16 .. 1 inside warp 0
+  if (l >= 64) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[l - 64][e] = acc[e];
+  }
+  __syncthreads();
+  if (l < 64) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += part[l][e];
+  }
+  __syncthreads();
+  if (l >= 32 && l < 64) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[l - 32][e] = acc[e];
+  }
+  __syncthreads();
+  if (l < 32) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += part[l][e];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += __shfl_down_sync(0xffffffffu, acc[e], off);
+    }
+    if (l == 0) {
+      __align__(16) __half o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(acc[e] / (float)HW);
+      *reinterpret_cast<uint4 *>(y + (long long)b * x.C + q * 8) = *reinterpret_cast<const uint4 *>(o);
+    }
+  }
+}
+
 __global__ void bmm_k(const __half *__restrict__ A, const __half *__restrict__ B, __half *__restrict__ Y, long long n,
                       int B1, int M, int K, int N, long long a_bs, long long b_bs) {
   pdl_wait_and_release();
@@ -1344,6 +1416,11 @@ cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, i
   return cudaGetLastError();
 }
 cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st) {
+  if (vec8_ok(x) && (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (long long)batch * (x.C / 8) < (1LL << 31)) {
+    const int nq = x.C / 8;
+    launch_kernel(gap_nhwc8_k, dim3((unsigned)(batch * nq)), dim3(128), 0, st, x, y, nq);
+    return cudaGetLastError();
+  }
   dim3 grid(batch, (x.C + 31) / 32);
   launch_kernel(gap_v4_k, dim3(grid), dim3(256), 0, st, x, y);
   return cudaGetLastError();

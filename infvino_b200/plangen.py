@@ -608,6 +608,16 @@ def op_sppf(out_dir: str, c: int, h: int, w: int, levels: int = 3, seed: int = 7
     return pw.save(out_dir)
 
 
+def op_gap(out_dir: str, c: int, h: int, w: int, seed: int = 7) -> str:
+    """conv1x1 -> global average pool (a channels-last input, as in the SE
+    blocks and the classifier of MobileNetV3)."""
+    pw = PlanWriter(seed)
+    x = pw.input("x", [1, c, h, w])
+    x = pw.conv(x, c, 1, act=1, name="pre")
+    pw.output(pw.gap(x))
+    return pw.save(out_dir)
+
+
 def op_upsample(out_dir: str, c: int, h: int, w: int, s: int = 2, seed: int = 7) -> str:
     """conv1x1 -> nearest upsample by s -> conv1x1 (channels-last both sides)."""
     pw = PlanWriter(seed)

@@ -160,6 +160,20 @@ def test_upsample_nearest(plan_dir, c, hw, s, batch):
     check_op(p, batch)
 
 
+# the SE-block and classifier shapes of MobileNetV3-small (56^2 .. 7^2), plus
+# fewer pixels than the 128 summation lanes and a ragged last round
+@pytest.mark.parametrize("c,hw,batch", [(16, 56, 3), (96, 14, 2), (576, 7, 4), (40, 11, 5), (24, 13, 1)])
+def test_gap_reference_order(plan_dir, c, hw, batch):
+    """The channels-last global average pool sums in the reference's lane
+    order (128 lane-strided sums, then the tree): bit-identical to the oracle."""
+    p = plangen.op_gap(os.path.join(plan_dir, f"gap_{c}_{hw}"), c, hw, hw)
+    m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
+    assert any(" nhwc " in ln for ln in m.describe().splitlines() if ln.startswith("tensor pre.out"))
+    o, m = run_both(p, batch)
+    assert np.array_equal(m.readOutput(0, batch), o.read_f16(m.outputName(0)))
+    m.close()
+
+
 @pytest.mark.parametrize("batch", [4, 48])
 def test_concat_conv1x1_cat4(plan_dir, batch):
     p = plangen.op_cat_conv1x1(os.path.join(plan_dir, "cat"), [16, 16, 32, 64], 64, 40, 40)
