@@ -623,8 +623,12 @@ bool conv_geom(const ConvCfg &c, int mb, ConvGeom *g) {
   const int b_tile = (int)round_up((int64_t)c.BN * c.BK * 2, 1024);
   const int bres = b_tile * c.num_kb;
   // weights resident when they fit beside two stages; otherwise they travel
-  // with the A tiles (halo: each stage carries its chunk's nine tap blocks)
-  r.resident_b = (c.n_tiles == 1 && bres <= 96 * 1024 && kConvSmemCap - bres >= 2 * r.a_tile) ? 1 : 0;
+  // with the A tiles (halo: each stage carries its chunk's nine tap blocks).
+  // A halo conv split into several N tiles keeps one N tile's weights per CTA
+  // (the launch grid is then a multiple of n_tiles), and only that way.
+  const bool split = c.n_tiles > 1 && c.halo;
+  r.resident_b = ((split || (c.n_tiles == 1 && bres <= 96 * 1024)) && kConvSmemCap - bres >= 2 * r.a_tile) ? 1 : 0;
+  if (split && !r.resident_b) return false;
   const int kb_bytes = r.a_tile + (r.resident_b ? 0 : (c.halo ? 9 : 1) * b_tile);
   const int ring = kConvSmemCap - (r.resident_b ? bres : 0);
   // k-blocks per pipeline stage: one full/empty handshake costs a few hundred
@@ -643,6 +647,14 @@ bool conv_geom(const ConvCfg &c, int mb, ConvGeom *g) {
   r.smem = std::max(r.smem, 120 * 1024);  // one CTA per SM (TMEM never contended)
   *g = r;
   return true;
+}
+
+// Launch grid of a conv: one CTA per SM at most; with resident weights over
+// several N tiles, a multiple of n_tiles (each CTA keeps one N tile).
+int conv_grid(const ConvTcArgs &a, int sms) {
+  int g = std::max(1, std::min(a.m_tiles * a.n_tiles, sms));
+  if (a.resident_b && a.n_tiles > 1) g = std::max(a.n_tiles, g / a.n_tiles * a.n_tiles);
+  return g;
 }
 
 // M tiles of one launch at batch B with geometry g.
@@ -674,6 +686,7 @@ struct ConvCand {
   ConvGeom g;
   int nteams = 1, nbuf = 1;
   double cost = 0.0;
+  int mode = 0;  // index of the conv's layout (ConvCfg variant)
 };
 std::vector<ConvCand> conv_candidates(const ConvCfg &c, int B, int sms) {
   std::vector<ConvCand> out;
@@ -1320,18 +1333,53 @@ void Engine::lower() {
         c.halo = c.stride;
         c.kern_kb = c.chunks[0];
         ConvGeom g1;
-        if (!conv_geom(c, 1, &g1)) {  // weights too large to stay resident beside two stages
-          c.halo = 0;
-          c.kern_kb = c.num_kb;
+        if (!conv_geom(c, 1, &g1)) {
+          // weights too large to stay resident beside two stages, or to travel
+          // with each stage: split N in two or four so that each CTA keeps one
+          // N tile's weights resident, else one box per tap
+          bool ok = false;
+          if (c.n_tiles == 1)
+            for (int sp = 2; sp <= 4 && !ok; sp *= 2) {
+              ConvCfg t = c;
+              t.BN = (int)round_up((np16 + sp - 1) / sp, 16);
+              t.n_tiles = sp;
+              t.Np = t.BN * sp;
+              if (conv_geom(t, 1, &g1)) {
+                c = t;
+                ok = true;
+              }
+            }
+          if (!ok) {
+            c.halo = 0;
+            c.kern_kb = c.num_kb;
+          }
         }
       }
       {
         ConvGeom g1;
         if (!conv_geom(c, 1, &g1)) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
       }
+      // Layouts the load-time tuning chooses between (the first is the
+      // untuned pick): a halo conv split over N tiles also keeps the one-box-
+      // per-tap layout, which is faster where the halo tiles cover the image
+      // poorly.  Both read the same packed weights (same K order, the larger
+      // N padding).
+      std::vector<ConvCfg> modes{c};
+      if (c.halo && c.n_tiles > 1) {
+        ConvCfg t = c;
+        t.halo = 0;
+        t.kern_kb = t.num_kb;
+        t.BN = np16;
+        t.n_tiles = 1;
+        t.Np = np16;
+        ConvGeom gt;
+        if (conv_geom(t, 1, &gt)) modes.push_back(t);
+      }
+      int np_alloc = 0;
+      for (const ConvCfg &m : modes) np_alloc = std::max(np_alloc, m.Np);
       // ---- weight repack: Wp[Np][Kp], K order (source, tap, chunk, channel)
       const int Kp = c.num_kb * c.BK;
-      std::vector<uint16_t> wp((size_t)c.Np * Kp, 0), bp((size_t)c.Np, 0);
+      std::vector<uint16_t> wp((size_t)np_alloc * Kp, 0), bp((size_t)np_alloc, 0);
       const PlanTensor &pw = p.ref(wt.name);
       const int wcin = (int)(pw.numel() / (c.cout * c.taps));
       {
@@ -1364,13 +1412,17 @@ void Engine::lower() {
         dev_allocs_.push_back(db);
         check(cudaMemcpy(dw, wp.data(), wp.size() * 2, cudaMemcpyHostToDevice), "upload packed weights");
         check(cudaMemcpy(db, bp.data(), bp.size() * 2, cudaMemcpyHostToDevice), "upload packed bias");
-        c.wp = static_cast<__half *>(dw);
-        c.bias = bias >= 0 ? static_cast<__half *>(db) : nullptr;
+        for (ConvCfg &m : modes) {
+          m.wp = static_cast<__half *>(dw);
+          m.bias = bias >= 0 ? static_cast<__half *>(db) : nullptr;
+        }
+        c = modes[0];
       }
       st.family = c.ksize == 3 ? "conv3x3_tc" : "conv1x1_tc";
       // Launch parameters of one batch size and tile geometry.
       auto build = std::make_shared<std::function<ConvTcArgs(int, const ConvCand &)>>(
-          [this, c, status](int B, const ConvCand &cand) -> ConvTcArgs {
+          [this, modes, status](int B, const ConvCand &cand) -> ConvTcArgs {
+        const ConvCfg &c = modes[(size_t)cand.mode];
         const ConvGeom &g = cand.g;
         const int nteams = cand.nteams, nbuf = cand.nbuf;
         ConvTcArgs a;
@@ -1501,8 +1553,7 @@ void Engine::lower() {
           it = cache->emplace(B, a).first;
         }
         const ConvTcArgs &a = it->second;
-        const int tiles = a.m_tiles * a.n_tiles;
-        const int grid = std::max(1, std::min(tiles, sms));
+        const int grid = conv_grid(a, sms);
         if (wait->probe || wait->limit != kConvWaitLimitDefault) {  // test settings of the bounded waits
           ConvTcArgs b = a;
           b.wait_limit = wait->limit;
@@ -1515,8 +1566,18 @@ void Engine::lower() {
       // best few tile geometries of this conv (each geometry accumulates every
       // output in the same order, so the choice changes no result) and keeps
       // the fastest.
-      st.tune = [c, cache, build, record, sms](int B, cudaStream_t s) {
-        const std::vector<ConvCand> cands = conv_candidates(c, B, sms);
+      st.tune = [modes, cache, build, record, sms](int B, cudaStream_t s) {
+        // the best few of every layout by the cost model (which compares
+        // geometries of one layout only)
+        std::vector<ConvCand> cands;
+        for (size_t mi = 0; mi < modes.size(); ++mi) {
+          std::vector<ConvCand> cm = conv_candidates(modes[mi], B, sms);
+          const size_t keep = modes.size() == 1 ? cm.size() : (size_t)kConvTuneCands / modes.size();
+          for (size_t k = 0; k < cm.size() && k < keep; ++k) {
+            cm[k].mode = (int)mi;
+            cands.push_back(cm[k]);
+          }
+        }
         if (cands.size() < 2) return;
         float best_ms = 0.0f;
         ConvTcArgs best{};
@@ -1530,7 +1591,7 @@ void Engine::lower() {
           } catch (const std::exception &) {
             continue;
           }
-          const int grid = std::max(1, std::min(a.m_tiles * a.n_tiles, sms));
+          const int grid = conv_grid(a, sms);
           if (launch_conv_tc(a, grid, s) != cudaSuccess) continue;  // warm-up
           cudaEventRecord(e0, s);
           bool ok = true;

@@ -100,7 +100,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
   const long long o_sb = a.o_sb, o_sc = a.o_sc, o_sy = a.o_sy, o_sx = a.o_sx;
   const long long r_sb = a.r_sb, r_sc = a.r_sc, r_sy = a.r_sy, r_sx = a.r_sx;
   const bool out_vec = a.out_vec != 0, res_vec = a.res_vec != 0, has_res = res != nullptr;
-  const bool bias_in_smem = n_tiles == 1 && bias != nullptr;
+  const bool bias_in_smem = (n_tiles == 1 || a.resident_b != 0) && bias != nullptr;  // one N tile per CTA
   int *status = a.status;
   const long long wait_limit = a.wait_limit;
   // 3x3: this thread's pixel inside the tile is fixed
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
   __shared__ volatile int epi_go[2 * kConvMaxTeams];
-  __shared__ uint4 bias_sh[256 / 8];  // the bias of the single N tile (n_tiles == 1)
+  __shared__ uint4 bias_sh[256 / 8];  // the bias of the CTA's N tile (one N tile, or resident weights)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -299,6 +299,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
   const int num_tiles = a.m_tiles * n_tiles;
   int *const status = a.status;
   const long long wait_limit = a.wait_limit;
+  // Resident weights with several N tiles: tile t is N tile t % n_tiles, and a
+  // grid that is a multiple of n_tiles gives each CTA one N tile for all its
+  // tiles, whose weights it keeps (checked before anything is set up).
+  if (resident_b && n_tiles > 1 && gridDim.x % (unsigned)n_tiles != 0u) {
+    if (threadIdx.x == 0 && status) atomicCAS(status, 0, kStatusBadConfig);
+    return;
+  }
+  const int nt_cta = (int)(blockIdx.x % (unsigned)n_tiles);
   // 1024-byte aligned operand area (128B-swizzle atoms repeat every 1024 B)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -341,17 +349,17 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     if (resident_b) {
       mbar_expect_tx(smem_u32(&bres_bar), (uint32_t)BN * (uint32_t)BK * 2u * (uint32_t)b_blocks);
       for (int kb = 0; kb < b_blocks; ++kb)
-        tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * BK, 0);
+        tma_load_2d(bres_base + (uint32_t)kb * b_tile, &a.mapB, smem_u32(&bres_bar), kb * BK, nt_cta * BN);
     }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&tmem_base_sh), (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
-  if (warp >= 2 && n_tiles == 1 && a.bias != nullptr) {  // (a constant too)
-    // bias padded to BN (a multiple of 16), 16 B per thread
+  if (warp >= 2 && (n_tiles == 1 || resident_b) && a.bias != nullptr) {  // (a constant too)
+    // the bias of this CTA's N tile, padded to BN (a multiple of 16), 16 B per thread
     const int i = threadIdx.x - 64;
-    if (i < BN / 8) bias_sh[i] = reinterpret_cast<const uint4 *>(a.bias)[i];
+    if (i < BN / 8) bias_sh[i] = reinterpret_cast<const uint4 *>(a.bias + nt_cta * BN)[i];
   }
   // everything above touched only shared memory, TMEM, the parameter block and
   // the constant weights and bias; activations are read after the previous grid

@@ -83,6 +83,33 @@ def test_conv3x3(plan_dir, cin, cout, hw, s, batch):
     check_op(p, batch)
 
 
+# 3x3 convs whose weights fit neither resident nor travelling with each halo
+# stage: N split in two or four tiles, each CTA keeping one N tile's weights
+# (the YOLOv8 head's merged P3 conv, the 20x20 128-channel bottlenecks, a
+# stride-2 conv, Cout not a multiple of the N tile)
+SPLIT3 = [(128, 128, 20, 1, 64), (64, 179, 40, 1, 16), (64, 128, 40, 2, 8), (128, 179, 20, 1, 2), (128, 128, 10, 1, 3)]
+
+
+@pytest.mark.parametrize("cin,cout,hw,s,batch", SPLIT3)
+def test_conv3x3_split_resident(plan_dir, cin, cout, hw, s, batch):
+    p = plangen.op_conv(os.path.join(plan_dir, f"sp_{cin}_{cout}_{hw}_{s}"), cin, cout, hw, hw, 3, s, act=1,
+                        producer=True, consumer=True)
+    o, m = run_both(p, batch, flags=ivb.FLAG_NO_POOL | ivb.FLAG_NO_TUNE)
+    geo = [ln for ln in m.describe().splitlines() if ln.startswith("step conv3x3_tc conv3x3:op.out")]
+    assert geo and f"halo={s}" in geo[0], geo
+    # the op's own output against the oracle (the usual bar), and the consumer's
+    # (which amplifies the op's rounding flips: the max-abs bound only)
+    for name, frac_bound in (("op.out", 0.01), (m.outputName(0), None)):
+        got = m.readTensor(name, batch)
+        ref = o.read_f16(name)
+        g, r = ivref.f16_to_f32(got), ivref.f16_to_f32(ref)
+        scale = float(np.abs(r).max())
+        assert np.abs(g.astype(np.float64) - r).max() <= 2.0 * 2.0 ** -10 * scale, name
+        if frac_bound is not None:
+            assert float(np.mean(ulp_diff(got, ref) > 0)) <= frac_bound, name
+    m.close()
+
+
 @pytest.mark.parametrize("act", [0, 3])
 def test_conv3x3_activations(plan_dir, act):
     p = plangen.op_conv(os.path.join(plan_dir, f"c3act{act}"), 32, 32, 20, 20, 3, 1, act=act)
