@@ -1700,6 +1700,28 @@ void Engine::lower() {
       }
     }
 
+    // ------------------------- transposing permute that only feeds a bmm operand
+    // permute_0213 mode 1 swaps the last two axes of [B1][D2][I]; when its one
+    // reader is a bmm taking it as A ([B1][M=I][K=D2]) or B ([B1][K=I][N=D2]),
+    // the bmm reads the source transposed instead (the values are the same)
+    if (op == "permute_0213" && n.ai("mode", 0) == 1 && !(flags_ & kFlagNoFusion)) {
+      const int x = tid(n.ins[0]);
+      const int bj = sole_reader(out);
+      const PlanNode *bm = bj >= 0 ? &nodes[(size_t)bj] : nullptr;
+      const auto &od = T_[(size_t)out].dims;
+      bool fold = bm && bm->op == "bmm" && T_[(size_t)x].dense && T_[(size_t)x].root == x && !T_[(size_t)x].is_init &&
+                  T_[(size_t)x].numel == T_[(size_t)out].numel && od.size() == 4 && od[1] == n.ai("D1", 1) &&
+                  od[2] == n.ai("I", 1) && od[3] == n.ai("D2", 1);
+      if (fold) {
+        const bool as_a = bm->ins[0] == n.outs[0], as_b = bm->ins.size() > 1 && bm->ins[1] == n.outs[0];
+        fold = as_a != as_b;
+      }
+      if (fold) {
+        folded_transpose_[out] = {x, (int)ni};
+        continue;
+      }
+    }
+
     // ---------------------------------------------------------------- small ops
     for (const auto &in : n.ins)
       if (in != "-") st.bytes_img += act_bytes(tid(in)), st.bytes_fixed += init_bytes(tid(in));
@@ -1900,13 +1922,33 @@ void Engine::lower() {
       const int x = tid(n.ins[0]);
       st.launch = [this, x, out](int B, cudaStream_t s) { return launch_gap_v4(view(x), T_[(size_t)out].dptr, B, s); };
     } else if (op == "bmm") {
-      const int a = tid(n.ins[0]), b = tid(n.ins[1]);
+      int a = tid(n.ins[0]), b = tid(n.ins[1]);
       const auto &ad = T_[(size_t)a].dims, &bd = T_[(size_t)b].dims;
       if (ad.size() != 4 || bd.size() != 4) throw std::runtime_error("CudaPlanModel: bmm expects 4-D operands");
       const int B1 = (int)ad[1], M = (int)ad[2], K = (int)ad[3], Nn = (int)bd[3];
       st.flops_img = 2.0 * B1 * M * K * Nn;
-      st.launch = [this, a, b, out, B1, M, K, Nn](int B, cudaStream_t s) {
+      // operands produced by a folded transposing permute: read its source
+      int ta_flag = 0, tb_flag = 0;
+      auto fa = folded_transpose_.find(a), fb = folded_transpose_.find(b);
+      if (fa != folded_transpose_.end()) {
+        a = fa->second.first;
+        ta_flag = 1;
+        st.nodes.insert(st.nodes.begin(), fa->second.second);
+      }
+      if (fb != folded_transpose_.end()) {
+        b = fb->second.first;
+        tb_flag = 1;
+        st.nodes.insert(st.nodes.begin(), fb->second.second);
+      }
+      if (ta_flag || tb_flag) {
+        st.bytes_img = act_bytes(a) + act_bytes(b) + act_bytes(out);
+        st.family = "bmm";
+      }
+      st.launch = [this, a, b, out, B1, M, K, Nn, ta_flag, tb_flag](int B, cudaStream_t s) {
         const TensorRt &ta = T_[(size_t)a], &tb = T_[(size_t)b];
+        if (ta_flag || tb_flag)
+          return launch_bmm_t(ta.dptr, tb.dptr, T_[(size_t)out].dptr, B, B1, M, K, Nn, ta.is_init ? 0 : ta.numel,
+                              tb.is_init ? 0 : tb.numel, ta_flag, tb_flag, s);
         return launch_bmm(ta.dptr, tb.dptr, T_[(size_t)out].dptr, B, B1, M, K, Nn, ta.is_init ? 0 : ta.numel,
                           tb.is_init ? 0 : tb.numel, s);
       };
@@ -1999,7 +2041,7 @@ void Engine::plan_streams() {
   }
   for (int j = 0; j < S; ++j) {
     const Step &stp = steps_[(size_t)j];
-    if (stp.family == "decode_tail" || stp.family == "dfl_fused") {
+    if (stp.family == "decode_tail" || stp.family == "dfl_fused" || (stp.family == "bmm" && stp.nodes.size() > 1)) {
       // computed in registers: the values the fused nodes pass to each other
       // (written by this step alone, other than its last node's output) never
       // reach memory and are no accesses; tensors other steps write (the

@@ -190,6 +190,7 @@ class Engine {
   std::vector<TensorRt> T_;
   std::map<std::string, int> tid_;
   std::set<std::string> nhwc_names_;
+  std::map<int, std::pair<int, int>> folded_transpose_;  // permute output -> (its source, the permute node)
   std::set<int> elided_nodes_;       // concat4 nodes whose sources write in place
   std::map<int, Step> tail_steps_;   // fused planar tails, keyed by the node whose place they take
   std::vector<std::pair<int, int>> tail_uses_;  // (tensor, node) reads of fused tails, for liveness

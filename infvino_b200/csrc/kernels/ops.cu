@@ -196,6 +196,43 @@ __global__ void softmax_axis_k(const __half *__restrict__ x, __half *__restrict_
   }
 }
 
+// Softmax over the last axis (inner == 1), one warp per row, with softmax_axis_k's
+// arithmetic: the max (order-free), expf(x - max) per element, their sum added
+// in axis order by one lane, then each value over the sum, rounded once.
+constexpr int kSoftmaxRowMax = 1024;
+__global__ void __launch_bounds__(256) softmax_rows_k(const __half *__restrict__ x, __half *__restrict__ y,
+                                                      long long rows, int axdim) {
+  pdl_wait_and_release();
+  __shared__ float e_sh[8][kSoftmaxRowMax];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float *e = e_sh[warp];
+  for (long long r = (long long)blockIdx.x * 8 + warp; r < rows; r += (long long)gridDim.x * 8) {
+    const __half *xr = x + r * axdim;
+    __half *yr = y + r * axdim;
+    float m = -3.4e38f;
+    for (int a = lane; a < axdim; a += 32) m = fmaxf(m, __half2float(xr[a]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    for (int a = lane; a < axdim; a += 32) e[a] = expf(__half2float(xr[a]) - m);
+    __syncwarp();
+    float s = 0.0f;
+    if (lane == 0) {
+      int a = 0;
+      for (; a + 8 <= axdim; a += 8) {  // loads ahead of the dependent adds
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = e[a + u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s += v[u];
+      }
+      for (; a < axdim; ++a) s += e[a];
+    }
+    s = __shfl_sync(0xffffffffu, s, 0);
+    for (int a = lane; a < axdim; a += 32) yr[a] = __float2half_rn(e[a] / s);
+    __syncwarp();  // e is rewritten by the next row
+  }
+}
+
 __global__ void permute_0213_k(const __half *__restrict__ x, __half *__restrict__ y, long long n, int D1, int D2,
                                long long I, int mode) {
   pdl_wait_and_release();
@@ -301,6 +338,77 @@ __global__ void __launch_bounds__(128) gap_nhwc8_k(View4 x, __half *__restrict__
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(acc[e] / (float)HW);
       *reinterpret_cast<uint4 *>(y + (long long)b * x.C + q * 8) = *reinterpret_cast<const uint4 *>(o);
+    }
+  }
+}
+
+// Batched matmul Y[z] = A[z] B[z] on the CUDA cores in 64 x 64 output tiles
+// (4 x 4 per thread), K in 32-wide slices staged in shared memory as f32.
+// Every output accumulates its K products in order with one fused multiply-add
+// each, as bmm_k does, so the two kernels agree bit for bit.  TA / TB: the
+// operand is stored transposed (A as [K][M], B as [N][K]), which lets a
+// transposing permute that only feeds this product be folded into it.
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A, const __half *__restrict__ B,
+                                                   __half *__restrict__ Y, int B1, int M, int K, int N, long long a_bs,
+                                                   long long b_bs, int tiles_m, int tiles_n) {
+  pdl_wait_and_release();
+  constexpr int TM = 64, TN = 64, KT = 32;
+  __shared__ float As[KT][TM + 4];
+  __shared__ float Bs[KT][TN + 4];
+  const int tile = blockIdx.x % (tiles_m * tiles_n);
+  const long long z = blockIdx.x / (tiles_m * tiles_n);  // b0 * B1 + b1
+  const long long b0 = z / B1, b1 = z - b0 * B1;
+  const int m0 = (tile / tiles_n) * TM, n0 = (tile % tiles_n) * TN;
+  const __half *Az = A + b0 * a_bs + b1 * (long long)M * K;
+  const __half *Bz = B + b0 * b_bs + b1 * (long long)K * N;
+  __half *Yz = Y + z * (long long)M * N;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // outputs n0 + tx + 16 j, m0 + ty + 16 i
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  for (int k0 = 0; k0 < K; k0 += KT) {
+    const int kl = min(KT, K - k0);
+    for (int e = threadIdx.x; e < KT * TM; e += 256) {  // A slice -> As[k][m]
+      int kk, mm;
+      if (TA) { kk = e / TM; mm = e - kk * TM; } else { mm = e / KT; kk = e - mm * KT; }
+      const int gm = m0 + mm, gk = k0 + kk;
+      float v = 0.0f;
+      if (gm < M && kk < kl) v = __half2float(TA ? Az[(long long)gk * M + gm] : Az[(long long)gm * K + gk]);
+      As[kk][mm] = v;
+    }
+    for (int e = threadIdx.x; e < KT * TN; e += 256) {  // B slice -> Bs[k][n]
+      int kk, nn;
+      if (TB) { nn = e / KT; kk = e - nn * KT; } else { kk = e / TN; nn = e - kk * TN; }
+      const int gn = n0 + nn, gk = k0 + kk;
+      float v = 0.0f;
+      if (gn < N && kk < kl) v = __half2float(TB ? Bz[(long long)gn * K + gk] : Bz[(long long)gk * N + gn]);
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+    for (int kk = 0; kk < kl; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty + 16 * i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx + 16 * j;
+      if (gn < N) Yz[(long long)gm * N + gn] = __float2half_rn(acc[i][j]);
     }
   }
 }
@@ -1401,6 +1509,11 @@ cudaError_t launch_resize_nn_v4(View4 x, View4 y, int batch, int S, cudaStream_t
 }
 cudaError_t launch_softmax_axis(const __half *x, __half *y, long long outer, int axdim, long long inner,
                                 cudaStream_t st) {
+  if (inner == 1 && axdim >= 32 && axdim <= kSoftmaxRowMax) {
+    const long long blocks = std::min<long long>((outer + 7) / 8, 148LL * 8);
+    launch_kernel(softmax_rows_k, dim3((unsigned)blocks), dim3(256), 0, st, x, y, outer, axdim);
+    return cudaGetLastError();
+  }
   launch_kernel(softmax_axis_k, dim3(grid_for(outer * inner)), dim3(kThreads), 0, st, x, y, outer, axdim, inner);
   return cudaGetLastError();
 }
@@ -1425,8 +1538,21 @@ cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st) {
   launch_kernel(gap_v4_k, dim3(grid), dim3(256), 0, st, x, y);
   return cudaGetLastError();
 }
+cudaError_t launch_bmm_t(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
+                         long long a_bs, long long b_bs, int ta, int tb, cudaStream_t st) {
+  const int tiles_m = (M + 63) / 64, tiles_n = (N + 63) / 64;
+  const long long blocks = (long long)batch * B1 * tiles_m * tiles_n;
+  if (blocks >= (1LL << 31)) return cudaErrorInvalidValue;
+  const dim3 g((unsigned)blocks), b(256);
+  if (ta && tb) launch_kernel(bmm_tiled_k<true, true>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
+  else if (ta) launch_kernel(bmm_tiled_k<true, false>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
+  else if (tb) launch_kernel(bmm_tiled_k<false, true>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
+  else launch_kernel(bmm_tiled_k<false, false>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
+  return cudaGetLastError();
+}
 cudaError_t launch_bmm(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
                        long long a_bs, long long b_bs, cudaStream_t st) {
+  if ((long long)M * N >= 64 * 64) return launch_bmm_t(A, B, Y, batch, B1, M, K, N, a_bs, b_bs, 0, 0, st);
   const long long n = (long long)batch * B1 * M * N;
   launch_kernel(bmm_k, dim3(grid_for(n)), dim3(kThreads), 0, st, A, B, Y, n, B1, M, K, N, a_bs, b_bs);
   return cudaGetLastError();

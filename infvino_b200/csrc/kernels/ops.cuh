@@ -57,6 +57,9 @@ cudaError_t launch_permute_0213(const __half *x, __half *y, int batch, int D1, i
 cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st);
 cudaError_t launch_bmm(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
                        long long a_bstride, long long b_bstride, cudaStream_t st);
+// ta / tb: A stored as [K][M], B as [N][K] (a folded transposing permute)
+cudaError_t launch_bmm_t(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
+                         long long a_bstride, long long b_bstride, int ta, int tb, cudaStream_t st);
 cudaError_t launch_bias_add(const __half *x, const __half *b, __half *y, long long per_img, int HW, int batch,
                             cudaStream_t st);
 

@@ -618,6 +618,17 @@ def op_gap(out_dir: str, c: int, h: int, w: int, seed: int = 7) -> str:
     return pw.save(out_dir)
 
 
+def op_attention(out_dir: str, c: int, h: int, w: int, heads: int = 0, seed: int = 7) -> str:
+    """conv1x1 -> the position-sensitive attention block of YOLO11's C2PSA
+    (qkv conv, slices, transposing permutes, two bmm, scale, softmax, pe
+    depthwise conv, proj conv)."""
+    pw = PlanWriter(seed)
+    x = pw.input("x", [1, c, h, w])
+    x = pw.conv(x, c, 1, act=1, name="pre")
+    pw.output(_attention(pw, x, c, heads or max(1, c // 64), "op"))
+    return pw.save(out_dir)
+
+
 def op_upsample(out_dir: str, c: int, h: int, w: int, s: int = 2, seed: int = 7) -> str:
     """conv1x1 -> nearest upsample by s -> conv1x1 (channels-last both sides)."""
     pw = PlanWriter(seed)

@@ -201,6 +201,31 @@ def test_gap_reference_order(plan_dir, c, hw, batch):
     m.close()
 
 
+# YOLO11's C2PSA attention at its P5 size (20x20, 2 heads), one head, and
+# sizes that leave partial 64 x 64 product tiles and K slices
+@pytest.mark.parametrize("c,hw,heads,batch", [(128, 20, 2, 2), (64, 12, 1, 3), (128, 7, 2, 1), (64, 9, 2, 4)])
+def test_attention_block(plan_dir, c, hw, heads, batch):
+    """Both transposing permutes fold into their bmm (no permute launch), the
+    tiled bmm and the row softmax match the oracle, and the folded network
+    equals the unfolded one bit for bit."""
+    p = plangen.op_attention(os.path.join(plan_dir, f"att_{c}_{hw}_{heads}"), c, hw, hw, heads)
+    m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
+    fams = [st["family"] for st in m.steps()]
+    assert "permute_0213" not in fams and fams.count("bmm") == 2, fams
+    # eight rounding points in a row, and a flipped score changes its whole
+    # softmax row: at most 2 ulps anywhere, and at most 5% of the elements off
+    check_op(p, batch, max_frac=0.05)
+    x = np.random.default_rng(9).random(batch * m.inputNumel(), dtype=np.float32)
+    outs = []
+    for flags in (0, ivb.FLAG_NO_FUSION):
+        mm = ivb.PlanModel(p, device=0, max_batch=batch, flags=flags)
+        mm.setInput(ivb.f32_to_f16(x), batch)
+        mm.run(batch)
+        outs.append(mm.readOutput(0, batch))
+        mm.close()
+    assert np.array_equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("batch", [4, 48])
 def test_concat_conv1x1_cat4(plan_dir, batch):
     p = plangen.op_cat_conv1x1(os.path.join(plan_dir, "cat"), [16, 16, 32, 64], 64, 40, 40)
