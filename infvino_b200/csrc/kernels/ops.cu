@@ -354,8 +354,8 @@ __global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A,
                                                    long long b_bs, int tiles_m, int tiles_n) {
   pdl_wait_and_release();
   constexpr int TM = 64, TN = 64, KT = 32;
-  __shared__ float As[KT][TM + 4];
-  __shared__ float Bs[KT][TN + 4];
+  __shared__ __align__(16) float As[KT][TM + 4];  // rows of 68 floats: 16-byte aligned float4 reads
+  __shared__ __align__(16) float Bs[KT][TN + 4];
   const int tile = blockIdx.x % (tiles_m * tiles_n);
   const long long z = blockIdx.x / (tiles_m * tiles_n);  // b0 * B1 + b1
   const long long b0 = z / B1, b1 = z - b0 * B1;
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A,
   const __half *Az = A + b0 * a_bs + b1 * (long long)M * K;
   const __half *Bz = B + b0 * b_bs + b1 * (long long)K * N;
   __half *Yz = Y + z * (long long)M * N;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // outputs n0 + tx + 16 j, m0 + ty + 16 i
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // outputs m0 + 4 ty + i, n0 + 4 tx + j
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -389,11 +389,9 @@ __global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A,
     }
     __syncthreads();
     for (int kk = 0; kk < kl; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+      const float4 av = *reinterpret_cast<const float4 *>(&As[kk][4 * ty]);
+      const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][4 * tx]);
+      const float a[4] = {av.x, av.y, av.z, av.w}, b[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -403,11 +401,11 @@ __global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A,
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int gm = m0 + ty + 16 * i;
+    const int gm = m0 + 4 * ty + i;
     if (gm >= M) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + tx + 16 * j;
+      const int gn = n0 + 4 * tx + j;
       if (gn < N) Yz[(long long)gm * N + gn] = __float2half_rn(acc[i][j]);
     }
   }
@@ -554,6 +552,108 @@ __global__ void __launch_bounds__(256) depthwise_nhwc8_rows_k(View4 x, const __h
       for (int j = 0; j < 8; ++j) out[j] = dw_epilogue<FN>(acc[j], bias ? __half2float(__ldg(bias + c + j)) : 0.0f);
       *reinterpret_cast<uint4 *>(yrow + (long long)ox * y.sx + c) = *reinterpret_cast<const uint4 *>(out);
     }
+  }
+}
+
+// Depthwise K x K (3 or 5), stride S (1 or 2), channels-last, in strips: a
+// thread computes four neighbouring output pixels of one 8-channel group, so
+// each weight vector is loaded once for the four and each input vector once
+// per kernel row for all the outputs that use it.  Same fp32 accumulation
+// order (ky, kx), same skipped padding taps and epilogue as above, so the
+// results are identical.  Threads run over (output row, strip, channel
+// group) with the channel group fastest (consecutive threads, consecutive
+// 16-byte vectors).
+template <int FN, int K, int S>
+__global__ void __launch_bounds__(256) depthwise_nhwc8_strip_k(View4 x, const __half *__restrict__ w,
+                                                              const __half *__restrict__ bias, View4 y,
+                                                              long long items, int P, int C8, int strips,
+                                                              DwDiv d_item, DwDiv d_c8, DwDiv d_ho) {
+  pdl_wait_and_release();
+  constexpr int NX = 3 * S + K;  // input columns the four outputs read
+  const int per_row = strips * C8;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < items;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const uint32_t r = dw_div((uint32_t)idx, d_item);          // output row b * Ho + oy
+    const uint32_t it = (uint32_t)idx - r * (uint32_t)per_row;  // strip * C8 + channel group
+    const uint32_t sx = dw_div(it, d_c8);
+    const int c = (int)(it - sx * (uint32_t)C8) * 8;
+    const uint32_t b = dw_div(r, d_ho);
+    const int oy = (int)(r - b * (uint32_t)y.H), ox0 = (int)sx * 4;
+    const __half *xb = x.ptr + (long long)b * x.sb + c;
+    float acc[4][8];
+#pragma unroll
+    for (int o = 0; o < 4; ++o)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[o][j] = 0.0f;
+#pragma unroll
+    for (int ky = 0; ky < K; ++ky) {
+      const int iy = oy * S - P + ky;
+      if (iy < 0 || iy >= x.H) continue;
+      const __half *xr = xb + (long long)iy * x.sy;
+      uint4 xv[NX];
+      bool ok[NX];
+#pragma unroll
+      for (int q = 0; q < NX; ++q) {
+        const int ix = ox0 * S - P + q;
+        ok[q] = ix >= 0 && ix < x.W;
+        xv[q] = ok[q] ? __ldg(reinterpret_cast<const uint4 *>(xr + (long long)ix * x.sx)) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int kx = 0; kx < K; ++kx) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(w + (ky * K + kx) * y.C + c));
+        const __half *wh = reinterpret_cast<const __half *>(&wv);
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+          const int q = o * S + kx;
+          if (!ok[q]) continue;
+          const __half *xh = reinterpret_cast<const __half *>(&xv[q]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[o][j] += __half2float(xh[j]) * __half2float(wh[j]);
+        }
+      }
+    }
+    __align__(16) float bv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bv[j] = bias ? __half2float(__ldg(bias + c + j)) : 0.0f;
+    __half *yrow = y.ptr + (long long)b * y.sb + (long long)oy * y.sy + c;
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      if (ox0 + o >= y.W) break;
+      __align__(16) __half out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = dw_epilogue<FN>(acc[o][j], bv[j]);
+      *reinterpret_cast<uint4 *>(yrow + (long long)(ox0 + o) * y.sx) = *reinterpret_cast<const uint4 *>(out);
+    }
+  }
+}
+
+// Planar depthwise, one output per thread over (plane, oy, ox) flattened, so
+// small planes still fill whole blocks; same arithmetic as the kernels above.
+template <int FN>
+__global__ void __launch_bounds__(256) depthwise_planar_flat_k(View4 x, const __half *__restrict__ w,
+                                                              const __half *__restrict__ bias, View4 y,
+                                                              long long n, int K, int S, int P, DwDiv d_hw,
+                                                              DwDiv d_wo, DwDiv d_c) {
+  pdl_wait_and_release();
+  const uint32_t hw = (uint32_t)(y.H * y.W);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const uint32_t plane = dw_div((uint32_t)i, d_hw), p = (uint32_t)i - plane * hw;
+    const uint32_t b = dw_div(plane, d_c), c = plane - b * (uint32_t)y.C;
+    const uint32_t oy = dw_div(p, d_wo), ox = p - oy * (uint32_t)y.W;
+    const __half *xp = x.ptr + (long long)b * x.sb + (long long)c * x.sc;
+    float acc = 0.0f;
+    for (int ky = 0; ky < K; ++ky) {
+      const int iy = (int)oy * S - P + ky;
+      if (iy < 0 || iy >= x.H) continue;
+      const __half *xr = xp + (long long)iy * x.sy;
+      for (int kx = 0; kx < K; ++kx) {
+        const int ix = (int)ox * S - P + kx;
+        if (ix < 0 || ix >= x.W) continue;
+        acc += __half2float(xr[(long long)ix * x.sx]) * __half2float(__ldg(w + (ky * K + kx) * y.C + c));
+      }
+    }
+    y.ptr[(long long)b * y.sb + (long long)c * y.sc + (long long)oy * y.sy + (long long)ox * y.sx] =
+        dw_epilogue<FN>(acc, bias ? __half2float(bias[c]) : 0.0f);
   }
 }
 
@@ -1572,7 +1672,55 @@ cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, Vi
   const long long rows_nhwc = (long long)batch * y.H, rows_planar = rows_nhwc * y.C;
   const int fn = resolve_act(act, kActDepthwise);
   const bool known = fn == kFnNone || fn == kFnSilu || fn == kFnRelu || fn == kFnHswishB || fn == kFnHsigmoid;
-  if (vec && known && rows_nhwc < (1LL << 31) && (long long)y.W * (y.C / 8) < (1LL << 30)) {
+  auto make_div = [](uint32_t dv) {
+    DwDiv d{0u, 0u};
+    uint32_t sh = 0;
+    while ((1ull << sh) < dv) ++sh;
+    d.s = sh;
+    d.m = (uint32_t)(((1ull << (31 + sh)) / dv) + 1ull);
+    return d;
+  };
+  const int strips = (y.W + 3) / 4;
+  const long long strip_items = rows_nhwc * strips * (y.C / 8);
+  // strips when they still fill the GPU twice over (at small batch the
+  // one-pixel-per-thread rows kernel below has the shorter critical path)
+  if (vec && known && (K == 3 || K == 5) && (S == 1 || S == 2) && strip_items < (1LL << 31) &&
+      strip_items >= 148LL * 512) {
+    const int C8 = y.C / 8;
+    const DwDiv di = make_div((uint32_t)(strips * C8)), dc = make_div((uint32_t)C8), dh = make_div((uint32_t)y.H);
+    const unsigned blocks = (unsigned)std::min<long long>((strip_items + 255) / 256, 148LL * 64);
+#define IVB_DW_STRIP(F, KK, SS) \
+  launch_kernel(depthwise_nhwc8_strip_k<F, KK, SS>, dim3(blocks), dim3(256), 0, st, x, w, bias, y, strip_items, P, C8, strips, di, dc, dh)
+#define IVB_DW_STRIP_KS(F)                                   \
+  do {                                                       \
+    if (K == 3 && S == 1) IVB_DW_STRIP(F, 3, 1);             \
+    else if (K == 3) IVB_DW_STRIP(F, 3, 2);                  \
+    else if (S == 1) IVB_DW_STRIP(F, 5, 1);                  \
+    else IVB_DW_STRIP(F, 5, 2);                              \
+  } while (0)
+    switch (fn) {
+      case kFnSilu: IVB_DW_STRIP_KS(kFnSilu); break;
+      case kFnRelu: IVB_DW_STRIP_KS(kFnRelu); break;
+      case kFnHswishB: IVB_DW_STRIP_KS(kFnHswishB); break;
+      case kFnHsigmoid: IVB_DW_STRIP_KS(kFnHsigmoid); break;
+      default: IVB_DW_STRIP_KS(kFnNone); break;
+    }
+#undef IVB_DW_STRIP_KS
+#undef IVB_DW_STRIP
+  } else if (!vec && known && rows_planar * y.W < (1LL << 31)) {
+    const long long n = rows_planar * y.W;
+    const DwDiv dhw = make_div((uint32_t)(y.H * y.W)), dwo = make_div((uint32_t)y.W), dcc = make_div((uint32_t)y.C);
+    const unsigned blocks = (unsigned)std::min<long long>((n + 255) / 256, 148LL * 64);
+#define IVB_DW_PFLAT(F) launch_kernel(depthwise_planar_flat_k<F>, dim3(blocks), dim3(256), 0, st, x, w, bias, y, n, K, S, P, dhw, dwo, dcc)
+    switch (fn) {
+      case kFnSilu: IVB_DW_PFLAT(kFnSilu); break;
+      case kFnRelu: IVB_DW_PFLAT(kFnRelu); break;
+      case kFnHswishB: IVB_DW_PFLAT(kFnHswishB); break;
+      case kFnHsigmoid: IVB_DW_PFLAT(kFnHsigmoid); break;
+      default: IVB_DW_PFLAT(kFnNone); break;
+    }
+#undef IVB_DW_PFLAT
+  } else if (vec && known && rows_nhwc < (1LL << 31) && (long long)y.W * (y.C / 8) < (1LL << 30)) {
     // one block row per output row; blocks of 256 threads over its (ox, 8-channel) positions
     const int per_row = y.W * (y.C / 8);
     DwDiv d{0u, 0u};
