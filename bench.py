@@ -293,6 +293,9 @@ def run_kernels_only(args, local: int) -> int:
     n_dets = None
     if args.decode:  # pose decode + NMS of the last replay's output, inside the profiled range
         n_dets = [len(d) for d in m.decodePose(args.batch)]
+    if args.frames:  # one ivc_infer_bgr_u8 pass over 1280x720 BGR frames (device letterbox), in the range
+        fr = np.random.default_rng(SEED + 100).integers(0, 256, (args.batch, 720, 1280, 3), dtype=np.uint8)
+        m.inferBgr(fr, [np.empty(args.batch * m.outputNumel(0), dtype=np.float32)])
     if cu is not None:
         cu.cuProfilerStop()
     print(json.dumps({"mode": "kernels", "workload": args.workload, "batch": args.batch,
@@ -527,6 +530,8 @@ def main() -> int:
                     help="full: the headline bench line; kernels: graph replays only (for launch lists and ncu); "
                          "model: latency / throughput of --workload (any emitted model); sweep: the config-2 op sweep")
     ap.add_argument("--layers", action="store_true", help="model mode: also one JSON line per step")
+    ap.add_argument("--frames", action="store_true",
+                    help="kernels mode: also one pass from 8-bit BGR frames (device letterbox) in the profiled range")
     ap.add_argument("--decode", action="store_true", help="kernels mode: also run the device pose decode + NMS")
     ap.add_argument("--min-replays", type=int, default=200,
                     help="device-resident timing: each step repeats the graph replay so that at least this many "
