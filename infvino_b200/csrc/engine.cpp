@@ -1360,12 +1360,18 @@ void Engine::lower() {
         if (!conv_geom(c, 1, &g1)) throw std::runtime_error("CudaPlanModel: conv tile does not fit shared memory");
       }
       // Layouts the load-time tuning chooses between (the first is the
-      // untuned pick): a halo conv split over N tiles also keeps the one-box-
-      // per-tap layout, which is faster where the halo tiles cover the image
-      // poorly.  Both read the same packed weights (same K order, the larger
-      // N padding).
+      // untuned pick).  All of them accumulate every output in the same K
+      // order, so the choice changes no bit, and all read the same packed
+      // weights (the largest N padding among them):
+      // - a halo conv split over N tiles also keeps the one-box-per-tap
+      //   layout, faster where halo tiles cover the image poorly; with one
+      //   channel chunk only, where the two walks share the K order (halo
+      //   tiles go chunk by chunk, boxes per tap tap by tap);
+      // - the N tile split in two or four, for launches with few M tiles
+      //   (batch 1, the SE blocks' one-pixel convs), where more CTAs each
+      //   stream less of the weights.
       std::vector<ConvCfg> modes{c};
-      if (c.halo && c.n_tiles > 1) {
+      if (c.halo && c.n_tiles > 1 && c.chunks[0] == 1) {
         ConvCfg t = c;
         t.halo = 0;
         t.kern_kb = t.num_kb;
@@ -1375,6 +1381,15 @@ void Engine::lower() {
         ConvGeom gt;
         if (conv_geom(t, 1, &gt)) modes.push_back(t);
       }
+      if (c.n_tiles == 1 && np16 >= 64)
+        for (int sp = 2; sp <= 4; sp *= 2) {
+          ConvCfg t = c;
+          t.BN = (int)round_up((np16 + sp - 1) / sp, 16);
+          t.n_tiles = (np16 + t.BN - 1) / t.BN;
+          t.Np = t.BN * t.n_tiles;
+          ConvGeom gt;
+          if (t.n_tiles > 1 && conv_geom(t, 1, &gt)) modes.push_back(t);
+        }
       int np_alloc = 0;
       for (const ConvCfg &m : modes) np_alloc = std::max(np_alloc, m.Np);
       // ---- weight repack: Wp[Np][Kp], K order (source, tap, chunk, channel)
@@ -1572,7 +1587,7 @@ void Engine::lower() {
         std::vector<ConvCand> cands;
         for (size_t mi = 0; mi < modes.size(); ++mi) {
           std::vector<ConvCand> cm = conv_candidates(modes[mi], B, sms);
-          const size_t keep = modes.size() == 1 ? cm.size() : (size_t)kConvTuneCands / modes.size();
+          const size_t keep = mi > 0 ? 2 : modes.size() == 1 ? (size_t)kConvTuneCands : (size_t)kConvTuneCands - 4;
           for (size_t k = 0; k < cm.size() && k < keep; ++k) {
             cm[k].mode = (int)mi;
             cands.push_back(cm[k]);
@@ -1584,7 +1599,7 @@ void Engine::lower() {
         bool have = false;
         cudaEvent_t e0 = nullptr, e1 = nullptr;
         if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) return;
-        for (size_t k = 0; k < cands.size() && k < (size_t)kConvTuneCands; ++k) {
+        for (size_t k = 0; k < cands.size(); ++k) {
           ConvTcArgs a;
           try {
             a = (*build)(B, cands[k]);
