@@ -1526,6 +1526,11 @@ void Engine::lower() {
                      (reinterpret_cast<uintptr_t>(ov.ptr) & 15) == 0)
                         ? 1
                         : 0;
+        a.out_dense = (c.ksize == 1 && ov.sc == 1 && ov.sy == (long long)ov.W * ov.sx &&
+                       ov.sb == (long long)ov.H * ov.sy)
+                          ? 1
+                          : 0;
+        a.epi_fast = (a.out_vec && c.res < 0 && c.BN * c.n_tiles == c.cout) ? 1 : 0;
         if (c.res >= 0) {
           const View4 rv = view(c.res);
           a.res = rv.ptr;

@@ -65,7 +65,10 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, FastDiv f) {
 // its quarter splits the accumulator columns in 8-column chunks.  Every field
 // of the parameter block is read once, before the tile loop: inside the loop
 // the global stores and the barrier asm would otherwise force reloads.
-template <int FN>
+// FAST (the common case, `epi_fast`): vector stores of whole 8-channel chunks,
+// no residual, no padded N columns, so the chunk loop carries no per-chunk
+// tests; with a dense channels-last 1x1 output a pixel's offset is p * o_sx.
+template <int FN, bool FAST>
 __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int lane, uint32_t tmem_base,
                                               uint64_t *accf_bar, uint64_t *acce_bar, volatile int *abort_sh,
                                               volatile int *epi_go, const uint4 *bias_sh) {
@@ -100,6 +103,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
   const long long o_sb = a.o_sb, o_sc = a.o_sc, o_sy = a.o_sy, o_sx = a.o_sx;
   const long long r_sb = a.r_sb, r_sc = a.r_sc, r_sy = a.r_sy, r_sx = a.r_sx;
   const bool out_vec = a.out_vec != 0, res_vec = a.res_vec != 0, has_res = res != nullptr;
+  const bool out_dense = a.out_dense != 0;
   const bool bias_in_smem = (n_tiles == 1 || a.resident_b != 0) && bias != nullptr;  // one N tile per CTA
   int *status = a.status;
   const long long wait_limit = a.wait_limit;
@@ -155,11 +159,16 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
       if (ksize == 1) {
         const uint32_t p = ((uint32_t)mt * (uint32_t)mb + (uint32_t)j) * 128u + (uint32_t)row;
         valid = p < m_total;
-        const uint32_t bimg = valid ? fdiv(p, fd_hw) : 0u;
-        const uint32_t r2 = valid ? p - bimg * hw : 0u;
-        const uint32_t oy = fdiv(r2, fd_wo), ox = r2 - oy * (uint32_t)Wo;
-        obase = (long long)bimg * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
-        rbase = (long long)bimg * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
+        if (FAST && out_dense) {
+          obase = valid ? (long long)p * o_sx : 0;
+          rbase = 0;
+        } else {
+          const uint32_t bimg = valid ? fdiv(p, fd_hw) : 0u;
+          const uint32_t r2 = valid ? p - bimg * hw : 0u;
+          const uint32_t oy = fdiv(r2, fd_wo), ox = r2 - oy * (uint32_t)Wo;
+          obase = (long long)bimg * o_sb + (long long)oy * o_sy + (long long)ox * o_sx;
+          rbase = (long long)bimg * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
+        }
       } else {
         const int b = (int)fdiv((uint32_t)mt, fd_tpi);
         const int rem = mt - b * tiles_per_img;
@@ -170,6 +179,29 @@ __device__ __forceinline__ void epilogue_role(const ConvTcArgs &a, int warp, int
         rbase = (long long)b * r_sb + (long long)oy * r_sy + (long long)ox * r_sx;
       }
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (buf * (uint32_t)mb + (uint32_t)j) * (uint32_t)BN;
+      if (FAST) {
+        __half *const orow = out + obase + n0;
+        for (int c0 = sub * 8; c0 < BN; c0 += 16 * kq) {
+          const int c1 = c0 + 8 * kq;
+          const bool two = c1 < BN;  // warp-uniform
+          uint32_t r[2][8];
+          tmem_ld8(taddr + (uint32_t)c0, r[0]);
+          if (two) tmem_ld8(taddr + (uint32_t)c1, r[1]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) asm volatile("" : "+r"(r[h][k]));  // uses stay after the wait
+          }
+          const uint4 p0 = epilogue8<FN>(r[0], load_bias8(c0));
+          if (valid) *reinterpret_cast<uint4 *>(orow + c0) = p0;
+          if (two) {
+            const uint4 p1 = epilogue8<FN>(r[1], load_bias8(c1));
+            if (valid) *reinterpret_cast<uint4 *>(orow + c1) = p1;
+          }
+        }
+        continue;
+      }
       // two chunks per TMEM wait: c0 and c0 + 8 * kq
       for (int c0 = sub * 8; c0 < BN; c0 += 16 * kq) {
         const int c1 = c0 + 8 * kq;
@@ -562,14 +594,18 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
   } else {
     // -------------------------------------------------------------- epilogue
+#define IVB_EPI(F)                                                                                    \
+  (a.epi_fast ? epilogue_role<F, true>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh) \
+              : epilogue_role<F, false>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh))
     switch (a.act_fn) {
-      case kFnSilu: epilogue_role<kFnSilu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
-      case kFnRelu: epilogue_role<kFnRelu>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
-      case kFnHswishA: epilogue_role<kFnHswishA>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
-      case kFnHsigmoid: epilogue_role<kFnHsigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
-      case kFnSigmoid: epilogue_role<kFnSigmoid>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
-      default: epilogue_role<kFnNone>(a, warp, lane, tmem_base, accf_bar, acce_bar, &abort_sh, epi_go, bias_sh); break;
+      case kFnSilu: IVB_EPI(kFnSilu); break;
+      case kFnRelu: IVB_EPI(kFnRelu); break;
+      case kFnHswishA: IVB_EPI(kFnHswishA); break;
+      case kFnHsigmoid: IVB_EPI(kFnHsigmoid); break;
+      case kFnSigmoid: IVB_EPI(kFnSigmoid); break;
+      default: IVB_EPI(kFnNone); break;
     }
+#undef IVB_EPI
   }
 
   tc_fence_before();

@@ -65,6 +65,8 @@ struct alignas(64) ConvTcArgs {
   __half *out;
   long long o_sb, o_sc, o_sy, o_sx;
   int out_vec;                    // NHWC-contiguous channels, 16B aligned
+  int out_dense;                  // 1x1: dense channels-last output (pixel p at p * o_sx)
+  int epi_fast;                   // out_vec, no residual, no padded N columns: the plain epilogue
   const __half *res;
   long long r_sb, r_sc, r_sy, r_sx;
   int res_vec;
