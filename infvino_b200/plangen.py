@@ -618,6 +618,19 @@ def op_gap(out_dir: str, c: int, h: int, w: int, seed: int = 7) -> str:
     return pw.save(out_dir)
 
 
+def op_se(out_dir: str, c: int, h: int, w: int, seed: int = 7) -> str:
+    """conv1x1 -> MobileNetV3's squeeze-excitation: global pool, fc1 (ReLU) and
+    fc2 (HardSigmoid) as one-pixel 1x1 convs, channel-wise multiply."""
+    pw = PlanWriter(seed)
+    x = pw.input("x", [1, c, h, w])
+    x = pw.conv(x, c, 1, act=1, name="pre")
+    g = pw.gap(x)
+    g = pw.conv(g, _make_divisible(c // 4, 8), 1, act=2, name="op.fc1")
+    g = pw.conv(g, c, 1, act=4, name="op.fc2")
+    pw.output(pw.add(g, x, 2, name="op.mul"))
+    return pw.save(out_dir)
+
+
 def op_attention(out_dir: str, c: int, h: int, w: int, heads: int = 0, seed: int = 7) -> str:
     """conv1x1 -> the position-sensitive attention block of YOLO11's C2PSA
     (qkv conv, slices, transposing permutes, two bmm, scale, softmax, pe

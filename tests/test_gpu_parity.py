@@ -201,6 +201,18 @@ def test_gap_reference_order(plan_dir, c, hw, batch):
     m.close()
 
 
+# MobileNetV3-small's squeeze-excitation blocks (channels, squeeze width, plane)
+@pytest.mark.parametrize("c,hw,batch", [(16, 56, 3), (96, 14, 2), (576, 7, 4), (240, 14, 1)])
+def test_se_block(plan_dir, c, hw, batch):
+    """Pool, the one-pixel fc1 / fc2 convs on the tensor cores (M = the batch)
+    and the broadcast multiply match the oracle."""
+    p = plangen.op_se(os.path.join(plan_dir, f"se_{c}_{hw}"), c, hw, hw)
+    m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
+    fams = [st["family"] for st in m.steps()]
+    assert fams == ["conv_direct", "gap", "conv1x1_tc", "conv1x1_tc", "ew_binary"], fams
+    check_op(p, batch)
+
+
 # YOLO11's C2PSA attention at its P5 size (20x20, 2 heads), one head, and
 # sizes that leave partial 64 x 64 product tiles and K slices
 @pytest.mark.parametrize("c,hw,heads,batch", [(128, 20, 2, 2), (64, 12, 1, 3), (128, 7, 2, 1), (64, 9, 2, 4)])
