@@ -13,8 +13,8 @@ prints ONE JSON line.
            stream, max over ranks.
   e2e    : the same metric through the public C ABI call `ivc_infer_f32`
            (ClBackend::infer): pinned host f32 input -> H2D (batches of 32 or
-           more: half the images cast to fp16 on the host first, with the
-           reference's truncation) -> network -> f32 outputs D2H into pinned
+           more: five eighths of the images cast to fp16 on the host first,
+           with the reference's truncation) -> network -> f32 outputs D2H into pinned
            host memory, every step, all inside the timed region.
   roofline: the dominant kernel (the tcgen05 implicit-GEMM convolution) from a
            per-launch CUDA-event profile: algorithmic bytes / launch time vs the
@@ -121,9 +121,9 @@ def make_plan(rank: int, workload: str = MODEL) -> str:
 
 def h2d_bytes(B: int, n_in: int) -> int:
     """Input bytes `ivc_infer_f32` copies per call: batches of 32 or more cast
-    the first half (rounded down to a multiple of 4 images) to fp16 on the host
-    and copy the rest as f32; smaller batches copy f32."""
-    n16 = B // 2 // 4 * 4 if B >= 32 else 0
+    the first five eighths (rounded down to a multiple of 4 images) to fp16 on
+    the host and copy the rest as f32; smaller batches copy f32."""
+    n16 = B * 5 // 8 // 4 * 4 if B >= 32 else 0
     return n16 * n_in * 2 + (B - n16) * n_in * 4
 
 

@@ -2362,12 +2362,14 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   // Split: images [0, n16) are cast on the host and cross as fp16, images
   // [n16, batch) cross as f32 first (no host work, so the link starts at once)
   // and are cast on the device.  A host cast moves 8 bytes of host memory per
-  // element (f32 read, fp16 write, fp16 read by the copy) against 4 for an
-  // f32 copy, so on a host whose memory bandwidth the copy engines already
-  // share, casting everything on the host is slower than casting nothing; half
-  // the batch (a multiple of 4, so that chunks take sizes 16, 8, 4, 2 or 1,
-  // each with its graph captured once) was the fastest split measured.
-  const int n16 = batch / 2 / 4 * 4;
+  // element (f32 read, fp16 write with streaming stores, fp16 read by the
+  // copy) against 4 for an f32 copy, so on a host whose memory bandwidth the
+  // copy engines already share, casting everything on the host is slower
+  // than casting nothing; five eighths of the batch (a multiple of 4, so that
+  // chunks take sizes 16, 8, 4, 2 or 1, each with its graph captured once)
+  // was the fastest split measured (b=64: 5.9 ms against 6.1 ms for half and
+  // 6.8 ms for all).
+  const int n16 = batch * 5 / 8 / 4 * 4;
   // the fp16 images [0, n16) travel into the front of the f32 staging (2 bytes
   // per element), the f32 images [n16, batch) into their own place (4 bytes)
   uint16_t *in_f16_dev = reinterpret_cast<uint16_t *>(in_f32_);

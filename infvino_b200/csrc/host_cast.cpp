@@ -49,13 +49,25 @@ __attribute__((target("avx2"))) __m256i trunc8(__m256i x) {
 }
 
 __attribute__((target("avx2"))) void span_avx2(const float *in, uint16_t *out, size_t n) {
+  // Streaming (non-temporal) stores from the first 32-byte boundary on: the
+  // fp16 output is read next by the copy engine, not by this core, and a
+  // streaming store skips the read-for-ownership of each destination line,
+  // which takes a third of the host memory traffic off the cast.
   size_t i = 0;
+  const size_t head = std::min(n, (size_t)(((32u - (reinterpret_cast<uintptr_t>(out) & 31u)) & 31u) / 2u));
+  span_scalar(in, out, head);
+  i = head;
+  const bool aligned = (reinterpret_cast<uintptr_t>(out + i) & 31u) == 0;
   for (; i + 16 <= n; i += 16) {
     const __m256i a = trunc8(_mm256_loadu_si256(reinterpret_cast<const __m256i *>(in + i)));
     const __m256i b = trunc8(_mm256_loadu_si256(reinterpret_cast<const __m256i *>(in + i + 8)));
     const __m256i p = _mm256_permute4x64_epi64(_mm256_packus_epi32(a, b), 0xd8);  // 0, 2, 1, 3
-    _mm256_storeu_si256(reinterpret_cast<__m256i *>(out + i), p);
+    if (aligned)
+      _mm256_stream_si256(reinterpret_cast<__m256i *>(out + i), p);
+    else
+      _mm256_storeu_si256(reinterpret_cast<__m256i *>(out + i), p);
   }
+  _mm_sfence();  // the streamed lines reach memory before the copy that reads them is queued
   span_scalar(in + i, out + i, n - i);
 }
 

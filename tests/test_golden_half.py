@@ -105,3 +105,21 @@ def test_product_host_cast_large_and_concurrent():
     for t in threads:
         t.join()
     assert not errors and all(results.get(k) for k in range(6)), (errors, results)
+
+
+def test_product_host_cast_any_destination_alignment():
+    """The host cast streams its stores from the first 32-byte boundary of the
+    destination on (scalar head before it): every start offset inside a line,
+    short and long spans, give the reference's truncation bit for bit."""
+    from infvino_b200 import _native
+    L = _native.lib()
+    rng = np.random.default_rng(43)
+    x = rng.integers(0, 1 << 32, size=300000, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    want = ivref.f32_to_f16_trunc(x)
+    buf = np.zeros(x.size + 64, dtype=np.uint16)
+    for off in range(0, 17):
+        for n in (1, 7, 16, 33, 100, 299000):
+            dst = buf[off:off + n]
+            dst[:] = 0xFFFF
+            L.ivc_f32_to_f16(x.ctypes.data, dst.ctypes.data, n)
+            assert np.array_equal(dst, want[:n]), (off, n)
