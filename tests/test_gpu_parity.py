@@ -343,7 +343,7 @@ def test_yolov8n_pose(model_plans, batch):
     m.close()
 
 
-@pytest.mark.parametrize("seed", [11, 13, 17])
+@pytest.mark.parametrize("seed", [11, 13, 17, 19, 23, 29, 31, 37])
 def test_yolov8n_pose_nms_identical(plan_dir, seed):
     """Random-init class scores are all ~sigmoid(0.01) ~ 0.5 (ties everywhere,
     300 detections cut by max_det), so the NMS set is checked on a variant whose
@@ -357,6 +357,13 @@ def test_yolov8n_pose_nms_identical(plan_dir, seed):
     ref = ivref.f16_to_f32(o.read_f16("output0")).reshape(56, 8400)
     n_und = decode_check(got, ref)
     assert n_und <= 4, n_und
+    sets = [{a for a, *_ in decode.pose_decode(v)} for v in (got, ref)]
+    path = os.environ.get("IVB_PARITY_REPORT")
+    if path:  # the achieved agreement, for the record
+        import json
+        with open(path, "a") as f:
+            f.write(json.dumps({"test": "nms_identical", "seed": seed, "identical": sets[0] == sets[1],
+                                "detections": len(sets[1]), "undecided": n_und}) + "\n")
     m.close()
 
 
