@@ -13,6 +13,7 @@
 #include "host_cast.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <functional>
 #include <cstring>
@@ -2367,9 +2368,24 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   // copy engines already share, casting everything on the host is slower
   // than casting nothing; five eighths of the batch (a multiple of 4, so that
   // chunks take sizes 16, 8, 4, 2 or 1, each with its graph captured once)
-  // was the fastest split measured (b=64: 5.9 ms against 6.1 ms for half and
-  // 6.8 ms for all).
-  const int n16 = batch * 5 / 8 / 4 * 4;
+  // was the fastest split measured alone on one GPU (b=64: 5.9 ms against
+  // 6.1 ms for half and 6.8 ms for all).  Where several processes share the
+  // host (one per GPU) its memory bandwidth per process shrinks and less host
+  // casting pays, so the split is tuned per batch size on the first calls:
+  // the first (graph captures) runs at 5/8, the next ten try 0, 2, 4, 5 and 6
+  // eighths twice each (wall time of the whole call), then the fastest stays.
+  // Every split gives the same bits (host and device casts are the same
+  // truncation).
+  SplitTune &tune = split_tune_[batch];
+  static constexpr int kSplitEighths[5] = {0, 2, 4, 5, 6};
+  int eighths = 5;
+  const int round = tune.calls - 1;
+  if (tune.best >= 0)
+    eighths = kSplitEighths[tune.best];
+  else if (round >= 0 && round < 10)
+    eighths = kSplitEighths[round % 5];
+  const int n16 = batch * eighths / 8 / 4 * 4;
+  const auto call_t0 = std::chrono::steady_clock::now();
   // the fp16 images [0, n16) travel into the front of the f32 staging (2 bytes
   // per element), the f32 images [n16, batch) into their own place (4 bytes)
   uint16_t *in_f16_dev = reinterpret_cast<uint16_t *>(in_f32_);
@@ -2452,6 +2468,19 @@ void Engine::infer_f32_host(const float *src, int batch, float *const *outs) {
   check(cudaStreamWaitEvent(stream_, chunk_events_[3 * n_chunks], 0), "cudaStreamWaitEvent");
   synchronize();
   last_f32_batch_ = batch;  // the whole batch's outputs are in the f32 staging
+  if (tune.best < 0) {
+    const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - call_t0).count();
+    if (round >= 0 && round < 10) {
+      const int k = round % 5;
+      tune.ms[k] = tune.ms[k] > 0.0 ? std::min(tune.ms[k], ms) : ms;
+    }
+    if (++tune.calls > 10) {
+      int b = 3;  // 5/8 unless another split measured faster
+      for (int k = 0; k < 5; ++k)
+        if (tune.ms[k] > 0.0 && tune.ms[k] < tune.ms[b]) b = k;
+      tune.best = b;
+    }
+  }
 }
 
 void Engine::infer_f32_host_staged(const float *src, int batch, float *const *outs) {

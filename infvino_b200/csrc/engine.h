@@ -222,6 +222,12 @@ class Engine {
   float *in_f32_ = nullptr;         // device staging for f32 input
   float *out_f32_ = nullptr;        // device staging for f32 outputs (pipelined infer)
   uint16_t *in_f16_host_ = nullptr; // pinned fp16 input, two chunks (pipelined infer)
+  struct SplitTune {                // host/device cast split of infer_f32, per batch size
+    int calls = 0;                  // calls so far
+    int best = -1;                  // index of the chosen split, once tuned
+    double ms[5] = {0, 0, 0, 0, 0}; // fastest call per candidate split
+  };
+  std::map<int, SplitTune> split_tune_;
   float *out_host_ = nullptr;       // pinned f32 outputs, two chunks (pageable callers)
   int last_f32_batch_ = 0;          // images of the last chunked infer whose outputs are all in out_f32_
   // device preprocessing: OpenCV coordinate tables of the last frame size, frame staging

@@ -539,6 +539,26 @@ def test_infer_f32_chunked_equals_device_path(model_plans):
     m.close()
 
 
+def test_infer_f32_split_tuning_changes_no_bit(model_plans):
+    """The first calls of ivc_infer_f32 at a batch of 32 or more try five
+    host / device cast splits; every call returns the same bits."""
+    import torch
+    p = model_plans["yolov8n-pose"]
+    m = ivb.PlanModel(p, device=0, max_batch=32)
+    n = m.inputNumel()
+    x = torch.empty(32 * n, dtype=torch.float32, pin_memory=True)
+    x.numpy()[:] = np.random.default_rng(41).random(32 * n, dtype=np.float32)
+    y = torch.empty(32 * m.outputNumel(0), dtype=torch.float32, pin_memory=True)
+    ref = None
+    for _ in range(13):
+        m.infer_f32(x.numpy(), 32, [y.numpy()])
+        if ref is None:
+            ref = y.numpy().copy()
+        else:
+            assert np.array_equal(y.numpy(), ref)
+    m.close()
+
+
 @pytest.mark.parametrize("batch", [1, 3, 40])
 def test_infer_f32_pinned_and_pageable_agree(model_plans, batch):
     """ClBackend::infer from page-locked buffers (copied directly, half the
