@@ -657,6 +657,137 @@ __global__ void __launch_bounds__(256) depthwise_planar_flat_k(View4 x, const __
   }
 }
 
+// Planar depthwise over small planes (H * W <= 512, e.g. the 20 x 20 maps of
+// YOLO11's attention): a block stages 16 whole input planes in shared memory
+// with coalesced loads, and 16 threads per plane, each holding the plane's
+// K*K weights in registers, compute its outputs from shared memory.  Same
+// arithmetic as the kernels above (taps in (ky, kx) order, out-of-image taps
+// skipped, one fused multiply-add each).
+constexpr int kDwPlanesPerBlock = 16, kDwPlaneMax = 512;
+template <int FN, int K, int S>
+__global__ void __launch_bounds__(256) depthwise_planar_plane_k(View4 x, const __half *__restrict__ w,
+                                                               const __half *__restrict__ bias, View4 y, int planes,
+                                                               int P, int dense, DwDiv d_hw, DwDiv d_w, DwDiv d_wo,
+                                                               DwDiv d_c) {
+  pdl_wait_and_release();
+  __shared__ __align__(16) __half xs[kDwPlanesPerBlock * kDwPlaneMax];
+  const int H = x.H, W = x.W, HW = H * W, Ho = y.H, Wo = y.W, HWo = Ho * Wo, C = y.C;
+  const int p0 = blockIdx.x * kDwPlanesPerBlock;
+  const int np = min(kDwPlanesPerBlock, planes - p0);
+  if (dense) {
+    // the block's planes are one contiguous, 16-byte aligned run of np * HW
+    // halves (planes packed, C a multiple of 16): 16-byte loads, all issued
+    // before the first store; plane q lands at q * HW
+    const uint32_t b0 = dw_div((uint32_t)p0, d_c), c0 = (uint32_t)p0 - b0 * (uint32_t)C;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x.ptr + (long long)b0 * x.sb + (long long)c0 * x.sc);
+    uint4 *dst = reinterpret_cast<uint4 *>(xs);
+    const int n16 = np * HW / 8;
+    constexpr int kLd = 4;
+    for (int e0 = threadIdx.x; e0 < n16; e0 += kLd * (int)blockDim.x) {
+      uint4 v[kLd];
+#pragma unroll
+      for (int j = 0; j < kLd; ++j)
+        if (e0 + j * (int)blockDim.x < n16) v[j] = __ldg(src + e0 + j * (int)blockDim.x);
+#pragma unroll
+      for (int j = 0; j < kLd; ++j)
+        if (e0 + j * (int)blockDim.x < n16) dst[e0 + j * (int)blockDim.x] = v[j];
+    }
+  } else {
+    constexpr int kLd = 8;  // loads in flight per thread before their stores
+    for (int e0 = threadIdx.x; e0 < np * HW; e0 += kLd * (int)blockDim.x) {
+      __half v[kLd];
+#pragma unroll
+      for (int j = 0; j < kLd; ++j) {
+        const int e = e0 + j * (int)blockDim.x;
+        if (e >= np * HW) break;
+        const uint32_t q = dw_div((uint32_t)e, d_hw), r = (uint32_t)e - q * (uint32_t)HW;
+        const uint32_t yy = dw_div(r, d_w), xx = r - yy * (uint32_t)W;
+        const uint32_t pl = (uint32_t)p0 + q, b = dw_div(pl, d_c), c = pl - b * (uint32_t)C;
+        v[j] = x.ptr[(long long)b * x.sb + (long long)c * x.sc + (long long)yy * x.sy + (long long)xx * x.sx];
+      }
+#pragma unroll
+      for (int j = 0; j < kLd; ++j) {
+        const int e = e0 + j * (int)blockDim.x;
+        if (e >= np * HW) break;
+        xs[e] = v[j];  // plane q at q * HW
+      }
+    }
+  }
+  __syncthreads();
+  const int q = threadIdx.x >> 4, sub = threadIdx.x & 15;  // plane of this thread, its place among 16
+  if (q >= np) return;
+  const uint32_t pl = (uint32_t)(p0 + q), b = dw_div(pl, d_c), c = pl - b * (uint32_t)C;
+  float wv[K * K];
+#pragma unroll
+  for (int t = 0; t < K * K; ++t) wv[t] = __half2float(__ldg(w + t * C + (int)c));
+  const float bv = bias ? __half2float(bias[c]) : 0.0f;
+  const __half *xp = xs + q * HW;
+  __half *yp = y.ptr + (long long)b * y.sb + (long long)c * y.sc;
+  for (int r = sub; r < HWo; r += 16) {
+    const int oy = (int)dw_div((uint32_t)r, d_wo), ox = r - oy * Wo;
+    float acc = 0.0f;
+#pragma unroll
+    for (int ky = 0; ky < K; ++ky) {
+      const int iy = oy * S - P + ky;
+      if (iy < 0 || iy >= H) continue;
+#pragma unroll
+      for (int kx = 0; kx < K; ++kx) {
+        const int ix = ox * S - P + kx;
+        if (ix < 0 || ix >= W) continue;
+        acc += __half2float(xp[iy * W + ix]) * wv[ky * K + kx];
+      }
+    }
+    yp[(long long)oy * y.sy + (long long)ox * y.sx] = dw_epilogue<FN>(acc, bv);
+  }
+}
+
+// Planar depthwise, four neighbouring outputs of one row per thread: each
+// input row segment is loaded once for the four, the K*K weights once per
+// thread.  Same arithmetic as the kernels above: taps in (ky, kx) order, one
+// fused multiply-add each; an out-of-image tap reads 0, which leaves the sum
+// unchanged (it never holds -0), so it equals skipping the tap.
+template <int FN, int K, int S>
+__global__ void __launch_bounds__(256) depthwise_planar_strip_k(View4 x, const __half *__restrict__ w,
+                                                               const __half *__restrict__ bias, View4 y,
+                                                               long long items, int P, int strips, DwDiv d_strips,
+                                                               DwDiv d_ho, DwDiv d_c) {
+  pdl_wait_and_release();
+  constexpr int IW = 3 * S + K;  // input columns under four outputs
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += (long long)gridDim.x * blockDim.x) {
+    const uint32_t row = dw_div((uint32_t)i, d_strips), sx = (uint32_t)i - row * (uint32_t)strips;
+    const uint32_t plane = dw_div(row, d_ho), oy = row - plane * (uint32_t)y.H;
+    const uint32_t b = dw_div(plane, d_c), c = plane - b * (uint32_t)y.C;
+    const int ox0 = (int)sx * 4, ix0 = ox0 * S - P;
+    const __half *xp = x.ptr + (long long)b * x.sb + (long long)c * x.sc;
+    float wv[K * K];
+#pragma unroll
+    for (int t = 0; t < K * K; ++t) wv[t] = __half2float(__ldg(w + t * y.C + c));
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int ky = 0; ky < K; ++ky) {
+      const int iy = (int)oy * S - P + ky;
+      const bool row_ok = iy >= 0 && iy < x.H;
+      const __half *xr = xp + (long long)(row_ok ? iy : 0) * x.sy;
+      float v[IW];
+#pragma unroll
+      for (int j = 0; j < IW; ++j) {
+        const int ix = ix0 + j;
+        v[j] = (row_ok && ix >= 0 && ix < x.W) ? __half2float(xr[(long long)ix * x.sx]) : 0.0f;
+      }
+#pragma unroll
+      for (int kx = 0; kx < K; ++kx) {
+#pragma unroll
+        for (int o = 0; o < 4; ++o) acc[o] += v[o * S + kx] * wv[ky * K + kx];
+      }
+    }
+    const float bv = bias ? __half2float(bias[c]) : 0.0f;
+    __half *yr = y.ptr + (long long)b * y.sb + (long long)c * y.sc + (long long)oy * y.sy;
+#pragma unroll
+    for (int o = 0; o < 4; ++o)
+      if (ox0 + o < y.W) yr[(long long)(ox0 + o) * y.sx] = dw_epilogue<FN>(acc[o], bv);
+  }
+}
+
 // Planar depthwise in plane rows: blockIdx.y is one (image, channel, output
 // row), threads run over the row's output columns (coalesced stores).
 template <int FN>
@@ -1085,11 +1216,15 @@ __global__ void resize_up_nhwc8_k(View4 x, View4 y, int S, unsigned row8, unsign
   }
 }
 
-// Chained KxK stride-1 max pools (pad P, out-of-image taps skipped), one block
-// per (8-channel group, image) with the plane in shared memory: level l pools
-// level l-1's result, like the separate pool nodes, as a row pass then a
-// column pass (max is exact, so the split changes no value), on packed halves.
+// Chained KxK stride-1 max pools (K = 2P + 1, pad P, out-of-image taps
+// skipped), one block per (8-channel group, image) with the plane in shared
+// memory: level l pools level l-1's result, like the separate pool nodes, as a
+// row pass then a column pass (max is exact, so the split changes no value),
+// on packed halves.  The block has a thread per pixel (up to 1024), and each
+// pass reads its 2P neighbours with independent loads, so a level costs two
+// shared-memory round trips and two barriers.
 constexpr int kPoolChainMax = 3;
+constexpr int kPoolChainMaxP = 3;
 struct PoolChainOut {
   View4 y[kPoolChainMax];
 };
@@ -1103,7 +1238,7 @@ __device__ __forceinline__ uint4 hmax8(uint4 a, uint4 b) {
   return r;
 }
 
-__global__ void maxpool_chain_nhwc8_k(View4 x, PoolChainOut outs, int levels, int P) {
+__global__ void __launch_bounds__(1024) maxpool_chain_nhwc8_k(View4 x, PoolChainOut outs, int levels, int P) {
   pdl_wait_and_release();
   extern __shared__ uint4 pool_sm[];
   const int H = x.H, W = x.W, HW = H * W;
@@ -1117,18 +1252,26 @@ __global__ void maxpool_chain_nhwc8_k(View4 x, PoolChainOut outs, int levels, in
   for (int l = 0; l < levels; ++l) {
     for (int p = threadIdx.x; p < HW; p += blockDim.x) {  // row pass A -> T
       const int yy = p / W, xx = p - yy * W;
-      const int x0 = max(0, xx - P), x1 = min(W - 1, xx + P);
-      uint4 m = A[yy * W + x0];
-      for (int q = x0 + 1; q <= x1; ++q) m = hmax8(m, A[yy * W + q]);
+      uint4 m = A[p];
+#pragma unroll
+      for (int d = 1; d <= kPoolChainMaxP; ++d) {
+        if (d > P) break;
+        if (xx - d >= 0) m = hmax8(m, A[p - d]);
+        if (xx + d < W) m = hmax8(m, A[p + d]);
+      }
       T[p] = m;
     }
     __syncthreads();
     const View4 &y = outs.y[l == 0 ? 0 : l == 1 ? 1 : 2];
     for (int p = threadIdx.x; p < HW; p += blockDim.x) {  // column pass T -> A, and out
       const int yy = p / W, xx = p - yy * W;
-      const int y0 = max(0, yy - P), y1 = min(H - 1, yy + P);
-      uint4 m = T[y0 * W + xx];
-      for (int q = y0 + 1; q <= y1; ++q) m = hmax8(m, T[q * W + xx]);
+      uint4 m = T[p];
+#pragma unroll
+      for (int d = 1; d <= kPoolChainMaxP; ++d) {
+        if (d > P) break;
+        if (yy - d >= 0) m = hmax8(m, T[p - d * W]);
+        if (yy + d < H) m = hmax8(m, T[p + d * W]);
+      }
       A[p] = m;
       *reinterpret_cast<uint4 *>(y.ptr + at8(y, b, yy, xx, c)) = m;
     }
@@ -1572,7 +1715,8 @@ cudaError_t launch_maxpool_v4(View4 x, View4 y, int batch, int K, int S, int P, 
 cudaError_t launch_maxpool_chain_v4(View4 x, const View4 *ys, int levels, int batch, int K, int P,
                                     cudaStream_t st) {
   if (levels < 1 || levels > kPoolChainMax) return cudaErrorInvalidValue;
-  bool fused = vec8_ok(x) && 2LL * x.H * x.W * 16 <= 48 * 1024 && batch <= 65535;
+  bool fused = vec8_ok(x) && 2LL * x.H * x.W * 16 <= 48 * 1024 && batch <= 65535 && K == 2 * P + 1 && P >= 0 &&
+               P <= kPoolChainMaxP;
   for (int l = 0; l < levels; ++l) fused = fused && vec8_ok(ys[l]) && ys[l].H == x.H && ys[l].W == x.W && ys[l].C == x.C;
   if (!fused) {  // one pool per level
     View4 src = x;
@@ -1586,7 +1730,8 @@ cudaError_t launch_maxpool_chain_v4(View4 x, const View4 *ys, int levels, int ba
   PoolChainOut outs{};
   for (int l = 0; l < levels; ++l) outs.y[l] = ys[l];
   const size_t smem = 2ull * (size_t)x.H * x.W * 16;
-  launch_kernel(maxpool_chain_nhwc8_k, dim3((unsigned)(x.C / 8), (unsigned)batch), dim3(128), smem, st, x, outs,
+  const int threads = (int)std::max<long long>(32, std::min<long long>(1024, ((long long)x.H * x.W + 31) / 32 * 32));
+  launch_kernel(maxpool_chain_nhwc8_k, dim3((unsigned)(x.C / 8), (unsigned)batch), dim3((unsigned)threads), smem, st, x, outs,
                 levels, P);
   return cudaGetLastError();
 }
@@ -1707,6 +1852,62 @@ cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, Vi
     }
 #undef IVB_DW_STRIP_KS
 #undef IVB_DW_STRIP
+  } else if (!vec && known && (K == 3 || K == 5) && (S == 1 || S == 2) && x.H * x.W >= 1 && y.H * y.W >= 1 &&
+             x.H * x.W <= kDwPlaneMax &&
+             (long long)batch * y.C < (1LL << 31) && (long long)batch * y.C >= 148LL * kDwPlanesPerBlock) {
+    // small planes staged whole in shared memory (while they fill the GPU)
+    const int planes = batch * y.C;
+    const DwDiv dhw = make_div((uint32_t)(x.H * x.W)), dw = make_div((uint32_t)x.W), dwo = make_div((uint32_t)y.W),
+                dcc = make_div((uint32_t)y.C);
+    const unsigned blocks = (unsigned)((planes + kDwPlanesPerBlock - 1) / kDwPlanesPerBlock);
+    // packed planes: every block's 16 planes are one aligned run of halves
+    const int dense = (x.sx == 1 && x.sy == x.W && x.sc == (long long)x.H * x.W && y.C % kDwPlanesPerBlock == 0 &&
+                       x.sb % 8 == 0 && (reinterpret_cast<uintptr_t>(x.ptr) & 15) == 0)
+                          ? 1
+                          : 0;
+#define IVB_DW_PLANE(F, KK, SS)                                                                                  \
+  launch_kernel(depthwise_planar_plane_k<F, KK, SS>, dim3(blocks), dim3(256), 0, st, x, w, bias, y, planes, P, dense, \
+                dhw, dw, dwo, dcc)
+#define IVB_DW_PLANE_KS(F)                                   \
+  do {                                                       \
+    if (K == 3 && S == 1) IVB_DW_PLANE(F, 3, 1);             \
+    else if (K == 3) IVB_DW_PLANE(F, 3, 2);                  \
+    else if (S == 1) IVB_DW_PLANE(F, 5, 1);                  \
+    else IVB_DW_PLANE(F, 5, 2);                              \
+  } while (0)
+    switch (fn) {
+      case kFnSilu: IVB_DW_PLANE_KS(kFnSilu); break;
+      case kFnRelu: IVB_DW_PLANE_KS(kFnRelu); break;
+      case kFnHswishB: IVB_DW_PLANE_KS(kFnHswishB); break;
+      case kFnHsigmoid: IVB_DW_PLANE_KS(kFnHsigmoid); break;
+      default: IVB_DW_PLANE_KS(kFnNone); break;
+    }
+#undef IVB_DW_PLANE_KS
+#undef IVB_DW_PLANE
+  } else if (!vec && known && (K == 3 || K == 5) && (S == 1 || S == 2) && rows_planar * strips < (1LL << 31) &&
+             rows_planar * strips >= 148LL * 256) {
+    // planar strips of four outputs (while they fill the GPU)
+    const long long items = rows_planar * strips;
+    const DwDiv ds = make_div((uint32_t)strips), dho = make_div((uint32_t)y.H), dcc = make_div((uint32_t)y.C);
+    const unsigned blocks = (unsigned)std::min<long long>((items + 255) / 256, 148LL * 64);
+#define IVB_DW_PSTRIP(F, KK, SS) \
+  launch_kernel(depthwise_planar_strip_k<F, KK, SS>, dim3(blocks), dim3(256), 0, st, x, w, bias, y, items, P, strips, ds, dho, dcc)
+#define IVB_DW_PSTRIP_KS(F)                                  \
+  do {                                                       \
+    if (K == 3 && S == 1) IVB_DW_PSTRIP(F, 3, 1);            \
+    else if (K == 3) IVB_DW_PSTRIP(F, 3, 2);                 \
+    else if (S == 1) IVB_DW_PSTRIP(F, 5, 1);                 \
+    else IVB_DW_PSTRIP(F, 5, 2);                             \
+  } while (0)
+    switch (fn) {
+      case kFnSilu: IVB_DW_PSTRIP_KS(kFnSilu); break;
+      case kFnRelu: IVB_DW_PSTRIP_KS(kFnRelu); break;
+      case kFnHswishB: IVB_DW_PSTRIP_KS(kFnHswishB); break;
+      case kFnHsigmoid: IVB_DW_PSTRIP_KS(kFnHsigmoid); break;
+      default: IVB_DW_PSTRIP_KS(kFnNone); break;
+    }
+#undef IVB_DW_PSTRIP_KS
+#undef IVB_DW_PSTRIP
   } else if (!vec && known && rows_planar * y.W < (1LL << 31)) {
     const long long n = rows_planar * y.W;
     const DwDiv dhw = make_div((uint32_t)(y.H * y.W)), dwo = make_div((uint32_t)y.W), dcc = make_div((uint32_t)y.C);

@@ -173,12 +173,25 @@ def test_conv_multiblock_tiles(plan_dir, cin, cout, hw, k, s, batch, res, boxes)
     m.close()
 
 
-@pytest.mark.parametrize("c,hw,levels,batch", [(128, 20, 3, 1), (128, 20, 3, 9), (64, 13, 2, 5), (32, 7, 3, 3)])
+# (a thread per pixel up to 1024 pixels; the 36x36 plane takes two per thread)
+@pytest.mark.parametrize("c,hw,levels,batch", [(128, 20, 3, 1), (128, 20, 3, 9), (64, 13, 2, 5), (32, 7, 3, 3),
+                                               (16, 32, 3, 2), (16, 36, 3, 2)])
 def test_sppf_pool_chain(plan_dir, c, hw, levels, batch):
     p = plangen.op_sppf(os.path.join(plan_dir, f"sppf_{c}_{hw}_{levels}"), c, hw, hw, levels)
     m = ivb.PlanModel(p, max_batch=1, flags=ivb.FLAG_DRY_RUN)
     assert [s["family"] for s in m.steps()].count("maxpool_chain") == 1
+    m.close()
     check_op(p, batch)
+    # max is exact: each level equals 5x5 max pools (out-of-image taps skipped)
+    # of this handle's own pool input, restated in numpy, value for value
+    o, m = run_both(p, batch)
+    cur = m.readTensor("pre.out", batch).view(np.float16).reshape(batch, c, hw, hw)
+    for lv in range(levels):
+        pad = np.pad(cur, ((0, 0), (0, 0), (2, 2), (2, 2)), constant_values=-np.inf)
+        cur = np.lib.stride_tricks.sliding_window_view(pad, (5, 5), axis=(2, 3)).max(axis=(4, 5))
+        got = m.readTensor(f"mp_{lv + 1}", batch).view(np.float16).reshape(batch, c, hw, hw)
+        assert np.array_equal(got, cur), lv
+    m.close()
 
 
 @pytest.mark.parametrize("c,hw,s,batch", [(128, 20, 2, 1), (256, 20, 2, 6), (64, 9, 3, 4)])
@@ -257,11 +270,13 @@ def test_depthwise(plan_dir, c, k, s, act):
 # BASELINE config 2's depthwise resolutions (112..7) with MobileNet's channel
 # counts; `producer` puts a 1x1 conv in front and one behind (channels-last
 # input and output, the 8-channel kernel), without them the depthwise reads
-# the planar plan input and writes the planar output
+# the planar plan input and writes the planar output (four-output strips for
+# all four K / S pairs, a partial last strip, and the one-output kernel)
 @pytest.mark.parametrize("c,k,s,hw,act,producer", [
     (16, 3, 2, 112, 2, True), (72, 3, 2, 56, 2, True), (96, 5, 2, 28, 3, True), (240, 5, 1, 14, 3, True),
     (576, 5, 1, 7, 3, True), (88, 3, 1, 56, 2, True), (16, 3, 1, 112, 1, False), (72, 5, 2, 28, 4, False),
-    (24, 3, 2, 7, 3, False)])
+    (24, 3, 2, 7, 3, False), (32, 3, 2, 112, 2, False), (40, 5, 1, 56, 3, False), (24, 5, 2, 112, 0, False),
+    (32, 3, 1, 50, 1, False)])
 def test_depthwise_resolutions(plan_dir, c, k, s, hw, act, producer):
     p = plangen.op_conv(os.path.join(plan_dir, f"dwr_{c}_{k}_{s}_{hw}_{int(producer)}"), c, c, hw, hw, k, s, act=act,
                         groups=c, producer=producer, consumer=producer)
@@ -269,6 +284,16 @@ def test_depthwise_resolutions(plan_dir, c, k, s, hw, act, producer):
     lay = {ln.split()[1]: " nhwc " in ln for ln in m.describe().splitlines() if ln.startswith("tensor")}
     assert lay["op.out"] == producer
     check_op(p, 3)
+
+
+# planar depthwise over planes of at most 512 pixels with enough planes to fill
+# the GPU: whole planes staged in shared memory, 16 per block (the last block
+# partial in the 120-channel cases)
+@pytest.mark.parametrize("c,k,s,hw,act,batch", [(128, 3, 1, 20, 0, 20), (120, 5, 2, 14, 3, 21), (96, 3, 2, 20, 2, 25),
+                                                (120, 5, 1, 7, 1, 21)])
+def test_depthwise_planar_small_planes(plan_dir, c, k, s, hw, act, batch):
+    p = plangen.op_conv(os.path.join(plan_dir, f"dwp_{c}_{k}_{s}_{hw}"), c, c, hw, hw, k, s, act=act, groups=c)
+    check_op(p, batch)
 
 
 def test_generic_grouped_conv(plan_dir):
