@@ -103,6 +103,26 @@ inline cudaError_t ensure_dynamic_smem(void (*kernel)(KArgs...), int bytes, std:
   return cudaSuccess;
 }
 
+// The shared-memory carveout (percent of the unified L1 / shared storage) a
+// kernel prefers, set once per device like the dynamic ceiling above: kernels
+// whose occupancy is bound by static shared memory ask for the largest.
+template <typename... KArgs>
+inline cudaError_t ensure_smem_carveout(void (*kernel)(KArgs...), int percent,
+                                        std::atomic<bool> (&done)[kAttrMaxDevices]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < kAttrMaxDevices;
+  if (tracked && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, percent);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return e;
+  }
+  if (tracked) done[dev].store(true, std::memory_order_release);
+  return cudaSuccess;
+}
+
 // ------------------------------------------------------------------ resolved activations
 // The (act code, kernel family) pair resolved on the host to one function, so
 // epilogues are compiled per function with no per-element dispatch.

@@ -924,22 +924,30 @@ __global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant_
                                                  const __grid_constant__ CUtensorMap pmap, View4 y, int P,
                                                  int tiles_x, int tiles_per_img, long long n_tiles, int vec_out,
                                                  int *status) {
-  // TMA: the planar patch of the next tile is fetched into the other buffer
-  // while this tile computes (box {40, rows, 3, 1}, x start rounded down to 8)
-  // each buffer starts on a 128-byte boundary (TMA destination alignment)
+  // TMA: the planar patch of the next tile is fetched into the one patch
+  // buffer as soon as this tile's A rows are built, so the copy overlaps the
+  // MMA and the epilogue (box {40, rows, 3, 1}, x start rounded down to 8; the
+  // buffer starts on a 128-byte boundary, the TMA destination alignment).  One
+  // buffer keeps the CTA near 13 KB of shared memory, so 16 CTAs fit an SM and
+  // the 148 * 16 grid runs in one wave.
+  // One block of shared memory laid out by hand (no alignment padding between
+  // arrays): A slices at 0 (1024-aligned, 2 x 4 KB), B slices at 8 KB, the
+  // patch at 9 KB (128-aligned), then the barriers and the TMEM address.
   constexpr int kBufHalves = ((3 * kStemPR * kStemTmaW + 63) / 64) * 64;
-  __shared__ __align__(128) __half patch_t[TMA ? 2 : 1][kBufHalves];
-  __shared__ __align__(8) uint64_t pbar[2];
-  __shared__ __align__(1024) uint8_t a_sm[2][128 * 32];
-  __shared__ __align__(1024) uint8_t b_sm[2][16 * 32];
-  __shared__ __half patch[3][kStemPR][kStemPC + 1];
-  __shared__ __align__(8) uint64_t mma_bar;
-  __shared__ uint32_t tmem_sh;
+  constexpr int kOffB = 2 * 128 * 32, kOffPatch = kOffB + 2 * 16 * 32;
+  constexpr int kOffBar = kOffPatch + (TMA ? kBufHalves * 2 : 0), kSmemBytes = kOffBar + 24;
+  __shared__ __align__(1024) uint8_t stem_sm[kSmemBytes];
+  uint8_t(*const a_sm)[128 * 32] = reinterpret_cast<uint8_t(*)[128 * 32]>(stem_sm);
+  uint8_t(*const b_sm)[16 * 32] = reinterpret_cast<uint8_t(*)[16 * 32]>(stem_sm + kOffB);
+  __half *const patch_t = reinterpret_cast<__half *>(stem_sm + kOffPatch);
+  uint64_t &pbar = *reinterpret_cast<uint64_t *>(stem_sm + kOffBar);
+  uint64_t &mma_bar = *reinterpret_cast<uint64_t *>(stem_sm + kOffBar + 8);
+  uint32_t &tmem_sh = *reinterpret_cast<uint32_t *>(stem_sm + kOffBar + 16);
+  __shared__ __half patch[TMA ? 1 : 3][TMA ? 1 : kStemPR][TMA ? 2 : kStemPC + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     mbar_init(smem_u32(&mma_bar), 1);
-    mbar_init(smem_u32(&pbar[0]), 1);
-    mbar_init(smem_u32(&pbar[1]), 1);
+    mbar_init(smem_u32(&pbar), 1);
     fence_mbar_init();
     if (TMA) tma_prefetch_desc(&pmap);
   }
@@ -962,15 +970,20 @@ __global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant_
   constexpr int pr = (kStemTH - 1) * S + 3, pc = (kStemTW - 1) * S + 3;
   constexpr uint32_t kPatchBytes = (uint32_t)(kStemTmaW * pr * 3 * 2);
   static_assert(kBufHalves * 2 % 128 == 0 && kStemTmaW * pr * 3 <= kBufHalves, "patch buffer");
-  auto issue_patch = [&](long long t, int buf) {  // thread 0
+  auto issue_patch = [&](long long t) {  // thread 0
     const long long img = t / tiles_per_img;
     const int rem = (int)(t - img * tiles_per_img);
     const int iy0 = (rem / tiles_x) * kStemTH * S - P, ix0 = (rem % tiles_x) * kStemTW * S - P;
-    mbar_expect_tx(smem_u32(&pbar[buf]), kPatchBytes);
-    tma_load_4d(smem_u32(&patch_t[buf][0]), &pmap, smem_u32(&pbar[buf]), ix0 & ~7, iy0, 0, (int)img);
+    mbar_expect_tx(smem_u32(&pbar), kPatchBytes);
+    tma_load_4d(smem_u32(&patch_t[0]), &pmap, smem_u32(&pbar), ix0 & ~7, iy0, 0, (int)img);
   };
-  int pending = 0;  // thread 0: a prefetch for the next iteration is in flight
-  if (TMA && tid == 0 && (long long)blockIdx.x < n_tiles) issue_patch(blockIdx.x, 0);
+  // thread 0: the iteration whose patch copy is in flight (copy j completes
+  // phase j of pbar), or -1
+  int in_flight = -1;
+  if (TMA && tid == 0 && (long long)blockIdx.x < n_tiles) {
+    issue_patch(blockIdx.x);
+    in_flight = 0;
+  }
   uint32_t phase = 0;
   int k_iter = 0;
   for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, phase ^= 1u, ++k_iter) {
@@ -978,18 +991,13 @@ __global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant_
     const int rem = (int)(t - img * tiles_per_img);
     const int oy0 = (rem / tiles_x) * kStemTH, ox0 = (rem % tiles_x) * kStemTW;
     const int iy0 = oy0 * S - P, ix0 = ox0 * S - P;
-    const int buf = TMA ? (k_iter & 1) : 0;
     const int xoff = TMA ? ix0 - (ix0 & ~7) : 0;  // window start inside the TMA row
     if (TMA) {
       int bad = 0;
       if (tid == 0) {
-        if (t + gridDim.x < n_tiles) {
-          issue_patch(t + gridDim.x, buf ^ 1);  // freed by the previous iteration
-          pending = 1;
+        if (mbar_wait_poll(smem_u32(&pbar), (uint32_t)k_iter & 1u, 2000000000LL)) {
+          in_flight = -1;
         } else {
-          pending = 0;
-        }
-        if (!mbar_wait_poll(smem_u32(&pbar[buf]), (uint32_t)(k_iter >> 1) & 1u, 2000000000LL)) {
           bad = 1;
           if (status) atomicCAS(status, 0, (int)kStatusTimeoutFull);
         }
@@ -1029,7 +1037,7 @@ __global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant_
         uint16_t lo = 0, hi = 0;
         const int k0 = 2 * j, k1 = 2 * j + 1;
         if (TMA) {  // the box lands as [channel][pr rows][40]
-          const __half *pt = &patch_t[buf][0];
+          const __half *pt = &patch_t[0];
           if (k0 < 27) lo = __half_as_ushort(pt[((k0 / 9) * pr + ty * S + (k0 % 9) / 3) * kStemTmaW + xoff + tx * S + k0 % 3]);
           if (k1 < 27) hi = __half_as_ushort(pt[((k1 / 9) * pr + ty * S + (k1 % 9) / 3) * kStemTmaW + xoff + tx * S + k1 % 3]);
         } else {
@@ -1050,6 +1058,11 @@ __global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant_
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
+      // every thread has read the patch: the next tile's copy may land now
+      if (TMA && t + gridDim.x < n_tiles) {
+        issue_patch(t + gridDim.x);
+        in_flight = k_iter + 1;
+      }
       tc_fence_after();
 #pragma unroll
       for (int sl = 0; sl < 2; ++sl)
@@ -1090,8 +1103,8 @@ __global__ void __launch_bounds__(128) stem_tc_k(View4 x, const __grid_constant_
     tc_fence_before();
     __syncthreads();  // patch, A tile and accumulator are reused by the next tile
   }
-  if (TMA && tid == 0 && pending)  // only after an early exit: let the last prefetch land (bounded)
-    mbar_wait_poll(smem_u32(&pbar[(k_iter + 1) & 1]), (uint32_t)((k_iter + 1) >> 1) & 1u, 400000000LL);
+  if (TMA && tid == 0 && in_flight >= 0)  // only after an early exit: let the last copy land (bounded)
+    mbar_wait_poll(smem_u32(&pbar), (uint32_t)in_flight & 1u, 400000000LL);
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
@@ -1120,15 +1133,13 @@ cudaError_t launch_stem_tc_fn(View4 x, const StemTcParams &p, View4 y, int batch
     tma = encode_tiled_f16(&map, 4, x.ptr, dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_NONE, &err);
   }
   const dim3 g((unsigned)grid), b(128);
-  if (S == 2)
-    return tma ? launch_kernel(stem_tc_k<FN, 2, true>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y,
-                               n_tiles, vec_out, status)
-               : launch_kernel(stem_tc_k<FN, 2, false>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y,
-                               n_tiles, vec_out, status);
-  return tma ? launch_kernel(stem_tc_k<FN, 1, true>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y, n_tiles,
-                             vec_out, status)
-             : launch_kernel(stem_tc_k<FN, 1, false>, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y,
-                             n_tiles, vec_out, status);
+  // 16 CTAs of ~14 KB shared memory per SM (one wave) need the largest carveout
+  static std::atomic<bool> carve[4][kAttrMaxDevices];
+  auto kern = S == 2 ? (tma ? stem_tc_k<FN, 2, true> : stem_tc_k<FN, 2, false>)
+                     : (tma ? stem_tc_k<FN, 1, true> : stem_tc_k<FN, 1, false>);
+  const cudaError_t ce = ensure_smem_carveout(kern, 100, carve[(S == 2 ? 2 : 0) + (tma ? 1 : 0)]);
+  if (ce != cudaSuccess) return ce;
+  return launch_kernel(kern, g, b, 0, st, x, p, map, y, P, tiles_x, tiles_x * tiles_y, n_tiles, vec_out, status);
 }
 
 // ------------------------------------------------------------------ conversions
