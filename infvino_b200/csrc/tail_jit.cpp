@@ -148,12 +148,22 @@ typedef unsigned short h16;
 __device__ __forceinline__ float h2f(h16 h) { float f; asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h)); return f; }
 __device__ __forceinline__ h16 f2h(float f) { h16 h; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f)); return h; }
 __device__ __forceinline__ float rh(float f) { return h2f(f2h(f)); }
+// a / b with rb = RN(1 / b) (__frcp_rn) shared by several quotients: Markstein's
+// method (P. Markstein, IBM J. Res. Dev. 34(1), 1990): q = RN(a rb), the exact
+// residual r = a - b q by one FMA, then RN(q + r rb) is the correctly rounded
+// a / b while q and r stay in the normal range.  Used where a in [0, 1] and
+// b in [1, 16] (the DFL softmax): a quotient below the normal range rounds to
+// fp16 zero either way.
+__device__ __forceinline__ float div_rcp(float a, float b, float rb) {
+  const float q = a * rb;
+  return fmaf(fmaf(-q, b, a), rb, q);
+}
 struct TailArgs { const h16 *leaf[8]; h16 *out; int batch; int blk0[33]; };
 )";
 
 std::string unop_expr(int op, const std::string &v) {
   switch (op) {
-    case 0: return "1.0f / (1.0f + expf(-" + v + "))";
+    case 0: return "__frcp_rn(1.0f + expf(-" + v + "))";  // 1 / x correctly rounded, as the division
     case 1: return v + " / (1.0f + expf(-" + v + "))";
     case 2: return "fmaxf(" + v + ", 0.0f)";
     case 3: return v + " * fminf(fmaxf(" + v + " + 3.0f, 0.0f), 6.0f) / 6.0f";
@@ -169,7 +179,7 @@ std::string gemm_act_expr(int act, const std::string &f) {
     case 2: return "fmaxf(" + f + ", 0.0f)";
     case 3: return f + " * fminf(fmaxf(" + f + " + 3.0f, 0.0f), 6.0f) / 6.0f";
     case 4: return "fminf(fmaxf(" + f + " + 3.0f, 0.0f), 6.0f) / 6.0f";
-    case 5: return "1.0f / (1.0f + expf(-" + f + "))";
+    case 5: return "__frcp_rn(1.0f + expf(-" + f + "))";
     default: return f;
   }
 }
@@ -283,9 +293,10 @@ std::string tail_jit_source(const TailProgram &P, const TailJitLayout &L) {
              << "#pragma unroll\n      for (int q = 0; q < 16; ++q) m = fmaxf(m, e[q][j]);\n"
              << "      float s = 0.0f;\n"
              << "#pragma unroll\n      for (int q = 0; q < 16; ++q) { e[q][j] = expf(e[q][j] - m); s += e[q][j]; }\n"
+             << "      const float rs = __frcp_rn(s);  // e / s below: e in [0, 1], s in [1, 16]\n"
              << "      float acc = 0.0f;\n";
           for (int q = 0; q < 16; ++q)
-            os << "      acc = fmaf(rh(e[" << q << "][j] / s), " << flit(D.w[q]) << ", acc);\n";
+            os << "      acc = fmaf(rh(div_rcp(e[" << q << "][j], s, rs)), " << flit(D.w[q]) << ", acc);\n";
           os << "      const float v = rh(acc) + " << flit(D.bias) << ";\n"
              << "      const float f = rh(v);\n"
              << "      " << r << "[j] = rh(" << gemm_act_expr(D.act, "f") << ");\n"
