@@ -343,70 +343,130 @@ __global__ void __launch_bounds__(128) gap_nhwc8_k(View4 x, __half *__restrict__
 }
 
 // Batched matmul Y[z] = A[z] B[z] on the CUDA cores in 64 x 64 output tiles
-// (4 x 4 per thread), K in 32-wide slices staged in shared memory as f32.
-// Every output accumulates its K products in order with one fused multiply-add
-// each, as bmm_k does, so the two kernels agree bit for bit.  TA / TB: the
-// operand is stored transposed (A as [K][M], B as [N][K]), which lets a
-// transposing permute that only feeds this product be folded into it.
+// (4 x 4 per thread), K in 32-wide slices staged in shared memory as f32, two
+// slice buffers: the next slice's global loads (one 16-byte load per operand
+// per thread, eight halves) are in flight while the current slice computes.
+// Every output accumulates its K products in order with one fused
+// multiply-add each, as bmm_k does, so the two kernels agree bit for bit.
+// TA / TB: the operand is stored transposed (A as [K][M], B as [N][K]), which
+// lets a transposing permute that only feeds this product be folded into it.
+// `vec`: both operands' rows and batch offsets are 16-byte aligned, so full
+// eight-half chunks are read with one load (edge chunks element by element).
+constexpr int kBmmT = 64, kBmmKT = 32, kBmmPad = 68;  // rows of 68 floats: aligned float4 reads
+// One operand's slice: 64 rows (m or n) x 32 k as eight-half chunks, one per
+// thread.  K-contiguous storage ([rows][K]): thread t takes row t % 64 and k
+// chunk (t / 64) * 8 (stores across consecutive rows, no bank conflicts);
+// row-contiguous storage ([K][rows]): k = t / 8, rows (t % 8) * 8 .. +7.
+template <bool KCONTIG>
+__device__ __forceinline__ void bmm_load_slice(const __half *__restrict__ base, int rows, int K, int r0, int k0,
+                                               bool vec, float (&v)[8]) {
+  const int t = threadIdx.x;
+  const int r = KCONTIG ? r0 + (t & 63) : r0 + (t & 7) * 8;
+  const int k = KCONTIG ? k0 + (t >> 6) * 8 : k0 + (t >> 3);
+  if (KCONTIG) {  // eight k of one row
+    if (r < rows && vec && k + 8 <= K) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(base + (long long)r * K + k));
+      const __half *h = reinterpret_cast<const __half *>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __half2float(h[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = (r < rows && k + j < K) ? __half2float(base[(long long)r * K + k + j]) : 0.0f;
+    }
+  } else {  // eight rows of one k
+    if (k < K && vec && r + 8 <= rows) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(base + (long long)k * rows + r));
+      const __half *h = reinterpret_cast<const __half *>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __half2float(h[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = (k < K && r + j < rows) ? __half2float(base[(long long)k * rows + r + j]) : 0.0f;
+    }
+  }
+}
+template <bool KCONTIG>
+__device__ __forceinline__ void bmm_store_slice(float (*S)[kBmmPad], const float (&v)[8]) {
+  const int t = threadIdx.x;
+  if (KCONTIG) {
+    const int r = t & 63, k = (t >> 6) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) S[k + j][r] = v[j];
+  } else {
+    const int k = t >> 3, r = (t & 7) * 8;
+    *reinterpret_cast<float4 *>(&S[k][r]) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4 *>(&S[k][r + 4]) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
 template <bool TA, bool TB>
 __global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A, const __half *__restrict__ B,
                                                    __half *__restrict__ Y, int B1, int M, int K, int N, long long a_bs,
-                                                   long long b_bs, int tiles_m, int tiles_n) {
+                                                   long long b_bs, int tiles_m, int tiles_n, int vec) {
   pdl_wait_and_release();
-  constexpr int TM = 64, TN = 64, KT = 32;
-  __shared__ __align__(16) float As[KT][TM + 4];  // rows of 68 floats: 16-byte aligned float4 reads
-  __shared__ __align__(16) float Bs[KT][TN + 4];
+  __shared__ __align__(16) float As[2][kBmmKT][kBmmPad];  // As[k][m]
+  __shared__ __align__(16) float Bs[2][kBmmKT][kBmmPad];  // Bs[k][n]
   const int tile = blockIdx.x % (tiles_m * tiles_n);
   const long long z = blockIdx.x / (tiles_m * tiles_n);  // b0 * B1 + b1
   const long long b0 = z / B1, b1 = z - b0 * B1;
-  const int m0 = (tile / tiles_n) * TM, n0 = (tile % tiles_n) * TN;
+  const int m0 = (tile / tiles_n) * kBmmT, n0 = (tile % tiles_n) * kBmmT;
   const __half *Az = A + b0 * a_bs + b1 * (long long)M * K;
   const __half *Bz = B + b0 * b_bs + b1 * (long long)K * N;
   __half *Yz = Y + z * (long long)M * N;
+  const bool vc = vec != 0;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // outputs m0 + 4 ty + i, n0 + 4 tx + j
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-  for (int k0 = 0; k0 < K; k0 += KT) {
-    const int kl = min(KT, K - k0);
-    for (int e = threadIdx.x; e < KT * TM; e += 256) {  // A slice -> As[k][m]
-      int kk, mm;
-      if (TA) { kk = e / TM; mm = e - kk * TM; } else { mm = e / KT; kk = e - mm * KT; }
-      const int gm = m0 + mm, gk = k0 + kk;
-      float v = 0.0f;
-      if (gm < M && kk < kl) v = __half2float(TA ? Az[(long long)gk * M + gm] : Az[(long long)gm * K + gk]);
-      As[kk][mm] = v;
+  // A non-transposed is [M][K] (K-contiguous); B transposed is [N][K] (K-contiguous)
+  float va[8], vb[8];
+  bmm_load_slice<!TA>(Az, M, K, m0, 0, vc, va);
+  bmm_load_slice<TB>(Bz, N, K, n0, 0, vc, vb);
+  bmm_store_slice<!TA>(As[0], va);
+  bmm_store_slice<TB>(Bs[0], vb);
+  __syncthreads();
+  int cur = 0;
+  for (int k0 = 0; k0 < K; k0 += kBmmKT) {
+    const bool more = k0 + kBmmKT < K;
+    if (more) {  // the next slice's loads fly while this one computes
+      bmm_load_slice<!TA>(Az, M, K, m0, k0 + kBmmKT, vc, va);
+      bmm_load_slice<TB>(Bz, N, K, n0, k0 + kBmmKT, vc, vb);
     }
-    for (int e = threadIdx.x; e < KT * TN; e += 256) {  // B slice -> Bs[k][n]
-      int kk, nn;
-      if (TB) { nn = e / KT; kk = e - nn * KT; } else { kk = e / TN; nn = e - kk * TN; }
-      const int gn = n0 + nn, gk = k0 + kk;
-      float v = 0.0f;
-      if (gn < N && kk < kl) v = __half2float(TB ? Bz[(long long)gn * K + gk] : Bz[(long long)gk * N + gn]);
-      Bs[kk][nn] = v;
-    }
-    __syncthreads();
+    const int kl = min(kBmmKT, K - k0);
     for (int kk = 0; kk < kl; ++kk) {
-      const float4 av = *reinterpret_cast<const float4 *>(&As[kk][4 * ty]);
-      const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][4 * tx]);
+      const float4 av = *reinterpret_cast<const float4 *>(&As[cur][kk][4 * ty]);
+      const float4 bv = *reinterpret_cast<const float4 *>(&Bs[cur][kk][4 * tx]);
       const float a[4] = {av.x, av.y, av.z, av.w}, b[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
     }
+    if (more) {  // the other buffer was last read before the previous barrier
+      bmm_store_slice<!TA>(As[cur ^ 1], va);
+      bmm_store_slice<TB>(Bs[cur ^ 1], vb);
+    }
     __syncthreads();
+    cur ^= 1;
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int gm = m0 + 4 * ty + i;
     if (gm >= M) continue;
+    const int gn = n0 + 4 * tx;
+    __half *yr = Yz + (long long)gm * N;
+    if (vc && (N & 3) == 0 && gn + 4 <= N) {  // four consecutive outputs, 8 bytes
+      const __half2 lo = __floats2half2_rn(acc[i][0], acc[i][1]), hi = __floats2half2_rn(acc[i][2], acc[i][3]);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t *>(&lo);
+      u.y = *reinterpret_cast<const uint32_t *>(&hi);
+      *reinterpret_cast<uint2 *>(yr + gn) = u;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + 4 * tx + j;
-      if (gn < N) Yz[(long long)gm * N + gn] = __float2half_rn(acc[i][j]);
+      for (int j = 0; j < 4; ++j)
+        if (gn + j < N) yr[gn + j] = __float2half_rn(acc[i][j]);
     }
   }
 }
@@ -1796,14 +1856,20 @@ cudaError_t launch_gap_v4(View4 x, __half *y, int batch, cudaStream_t st) {
 }
 cudaError_t launch_bmm_t(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
                          long long a_bs, long long b_bs, int ta, int tb, cudaStream_t st) {
-  const int tiles_m = (M + 63) / 64, tiles_n = (N + 63) / 64;
+  const int tiles_m = (M + kBmmT - 1) / kBmmT, tiles_n = (N + kBmmT - 1) / kBmmT;
   const long long blocks = (long long)batch * B1 * tiles_m * tiles_n;
   if (blocks >= (1LL << 31)) return cudaErrorInvalidValue;
+  // 16-byte chunks: aligned bases and batch offsets, rows of a multiple of 8 halves
+  const int a_row = ta ? M : K, b_row = tb ? K : N;
+  const int vec = (al16(A) && al16(B) && al16(Y) && a_bs % 8 == 0 && b_bs % 8 == 0 && ((long long)M * K) % 8 == 0 &&
+                   ((long long)K * N) % 8 == 0 && ((long long)M * N) % 8 == 0 && a_row % 8 == 0 && b_row % 8 == 0)
+                      ? 1
+                      : 0;
   const dim3 g((unsigned)blocks), b(256);
-  if (ta && tb) launch_kernel(bmm_tiled_k<true, true>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
-  else if (ta) launch_kernel(bmm_tiled_k<true, false>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
-  else if (tb) launch_kernel(bmm_tiled_k<false, true>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
-  else launch_kernel(bmm_tiled_k<false, false>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n);
+  if (ta && tb) launch_kernel(bmm_tiled_k<true, true>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n, vec);
+  else if (ta) launch_kernel(bmm_tiled_k<true, false>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n, vec);
+  else if (tb) launch_kernel(bmm_tiled_k<false, true>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n, vec);
+  else launch_kernel(bmm_tiled_k<false, false>, g, b, 0, st, A, B, Y, B1, M, K, N, a_bs, b_bs, tiles_m, tiles_n, vec);
   return cudaGetLastError();
 }
 cudaError_t launch_bmm(const __half *A, const __half *B, __half *Y, int batch, int B1, int M, int K, int N,
