@@ -616,20 +616,23 @@ __global__ void __launch_bounds__(256) depthwise_nhwc8_rows_k(View4 x, const __h
 }
 
 // Depthwise K x K (3 or 5), stride S (1 or 2), channels-last, in strips: a
-// thread computes four neighbouring output pixels of one 8-channel group, so
-// each weight vector is loaded once for the four and each input vector once
-// per kernel row for all the outputs that use it.  Same fp32 accumulation
+// thread computes kDwNhwcStrip neighbouring output pixels of one 8-channel
+// group, so each weight vector is loaded once for them and each input vector
+// once per kernel row for all the outputs that use it (two outputs keep the
+// registers at 80, three blocks per SM, which measured faster than four
+// outputs at two blocks per SM).  Same fp32 accumulation
 // order (ky, kx), same skipped padding taps and epilogue as above, so the
 // results are identical.  Threads run over (output row, strip, channel
 // group) with the channel group fastest (consecutive threads, consecutive
 // 16-byte vectors).
+constexpr int kDwNhwcStrip = 2;  // outputs per thread of the channels-last strip kernel
 template <int FN, int K, int S>
 __global__ void __launch_bounds__(256) depthwise_nhwc8_strip_k(View4 x, const __half *__restrict__ w,
                                                               const __half *__restrict__ bias, View4 y,
                                                               long long items, int P, int C8, int strips,
                                                               DwDiv d_item, DwDiv d_c8, DwDiv d_ho) {
   pdl_wait_and_release();
-  constexpr int NX = 3 * S + K;  // input columns the four outputs read
+  constexpr int NO = kDwNhwcStrip, NX = (NO - 1) * S + K;  // input columns the NO outputs read
   const int per_row = strips * C8;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < items;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -638,11 +641,11 @@ __global__ void __launch_bounds__(256) depthwise_nhwc8_strip_k(View4 x, const __
     const uint32_t sx = dw_div(it, d_c8);
     const int c = (int)(it - sx * (uint32_t)C8) * 8;
     const uint32_t b = dw_div(r, d_ho);
-    const int oy = (int)(r - b * (uint32_t)y.H), ox0 = (int)sx * 4;
+    const int oy = (int)(r - b * (uint32_t)y.H), ox0 = (int)sx * NO;
     const __half *xb = x.ptr + (long long)b * x.sb + c;
-    float acc[4][8];
+    float acc[NO][8];
 #pragma unroll
-    for (int o = 0; o < 4; ++o)
+    for (int o = 0; o < NO; ++o)
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[o][j] = 0.0f;
 #pragma unroll
@@ -663,7 +666,7 @@ __global__ void __launch_bounds__(256) depthwise_nhwc8_strip_k(View4 x, const __
         const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(w + (ky * K + kx) * y.C + c));
         const __half *wh = reinterpret_cast<const __half *>(&wv);
 #pragma unroll
-        for (int o = 0; o < 4; ++o) {
+        for (int o = 0; o < NO; ++o) {
           const int q = o * S + kx;
           if (!ok[q]) continue;
           const __half *xh = reinterpret_cast<const __half *>(&xv[q]);
@@ -677,7 +680,7 @@ __global__ void __launch_bounds__(256) depthwise_nhwc8_strip_k(View4 x, const __
     for (int j = 0; j < 8; ++j) bv[j] = bias ? __half2float(__ldg(bias + c + j)) : 0.0f;
     __half *yrow = y.ptr + (long long)b * y.sb + (long long)oy * y.sy + c;
 #pragma unroll
-    for (int o = 0; o < 4; ++o) {
+    for (int o = 0; o < NO; ++o) {
       if (ox0 + o >= y.W) break;
       __align__(16) __half out[8];
 #pragma unroll
@@ -1902,17 +1905,18 @@ cudaError_t launch_depthwise_v4(View4 x, const __half *w, const __half *bias, Vi
     d.m = (uint32_t)(((1ull << (31 + sh)) / dv) + 1ull);
     return d;
   };
-  const int strips = (y.W + 3) / 4;
-  const long long strip_items = rows_nhwc * strips * (y.C / 8);
+  const int strips = (y.W + 3) / 4;  // planar strips of four
+  const int nstrips = (y.W + kDwNhwcStrip - 1) / kDwNhwcStrip;
+  const long long strip_items = rows_nhwc * nstrips * (y.C / 8);
   // strips when they still fill the GPU twice over (at small batch the
   // one-pixel-per-thread rows kernel below has the shorter critical path)
   if (vec && known && (K == 3 || K == 5) && (S == 1 || S == 2) && strip_items < (1LL << 31) &&
       strip_items >= 148LL * 512) {
     const int C8 = y.C / 8;
-    const DwDiv di = make_div((uint32_t)(strips * C8)), dc = make_div((uint32_t)C8), dh = make_div((uint32_t)y.H);
+    const DwDiv di = make_div((uint32_t)(nstrips * C8)), dc = make_div((uint32_t)C8), dh = make_div((uint32_t)y.H);
     const unsigned blocks = (unsigned)std::min<long long>((strip_items + 255) / 256, 148LL * 64);
 #define IVB_DW_STRIP(F, KK, SS) \
-  launch_kernel(depthwise_nhwc8_strip_k<F, KK, SS>, dim3(blocks), dim3(256), 0, st, x, w, bias, y, strip_items, P, C8, strips, di, dc, dh)
+  launch_kernel(depthwise_nhwc8_strip_k<F, KK, SS>, dim3(blocks), dim3(256), 0, st, x, w, bias, y, strip_items, P, C8, nstrips, di, dc, dh)
 #define IVB_DW_STRIP_KS(F)                                   \
   do {                                                       \
     if (K == 3 && S == 1) IVB_DW_STRIP(F, 3, 1);             \
