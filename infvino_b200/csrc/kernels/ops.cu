@@ -570,6 +570,42 @@ struct DwDiv {
   uint32_t m, s;  // q = (n * m) >> (31 + s), exact for n < 2^31
 };
 __device__ __forceinline__ uint32_t dw_div(uint32_t n, DwDiv d) { return (uint32_t)(((uint64_t)n * d.m) >> (31u + d.s)); }
+inline DwDiv dw_make_div(uint32_t dv) {  // host: the multiplier and shift of division by dv >= 1
+  DwDiv d{0u, 0u};
+  uint32_t sh = 0;
+  while ((1ull << sh) < dv) ++sh;
+  d.s = sh;
+  d.m = (uint32_t)(((1ull << (31 + sh)) / dv) + 1ull);
+  return d;
+}
+
+// ew_binary_flat_k eight elements at a time: 16-byte loads and stores, the
+// image of a chunk from a 32-bit multiply-high division (per_img and the
+// batch offsets are multiples of 8, so a chunk never straddles two images);
+// each element is the same f32 operation rounded once.
+__global__ void ew_binary_flat8_k(const __half *__restrict__ a, const __half *__restrict__ b, __half *__restrict__ y,
+                                  long long n8, int op, int b_scalar, uint32_t per8, long long a_bs, long long b_bs,
+                                  DwDiv d_per8) {
+  pdl_wait_and_release();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    const uint32_t img = dw_div((uint32_t)i, d_per8), r = ((uint32_t)i - img * per8) * 8u;
+    const uint4 au = *reinterpret_cast<const uint4 *>(a + (long long)img * a_bs + r);
+    uint4 bu;
+    if (b_scalar) {
+      const __half s = b[(long long)img * b_bs];
+      const __half2 s2 = __halves2half2(s, s);
+      bu.x = bu.y = bu.z = bu.w = *reinterpret_cast<const uint32_t *>(&s2);
+    } else {
+      bu = *reinterpret_cast<const uint4 *>(b + (long long)img * b_bs + r);
+    }
+    const __half *ah = reinterpret_cast<const __half *>(&au), *bh = reinterpret_cast<const __half *>(&bu);
+    uint4 ou;
+    __half *oh = reinterpret_cast<__half *>(&ou);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) oh[j] = __float2half_rn(binop(__half2float(ah[j]), __half2float(bh[j]), op));
+    *reinterpret_cast<uint4 *>(y + i * 8) = ou;
+  }
+}
 
 template <int FN>
 __device__ __forceinline__ __half dw_epilogue(float acc, float bias) {
@@ -1686,6 +1722,14 @@ inline long long numel4(const View4 &v, int batch) { return (long long)batch * v
 cudaError_t launch_ew_binary_flat(const __half *a, const __half *b, __half *y, long long n, int op, int b_scalar,
                                   long long per_img, int batch, long long a_bs, long long b_bs, cudaStream_t st) {
   (void)batch;
+  if (per_img % 8 == 0 && a_bs % 8 == 0 && (b_scalar || b_bs % 8 == 0) && al16(a) && al16(y) && (b_scalar || al16(b)) &&
+      n / 8 < (1LL << 31) && per_img >= 8) {
+    const long long n8 = n / 8;
+    const uint32_t per8 = (uint32_t)(per_img / 8);
+    launch_kernel(ew_binary_flat8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, a, b, y, n8, op, b_scalar, per8, a_bs,
+                  b_bs, dw_make_div(per8));
+    return cudaGetLastError();
+  }
   launch_kernel(ew_binary_flat_k, dim3(grid_for(n)), dim3(kThreads), 0, st, a, b, y, n, op, b_scalar, per_img, a_bs, b_bs);
   return cudaGetLastError();
 }
