@@ -1437,6 +1437,38 @@ __global__ void ew_binary_nhwc8_k(View4 a, View4 b, View4 y, long long n8, int o
   }
 }
 
+// Binary op into a channels-last output whose operands need not be
+// channels-last (a planar operand, as where YOLO11's attention adds the planar
+// product to the channels-last `pe` conv): a thread writes eight channels of
+// one pixel, threads run over pixels fastest, so a planar operand's eight
+// scalar loads are each coalesced across the warp; a channels-last operand is
+// one 16-byte load.  32-bit indices through multiply-high divisions.
+__device__ __forceinline__ void ew_load8(const View4 &v, bool vec, int b, int y, int x, int c, __half (&h)[8]) {
+  if (vec) {
+    *reinterpret_cast<uint4 *>(h) = *reinterpret_cast<const uint4 *>(v.ptr + at8(v, b, y, x, c));
+  } else {
+    const __half *p = v.ptr + (long long)b * v.sb + (long long)y * v.sy + (long long)x * v.sx;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = p[(long long)(c + j) * v.sc];
+  }
+}
+__global__ void ew_binary_mixed8_k(View4 a, View4 b, View4 y, int n8, int op, int a_vec, int b_vec, DwDiv d_w,
+                                   DwDiv d_hw, DwDiv d_c8) {
+  pdl_wait_and_release();
+  const uint32_t HW = (uint32_t)(y.H * y.W), C8 = (uint32_t)(y.C / 8);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += gridDim.x * blockDim.x) {
+    const uint32_t rest = dw_div((uint32_t)i, d_hw), p = (uint32_t)i - rest * HW;
+    const uint32_t img = dw_div(rest, d_c8), c = (rest - img * C8) * 8u;
+    const uint32_t yy = dw_div(p, d_w), xx = p - yy * (uint32_t)y.W;
+    __align__(16) __half ah[8], bh[8], o[8];
+    ew_load8(a, a_vec != 0, (int)img, (int)yy, (int)xx, (int)c, ah);
+    ew_load8(b, b_vec != 0, (int)img, (int)yy, (int)xx, (int)c, bh);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(binop(__half2float(ah[j]), __half2float(bh[j]), op));
+    *reinterpret_cast<uint4 *>(y.ptr + at8(y, (int)img, (int)yy, (int)xx, (int)c)) = *reinterpret_cast<const uint4 *>(o);
+  }
+}
+
 __global__ void ew_unary_nhwc8_k(View4 x, View4 y, long long n8, int op) {
   pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -1743,6 +1775,13 @@ cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cu
       launch_kernel(ew_binary_nhwc8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, a, b, y, n8, op, bpix ? 1 : 0, bscalar ? 1 : 0);
       return cudaGetLastError();
     }
+  }
+  if (vec8_ok(y) && numel4(y, batch) / 8 < (1LL << 31) && y.H * y.W >= 1) {  // channels-last output, mixed operands
+    const long long n8 = numel4(y, batch) / 8;
+    launch_kernel(ew_binary_mixed8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, a, b, y, (int)n8, op,
+                  vec8_ok(a) ? 1 : 0, vec8_ok(b) ? 1 : 0, dw_make_div((uint32_t)y.W),
+                  dw_make_div((uint32_t)(y.H * y.W)), dw_make_div((uint32_t)(y.C / 8)));
+    return cudaGetLastError();
   }
   const long long n = numel4(y, batch);
   launch_kernel(ew_binary_v4_k, dim3(grid_for(n)), dim3(kThreads), 0, st, a, b, y, n, op, cfast_of(y));
