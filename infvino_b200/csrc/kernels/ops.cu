@@ -607,10 +607,13 @@ __global__ void ew_binary_flat8_k(const __half *__restrict__ a, const __half *__
   }
 }
 
+// SiLU in the MUFU form the tensor-core epilogue uses (relative error below
+// 2^-19: the fp16 result is the correctly rounded one or its neighbour), the
+// other activations in the reference expression.
 template <int FN>
 __device__ __forceinline__ __half dw_epilogue(float acc, float bias) {
-  const float v = __half2float(__float2half_rn(acc)) + bias;
-  return __float2half_rn(act_exact<FN>(__half2float(__float2half_rn(v))));
+  const float v = __half2float(__float2half_rn(__half2float(__float2half_rn(acc)) + bias));
+  return __float2half_rn(FN == kFnSilu ? silu_fast(v) : act_exact<FN>(v));
 }
 
 template <int FN>
