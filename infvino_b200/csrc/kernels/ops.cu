@@ -1779,7 +1779,8 @@ cudaError_t launch_ew_binary_v4(View4 a, View4 b, View4 y, int batch, int op, cu
       return cudaGetLastError();
     }
   }
-  if (vec8_ok(y) && numel4(y, batch) / 8 < (1LL << 31) && y.H * y.W >= 1) {  // channels-last output, mixed operands
+  if (vec8_ok(y) && y.C >= 8 && y.H >= 1 && y.W >= 1 && batch >= 1 &&
+      numel4(y, batch) / 8 < (1LL << 31)) {  // channels-last output, mixed operands
     const long long n8 = numel4(y, batch) / 8;
     launch_kernel(ew_binary_mixed8_k, dim3(grid_for(n8)), dim3(kThreads), 0, st, a, b, y, (int)n8, op,
                   vec8_ok(a) ? 1 : 0, vec8_ok(b) ? 1 : 0, dw_make_div((uint32_t)y.W),
