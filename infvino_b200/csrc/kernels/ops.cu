@@ -352,6 +352,8 @@ __global__ void __launch_bounds__(128) gap_nhwc8_k(View4 x, __half *__restrict__
 // lets a transposing permute that only feeds this product be folded into it.
 // `vec`: both operands' rows and batch offsets are 16-byte aligned, so full
 // eight-half chunks are read with one load (edge chunks element by element).
+// At most 64 registers, so four blocks share an SM: YOLO11's v·attnᵀ launch
+// (896 blocks) then runs in two waves instead of three.
 constexpr int kBmmT = 64, kBmmKT = 32, kBmmPad = 68;  // rows of 68 floats: aligned float4 reads
 // One operand's slice: 64 rows (m or n) x 32 k as eight-half chunks, one per
 // thread.  K-contiguous storage ([rows][K]): thread t takes row t % 64 and k
@@ -400,7 +402,7 @@ __device__ __forceinline__ void bmm_store_slice(float (*S)[kBmmPad], const float
 }
 
 template <bool TA, bool TB>
-__global__ void __launch_bounds__(256) bmm_tiled_k(const __half *__restrict__ A, const __half *__restrict__ B,
+__global__ void __launch_bounds__(256, 4) bmm_tiled_k(const __half *__restrict__ A, const __half *__restrict__ B,
                                                    __half *__restrict__ Y, int B1, int M, int K, int N, long long a_bs,
                                                    long long b_bs, int tiles_m, int tiles_n, int vec) {
   pdl_wait_and_release();
