@@ -1382,8 +1382,11 @@ void Engine::lower() {
         ConvGeom gt;
         if (conv_geom(t, 1, &gt)) modes.push_back(t);
       }
+      // (convs over at most 16 pixels, such as the SE blocks' fully connected
+      // layers, also try 8 and 16 N tiles: with one M tile per image batch
+      // they have few tiles, and narrower ones spread over more SMs)
       if (c.n_tiles == 1 && np16 >= 64)
-        for (int sp = 2; sp <= 4; sp *= 2) {
+        for (int sp = 2; sp <= (c.Ho * c.Wo <= 16 ? 16 : 4); sp *= 2) {
           ConvCfg t = c;
           t.BN = (int)round_up((np16 + sp - 1) / sp, 16);
           t.n_tiles = (np16 + t.BN - 1) / t.BN;
