@@ -682,7 +682,7 @@ int conv_nteams(const ConvCfg &c, long long tiles, int sms) {
 constexpr double kTileCost = 2.0;
 constexpr double kSingleBufCost = 1.25;
 constexpr double kOtherTeamsCost = 1.5;
-constexpr int kConvTuneCands = 10;  // geometries timed by the load-time tuning
+constexpr int kConvTuneCands = 16;  // geometries timed by the load-time tuning
 struct ConvCand {
   ConvGeom g;
   int nteams = 1, nbuf = 1;
@@ -1596,7 +1596,7 @@ void Engine::lower() {
         std::vector<ConvCand> cands;
         for (size_t mi = 0; mi < modes.size(); ++mi) {
           std::vector<ConvCand> cm = conv_candidates(modes[mi], B, sms);
-          const size_t keep = mi > 0 ? 2 : modes.size() == 1 ? (size_t)kConvTuneCands : (size_t)kConvTuneCands - 4;
+          const size_t keep = mi > 0 ? 3 : modes.size() == 1 ? (size_t)kConvTuneCands : (size_t)kConvTuneCands - 4;
           for (size_t k = 0; k < cm.size() && k < keep; ++k) {
             cm[k].mode = (int)mi;
             cands.push_back(cm[k]);
@@ -1619,7 +1619,7 @@ void Engine::lower() {
           if (launch_conv_tc(a, grid, s) != cudaSuccess) continue;  // warm-up
           cudaEventRecord(e0, s);
           bool ok = true;
-          for (int r = 0; r < 3 && ok; ++r) ok = launch_conv_tc(a, grid, s) == cudaSuccess;
+          for (int r = 0; r < 6 && ok; ++r) ok = launch_conv_tc(a, grid, s) == cudaSuccess;
           cudaEventRecord(e1, s);
           if (!ok || cudaEventSynchronize(e1) != cudaSuccess) continue;
           float ms = 0.0f;
